@@ -1,0 +1,364 @@
+"""Benchmark of the MoE feed-forward layer (ornith-flight's hot path) on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload decode1|decode32]
+                    [--impl ours|reference]
+
+A step = one MoE layer forward (router, softmax/top-8/renormalise, dispatch,
+Q4_K/Q6_K expert SwiGLU, sigmoid-gated shared expert, weighted combine) over
+one batch of synthetic tokens, on the 2048-hidden, 256-expert, top-8 layer of
+BASELINE.json. Default workload: decode batch 1 (config 1).
+
+Timing: W untimed warm-up steps, then exactly K steps bracketed by a barrier
+and torch.cuda.synchronize(), timed with CUDA events on the launching stream;
+max over ranks. Step i runs layer copy i % L: L seeded layer copies (each
+522 MB of expert weights, > 8 GB in total) rotate so that no step finds its
+experts in the 126 MB L2 ("rotate" in config). Multi-GPU: one independent
+replica per GPU (weak scaling; the decode layer has no exchange step).
+
+--impl reference times the reference's CPU implementation of the same layer:
+the reference's own engine/src/gguf.c (compiled unmodified into oracle/_ref)
+for the expert dequant plus the C restatement of model.c:992-1143, on all
+host cores (one process per core), rank 0 only.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import multiprocessing as mp
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "oracle"))
+
+WORKLOADS = {
+    "decode1": dict(tokens=1, config="BASELINE config 1: decode batch 1"),
+    "decode32": dict(tokens=32, config="BASELINE config 2: decode batch 32"),
+}
+D, H, E, K = 2048, 512, 256, 8
+EXPERT_BYTES = 2 * (H * D // 256) * 144 + (H * D // 256) * 210  # 2,039,808
+
+
+def algorithmic_bytes(tokens: int, n_experts_touched: int) -> int:
+    # weights of the touched routed experts + shared expert + router + gate
+    # vector + x in and out (decode config 1: 20,480,000 B)
+    return (n_experts_touched * EXPERT_BYTES + EXPERT_BYTES + E * D * 4 + D * 4
+            + 2 * tokens * D * 4)
+
+
+def load_ofb():
+    import importlib.util
+    spec = importlib.util.spec_from_file_location(
+        "ornith_flight_b200.ofb", os.path.join(ROOT, "ornith-flight_b200", "ofb.py"))
+    mod = importlib.util.module_from_spec(spec)
+    sys.modules[spec.name] = mod
+    spec.loader.exec_module(mod)
+    return mod
+
+
+def peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return p["hbm_gbs"], "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled every 200 ms."""
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.Q}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except Exception:
+            self.proc = None
+        return self
+
+    def __exit__(self, *a):
+        self.lines = []
+        if self.proc:
+            self.proc.terminate()
+            try:
+                out, _ = self.proc.communicate(timeout=5)
+            except Exception:
+                self.proc.kill()
+                out = ""
+            self.lines = [l for l in out.splitlines() if l.strip()]
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for l in getattr(self, "lines", []):
+            f = [x.strip() for x in l.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = float(f[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ---------------------------------------------------------------- CPU arms ---
+
+def _cpu_worker(args):
+    seed, seconds, tokens_per_call, use_ref = args
+    import numpy as np
+    import binding
+    ofb = load_ofb()
+    if use_ref:
+        binding.use_reference_dequant(True)
+    shape = ofb.LayerShape()
+    lw = ofb.make_layer(shape, seed=seed, device="cpu")
+    w = {k: (None if v is None else v.numpy()) for k, v in vars(lw).items()}
+    cfg = dict(d_model=D, hidden=H, n_experts=E, top_k=K, layout=0, routing=0, renorm=1, shared_gate=1)
+    done, t0 = 0, time.perf_counter()
+    i = 0
+    while True:
+        x = ofb.make_tokens(shape, tokens_per_call, seed=seed * 1000 + i).numpy()
+        binding.moe_forward(cfg, w, x)
+        done += tokens_per_call
+        i += 1
+        if time.perf_counter() - t0 >= seconds:
+            break
+    return done, time.perf_counter() - t0
+
+
+def cpu_throughput(procs: int, seconds: float, tokens_per_call: int):
+    """Tokens/s of the reference CPU layer on `procs` processes (one per core).
+    The reference is single-threaded in compute; P independent processes is its
+    throughput on P cores."""
+    import binding
+    use_ref = binding.load_ref() is not None
+    ctx = mp.get_context("spawn")
+    with ctx.Pool(procs) as pool:
+        res = pool.map(_cpu_worker, [(s + 1, seconds, tokens_per_call, use_ref) for s in range(procs)])
+    tokens = sum(r[0] for r in res)
+    wall = max(r[1] for r in res)
+    kind = "reference" if use_ref else "port"
+    sample = (f"{tokens} tokens ({tokens_per_call}/call) over {wall:.1f} s on {procs} process(es); "
+              + ("reference engine/src/gguf.c compiled unmodified (oracle/_ref) for the expert "
+                 "dequant + C restatement of model.c:992-1143 (router, softmax, top-8, SwiGLU, "
+                 "combine)" if use_ref else "C restatement of gguf.c dequant and model.c MoE block"))
+    return tokens / wall, kind, sample
+
+
+# --------------------------------------------------------------- GPU arm ----
+
+def run_ours(args, rank, world, local_rank):
+    import torch
+    import torch.distributed as dist
+    ofb = load_ofb()
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    wl = WORKLOADS[args.workload]
+    T = wl["tokens"]
+    shape = ofb.LayerShape()
+    n_layers = args.layers
+    layers = [ofb.MoeLayer(shape, ofb.make_layer(shape, seed=1000 * rank + l, device=dev), T)
+              for l in range(n_layers)]
+    xs = [ofb.make_tokens(shape, T, seed=77 + i + 1000 * rank).to(dev) for i in range(n_layers)]
+    out = torch.empty(T, D, device=dev)
+    stream = torch.cuda.current_stream()
+    torch.cuda.synchronize()
+
+    def step(i):
+        layers[i % n_layers].forward(xs[i % n_layers], out=out)
+
+    for i in range(args.warmup):
+        step(i)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local_rank) as clk:
+        start.record(stream)
+        for i in range(args.steps):
+            step(i)
+        end.record(stream)
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        ms = start.elapsed_time(end)
+        # keep the sampler alive for >= 1 s of identical work so that clocks
+        # are observed even when K steps are shorter than one sample period
+        t_extra = time.perf_counter()
+        j = 0
+        while time.perf_counter() - t_extra < max(0.0, 1.2 - ms / 1e3):
+            for _ in range(200):
+                step(j)
+                j += 1
+            torch.cuda.synchronize()
+    t = torch.tensor([ms], device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = float(t.item())
+
+    # per-phase device times over the same step sequence (events on the stream)
+    phase = [0.0] * 4
+    n_prof = min(args.steps, 200)
+    for i in range(n_prof):
+        p = layers[i % n_layers].forward_profiled(xs[i % n_layers], out)
+        phase = [a + b for a, b in zip(phase, p)]
+    phase = [p / n_prof for p in phase]
+
+    # experts touched per step (for the algorithmic byte count)
+    touched = []
+    for l in range(min(n_layers, 8)):
+        idx, _ = layers[l].route(xs[l])
+        touched.append(len(set(idx.flatten().tolist())))
+    n_touched = statistics.mean(touched)
+
+    # end to end through the public API with host buffers: pinned x in, out back
+    hx = [xs[i].cpu().pin_memory() for i in range(n_layers)]
+    hout = torch.empty(T, D).pin_memory()
+    dx = torch.empty(T, D, device=dev)
+    for i in range(args.warmup):
+        dx.copy_(hx[i % n_layers], non_blocking=True)
+        layers[i % n_layers].forward(dx, out=out)
+        hout.copy_(out, non_blocking=True)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for i in range(args.steps):
+        dx.copy_(hx[i % n_layers], non_blocking=True)
+        layers[i % n_layers].forward(dx, out=out)
+        hout.copy_(out, non_blocking=True)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    te = torch.tensor([e0.elapsed_time(e1)], device=dev)
+    if world > 1:
+        dist.all_reduce(te, op=dist.ReduceOp.MAX)
+    e2e_ms = float(te.item())
+
+    if rank != 0:
+        return
+    peak, peak_kind = peaks()
+    layer_bytes = algorithmic_bytes(T, round(n_touched))
+    up_bytes = (round(n_touched) + 1) * 2 * (H * D // 256) * 144  # gate+up rows read by the up kernel
+    up_ms = phase[2]
+    achieved_up = up_bytes / (up_ms * 1e-3) / 1e9
+    step_ms = ms / args.steps
+    achieved_layer = layer_bytes / (step_ms * 1e-3) / 1e9
+    traffic = None
+    tp = os.path.join(ROOT, "profiles", "traffic.json")
+    if os.path.exists(tp):
+        try:
+            traffic = json.load(open(tp)).get(f"{args.workload}:expert_up_kernel")
+        except Exception:
+            traffic = None
+    clocks = clk.summary()
+    cpu = None
+    if not args.no_cpu_baseline:
+        v, kind, sample = cpu_throughput(1, args.cpu_seconds, T)
+        cpu = {"value": v, "unit": "tokens/s", "cores": 1, "kind": kind, "sample": sample}
+    line = {
+        "metric": "MoE-layer tokens/s (decode)",
+        "value": world * T * args.steps / (ms / 1e3),
+        "unit": "tokens/s",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": step_ms,
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "f32",
+        "data": "synthetic (seeded Q4_K/Q6_K blocks, N(0,1) tokens, N(0,0.02) router)",
+        "config": {"workload": args.workload, "desc": wl["config"], "tokens_per_step": T,
+                   "d_model": D, "hidden": H, "n_experts": E, "top_k": K,
+                   "routing": "softmax/top-8/renormalise, bit-exact", "shared_gate": True,
+                   "l2": f"rotate {n_layers} layer copies ({n_layers * 522} MB) > 126 MB L2",
+                   "parallelism": f"replicas x{world}"},
+        "roofline": {"bound": "hbm", "kernel": "expert_up_kernel (gate/up Q4_K dequant-GEMV)",
+                     "achieved": achieved_up, "peak": peak, "unit": "GB/s",
+                     "frac": achieved_up / peak, "traffic": traffic,
+                     "peak_source": peak_kind,
+                     "algorithmic_bytes_per_launch": up_bytes, "launch_ms": up_ms},
+        "layer_roofline": {"achieved": achieved_layer, "frac": achieved_layer / peak,
+                           "algorithmic_bytes_per_step": layer_bytes,
+                           "experts_touched": n_touched},
+        "phase_ms": {"routing": phase[0], "plan": phase[1], "up": phase[2], "down_combine": phase[3]},
+        "e2e": {"value": world * T * args.steps / (e2e_ms / 1e3), "unit": "tokens/s",
+                "h2d_bytes_per_step": T * D * 4, "d2h_bytes_per_step": T * D * 4},
+        "gpu_launches": 5 * args.steps,
+        "clocks": clocks,
+        "cpu_baseline": cpu,
+    }
+    print(json.dumps(line), flush=True)
+
+
+def run_reference(args, rank, world):
+    if rank != 0:
+        return
+    procs = os.cpu_count() or 1
+    T = WORKLOADS[args.workload]["tokens"]
+    # One token-layer takes ~0.1 s of CPU, so K steps of the GPU arm's size
+    # would run for hours: the arm runs one bounded sample (every core busy
+    # for args.cpu_seconds * 4, at most 90 s) and reports its throughput.
+    v, kind, sample = cpu_throughput(procs, min(90.0, 4 * args.cpu_seconds), T)
+    line = {
+        "impl": "reference",
+        "metric": "MoE-layer tokens/s (decode)", "value": v, "unit": "tokens/s",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": 1e3 * T / v, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": args.workload, "desc": WORKLOADS[args.workload]["config"],
+                   "tokens_per_step": T, "d_model": D, "hidden": H, "n_experts": E, "top_k": K},
+        "cpu_baseline": {"value": v, "unit": "tokens/s", "cores": procs, "kind": kind,
+                         "sample": sample},
+        "e2e": {"value": v, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=2000)
+    ap.add_argument("--warmup", type=int, default=50)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--workload", choices=sorted(WORKLOADS), default="decode1")
+    ap.add_argument("--layers", type=int, default=16, help="rotating layer copies (L2 flush)")
+    ap.add_argument("--cpu-seconds", type=float, default=12.0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    rank = int(os.environ.get("RANK", 0))
+    world = int(os.environ.get("WORLD_SIZE", 1))
+    local_rank = int(os.environ.get("LOCAL_RANK", 0))
+    if args.impl == "reference":
+        return run_reference(args, rank, world)
+    if world > 1:
+        import torch
+        import torch.distributed as dist
+        torch.cuda.set_device(local_rank)
+        dist.init_process_group("nccl", device_id=torch.device("cuda", local_rank))
+    try:
+        run_ours(args, rank, world, local_rank)
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,179 @@
+/*
+ * ornith_moe.h — C ABI of the B200 MoE feed-forward path (raw device pointers).
+ *
+ * Plain C: pointers, sizes and status codes only. All pointers named "device"
+ * are CUDA device (or managed) addresses; `stream` is a cudaStream_t passed as
+ * void* (NULL = the legacy default stream). Calls are stream-ordered and do not
+ * synchronise unless stated. Every entry point returns OFB_OK (0) or a
+ * non-zero OFB_E* status; ofb_last_error() gives a readable reason (per host
+ * thread). Nothing here falls back to the CPU.
+ *
+ * Each entry point names the reference interface it replaces
+ * (ornith-flight paths, file:line).
+ */
+#ifndef ORNITH_MOE_H
+#define ORNITH_MOE_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum {
+    OFB_OK = 0,
+    OFB_EINVAL = 1,      /* bad argument (NULL, size, alignment, type) */
+    OFB_ECUDA = 2,       /* a CUDA call failed; see ofb_last_error() */
+    OFB_ENOMEM = 3,      /* device allocation failed */
+    OFB_EUNSUPPORTED = 4,/* shape or mode not supported by this build */
+    OFB_ETOOLARGE = 5    /* request exceeds a fixed capacity */
+};
+
+/* ggml tensor types (engine/src/third_party/gguf.h:15-22) */
+#define OFB_TYPE_F32 0
+#define OFB_TYPE_F16 1
+#define OFB_TYPE_Q4_K 12
+#define OFB_TYPE_Q6_K 14
+
+/* output element types of the dequant entry points */
+#define OFB_OUT_F32 0
+#define OFB_OUT_BF16 1
+
+/* Expert-tensor layouts.
+ * CONTIGUOUS: expert e occupies blocks [e*nb, (e+1)*nb); gate/up rows are
+ *   [hidden][d_model] with d_model fastest, down rows [d_model][hidden]; the
+ *   router is f32 [n_experts][d_model]. This is the GGUF/llama.cpp layout.
+ * INTERLEAVED: the reference's expert-slice semantics
+ *   (engine/src/gguf.c:652-711): element i of expert e is linear element
+ *   i*n_experts+e; the slices are used as gate/up [d_model][hidden] and down
+ *   [hidden][d_model] (engine/src/model.c:351-357, :1085-1088); the router is
+ *   f32 [d_model][n_experts] (model.c:1022). Shared-expert tensors follow the
+ *   same row convention as the routed ones of the chosen layout. */
+#define OFB_LAYOUT_CONTIGUOUS 0
+#define OFB_LAYOUT_INTERLEAVED 1
+
+/* Routing variants.
+ * FORWARD: model_forward's inline router (engine/src/model.c:1017-1049):
+ *   softmax over all experts, exchange-sort the probabilities, keep top_k;
+ *   renorm=1 divides the kept probabilities by their sum.
+ * GET_ROUTING: model_get_routing (engine/src/model.c:264-321): exchange-sort
+ *   the logits, softmax over the kept top_k logits. */
+#define OFB_ROUTE_FORWARD 0
+#define OFB_ROUTE_GET_ROUTING 1
+
+typedef struct {
+    int32_t d_model;     /* multiple of 256 */
+    int32_t hidden;      /* expert and shared-expert width, multiple of 256 */
+    int32_t n_experts;   /* 1..1024 */
+    int32_t top_k;       /* 1..16, <= n_experts */
+    int32_t layout;      /* OFB_LAYOUT_* */
+    int32_t routing;     /* OFB_ROUTE_* */
+    int32_t renorm;      /* 0/1, FORWARD routing only */
+    int32_t shared_gate; /* 0/1: scale the shared expert by sigmoid(x . shexp_gate) */
+} ofb_moe_config;
+
+/* Device pointers to one layer's weights. gate/up are Q4_K, down is Q6_K.
+ * router NULL => uniform routing to experts 0..top_k-1 (model.c:283-289).
+ * gate_shexp NULL => no shared expert. */
+typedef struct {
+    const float *router;
+    const void *gate_exps;
+    const void *up_exps;
+    const void *down_exps;
+    const void *gate_shexp;
+    const void *up_shexp;
+    const void *down_shexp;
+    const float *shexp_gate; /* f32 [d_model]; read when shared_gate=1 */
+} ofb_moe_weights;
+
+const char *ofb_status_string(int status);
+const char *ofb_last_error(void);
+
+/* ---- dequantisation ------------------------------------------------------ */
+
+/* Whole-tensor decode of n_elems elements (multiple of 256 for K-quants) to
+ * f32 or bf16 (bf16 = round-to-nearest-even of the bit-exact f32 value).
+ * Replaces gguf_dequantize_tensor_from_buf (engine/src/gguf.c:605-638) for
+ * Q4_K and Q6_K; f32 output is bit-identical to it. Device pointers. */
+int ofb_dequantize(const void *blocks, int type, uint64_t n_elems, void *out, int out_type,
+                   void *stream);
+
+/* Expert-slice decode with the expert index fastest-varying: out[i] =
+ * element (i*n_experts + expert). Replaces
+ * gguf_dequantize_expert_slice_from_buf (engine/src/gguf.c:652-711); same
+ * argument checks (expert < 0 or >= n_experts => OFB_EINVAL). */
+int ofb_dequantize_expert_slice(const void *blocks, int type, uint64_t n_elems,
+                                uint64_t n_experts, int expert, void *out, int out_type,
+                                void *stream);
+
+typedef struct ofb_workspace ofb_workspace;
+
+/* ---- routing -------------------------------------------------------------- */
+
+/* Router projection, softmax and top-k for n_tokens rows of x (f32
+ * [n_tokens][d_model], device). Writes idx (u32 [n_tokens][top_k]) and w
+ * (f32 [n_tokens][top_k]) on the device, bit-identical to the reference's
+ * CPU routing (sequential fp32 dot products, the host C library's expf, the
+ * exchange sort's tie order). Replaces model_get_routing
+ * (engine/src/model.c:264-321) with routing=GET_ROUTING, and gpu_router +
+ * gpu_topk_softmax (engine/src/gpu.h:82-87) batched on the device. `ws` is
+ * a workspace created for this config with max_tokens >= n_tokens (its logits
+ * region is used as scratch). */
+int ofb_route(const ofb_moe_config *cfg, const float *router, const float *x, int n_tokens,
+              uint32_t *idx, float *w, ofb_workspace *ws, void *stream);
+
+/* ---- MoE layer --------------------------------------------------------- */
+
+/* Bytes of device scratch one ofb_moe_forward call needs for up to
+ * max_tokens tokens. */
+size_t ofb_workspace_size(const ofb_moe_config *cfg, int max_tokens);
+/* Allocates the scratch (cudaMalloc) on the current device. */
+int ofb_workspace_create(const ofb_moe_config *cfg, int max_tokens, ofb_workspace **ws);
+int ofb_workspace_destroy(ofb_workspace *ws);
+
+/* One MoE feed-forward layer for n_tokens tokens:
+ *   out = resid + g(x) * shared(x) + sum_a w_a * expert_{idx_a}(x)
+ * x: f32 [n_tokens][d_model] (the post-norm ffn input, model.c:996);
+ * resid: f32 [n_tokens][d_model] or NULL (treated as zero); out may alias
+ * resid. idx_out / w_out (optional, device) receive the routing.
+ * The routed path and its combine are the block engine/src/model.c:992-1143
+ * (refactored out of model_forward); expert SwiGLU = silu(x.G) * (x.U) then
+ * . Dn with silu clamped at +-50 (model.c:340-344); experts whose weight is
+ * below 1e-6 are skipped (model.c:1066). Stream-ordered, no host sync.
+ * Accumulation is fp32 (decode) or bf16 tensor-core with fp32 accumulate
+ * (prefill); routing is always bit-exact. */
+int ofb_moe_forward(const ofb_moe_config *cfg, const ofb_moe_weights *w, const float *x,
+                    const float *resid, float *out, int n_tokens, uint32_t *idx_out,
+                    float *w_out, ofb_workspace *ws, void *stream);
+
+/* Same as ofb_moe_forward (routing kept internal), then waits for the layer
+ * and reports the device time of its four phases in phase_ms[0..3]:
+ * routing (router GEMV + softmax/top-k), dispatch plan, gate/up expert
+ * kernel, down + combine. Timing uses CUDA events on `stream`. Diagnostic
+ * entry for the benchmark's per-kernel roofline; no reference counterpart. */
+int ofb_moe_forward_profiled(const ofb_moe_config *cfg, const ofb_moe_weights *w, const float *x,
+                             const float *resid, float *out, int n_tokens, ofb_workspace *ws,
+                             void *stream, float *phase_ms);
+
+/* ---- seeded synthetic inputs ---------------------------------------------- */
+
+/* Fills n_blocks Q4_K or Q6_K super-blocks on the device from a counter-based
+ * generator (SplitMix64 finaliser over (seed, stream_id, word index)): every
+ * quant and scale byte uniform; d and dmin = fp16(round-to-nearest-even of
+ * U(0, 0.01)). ofb_synth_blocks_host produces the same bytes on the host. */
+int ofb_synth_blocks(void *dst, int type, uint64_t n_blocks, uint64_t first_block,
+                     uint64_t seed, uint64_t stream_id, void *stream);
+void ofb_synth_blocks_host(void *dst, int type, uint64_t n_blocks, uint64_t first_block,
+                           uint64_t seed, uint64_t stream_id);
+/* n host floats drawn N(0, sigma^2) (Box-Muller over the same generator). */
+void ofb_synth_normal_host(float *dst, uint64_t n, uint64_t seed, uint64_t stream_id,
+                           float sigma);
+
+/* Library build identification (sm_100a kernels). */
+const char *ofb_build_info(void);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

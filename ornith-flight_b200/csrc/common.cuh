@@ -1,0 +1,107 @@
+// common.cuh — shared device helpers: bit-exact K-quant field decode, error
+// plumbing, warp reductions.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <cuda_bf16.h>
+#include <stdint.h>
+
+#include "ornith_moe.h"
+
+#define OFB_STR2(x) #x
+#define OFB_STR(x) OFB_STR2(x)
+
+namespace ofb {
+
+constexpr int QK = 256;
+constexpr int Q4K_BYTES = 144;
+constexpr int Q6K_BYTES = 210;
+
+// Per-host-thread error detail (ofb_last_error).
+void set_error(const char *fmt, ...);
+int cuda_status(cudaError_t e, const char *what);
+
+#define OFB_CHECK_LAUNCH(what)                                                  \
+    do {                                                                        \
+        cudaError_t e__ = cudaGetLastError();                                   \
+        if (e__ != cudaSuccess) return ::ofb::cuda_status(e__, what);           \
+    } while (0)
+
+// fp16 bits -> f32 with the reference's rebias rule (engine/src/gguf.c:16-26):
+// only 0x0000 maps to 0; every other pattern (subnormal, -0, exponent 31) is
+// decoded as if it were a normal number.
+__device__ __forceinline__ float half_bits_ref(uint32_t h) {
+    if (h == 0) return 0.0f;
+    uint32_t u = ((h & 0x8000u) << 16) | ((((h >> 10) & 0x1Fu) + 112u) << 23) | ((h & 0x3FFu) << 13);
+    return __uint_as_float(u);
+}
+
+// 6-bit (scale, min) of Q4_K sub-block j from the 12 packed bytes held as
+// three little-endian words s[0..2] (engine/src/gguf.c:31-40).
+__device__ __forceinline__ void q4k_scale_min(const uint32_t s[3], int j, int &sc, int &mn) {
+    auto byte = [&](int i) -> int { return (s[i >> 2] >> (8 * (i & 3))) & 0xFF; };
+    if (j < 4) {
+        sc = byte(j) & 63;
+        mn = byte(j + 4) & 63;
+    } else {
+        sc = (byte(j + 4) & 0xF) | ((byte(j - 4) >> 6) << 4);
+        mn = (byte(j + 4) >> 4) | ((byte(j) >> 6) << 4);
+    }
+}
+
+// Reference rounding of one Q4_K element: (d*sc)*q - (dmin*m), every product
+// rounded on its own (no contraction), engine/src/gguf.c:49-57.
+__device__ __forceinline__ float q4k_value(float dsc, float dmm, int q) {
+    return __fsub_rn(__fmul_rn(dsc, (float)q), dmm);
+}
+
+// Reference rounding of one Q6_K element: (d*sc)*q, engine/src/gguf.c:76-79.
+__device__ __forceinline__ float q6k_value(float d, int sc, int q) {
+    return __fmul_rn(__fmul_rn(d, (float)sc), (float)q);
+}
+
+// Single-element decode, used by the expert-slice entry point
+// (engine/src/gguf.c:511-571); also the
+// interleaved-layout MoE kernels.
+__device__ __forceinline__ float q4k_one(const uint8_t *blk, int pos) {
+    uint4 hdr = __ldg(reinterpret_cast<const uint4 *>(blk));
+    int chunk = pos >> 6, hi = (pos >> 5) & 1;
+    uint32_t s[3] = {hdr.y, hdr.z, hdr.w};
+    int sc, mn;
+    q4k_scale_min(s, 2 * chunk + hi, sc, mn);
+    uint8_t byte = __ldg(blk + 16 + chunk * 32 + (pos & 31));
+    int q = hi ? (byte >> 4) : (byte & 0xF);
+    float dsc = __fmul_rn(half_bits_ref(hdr.x & 0xFFFFu), (float)sc);
+    float dmm = __fmul_rn(half_bits_ref(hdr.x >> 16), (float)mn);
+    return q4k_value(dsc, dmm, q);
+}
+
+__device__ __forceinline__ float q6k_one(const uint8_t *blk, int pos) {
+    int half = pos >> 7, quad = (pos >> 5) & 3, l = pos & 31;
+    uint8_t lo = __ldg(blk + half * 64 + (quad & 1) * 32 + l);
+    int nib = (quad < 2) ? (lo & 0xF) : (lo >> 4);
+    int top = (__ldg(blk + 128 + half * 32 + l) >> (2 * quad)) & 3;
+    int q = (nib | (top << 4)) - 32;
+    int sc = (int)(int8_t)__ldg(blk + 192 + half * 8 + quad * 2 + (l >> 4));
+    float d = half_bits_ref((uint32_t)__ldg(blk + 208) | ((uint32_t)__ldg(blk + 209) << 8));
+    return q6k_value(d, sc, q);
+}
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+
+__device__ __forceinline__ uint16_t ld_u16(const uint8_t *p) {
+    return *reinterpret_cast<const uint16_t *>(p);
+}
+
+inline int grid_for(uint64_t work, int per_block, int cap) {
+    uint64_t g = (work + per_block - 1) / per_block;
+    if (g > (uint64_t)cap) g = cap;
+    if (g < 1) g = 1;
+    return (int)g;
+}
+
+}  // namespace ofb

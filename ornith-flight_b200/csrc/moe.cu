@@ -1,0 +1,602 @@
+// moe.cu — the MoE feed-forward layer: dispatch plan, expert SwiGLU and the
+// weighted combine (the block engine/src/model.c:992-1143, batched).
+//
+// Pipeline for n tokens (all stream-ordered, no host synchronisation):
+//   1. routing (route.cu): idx[T][K], w[T][K], bit-exact.
+//   2. plan_kernel: device histogram of the kept assignments per expert,
+//      scan, and a CSR "slot" list: slot u = one used expert (ascending id)
+//      with its assignment ids; the shared expert is the last slot with every
+//      token. Assignment id a < T*K is (token a/K, rank a%K); a >= T*K is the
+//      shared expert of token a-T*K. Also the shared-expert sigmoid gates.
+//   3. expert_up_kernel: per (slot, hidden row) one warp streams the Q4_K
+//      gate and up rows (144-byte blocks, 16-byte vector loads, dequant fused
+//      into the dot product) and writes h = silu(x.G) * (x.U) per token.
+//   4. decode (T <= 32): expert_down_fused — per output row one warp walks
+//      every slot's Q6_K down row (staged through shared memory because the
+//      210-byte blocks are only 2-byte aligned), dots it with h and
+//      accumulates w * y per token; the combine and residual happen in the
+//      same pass, so y never reaches HBM.
+//      larger T: expert_down_rows writes y per assignment, combine_kernel sums
+//      them per token in the reference's order.
+// The interleaved (reference-slice) layout uses the element-wise kernels at
+// the end of the file; it touches every block of a tensor by construction and
+// is the correctness path for that layout.
+#include <cstdlib>
+#include <cstring>
+
+#include "common.cuh"
+#include "moe.cuh"
+#include "route.cuh"
+
+namespace ofb {
+
+constexpr int MAX_DECODE_T = 32;
+
+__device__ __forceinline__ float silu_ref(float g) {
+    // engine/src/model.c:340-344
+    if (g < -50.0f) return 0.0f;
+    if (g > 50.0f) return g;
+    return g / (1.0f + expf(-g));
+}
+
+// ---- plan ------------------------------------------------------------------
+__global__ void __launch_bounds__(1024) plan_kernel(PlanArgs p) {
+    __shared__ int cnt[1024];
+    __shared__ int cursor[1024];
+    __shared__ int wsum[32][2];
+    const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
+    const int TK = p.T * p.K;
+    for (int e = tid; e < p.E; e += blockDim.x) cnt[e] = 0;
+    __syncthreads();
+    for (int i = tid; i < TK; i += blockDim.x)
+        if (!(p.w[i] < 1e-6f)) atomicAdd(&cnt[p.idx[i]], 1);  // model.c:1066 skip rule
+    __syncthreads();
+    // exclusive scan of (used flag, count) over experts; E <= blockDim
+    const int e = tid;
+    const int f = (e < p.E && cnt[e] > 0) ? 1 : 0;
+    const int c = (e < p.E) ? cnt[e] : 0;
+    int fi = f, ci = c;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        int nf = __shfl_up_sync(0xffffffffu, fi, o), nc = __shfl_up_sync(0xffffffffu, ci, o);
+        if (lane >= o) { fi += nf; ci += nc; }
+    }
+    if (lane == 31) { wsum[wid][0] = fi; wsum[wid][1] = ci; }
+    __syncthreads();
+    if (wid == 0) {
+        const int nw = blockDim.x >> 5;
+        int a = lane < nw ? wsum[lane][0] : 0, b = lane < nw ? wsum[lane][1] : 0;
+        int ai = a, bi = b;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            int na = __shfl_up_sync(0xffffffffu, ai, o), nb = __shfl_up_sync(0xffffffffu, bi, o);
+            if (lane >= o) { ai += na; bi += nb; }
+        }
+        if (lane < nw) { wsum[lane][0] = ai - a; wsum[lane][1] = bi - b; }
+    }
+    __syncthreads();
+    const int F = fi - f + wsum[wid][0], C = ci - c + wsum[wid][1];
+    if (e < p.E) {
+        if (f) { p.slot_expert[F] = e; p.slot_start[F] = C; }
+        cursor[e] = C;
+        if (e == p.E - 1) {
+            int nslots = F + f, total = C + c, u = nslots;
+            if (p.has_shared) {
+                p.slot_expert[u] = p.E;
+                p.slot_start[u] = total;
+                u++;
+                p.slot_start[u] = total + p.T;
+            } else {
+                p.slot_start[u] = total;
+            }
+            *p.n_slots = u;
+            if (p.has_shared)
+                for (int t = 0; t < p.T; t++) p.assign[total + t] = TK + t;
+        }
+    }
+    __syncthreads();
+    for (int i = tid; i < TK; i += blockDim.x)
+        if (!(p.w[i] < 1e-6f)) p.assign[atomicAdd(&cursor[p.idx[i]], 1)] = i;
+    if (p.has_shared && p.shared_gate) {
+        for (int t = wid; t < p.T; t += blockDim.x >> 5) {
+            float z = 0.0f;
+            for (int d = lane; d < p.D; d += 32) z += p.x[(size_t)t * p.D + d] * p.gate_v[d];
+            z = warp_sum(z);
+            if (lane == 0) p.gsc[t] = 1.0f / (1.0f + expf(-z));
+        }
+    }
+}
+
+// ---- contiguous layout: gate/up ------------------------------------------
+// Dot product of one 64-element chunk c of a Q4_K block with x[0..64):
+// sum_i (d*sc*q_i - dmin*m) x_i = d*sc * sum q_i x_i - dmin*m * sum x_i.
+__device__ __forceinline__ float q4k_chunk_dot(const uint8_t *blk, int c, const float *xs) {
+    const uint4 hdr = __ldg(reinterpret_cast<const uint4 *>(blk));
+    const uint4 qa = __ldg(reinterpret_cast<const uint4 *>(blk + 16 + c * 32));
+    const uint4 qb = __ldg(reinterpret_cast<const uint4 *>(blk + 32 + c * 32));
+    const uint32_t qw[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
+    const uint32_t s[3] = {hdr.y, hdr.z, hdr.w};
+    int sc0, m0, sc1, m1;
+    q4k_scale_min(s, 2 * c, sc0, m0);
+    q4k_scale_min(s, 2 * c + 1, sc1, m1);
+    const float d = half_bits_ref(hdr.x & 0xFFFFu), dmin = half_bits_ref(hdr.x >> 16);
+    float lo = 0.f, hi = 0.f, xl = 0.f, xh = 0.f;
+#pragma unroll
+    for (int w = 0; w < 8; w++) {
+        const float4 a = *reinterpret_cast<const float4 *>(xs + 4 * w);
+        const float4 b = *reinterpret_cast<const float4 *>(xs + 32 + 4 * w);
+        const uint32_t q = qw[w];
+        lo += (float)(q & 0xF) * a.x + (float)((q >> 8) & 0xF) * a.y +
+              (float)((q >> 16) & 0xF) * a.z + (float)((q >> 24) & 0xF) * a.w;
+        hi += (float)((q >> 4) & 0xF) * b.x + (float)((q >> 12) & 0xF) * b.y +
+              (float)((q >> 20) & 0xF) * b.z + (float)(q >> 28) * b.w;
+        xl += (a.x + a.y) + (a.z + a.w);
+        xh += (b.x + b.y) + (b.z + b.w);
+    }
+    return d * (float)sc0 * lo - dmin * (float)m0 * xl + d * (float)sc1 * hi - dmin * (float)m1 * xh;
+}
+
+__device__ __forceinline__ int asg_token(int a, int TK, int K) { return a < TK ? a / K : a - TK; }
+
+__global__ void __launch_bounds__(256) expert_up_kernel(LayerArgs a) {
+    const int lane = threadIdx.x & 31;
+    const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const int nwarps = (gridDim.x * blockDim.x) >> 5;
+    const int nbr = a.D / QK, items = nbr * 4, TK = a.T * a.K;
+    const size_t row_bytes = (size_t)nbr * Q4K_BYTES;
+    const size_t exp_bytes = row_bytes * a.H;
+    const int units = *a.n_slots * a.H;
+    for (int unit = warp; unit < units; unit += nwarps) {
+        const int u = unit / a.H, m = unit - u * a.H;
+        const int e = a.slot_expert[u];
+        const uint8_t *G = (e == a.E ? a.gate_sh : a.gate + e * exp_bytes) + m * row_bytes;
+        const uint8_t *U = (e == a.E ? a.up_sh : a.up + e * exp_bytes) + m * row_bytes;
+        const int s1 = a.slot_start[u + 1];
+        for (int s = a.slot_start[u]; s < s1; s++) {
+            const int asg = a.assign[s];
+            const float *xt = a.x + (size_t)asg_token(asg, TK, a.K) * a.D;
+            float gp = 0.f, up = 0.f;
+            for (int j = lane; j < items; j += 32) {
+                const int b = j >> 2, c = j & 3;
+                const float *xs = xt + b * QK + c * 64;
+                gp += q4k_chunk_dot(G + b * Q4K_BYTES, c, xs);
+                up += q4k_chunk_dot(U + b * Q4K_BYTES, c, xs);
+            }
+            gp = warp_sum(gp);
+            up = warp_sum(up);
+            if (lane == 0) a.h[(size_t)asg * a.H + m] = silu_ref(gp) * up;
+        }
+    }
+}
+
+// ---- contiguous layout: down ---------------------------------------------
+// Lane item j of a staged Q6_K row: block b = j/16, half = (j/8)%2,
+// l = 4*(j%8) .. +3; the item covers quads 0..3 => 16 outputs.
+__device__ __forceinline__ float q6k_item_dot(const uint8_t *blk, int j, const float *hrow_blk) {
+    const int half = (j >> 3) & 1, l0 = (j & 7) * 4;
+    const uint8_t *ql = blk + half * 64;
+    const uint8_t *qh = blk + 128 + half * 32;
+    const int8_t *sc = reinterpret_cast<const int8_t *>(blk + 192 + half * 8 + (l0 >> 4));
+    const float d = half_bits_ref((uint32_t)blk[208] | ((uint32_t)blk[209] << 8));
+    const float *hb = hrow_blk + half * 128 + l0;
+    float acc = 0.f;
+#pragma unroll
+    for (int quad = 0; quad < 4; quad++) {
+        const float4 hv = *reinterpret_cast<const float4 *>(hb + quad * 32);
+        const float hh[4] = {hv.x, hv.y, hv.z, hv.w};
+        float part = 0.f;
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            const int l = l0 + i;
+            const uint8_t lb = ql[(quad & 1) * 32 + l];
+            const int nib = (quad < 2) ? (lb & 0xF) : (lb >> 4);
+            const int top = (qh[l] >> (2 * quad)) & 3;
+            part += (float)((nib | (top << 4)) - 32) * hh[i];
+        }
+        acc += (float)sc[quad * 2] * part;
+    }
+    return d * acc;
+}
+
+__device__ __forceinline__ void stage_row(uint8_t *dst, const uint8_t *src, int bytes, int lane) {
+    const uint16_t *s2 = reinterpret_cast<const uint16_t *>(src);
+    uint16_t *d2 = reinterpret_cast<uint16_t *>(dst);
+    for (int i = lane; i < bytes / 2; i += 32) d2[i] = __ldg(s2 + i);
+}
+
+constexpr int DOWN_WARPS = 4;
+constexpr int MAX_ROW_BYTES = 16 * Q6K_BYTES;  // hidden <= 4096
+
+template <bool ONE>
+__global__ void __launch_bounds__(DOWN_WARPS * 32) expert_down_fused(LayerArgs a) {
+    __shared__ __align__(16) uint8_t rowbuf[DOWN_WARPS][MAX_ROW_BYTES];
+    __shared__ float accs[ONE ? 1 : DOWN_WARPS][ONE ? 1 : MAX_DECODE_T][33];
+    const int lane = threadIdx.x & 31, wib = threadIdx.x >> 5;
+    const int warp = blockIdx.x * DOWN_WARPS + wib;
+    const int nwarps = gridDim.x * DOWN_WARPS;
+    const int nbk = a.H / QK, items = nbk * 16, TK = a.T * a.K;
+    const int row_bytes = nbk * Q6K_BYTES;
+    const size_t exp_bytes = (size_t)row_bytes * a.D;
+    const int nslots = *a.n_slots;
+    uint8_t *rb = rowbuf[wib];
+    for (int n = warp; n < a.D; n += nwarps) {
+        float acc1 = 0.f;
+        if (!ONE)
+            for (int t = 0; t < a.T; t++) accs[wib][t][lane] = 0.f;
+        for (int u = 0; u < nslots; u++) {
+            const int e = a.slot_expert[u];
+            const uint8_t *Dn = (e == a.E ? a.down_sh : a.down + e * exp_bytes) + (size_t)n * row_bytes;
+            __syncwarp();
+            stage_row(rb, Dn, row_bytes, lane);
+            __syncwarp();
+            const int s1 = a.slot_start[u + 1];
+            for (int s = a.slot_start[u]; s < s1; s++) {
+                const int asg = a.assign[s];
+                const int t = asg_token(asg, TK, a.K);
+                const float wgt = asg < TK ? a.w[asg] : (a.shared_gate ? a.gsc[t] : 1.0f);
+                const float *hrow = a.h + (size_t)asg * a.H;
+                float part = 0.f;
+                for (int j = lane; j < items; j += 32)
+                    part += q6k_item_dot(rb + (j >> 4) * Q6K_BYTES, j, hrow + (j >> 4) * QK);
+                if (ONE) acc1 += wgt * part;
+                else accs[wib][t][lane] += wgt * part;
+            }
+        }
+        if (ONE) {
+            float v = warp_sum(acc1);
+            if (lane == 0) a.out[n] = (a.resid ? a.resid[n] : 0.f) + v;
+        } else {
+            __syncwarp();
+            for (int t = 0; t < a.T; t++) {
+                float v = warp_sum(accs[wib][t][lane]);
+                if (lane == 0) {
+                    size_t o = (size_t)t * a.D + n;
+                    a.out[o] = (a.resid ? a.resid[o] : 0.f) + v;
+                }
+            }
+        }
+    }
+}
+
+// Larger T: y[asg][n] for every assignment, one warp per (slot, row).
+__global__ void __launch_bounds__(DOWN_WARPS * 32) expert_down_rows(LayerArgs a) {
+    __shared__ __align__(16) uint8_t rowbuf[DOWN_WARPS][MAX_ROW_BYTES];
+    const int lane = threadIdx.x & 31, wib = threadIdx.x >> 5;
+    const int warp = blockIdx.x * DOWN_WARPS + wib;
+    const int nwarps = gridDim.x * DOWN_WARPS;
+    const int nbk = a.H / QK, items = nbk * 16;
+    const int row_bytes = nbk * Q6K_BYTES;
+    const size_t exp_bytes = (size_t)row_bytes * a.D;
+    const int units = *a.n_slots * a.D;
+    uint8_t *rb = rowbuf[wib];
+    for (int unit = warp; unit < units; unit += nwarps) {
+        const int u = unit / a.D, n = unit - u * a.D;
+        const int e = a.slot_expert[u];
+        const uint8_t *Dn = (e == a.E ? a.down_sh : a.down + e * exp_bytes) + (size_t)n * row_bytes;
+        __syncwarp();
+        stage_row(rb, Dn, row_bytes, lane);
+        __syncwarp();
+        const int s1 = a.slot_start[u + 1];
+        for (int s = a.slot_start[u]; s < s1; s++) {
+            const int asg = a.assign[s];
+            const float *hrow = a.h + (size_t)asg * a.H;
+            float part = 0.f;
+            for (int j = lane; j < items; j += 32)
+                part += q6k_item_dot(rb + (j >> 4) * Q6K_BYTES, j, hrow + (j >> 4) * QK);
+            part = warp_sum(part);
+            if (lane == 0) a.y[(size_t)asg * a.D + n] = part;
+        }
+    }
+}
+
+// out = resid + g*y_shared + sum_a w_a y_a (model.c:1007, :1090, :1142 order).
+__global__ void combine_kernel(LayerArgs a) {
+    const size_t total = (size_t)a.T * a.D;
+    const int TK = a.T * a.K;
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total;
+         i += (size_t)gridDim.x * blockDim.x) {
+        const int t = (int)(i / a.D), n = (int)(i - (size_t)t * a.D);
+        float o = a.resid ? a.resid[i] : 0.f;
+        if (a.has_shared) {
+            float ys = a.y[(size_t)(TK + t) * a.D + n];
+            o += a.shared_gate ? a.gsc[t] * ys : ys;
+        }
+        float r = 0.f;
+        for (int k = 0; k < a.K; k++) {
+            const int asg = t * a.K + k;
+            const float w = a.w[asg];
+            if (w < 1e-6f) continue;
+            r += w * a.y[(size_t)asg * a.D + n];
+        }
+        a.out[i] = o + r;
+    }
+}
+
+// ---- interleaved (reference-slice) layout ---------------------------------
+// Element i of expert e's slice is linear element i*E+e (gguf.c:683-705);
+// gate/up slices are [D][H] (index k*H+m), down [H][D] (index j*D+n),
+// model.c:351-357. The shared expert's tensors are plain [D][H] / [H][D].
+__global__ void __launch_bounds__(256) interleaved_up_kernel(LayerArgs a) {
+    const int lane = threadIdx.x & 31;
+    const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const int nwarps = (gridDim.x * blockDim.x) >> 5;
+    const int TK = a.T * a.K;
+    const int units = *a.n_slots * a.H;
+    for (int unit = warp; unit < units; unit += nwarps) {
+        const int u = unit / a.H, m = unit - u * a.H;
+        const int e = a.slot_expert[u];
+        const bool sh = (e == a.E);
+        const uint8_t *G = sh ? a.gate_sh : a.gate;
+        const uint8_t *U = sh ? a.up_sh : a.up;
+        const uint64_t es = sh ? 1 : (uint64_t)a.E, eo = sh ? 0 : (uint64_t)e;
+        const int s1 = a.slot_start[u + 1];
+        for (int s = a.slot_start[u]; s < s1; s++) {
+            const int asg = a.assign[s];
+            const float *xt = a.x + (size_t)asg_token(asg, TK, a.K) * a.D;
+            float gp = 0.f, up = 0.f;
+            for (int k = lane; k < a.D; k += 32) {
+                const uint64_t lin = ((uint64_t)k * a.H + m) * es + eo;
+                const int pos = (int)(lin % QK);
+                gp += xt[k] * q4k_one(G + (lin / QK) * Q4K_BYTES, pos);
+                up += xt[k] * q4k_one(U + (lin / QK) * Q4K_BYTES, pos);
+            }
+            gp = warp_sum(gp);
+            up = warp_sum(up);
+            if (lane == 0) a.h[(size_t)asg * a.H + m] = silu_ref(gp) * up;
+        }
+    }
+}
+
+__global__ void __launch_bounds__(256) interleaved_down_kernel(LayerArgs a) {
+    const int lane = threadIdx.x & 31;
+    const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const int nwarps = (gridDim.x * blockDim.x) >> 5;
+    const int units = *a.n_slots * a.D;
+    for (int unit = warp; unit < units; unit += nwarps) {
+        const int u = unit / a.D, n = unit - u * a.D;
+        const int e = a.slot_expert[u];
+        const bool sh = (e == a.E);
+        const uint8_t *Dn = sh ? a.down_sh : a.down;
+        const uint64_t es = sh ? 1 : (uint64_t)a.E, eo = sh ? 0 : (uint64_t)e;
+        const int s1 = a.slot_start[u + 1];
+        for (int s = a.slot_start[u]; s < s1; s++) {
+            const int asg = a.assign[s];
+            const float *hrow = a.h + (size_t)asg * a.H;
+            float part = 0.f;
+            for (int j = lane; j < a.H; j += 32) {
+                const uint64_t lin = ((uint64_t)j * a.D + n) * es + eo;
+                part += hrow[j] * q6k_one(Dn + (lin / QK) * Q6K_BYTES, (int)(lin % QK));
+            }
+            part = warp_sum(part);
+            if (lane == 0) a.y[(size_t)asg * a.D + n] = part;
+        }
+    }
+}
+
+// ---- workspace -----------------------------------------------------------
+static size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+
+WorkspaceLayout workspace_layout(const ofb_moe_config *c, int max_tokens) {
+    WorkspaceLayout L;
+    const size_t T = (size_t)max_tokens, K = c->top_k, E = c->n_experts;
+    const size_t A = T * K + T;  // routed + shared assignments
+    size_t off = 0;
+    auto take = [&](size_t bytes) { size_t o = off; off = align_up(off + bytes, 256); return o; };
+    L.logits = take(T * E * 4);
+    L.idx = take(T * K * 4);
+    L.w = take(T * K * 4);
+    L.gsc = take(T * 4);
+    L.n_slots = take(4);
+    L.slot_expert = take((E + 1) * 4);
+    L.slot_start = take((E + 2) * 4);
+    L.assign = take(A * 4);
+    L.h = take(A * (size_t)c->hidden * 4);
+    // y per assignment is only needed beyond the fused decode path
+    L.y = take(max_tokens > MAX_DECODE_T || c->layout == OFB_LAYOUT_INTERLEAVED
+                   ? A * (size_t)c->d_model * 4
+                   : 0);
+    L.total = off;
+    return L;
+}
+
+int check_config(const ofb_moe_config *c) {
+    if (!c) { set_error("NULL config"); return OFB_EINVAL; }
+    if (c->d_model <= 0 || c->d_model % QK || c->hidden <= 0 || c->hidden % QK) {
+        set_error("d_model (%d) and hidden (%d) must be positive multiples of 256", c->d_model, c->hidden);
+        return OFB_EINVAL;
+    }
+    if (c->hidden > 16 * QK) { set_error("hidden %d > 4096 unsupported", c->hidden); return OFB_EUNSUPPORTED; }
+    if (c->n_experts < 1 || c->n_experts > 1024) { set_error("n_experts %d not in [1,1024]", c->n_experts); return OFB_EINVAL; }
+    if (c->top_k < 1 || c->top_k > 16 || c->top_k > c->n_experts) { set_error("top_k %d invalid", c->top_k); return OFB_EINVAL; }
+    if (c->layout != OFB_LAYOUT_CONTIGUOUS && c->layout != OFB_LAYOUT_INTERLEAVED) { set_error("bad layout %d", c->layout); return OFB_EINVAL; }
+    if (c->routing != OFB_ROUTE_FORWARD && c->routing != OFB_ROUTE_GET_ROUTING) { set_error("bad routing %d", c->routing); return OFB_EINVAL; }
+    return OFB_OK;
+}
+
+static int sm_count() {
+    static int n = 0;
+    if (!n) {
+        int dev = 0;
+        cudaGetDevice(&dev);
+        cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+        if (n <= 0) n = 148;
+    }
+    return n;
+}
+
+int run_moe_layer(const ofb_moe_config *cfg, const ofb_moe_weights *wt, const float *x,
+                  const float *resid, float *out, int T, uint32_t *idx_out, float *w_out,
+                  uint8_t *base, const WorkspaceLayout &L, cudaStream_t s, cudaEvent_t *ev) {
+    const int D = cfg->d_model, H = cfg->hidden, E = cfg->n_experts, K = cfg->top_k;
+    auto mark = [&](int i) { if (ev) cudaEventRecord(ev[i], s); };
+    mark(0);
+    float *logits = (float *)(base + L.logits);
+    uint32_t *idx = idx_out ? idx_out : (uint32_t *)(base + L.idx);
+    float *w = w_out ? w_out : (float *)(base + L.w);
+    int st;
+    if (wt->router) {
+        if ((st = launch_router_logits(cfg->layout, wt->router, x, T, D, E, logits, s))) return st;
+        if ((st = launch_route_select(logits, T, E, K, cfg->routing, cfg->renorm, idx, w, s))) return st;
+    } else if ((st = launch_route_uniform(T, K, idx, w, s))) {
+        return st;
+    }
+    mark(1);
+    const bool has_shared = wt->gate_shexp && wt->up_shexp && wt->down_shexp;
+    PlanArgs p;
+    p.idx = idx; p.w = w; p.T = T; p.K = K; p.E = E; p.D = D;
+    p.has_shared = has_shared; p.shared_gate = cfg->shared_gate && wt->shexp_gate;
+    p.x = x; p.gate_v = wt->shexp_gate;
+    p.gsc = (float *)(base + L.gsc);
+    p.n_slots = (int *)(base + L.n_slots);
+    p.slot_expert = (int *)(base + L.slot_expert);
+    p.slot_start = (int *)(base + L.slot_start);
+    p.assign = (int *)(base + L.assign);
+    plan_kernel<<<1, 1024, 0, s>>>(p);
+    OFB_CHECK_LAUNCH("plan");
+    mark(2);
+
+    LayerArgs a;
+    a.T = T; a.D = D; a.H = H; a.E = E; a.K = K;
+    a.has_shared = has_shared; a.shared_gate = p.shared_gate;
+    a.x = x; a.resid = resid; a.out = out;
+    a.gate = (const uint8_t *)wt->gate_exps; a.up = (const uint8_t *)wt->up_exps;
+    a.down = (const uint8_t *)wt->down_exps;
+    a.gate_sh = (const uint8_t *)wt->gate_shexp; a.up_sh = (const uint8_t *)wt->up_shexp;
+    a.down_sh = (const uint8_t *)wt->down_shexp;
+    a.idx = idx; a.w = w; a.gsc = p.gsc;
+    a.n_slots = p.n_slots; a.slot_expert = p.slot_expert; a.slot_start = p.slot_start;
+    a.assign = p.assign;
+    a.h = (float *)(base + L.h);
+    a.y = (float *)(base + L.y);
+
+    const int max_slots = (T * K < E ? T * K : E) + 1;
+    const int sms = sm_count();
+    if (cfg->layout == OFB_LAYOUT_INTERLEAVED) {
+        interleaved_up_kernel<<<grid_for((uint64_t)max_slots * H, 8, sms * 8), 256, 0, s>>>(a);
+        mark(3);
+        interleaved_down_kernel<<<grid_for((uint64_t)max_slots * D, 8, sms * 8), 256, 0, s>>>(a);
+        combine_kernel<<<grid_for((uint64_t)T * D, 256, sms * 4), 256, 0, s>>>(a);
+        OFB_CHECK_LAUNCH("interleaved layer");
+        mark(4);
+        return OFB_OK;
+    }
+    expert_up_kernel<<<grid_for((uint64_t)max_slots * H, 8, sms * 16), 256, 0, s>>>(a);
+    mark(3);
+    if (T == 1) {
+        expert_down_fused<true><<<grid_for(D, DOWN_WARPS, sms * 16), DOWN_WARPS * 32, 0, s>>>(a);
+    } else if (T <= MAX_DECODE_T) {
+        expert_down_fused<false><<<grid_for(D, DOWN_WARPS, sms * 16), DOWN_WARPS * 32, 0, s>>>(a);
+    } else {
+        expert_down_rows<<<grid_for((uint64_t)max_slots * D, DOWN_WARPS, sms * 16), DOWN_WARPS * 32, 0, s>>>(a);
+        combine_kernel<<<grid_for((uint64_t)T * D, 256, sms * 4), 256, 0, s>>>(a);
+    }
+    OFB_CHECK_LAUNCH("expert kernels");
+    mark(4);
+    return OFB_OK;
+}
+
+}  // namespace ofb
+
+using namespace ofb;
+
+struct ofb_workspace {
+    ofb_moe_config cfg;
+    int max_tokens;
+    uint8_t *base;
+    WorkspaceLayout layout;
+};
+
+extern "C" size_t ofb_workspace_size(const ofb_moe_config *cfg, int max_tokens) {
+    if (check_config(cfg) || max_tokens < 1) return 0;
+    return workspace_layout(cfg, max_tokens).total;
+}
+
+extern "C" int ofb_workspace_create(const ofb_moe_config *cfg, int max_tokens, ofb_workspace **ws) {
+    int st = check_config(cfg);
+    if (st) return st;
+    if (!ws || max_tokens < 1) { set_error("workspace_create: bad arguments"); return OFB_EINVAL; }
+    ofb_workspace *w = (ofb_workspace *)calloc(1, sizeof(ofb_workspace));
+    if (!w) { set_error("workspace_create: host OOM"); return OFB_ENOMEM; }
+    w->cfg = *cfg;
+    w->max_tokens = max_tokens;
+    w->layout = workspace_layout(cfg, max_tokens);
+    cudaError_t e = cudaMalloc((void **)&w->base, w->layout.total);
+    if (e != cudaSuccess) { free(w); return cuda_status(e, "workspace cudaMalloc"); }
+    *ws = w;
+    return OFB_OK;
+}
+
+extern "C" int ofb_workspace_destroy(ofb_workspace *ws) {
+    if (!ws) return OFB_OK;
+    cudaError_t e = cudaFree(ws->base);
+    free(ws);
+    return e == cudaSuccess ? OFB_OK : cuda_status(e, "workspace cudaFree");
+}
+
+static int check_ws(const ofb_moe_config *cfg, const ofb_workspace *ws, int T) {
+    if (!ws) { set_error("NULL workspace"); return OFB_EINVAL; }
+    if (T > ws->max_tokens) { set_error("n_tokens %d > workspace max_tokens %d", T, ws->max_tokens); return OFB_ETOOLARGE; }
+    const ofb_moe_config &c = ws->cfg;
+    if (c.d_model != cfg->d_model || c.hidden != cfg->hidden || c.n_experts != cfg->n_experts ||
+        c.top_k != cfg->top_k || c.layout != cfg->layout) {
+        set_error("workspace was created for a different layer shape");
+        return OFB_EINVAL;
+    }
+    return OFB_OK;
+}
+
+extern "C" int ofb_route(const ofb_moe_config *cfg, const float *router, const float *x,
+                         int n_tokens, uint32_t *idx, float *w, ofb_workspace *ws, void *stream) {
+    int st = check_config(cfg);
+    if (st) return st;
+    if (!x || !idx || !w || n_tokens < 0) { set_error("ofb_route: bad arguments"); return OFB_EINVAL; }
+    if ((st = check_ws(cfg, ws, n_tokens))) return st;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    if (!router) return launch_route_uniform(n_tokens, cfg->top_k, idx, w, s);
+    float *logits = (float *)(ws->base + ws->layout.logits);
+    if ((st = launch_router_logits(cfg->layout, router, x, n_tokens, cfg->d_model, cfg->n_experts, logits, s))) return st;
+    return launch_route_select(logits, n_tokens, cfg->n_experts, cfg->top_k, cfg->routing, cfg->renorm, idx, w, s);
+}
+
+extern "C" int ofb_moe_forward(const ofb_moe_config *cfg, const ofb_moe_weights *w,
+                               const float *x, const float *resid, float *out, int n_tokens,
+                               uint32_t *idx_out, float *w_out, ofb_workspace *ws, void *stream) {
+    int st = check_config(cfg);
+    if (st) return st;
+    if (!w || n_tokens < 0) { set_error("ofb_moe_forward: bad arguments"); return OFB_EINVAL; }
+    if ((st = check_ws(cfg, ws, n_tokens))) return st;
+    if (n_tokens == 0) return OFB_OK;
+    if (!x || !out) { set_error("ofb_moe_forward: NULL activations"); return OFB_EINVAL; }
+    if (!w->gate_exps || !w->up_exps || !w->down_exps) { set_error("ofb_moe_forward: NULL expert tensor"); return OFB_EINVAL; }
+    if ((reinterpret_cast<uintptr_t>(w->gate_exps) | reinterpret_cast<uintptr_t>(w->up_exps) |
+         reinterpret_cast<uintptr_t>(w->down_exps) | reinterpret_cast<uintptr_t>(w->gate_shexp) |
+         reinterpret_cast<uintptr_t>(w->up_shexp) | reinterpret_cast<uintptr_t>(w->down_shexp) |
+         reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(w->router)) & 15) {
+        set_error("ofb_moe_forward: tensors must be 16-byte aligned");
+        return OFB_EINVAL;
+    }
+    return run_moe_layer(cfg, w, x, resid, out, n_tokens, idx_out, w_out, ws->base, ws->layout,
+                         static_cast<cudaStream_t>(stream), nullptr);
+}
+
+extern "C" int ofb_moe_forward_profiled(const ofb_moe_config *cfg, const ofb_moe_weights *w,
+                                        const float *x, const float *resid, float *out,
+                                        int n_tokens, ofb_workspace *ws, void *stream,
+                                        float *phase_ms) {
+    int st = check_config(cfg);
+    if (st) return st;
+    if (!w || !x || !out || !phase_ms || n_tokens < 1) { set_error("profiled: bad arguments"); return OFB_EINVAL; }
+    if ((st = check_ws(cfg, ws, n_tokens))) return st;
+    cudaEvent_t ev[5];
+    for (int i = 0; i < 5; i++)
+        if (cudaEventCreate(&ev[i]) != cudaSuccess) return cuda_status(cudaGetLastError(), "event create");
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    st = run_moe_layer(cfg, w, x, resid, out, n_tokens, nullptr, nullptr, ws->base, ws->layout, s, ev);
+    if (!st) {
+        cudaError_t e = cudaEventSynchronize(ev[4]);
+        if (e != cudaSuccess) st = cuda_status(e, "profiled sync");
+        for (int i = 0; !st && i < 4; i++) cudaEventElapsedTime(&phase_ms[i], ev[i], ev[i + 1]);
+    }
+    for (int i = 0; i < 5; i++) cudaEventDestroy(ev[i]);
+    return st;
+}

@@ -1,0 +1,47 @@
+// moe.cuh — internal structures of the MoE layer kernels.
+#pragma once
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+#include "ornith_moe.h"
+
+namespace ofb {
+
+struct PlanArgs {
+    const uint32_t *idx;
+    const float *w;
+    int T, K, E, D;
+    int has_shared, shared_gate;
+    const float *x, *gate_v;
+    float *gsc;
+    int *n_slots, *slot_expert, *slot_start, *assign;
+};
+
+struct LayerArgs {
+    int T, D, H, E, K;
+    int has_shared, shared_gate;
+    const float *x;
+    const float *resid;
+    float *out;
+    const uint8_t *gate, *up, *down;
+    const uint8_t *gate_sh, *up_sh, *down_sh;
+    const uint32_t *idx;
+    const float *w, *gsc;
+    const int *n_slots, *slot_expert, *slot_start, *assign;
+    float *h, *y;
+};
+
+// Byte offsets of the scratch regions inside one workspace allocation.
+struct WorkspaceLayout {
+    size_t logits, idx, w, gsc, n_slots, slot_expert, slot_start, assign, h, y, total;
+};
+
+WorkspaceLayout workspace_layout(const ofb_moe_config *c, int max_tokens);
+int check_config(const ofb_moe_config *c);
+int run_moe_layer(const ofb_moe_config *cfg, const ofb_moe_weights *wt, const float *x,
+                  const float *resid, float *out, int T, uint32_t *idx_out, float *w_out,
+                  uint8_t *base, const WorkspaceLayout &L, cudaStream_t s,
+                  cudaEvent_t *phase_events /* 5 events or NULL */);
+
+}  // namespace ofb
