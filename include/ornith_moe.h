@@ -156,6 +156,12 @@ int ofb_moe_forward_profiled(const ofb_moe_config *cfg, const ofb_moe_weights *w
                              const float *resid, float *out, int n_tokens, ofb_workspace *ws,
                              void *stream, float *phase_ms);
 
+/* Counts of tokens routed by ofb_moe_forward's certified decode path since
+ * the workspace was created: counts[0] certified directly, counts[1] after
+ * recomputing the uncertain candidates exactly, counts[2] after recomputing
+ * every logit exactly. Synchronous. Diagnostic; no reference counterpart. */
+int ofb_workspace_route_stats(ofb_workspace *ws, int counts[3]);
+
 /* ---- seeded synthetic inputs ---------------------------------------------- */
 
 /* Fills n_blocks Q4_K or Q6_K super-blocks on the device from a counter-based

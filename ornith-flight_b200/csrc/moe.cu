@@ -27,6 +27,7 @@
 #include "common.cuh"
 #include "moe.cuh"
 #include "route.cuh"
+#include "plan.cuh"
 
 namespace ofb {
 
@@ -39,72 +40,10 @@ __device__ __forceinline__ float silu_ref(float g) {
     return g / (1.0f + expf(-g));
 }
 
-// ---- plan ------------------------------------------------------------------
 __global__ void __launch_bounds__(1024) plan_kernel(PlanArgs p) {
-    __shared__ int cnt[1024];
-    __shared__ int cursor[1024];
-    __shared__ int wsum[32][2];
-    const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
-    const int TK = p.T * p.K;
-    for (int e = tid; e < p.E; e += blockDim.x) cnt[e] = 0;
-    __syncthreads();
-    for (int i = tid; i < TK; i += blockDim.x)
-        if (!(p.w[i] < 1e-6f)) atomicAdd(&cnt[p.idx[i]], 1);  // model.c:1066 skip rule
-    __syncthreads();
-    // exclusive scan of (used flag, count) over experts; E <= blockDim
-    const int e = tid;
-    const int f = (e < p.E && cnt[e] > 0) ? 1 : 0;
-    const int c = (e < p.E) ? cnt[e] : 0;
-    int fi = f, ci = c;
-#pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-        int nf = __shfl_up_sync(0xffffffffu, fi, o), nc = __shfl_up_sync(0xffffffffu, ci, o);
-        if (lane >= o) { fi += nf; ci += nc; }
-    }
-    if (lane == 31) { wsum[wid][0] = fi; wsum[wid][1] = ci; }
-    __syncthreads();
-    if (wid == 0) {
-        const int nw = blockDim.x >> 5;
-        int a = lane < nw ? wsum[lane][0] : 0, b = lane < nw ? wsum[lane][1] : 0;
-        int ai = a, bi = b;
-#pragma unroll
-        for (int o = 1; o < 32; o <<= 1) {
-            int na = __shfl_up_sync(0xffffffffu, ai, o), nb = __shfl_up_sync(0xffffffffu, bi, o);
-            if (lane >= o) { ai += na; bi += nb; }
-        }
-        if (lane < nw) { wsum[lane][0] = ai - a; wsum[lane][1] = bi - b; }
-    }
-    __syncthreads();
-    const int F = fi - f + wsum[wid][0], C = ci - c + wsum[wid][1];
-    if (e < p.E) {
-        if (f) { p.slot_expert[F] = e; p.slot_start[F] = C; }
-        cursor[e] = C;
-        if (e == p.E - 1) {
-            int nslots = F + f, total = C + c, u = nslots;
-            if (p.has_shared) {
-                p.slot_expert[u] = p.E;
-                p.slot_start[u] = total;
-                u++;
-                p.slot_start[u] = total + p.T;
-            } else {
-                p.slot_start[u] = total;
-            }
-            *p.n_slots = u;
-            if (p.has_shared)
-                for (int t = 0; t < p.T; t++) p.assign[total + t] = TK + t;
-        }
-    }
-    __syncthreads();
-    for (int i = tid; i < TK; i += blockDim.x)
-        if (!(p.w[i] < 1e-6f)) p.assign[atomicAdd(&cursor[p.idx[i]], 1)] = i;
-    if (p.has_shared && p.shared_gate) {
-        for (int t = wid; t < p.T; t += blockDim.x >> 5) {
-            float z = 0.0f;
-            for (int d = lane; d < p.D; d += 32) z += p.x[(size_t)t * p.D + d] * p.gate_v[d];
-            z = warp_sum(z);
-            if (lane == 0) p.gsc[t] = 1.0f / (1.0f + expf(-z));
-        }
-    }
+    __shared__ int cnt[1024], cursor[1024], wsum[66];
+    build_plan(p, cnt, cursor, wsum);
+    if (p.has_shared && p.shared_gate) shared_gates(p);
 }
 
 // ---- contiguous layout: gate/up ------------------------------------------
@@ -395,6 +334,9 @@ WorkspaceLayout workspace_layout(const ofb_moe_config *c, int max_tokens) {
     L.y = take(max_tokens > MAX_DECODE_T || c->layout == OFB_LAYOUT_INTERLEAVED
                    ? A * (size_t)c->d_model * 4
                    : 0);
+    L.cand = take((size_t)(max_tokens < FAST_ROUTE_MAX_T ? max_tokens : FAST_ROUTE_MAX_T) * (E + 1) * 16);
+    L.counters_bytes = (FAST_ROUTE_MAX_T + 1 + 3) * 4;
+    L.counters = take(L.counters_bytes);
     L.total = off;
     return L;
 }
@@ -433,14 +375,6 @@ int run_moe_layer(const ofb_moe_config *cfg, const ofb_moe_weights *wt, const fl
     float *logits = (float *)(base + L.logits);
     uint32_t *idx = idx_out ? idx_out : (uint32_t *)(base + L.idx);
     float *w = w_out ? w_out : (float *)(base + L.w);
-    int st;
-    if (wt->router) {
-        if ((st = launch_router_logits(cfg->layout, wt->router, x, T, D, E, logits, s))) return st;
-        if ((st = launch_route_select(logits, T, E, K, cfg->routing, cfg->renorm, idx, w, s))) return st;
-    } else if ((st = launch_route_uniform(T, K, idx, w, s))) {
-        return st;
-    }
-    mark(1);
     const bool has_shared = wt->gate_shexp && wt->up_shexp && wt->down_shexp;
     PlanArgs p;
     p.idx = idx; p.w = w; p.T = T; p.K = K; p.E = E; p.D = D;
@@ -451,9 +385,30 @@ int run_moe_layer(const ofb_moe_config *cfg, const ofb_moe_weights *wt, const fl
     p.slot_expert = (int *)(base + L.slot_expert);
     p.slot_start = (int *)(base + L.slot_start);
     p.assign = (int *)(base + L.assign);
-    plan_kernel<<<1, 1024, 0, s>>>(p);
-    OFB_CHECK_LAUNCH("plan");
-    mark(2);
+    int st;
+    const bool fast = wt->router && cfg->layout == OFB_LAYOUT_CONTIGUOUS && T <= FAST_ROUTE_MAX_T;
+    if (fast) {
+        // one launch: certified routing, shared-expert gates, dispatch plan
+        int *ctr = (int *)(base + L.counters);
+        if ((st = launch_route_fast(wt->router, x, p.shared_gate ? wt->shexp_gate : nullptr, T, D, E, K,
+                                    cfg->routing, cfg->renorm, (double2 *)(base + L.cand), ctr,
+                                    ctr + FAST_ROUTE_MAX_T, ctr + FAST_ROUTE_MAX_T + 1, idx, w, p.gsc, &p,
+                                    s)))
+            return st;
+        mark(1);
+        mark(2);
+    } else {
+        if (wt->router) {
+            if ((st = launch_router_logits(cfg->layout, wt->router, x, T, D, E, logits, s))) return st;
+            if ((st = launch_route_select(logits, T, E, K, cfg->routing, cfg->renorm, idx, w, s))) return st;
+        } else if ((st = launch_route_uniform(T, K, idx, w, s))) {
+            return st;
+        }
+        mark(1);
+        plan_kernel<<<1, 1024, 0, s>>>(p);
+        OFB_CHECK_LAUNCH("plan");
+        mark(2);
+    }
 
     LayerArgs a;
     a.T = T; a.D = D; a.H = H; a.E = E; a.K = K;
@@ -522,6 +477,10 @@ extern "C" int ofb_workspace_create(const ofb_moe_config *cfg, int max_tokens, o
     w->layout = workspace_layout(cfg, max_tokens);
     cudaError_t e = cudaMalloc((void **)&w->base, w->layout.total);
     if (e != cudaSuccess) { free(w); return cuda_status(e, "workspace cudaMalloc"); }
+    // routing tickets must start at zero (each call leaves them at zero)
+    e = cudaMemset(w->base + w->layout.counters, 0, w->layout.counters_bytes);
+    if (e == cudaSuccess) e = cudaDeviceSynchronize();
+    if (e != cudaSuccess) { cudaFree(w->base); free(w); return cuda_status(e, "workspace init"); }
     *ws = w;
     return OFB_OK;
 }
@@ -599,4 +558,11 @@ extern "C" int ofb_moe_forward_profiled(const ofb_moe_config *cfg, const ofb_moe
     }
     for (int i = 0; i < 5; i++) cudaEventDestroy(ev[i]);
     return st;
+}
+
+extern "C" int ofb_workspace_route_stats(ofb_workspace *ws, int counts[3]) {
+    if (!ws || !counts) { set_error("route_stats: NULL argument"); return OFB_EINVAL; }
+    cudaError_t e = cudaMemcpy(counts, ws->base + ws->layout.counters + (FAST_ROUTE_MAX_T + 1) * 4,
+                               3 * sizeof(int), cudaMemcpyDeviceToHost);
+    return e == cudaSuccess ? OFB_OK : cuda_status(e, "route_stats copy");
 }

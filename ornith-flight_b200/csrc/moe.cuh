@@ -34,8 +34,19 @@ struct LayerArgs {
 
 // Byte offsets of the scratch regions inside one workspace allocation.
 struct WorkspaceLayout {
-    size_t logits, idx, w, gsc, n_slots, slot_expert, slot_start, assign, h, y, total;
+    size_t logits, idx, w, gsc, n_slots, slot_expert, slot_start, assign, h, y;
+    size_t cand;      // fast routing: (approximate logit, bound) per (token, row)
+    size_t counters;  // fast routing tickets [T] + [1] and stats [3]; zero at creation
+    size_t counters_bytes;
+    size_t total;
 };
+
+// Token counts up to which routing uses the certified fast kernel.
+constexpr int FAST_ROUTE_MAX_T = 64;
+
+int launch_route_fast(const float *W, const float *x, const float *gate_v, int T, int D, int E, int K,
+                      int routing, int renorm, double2 *cand, int *tok_cnt, int *all_cnt, int *stats,
+                      uint32_t *idx, float *w, float *gsc, const PlanArgs *plan, cudaStream_t s);
 
 WorkspaceLayout workspace_layout(const ofb_moe_config *c, int max_tokens);
 int check_config(const ofb_moe_config *c);

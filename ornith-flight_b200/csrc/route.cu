@@ -18,6 +18,7 @@
 #include "common.cuh"
 #include "exact_expf.h"
 #include "route.cuh"
+#include "exchange.cuh"
 
 namespace ofb {
 
@@ -119,53 +120,6 @@ __global__ void __launch_bounds__(256) router_logits_tiled(const float *__restri
             if (e < E) logits[(size_t)t * E + e] = acc[i][j];
         }
     }
-}
-
-// ---- exchange-sort emulation ---------------------------------------------
-// One pass i of "for j>i: if a[j] > a[i] swap" over a[0..n): the holder at i
-// is replaced whenever a strictly larger element is met, and the displaced
-// holder lands where that element was. Equivalently, with records
-// j1<...<jr (positions whose value beats every earlier value in [i, j)):
-// a[j1] <- a[i], a[j2] <- a[j1], ..., a[i] <- a[jr]. Records come from a warp
-// scan of (value, first position of the running max). `old` holds a copy of
-// the arrays taken before the pass.
-struct MaxPos { float v; int p; };
-__device__ __forceinline__ MaxPos later_if_greater(MaxPos a, MaxPos b) { return (b.v > a.v) ? b : a; }
-
-__device__ void exchange_pass(float *val, int *id, float *oval, int *oid, int n, int i, int lane) {
-    const int per = (n + 31) / 32;
-    const int lo = lane * per, hi = min(n, lo + per);
-    for (int j = lo; j < hi; j++) { oval[j] = val[j]; oid[j] = id[j]; }
-    __syncwarp();
-    MaxPos seg = {-INFINITY, -1};
-    for (int j = max(lo, i + 1); j < hi; j++) seg = later_if_greater(seg, MaxPos{oval[j], j});
-    // inclusive scan over lanes (earlier lanes on the left)
-    MaxPos inc = seg;
-#pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-        MaxPos up;
-        up.v = __shfl_up_sync(0xffffffffu, inc.v, o);
-        up.p = __shfl_up_sync(0xffffffffu, inc.p, o);
-        if (lane >= o) inc = later_if_greater(up, inc);
-    }
-    MaxPos exc;
-    exc.v = __shfl_up_sync(0xffffffffu, inc.v, 1);
-    exc.p = __shfl_up_sync(0xffffffffu, inc.p, 1);
-    const MaxPos holder = {oval[i], i};
-    MaxPos run = (lane == 0) ? holder : later_if_greater(holder, exc);
-    for (int j = max(lo, i + 1); j < hi; j++) {
-        if (oval[j] > run.v) {
-            val[j] = oval[run.p];
-            id[j] = oid[run.p];
-            run = MaxPos{oval[j], j};
-        }
-    }
-    MaxPos last;
-    last.v = __shfl_sync(0xffffffffu, inc.v, 31);
-    last.p = __shfl_sync(0xffffffffu, inc.p, 31);
-    last = later_if_greater(holder, last);
-    if (lane == 0 && last.p != i) { val[i] = oval[last.p]; id[i] = oid[last.p]; }
-    __syncwarp();
 }
 
 // ---- softmax + top-k, one warp per token ---------------------------------

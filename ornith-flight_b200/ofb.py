@@ -66,6 +66,7 @@ def _load() -> ctypes.CDLL:
         "ofb_workspace_destroy": (i32, [vp]),
         "ofb_moe_forward": (i32, [cfgp, wp, vp, vp, vp, i32, vp, vp, vp, vp]),
         "ofb_moe_forward_profiled": (i32, [cfgp, wp, vp, vp, vp, i32, vp, vp, vp]),
+        "ofb_workspace_route_stats": (i32, [vp, ctypes.POINTER(ctypes.c_int * 3)]),
         "ofb_synth_blocks": (i32, [vp, i32, u64, u64, u64, u64, vp]),
         "ofb_synth_blocks_host": (None, [vp, i32, u64, u64, u64, u64]),
         "ofb_synth_normal_host": (None, [vp, u64, u64, u64, ctypes.c_float]),
@@ -83,7 +84,7 @@ lib = _load()
 EXPORTED = [
     "ofb_status_string", "ofb_last_error", "ofb_build_info", "ofb_dequantize",
     "ofb_dequantize_expert_slice", "ofb_route", "ofb_workspace_size", "ofb_workspace_create",
-    "ofb_workspace_destroy", "ofb_moe_forward", "ofb_moe_forward_profiled", "ofb_synth_blocks", "ofb_synth_blocks_host",
+    "ofb_workspace_destroy", "ofb_moe_forward", "ofb_moe_forward_profiled", "ofb_workspace_route_stats", "ofb_synth_blocks", "ofb_synth_blocks_host",
     "ofb_synth_normal_host",
 ]
 
@@ -252,6 +253,12 @@ class Workspace:
         h = ctypes.c_void_p()
         _check(lib.ofb_workspace_create(ctypes.byref(self._cfg), max_tokens, ctypes.byref(h)))
         self.handle = h
+
+    def route_stats(self):
+        """(certified, candidate recompute, full recompute) token counts."""
+        c = (ctypes.c_int * 3)()
+        _check(lib.ofb_workspace_route_stats(self.handle, ctypes.byref(c)))
+        return tuple(c)
 
     def close(self):
         if self.handle:

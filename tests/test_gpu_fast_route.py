@@ -1,0 +1,66 @@
+"""The certified decode routing inside ofb_moe_forward (T <= 64, contiguous
+router): top-k indices bit-exact against the reference's sequential CPU
+routing on every path — certified directly, uncertain candidates recomputed
+with the exact chain, and every logit recomputed (probability ties)."""
+import numpy as np
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+def run_layer(ofb, oracle, cuda, shape, router, x):
+    lw = ofb.make_layer(shape, seed=3, device=cuda)
+    lw.router = torch.from_numpy(np.ascontiguousarray(router, np.float32).reshape(-1)).to(cuda)
+    T = x.shape[0]
+    layer = ofb.MoeLayer(shape, lw, max_tokens=T)
+    idx = torch.empty(T, shape.top_k, dtype=torch.int32, device=cuda)
+    w = torch.empty(T, shape.top_k, dtype=torch.float32, device=cuda)
+    out = layer.forward(torch.from_numpy(x).to(cuda), idx=idx, w=w)
+    torch.cuda.synchronize()
+    cfg = dict(d_model=shape.d_model, hidden=shape.hidden, n_experts=shape.n_experts, top_k=shape.top_k,
+               layout=0, routing=shape.routing, renorm=shape.renorm, shared_gate=shape.shared_gate)
+    wd = {k: (None if v is None else v.cpu().numpy()) for k, v in vars(lw).items()}
+    want, oi, ow = oracle.moe_forward(cfg, wd, x)
+    return idx.cpu().numpy().view(np.uint32), w.cpu().numpy(), out.cpu().numpy(), oi, ow, want, \
+        layer.ws.route_stats()
+
+
+@pytest.mark.parametrize("routing", [0, 1])
+def test_many_tokens_certified(ofb, oracle, cuda, routing):
+    shape = ofb.LayerShape(routing=routing)
+    router = ofb.synth_normal(256 * 2048, 0, 7, 0.02).numpy().reshape(256, 2048)
+    x = ofb.make_tokens(shape, 64, seed=123).numpy()
+    gi, gw, out, oi, ow, want, stats = run_layer(ofb, oracle, cuda, shape, router, x)
+    assert np.array_equal(gi, oi)
+    np.testing.assert_allclose(gw, ow, rtol=1e-5)
+    assert stats[0] > 0 and sum(stats) == 64
+
+
+def test_near_ties_recompute_candidates(ofb, oracle, cuda):
+    # expert pairs whose logits differ by ~1e-6 relative: inside the error
+    # bound, so the block recomputes them with the reference's exact chain
+    shape = ofb.LayerShape(d_model=512, hidden=256, n_experts=32, top_k=4)
+    rng = np.random.default_rng(4)
+    base = rng.normal(0, 0.05, size=(16, 512)).astype(np.float32)
+    router = np.concatenate([base, base * np.float32(1 + 3e-6)])
+    x = rng.normal(size=(40, 512)).astype(np.float32)
+    gi, gw, out, oi, ow, want, stats = run_layer(ofb, oracle, cuda, shape, router, x)
+    assert np.array_equal(gi, oi)
+    np.testing.assert_allclose(gw, ow, rtol=1e-5)
+    assert stats[1] + stats[2] > 0
+
+
+@pytest.mark.parametrize("routing", [0, 1])
+def test_exact_ties_full_recompute(ofb, oracle, cuda, routing):
+    # duplicated rows: equal logits; the exchange sort's swap order decides
+    shape = ofb.LayerShape(d_model=256, hidden=256, n_experts=48, top_k=8, routing=routing)
+    rng = np.random.default_rng(5)
+    base = rng.normal(0, 0.05, size=(6, 256)).astype(np.float32)
+    router = base[rng.integers(0, 6, size=48)]
+    x = rng.normal(size=(30, 256)).astype(np.float32)
+    gi, gw, out, oi, ow, want, stats = run_layer(ofb, oracle, cuda, shape, router, x)
+    assert np.array_equal(gi, oi)
+    np.testing.assert_allclose(gw, ow, rtol=1e-5)
+    if routing == 0:
+        assert stats[2] > 0  # probabilities tie -> every logit recomputed

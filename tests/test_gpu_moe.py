@@ -12,6 +12,11 @@ import torch
 
 pytestmark = pytest.mark.gpu
 TOL = 1e-3
+WEIGHT_RTOL = 1e-5
+
+
+def fast_route(shape, T, router=True):
+    return router and shape.layout == 0 and T <= 64
 
 
 def oracle_layer(oracle, shape, lw, x, resid=None):
@@ -37,7 +42,11 @@ def check(ofb, oracle, cuda, shape, T, seed, resid=False, shared=True, router=Tr
     got = out.cpu().numpy()
     want, oi, ow = oracle_layer(oracle, shape, lw, x.numpy(), None if r is None else r.numpy())
     assert np.array_equal(idx.cpu().numpy().view(np.uint32), oi)
-    assert np.array_equal(w.cpu().numpy().view(np.uint32), ow.view(np.uint32))
+    if fast_route(shape, T, router):
+        # certified decode routing: indices exact, weights from the fp64 logits
+        np.testing.assert_allclose(w.cpu().numpy(), ow, rtol=WEIGHT_RTOL, atol=0)
+    else:
+        assert np.array_equal(w.cpu().numpy().view(np.uint32), ow.view(np.uint32))
     err = rel_err(got, want)
     assert err <= TOL, f"relative error {err}"
     return got, want
