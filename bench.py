@@ -40,6 +40,7 @@ WORKLOADS = {
 }
 D, H, E, K = 2048, 512, 256, 8
 EXPERT_BYTES = 2 * (H * D // 256) * 144 + (H * D // 256) * 210  # 2,039,808
+LAUNCHES_PER_STEP = 3  # route+plan, gate/up, down+combine
 
 
 def algorithmic_bytes(tokens: int, n_experts_touched: int) -> int:
@@ -221,6 +222,10 @@ def run_ours(args, rank, world, local_rank):
         phase = [a + b for a, b in zip(phase, p)]
     phase = [p / n_prof for p in phase]
 
+    route_stats = [0, 0, 0]
+    for l in layers:
+        route_stats = [a + b for a, b in zip(route_stats, l.ws.route_stats())]
+
     # experts touched per step (for the algorithmic byte count)
     touched = []
     for l in range(min(n_layers, 8)):
@@ -300,7 +305,9 @@ def run_ours(args, rank, world, local_rank):
         "phase_ms": {"routing": phase[0], "plan": phase[1], "up": phase[2], "down_combine": phase[3]},
         "e2e": {"value": world * T * args.steps / (e2e_ms / 1e3), "unit": "tokens/s",
                 "h2d_bytes_per_step": T * D * 4, "d2h_bytes_per_step": T * D * 4},
-        "gpu_launches": 5 * args.steps,
+        "route_paths": {"certified": route_stats[0], "candidates_recomputed": route_stats[1],
+                        "all_recomputed": route_stats[2]},
+        "gpu_launches": LAUNCHES_PER_STEP * args.steps,
         "clocks": clocks,
         "cpu_baseline": cpu,
     }

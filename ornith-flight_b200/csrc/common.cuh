@@ -105,3 +105,37 @@ inline int grid_for(uint64_t work, int per_block, int cap) {
 }
 
 }  // namespace ofb
+
+// ---- programmatic dependent launch (PDL) ----------------------------------
+// A kernel launched with launch_pdl may start while the previous kernel in
+// the stream is still running: it first does work that does not depend on
+// that kernel (loading static weights), then pdl_wait() blocks until the
+// previous grid has completed and its memory is visible. pdl_trigger() lets
+// the next PDL kernel in the stream be scheduled early.
+namespace ofb {
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                              cudaStream_t s, Args... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kernel, args...);
+}
+
+// L2 prefetch of [p, p + bytes) spread over the calling threads.
+__device__ __forceinline__ void prefetch_l2(const void *p, size_t bytes, int tid, int nthreads) {
+    const char *c = static_cast<const char *>(p);
+    for (size_t o = (size_t)tid * 128; o < bytes; o += (size_t)nthreads * 128)
+        asm volatile("prefetch.global.L2 [%0];" ::"l"(c + o));
+}
+}  // namespace ofb

@@ -31,7 +31,7 @@
 
 namespace ofb {
 
-constexpr int MAX_DECODE_T = 32;
+
 
 __device__ __forceinline__ float silu_ref(float g) {
     // engine/src/model.c:340-344
@@ -145,57 +145,6 @@ __device__ __forceinline__ void stage_row(uint8_t *dst, const uint8_t *src, int 
 
 constexpr int DOWN_WARPS = 4;
 constexpr int MAX_ROW_BYTES = 16 * Q6K_BYTES;  // hidden <= 4096
-
-template <bool ONE>
-__global__ void __launch_bounds__(DOWN_WARPS * 32) expert_down_fused(LayerArgs a) {
-    __shared__ __align__(16) uint8_t rowbuf[DOWN_WARPS][MAX_ROW_BYTES];
-    __shared__ float accs[ONE ? 1 : DOWN_WARPS][ONE ? 1 : MAX_DECODE_T][33];
-    const int lane = threadIdx.x & 31, wib = threadIdx.x >> 5;
-    const int warp = blockIdx.x * DOWN_WARPS + wib;
-    const int nwarps = gridDim.x * DOWN_WARPS;
-    const int nbk = a.H / QK, items = nbk * 16, TK = a.T * a.K;
-    const int row_bytes = nbk * Q6K_BYTES;
-    const size_t exp_bytes = (size_t)row_bytes * a.D;
-    const int nslots = *a.n_slots;
-    uint8_t *rb = rowbuf[wib];
-    for (int n = warp; n < a.D; n += nwarps) {
-        float acc1 = 0.f;
-        if (!ONE)
-            for (int t = 0; t < a.T; t++) accs[wib][t][lane] = 0.f;
-        for (int u = 0; u < nslots; u++) {
-            const int e = a.slot_expert[u];
-            const uint8_t *Dn = (e == a.E ? a.down_sh : a.down + e * exp_bytes) + (size_t)n * row_bytes;
-            __syncwarp();
-            stage_row(rb, Dn, row_bytes, lane);
-            __syncwarp();
-            const int s1 = a.slot_start[u + 1];
-            for (int s = a.slot_start[u]; s < s1; s++) {
-                const int asg = a.assign[s];
-                const int t = asg_token(asg, TK, a.K);
-                const float wgt = asg < TK ? a.w[asg] : (a.shared_gate ? a.gsc[t] : 1.0f);
-                const float *hrow = a.h + (size_t)asg * a.H;
-                float part = 0.f;
-                for (int j = lane; j < items; j += 32)
-                    part += q6k_item_dot(rb + (j >> 4) * Q6K_BYTES, j, hrow + (j >> 4) * QK);
-                if (ONE) acc1 += wgt * part;
-                else accs[wib][t][lane] += wgt * part;
-            }
-        }
-        if (ONE) {
-            float v = warp_sum(acc1);
-            if (lane == 0) a.out[n] = (a.resid ? a.resid[n] : 0.f) + v;
-        } else {
-            __syncwarp();
-            for (int t = 0; t < a.T; t++) {
-                float v = warp_sum(accs[wib][t][lane]);
-                if (lane == 0) {
-                    size_t o = (size_t)t * a.D + n;
-                    a.out[o] = (a.resid ? a.resid[o] : 0.f) + v;
-                }
-            }
-        }
-    }
-}
 
 // Larger T: y[asg][n] for every assignment, one warp per (slot, row).
 __global__ void __launch_bounds__(DOWN_WARPS * 32) expert_down_rows(LayerArgs a) {
@@ -331,11 +280,12 @@ WorkspaceLayout workspace_layout(const ofb_moe_config *c, int max_tokens) {
     L.assign = take(A * 4);
     L.h = take(A * (size_t)c->hidden * 4);
     // y per assignment is only needed beyond the fused decode path
-    L.y = take(max_tokens > MAX_DECODE_T || c->layout == OFB_LAYOUT_INTERLEAVED
-                   ? A * (size_t)c->d_model * 4
-                   : 0);
-    L.cand = take((size_t)(max_tokens < FAST_ROUTE_MAX_T ? max_tokens : FAST_ROUTE_MAX_T) * (E + 1) * 16);
-    L.counters_bytes = (FAST_ROUTE_MAX_T + 1 + 3) * 4;
+    L.y = take(A * (size_t)c->d_model * 4);
+    const size_t Tf = (size_t)(max_tokens < FAST_ROUTE_MAX_T ? max_tokens : FAST_ROUTE_MAX_T);
+    L.cand = take(Tf * (E + 1) * 16);
+    L.xq = take(Tf * xq_stride(c->d_model));
+    // route tickets [64] + [1], route stats [3], pad [1], down-combine tickets [D/8]
+    L.counters_bytes = (FAST_ROUTE_MAX_T + 4 + c->d_model / 8) * 4;
     L.counters = take(L.counters_bytes);
     L.total = off;
     return L;
@@ -391,9 +341,10 @@ int run_moe_layer(const ofb_moe_config *cfg, const ofb_moe_weights *wt, const fl
         // one launch: certified routing, shared-expert gates, dispatch plan
         int *ctr = (int *)(base + L.counters);
         if ((st = launch_route_fast(wt->router, x, p.shared_gate ? wt->shexp_gate : nullptr, T, D, E, K,
-                                    cfg->routing, cfg->renorm, (double2 *)(base + L.cand), ctr,
-                                    ctr + FAST_ROUTE_MAX_T, ctr + FAST_ROUTE_MAX_T + 1, idx, w, p.gsc, &p,
-                                    s)))
+                                    cfg->routing, cfg->renorm, (double2 *)(base + L.cand),
+                                    ctr + FAST_ROUTE_MAX_T, ctr + FAST_ROUTE_MAX_T + 1, idx, w, p.gsc,
+                                    (T <= MAX_DECODE_T && H <= MAX_DECODE_H) ? base + L.xq : nullptr,
+                                    &p, s)))
             return st;
         mark(1);
         mark(2);
@@ -435,13 +386,19 @@ int run_moe_layer(const ofb_moe_config *cfg, const ofb_moe_weights *wt, const fl
         mark(4);
         return OFB_OK;
     }
+    if (T <= MAX_DECODE_T && H <= MAX_DECODE_H) {
+        unsigned char *xq = base + L.xq;
+        if (!fast && (st = launch_quantize_x(x, T, D, xq, s))) return st;
+        if ((st = launch_up_q(a, xq, max_slots, s))) return st;
+        mark(3);
+        int *tickets = (int *)(base + L.counters) + FAST_ROUTE_MAX_T + 4;
+        if ((st = launch_down_q(a, tickets, max_slots, s))) return st;
+        mark(4);
+        return OFB_OK;
+    }
     expert_up_kernel<<<grid_for((uint64_t)max_slots * H, 8, sms * 16), 256, 0, s>>>(a);
     mark(3);
-    if (T == 1) {
-        expert_down_fused<true><<<grid_for(D, DOWN_WARPS, sms * 16), DOWN_WARPS * 32, 0, s>>>(a);
-    } else if (T <= MAX_DECODE_T) {
-        expert_down_fused<false><<<grid_for(D, DOWN_WARPS, sms * 16), DOWN_WARPS * 32, 0, s>>>(a);
-    } else {
+    {
         expert_down_rows<<<grid_for((uint64_t)max_slots * D, DOWN_WARPS, sms * 16), DOWN_WARPS * 32, 0, s>>>(a);
         combine_kernel<<<grid_for((uint64_t)T * D, 256, sms * 4), 256, 0, s>>>(a);
     }

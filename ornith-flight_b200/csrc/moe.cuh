@@ -36,6 +36,7 @@ struct LayerArgs {
 struct WorkspaceLayout {
     size_t logits, idx, w, gsc, n_slots, slot_expert, slot_start, assign, h, y;
     size_t cand;      // fast routing: (approximate logit, bound) per (token, row)
+    size_t xq;        // decode: quantised activations [T][xq_stride(D)]
     size_t counters;  // fast routing tickets [T] + [1] and stats [3]; zero at creation
     size_t counters_bytes;
     size_t total;
@@ -43,10 +44,22 @@ struct WorkspaceLayout {
 
 // Token counts up to which routing uses the certified fast kernel.
 constexpr int FAST_ROUTE_MAX_T = 64;
+// Decode expert kernels (decode.cu): token and hidden-width limits.
+constexpr int MAX_DECODE_T = 32;
+constexpr int MAX_DECODE_H = 1024;
+
+int launch_quantize_x(const float *x, int T, int D, unsigned char *xq, cudaStream_t s);
+int launch_up_q(const LayerArgs &a, const unsigned char *xq, int max_slots, cudaStream_t s);
+int launch_down_q(const LayerArgs &a, int *tickets, int max_slots, cudaStream_t s);
 
 int launch_route_fast(const float *W, const float *x, const float *gate_v, int T, int D, int E, int K,
-                      int routing, int renorm, double2 *cand, int *tok_cnt, int *all_cnt, int *stats,
-                      uint32_t *idx, float *w, float *gsc, const PlanArgs *plan, cudaStream_t s);
+                      int routing, int renorm, double2 *cand, int *all_cnt, int *stats,
+                      uint32_t *idx, float *w, float *gsc, unsigned char *xq, const PlanArgs *plan,
+                      cudaStream_t s);
+
+// Quantised activations of one token: int8 xh[D], uint8 xl[D], then per
+// 32-element sub-block the f32 scale s and the f32 sum of x.
+__host__ __device__ inline size_t xq_stride(int D) { return (size_t)2 * D + (size_t)8 * (D / 32); }
 
 WorkspaceLayout workspace_layout(const ofb_moe_config *c, int max_tokens);
 int check_config(const ofb_moe_config *c);

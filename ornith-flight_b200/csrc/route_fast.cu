@@ -1,5 +1,7 @@
-// route_fast.cu — certified routing for decode-sized batches, with the
-// shared-expert gates and the dispatch plan built in the same launch.
+// route_fast.cu — certified routing for decode-sized batches, in two PDL
+// kernels: router rows (logits + error bounds, shared-expert gates, the
+// activation quantisation for the decode expert kernels) and per-token
+// selection (top-k, certificate, weights) plus the dispatch plan.
 //
 // The reference's router logit is a sequential fp32 sum with separate
 // multiply and add (engine/src/model.c:1019-1025). Reproducing it literally
@@ -15,21 +17,25 @@
 //     so B = u*(A + S_P + n*gamma_n*A), A = sum|p_i|, S_P an upper bound of
 //     sum|P_i| from the segment scan (u = 2^-24, gamma_n = nu/(1-nu)),
 //     inflated by 2^-9 relative plus 2^-60 absolute for the fp64 arithmetic.
-//  2. The last block to finish a token (atomic ticket) ranks the experts by L~
-//     and CERTIFIES the reference's top-k: every adjacent gap in the top-k
-//     and the gap to every other expert must exceed the two bounds plus a
-//     margin M = 2^-14, large enough that expf(l - max) and the divided
-//     probabilities stay strictly ordered after fp32 rounding. Then the
-//     reference's exchange sort (model.c:1042-1049), which only ever swaps on
-//     strict '>', yields exactly this order: the indices are bit-exact.
-//  3. Otherwise (rare: two logits closer than ~1e-4) the block recomputes the
+//  2. One block per token ranks the experts by L~ (warp bitonic sorts, then a
+//     rank among the per-warp winners) and CERTIFIES the reference's top-k:
+//     every adjacent gap in the top-k and the gap to every other expert must
+//     exceed the two bounds plus a margin M = 2^-14, large enough that
+//     expf(l - max) and the divided probabilities stay strictly ordered after
+//     fp32 rounding. Then the reference's exchange sort (model.c:1042-1049),
+//     which only swaps on strict '>', yields exactly this order: the indices
+//     are bit-exact.
+//  3. Otherwise (two logits closer than ~1e-4) the block recomputes the
 //     uncertain candidates with the reference's exact sequential chain and the
 //     host library's expf (exact_expf.h), and emulates the exchange sort on
 //     them; if two candidate probabilities could round together, it
 //     recomputes every expert exactly (bit-exact softmax sum) before sorting.
 // Routing weights come from fp32 softmax of L~ (or the exact logits where
 // computed): within ~1e-6 relative of the reference's (bit-exact in the
-// full-recompute case). The last token's block builds the dispatch plan.
+// full-recompute case). The block finishing the last token builds the plan.
+// Both kernels are launched with programmatic dependent launch: the row
+// kernel loads its router rows before waiting for the previous kernel in the
+// stream, so the router read overlaps the previous layer's tail.
 // Interleaved-layout routers and large batches use the exact kernels of
 // route.cu.
 #include "common.cuh"
@@ -41,18 +47,22 @@
 
 namespace ofb {
 
+constexpr int RR_WARPS = 2;  // router rows per block in the row kernel
 constexpr int FR_WARPS = 8;
+constexpr int FR_THREADS = FR_WARPS * 32;
 constexpr double FR_MARGIN = 0x1.0p-14;
 
 struct FastRouteArgs {
     const float *W, *x, *gate_v;
     int T, D, E, K, routing, renorm;
-    double2 *cand;  // [T][E+1]: (L~, B)
-    int *tok_cnt;   // [T], zero between calls
-    int *all_cnt;   // [1], zero between calls
-    int *stats;     // [3]: certified, candidate recompute, full recompute
+    double bound_scale;  // (1 + 2^-9) * u, u = 2^-24
+    double ngam;         // n * gamma_n
+    double2 *cand;       // [T][E]: (L~, B)
+    int *all_cnt;        // [1], zero between calls
+    int *stats;          // [3]: certified, candidate recompute, full recompute
     uint32_t *idx;
     float *w, *gsc;
+    unsigned char *xq;  // [T][xq_stride(D)] quantised activations, or NULL
     PlanArgs plan;
 };
 
@@ -82,65 +92,131 @@ __device__ __forceinline__ bool close_ulps(float a, float b, int ulps) {
     return abs(ia - ib) <= ulps;
 }
 
-__global__ void __launch_bounds__(FR_WARPS * 32) route_fast_kernel(FastRouteArgs a) {
+// Quantised activations of 32-element sub-block sb (one warp):
+// x ~= s * (256*xh + xl), xh int8, xl uint8, s = max|x|/32767; plus sum(x).
+__device__ __forceinline__ void quantize_subblock(float v, unsigned char *q, int D, int sb, int lane) {
+    float m = fabsf(v);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    const float s = m / 32767.0f;
+    const int xi = (m > 0.0f) ? __float2int_rn(v / s) : 0;
+    q[sb * 32 + lane] = (unsigned char)(xi >> 8);       // floor(xi / 256), int8
+    q[D + sb * 32 + lane] = (unsigned char)(xi & 255);  // remainder, uint8
+    const float xsum = warp_sum(v);
+    if (lane == 0) {
+        reinterpret_cast<float *>(q + 2 * D)[sb] = s;
+        reinterpret_cast<float *>(q + 2 * D)[D / 32 + sb] = xsum;
+    }
+}
+
+// ---- kernel 1: router rows ---------------------------------------------------
+__global__ void __launch_bounds__(RR_WARPS * 32) route_rows_kernel(FastRouteArgs a) {
+    pdl_trigger();
     const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
     const int t = blockIdx.y;
-    const int E = a.E, D = a.D, K = a.K;
-    const int r = blockIdx.x * FR_WARPS + wid;  // router row; r == E is the gate vector
+    const int E = a.E, D = a.D;
+    const int r = blockIdx.x * RR_WARPS + wid;  // router row; r == E is the gate vector
     const float *xt = a.x + (size_t)t * D;
-
-    // ---- 1. approximate logit + bound, one warp per row -------------------
     const bool has_row = (r < E) || (r == E && a.gate_v);
+    const int seg = D / 32;  // multiple of 8
+    constexpr int PF = 16;   // float4 per lane held in flight
+    const float *wr = (r < E) ? a.W + (size_t)r * D : a.gate_v;
+    const float4 *w4 = reinterpret_cast<const float4 *>(wr + lane * seg);
+    const float4 *x4 = reinterpret_cast<const float4 *>(xt + lane * seg);
+    float4 wv[PF], xv[PF];
+    // the router is static: load it before waiting for the producer of x
     if (has_row) {
-        const float *wr = (r < E) ? a.W + (size_t)r * D : a.gate_v;
-        const int seg = D / 32;  // multiple of 8
-        const float4 *w4 = reinterpret_cast<const float4 *>(wr + lane * seg);
-        const float4 *x4 = reinterpret_cast<const float4 *>(xt + lane * seg);
-        double P = 0.0, SP = 0.0, A = 0.0;
-        for (int i = 0; i < seg / 4; i++) {
-            const float4 wv = __ldg(w4 + i), xv = __ldg(x4 + i);
-            const double p0 = (double)xv.x * wv.x, p1 = (double)xv.y * wv.y;
-            const double p2 = (double)xv.z * wv.z, p3 = (double)xv.w * wv.w;
+#pragma unroll
+        for (int j = 0; j < PF; j++)
+            if (j < seg / 4) wv[j] = __ldg(w4 + j);
+    }
+    pdl_wait();
+    if (has_row) {
+#pragma unroll
+        for (int j = 0; j < PF; j++)
+            if (j < seg / 4) xv[j] = __ldg(x4 + j);
+    }
+    if (a.xq) {
+        unsigned char *q = a.xq + (size_t)t * xq_stride(D);
+        for (int sb = r; sb < D / 32; sb += gridDim.x * RR_WARPS)
+            quantize_subblock(__ldg(xt + sb * 32 + lane), q, D, sb, lane);
+    }
+    if (!has_row) return;
+    double P = 0.0, SP = 0.0, A = 0.0;
+    for (int i0 = 0; i0 < seg / 4; i0 += PF) {
+        if (i0) {
+#pragma unroll
+            for (int j = 0; j < PF; j++)
+                if (i0 + j < seg / 4) { wv[j] = __ldg(w4 + i0 + j); xv[j] = __ldg(x4 + i0 + j); }
+        }
+#pragma unroll
+        for (int j = 0; j < PF; j++) {
+            if (i0 + j >= seg / 4) break;
+            const double p0 = (double)xv[j].x * wv[j].x, p1 = (double)xv[j].y * wv[j].y;
+            const double p2 = (double)xv[j].z * wv[j].z, p3 = (double)xv[j].w * wv[j].w;
             P += p0; SP += fabs(P);
             P += p1; SP += fabs(P);
             P += p2; SP += fabs(P);
             P += p3; SP += fabs(P);
-            A += fabs(p0) + fabs(p1) + fabs(p2) + fabs(p3);
+            A += (fabs(p0) + fabs(p1)) + (fabs(p2) + fabs(p3));
         }
-        // exclusive scan of segment sums -> |prefix| bound of this segment
-        double inc = P;
+    }
+    // exclusive scan of segment sums -> |prefix| bound of this segment
+    double inc = P;
 #pragma unroll
-        for (int o = 1; o < 32; o <<= 1) {
-            double up = __shfl_up_sync(0xffffffffu, inc, o);
-            if (lane >= o) inc += up;
-        }
-        const double base = inc - P;
-        const double sp_bound = (double)seg * fabs(base) + SP;
-        const double L = warp_sum_d(P);
-        const double SPt = warp_sum_d(sp_bound);
-        const double At = warp_sum_d(A);
-        if (lane == 0) {
-            if (r < E) {
-                const double u = 0x1.0p-24, n = (double)D;
-                const double gam = n * u / (1.0 - n * u);
-                const double B = (1.0 + 0x1.0p-9) * u * (At + SPt + n * gam * At) + 0x1.0p-60;
-                a.cand[(size_t)t * (E + 1) + r] = make_double2(L, B);
-            } else {
-                a.gsc[t] = 1.0f / (1.0f + expf(-(float)L));
-            }
-        }
+    for (int o = 1; o < 32; o <<= 1) {
+        double up = __shfl_up_sync(0xffffffffu, inc, o);
+        if (lane >= o) inc += up;
     }
+    const double sp_bound = (double)seg * fabs(inc - P) + SP;
+    const double L = warp_sum_d(P);
+    const double SPt = warp_sum_d(sp_bound);
+    const double At = warp_sum_d(A);
+    if (lane == 0) {
+        if (r < E)
+            a.cand[(size_t)t * E + r] = make_double2(L, a.bound_scale * (At + SPt + a.ngam * At) + 0x1.0p-60);
+        else
+            a.gsc[t] = 1.0f / (1.0f + expf(-(float)L));
+    }
+}
 
-    // ---- last block of this token does the selection ------------------------
-    __shared__ int s_last;
-    __syncthreads();
-    if (threadIdx.x == 0) {
-        __threadfence();
-        s_last = (atomicAdd(&a.tok_cnt[t], 1) == (int)gridDim.x - 1);
+// ---- kernel 2: selection, one block per token ---------------------------------
+struct KeyIdx { float k; int i; };
+__device__ __forceinline__ bool better(KeyIdx a, KeyIdx b) { return a.k > b.k || (a.k == b.k && a.i < b.i); }
+
+// Descending bitonic sort of one value per lane (lane 0 ends with the best).
+__device__ __forceinline__ KeyIdx warp_sort_desc(KeyIdx v, int lane) {
+#pragma unroll
+    for (int k = 2; k <= 32; k <<= 1) {
+#pragma unroll
+        for (int j = k >> 1; j > 0; j >>= 1) {
+            KeyIdx o;
+            o.k = __shfl_xor_sync(0xffffffffu, v.k, j);
+            o.i = __shfl_xor_sync(0xffffffffu, v.i, j);
+            const bool keep_better = (((lane & j) == 0) == ((lane & k) == 0));
+            if (keep_better ? better(o, v) : better(v, o)) v = o;
+        }
     }
+    return v;
+}
+
+__device__ __forceinline__ float block_sum(float v, float *red) {
+    v = warp_sum(v);
+    const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
     __syncthreads();
-    if (!s_last) return;
-    __threadfence();
+    if (lane == 0) red[wid] = v;
+    __syncthreads();
+    float r = 0.f;
+    for (int i = 0; i < FR_WARPS; i++) r += red[i];
+    return r;
+}
+
+__global__ void __launch_bounds__(FR_THREADS) route_select_fast(FastRouteArgs a) {
+    pdl_trigger();
+    const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5, tid = threadIdx.x;
+    const int t = blockIdx.x;
+    const int E = a.E, D = a.D, K = a.K;
+    const float *xt = a.x + (size_t)t * D;
 
     extern __shared__ __align__(16) unsigned char smem[];
     double *Ls = reinterpret_cast<double *>(smem);     // [E]
@@ -151,66 +227,76 @@ __global__ void __launch_bounds__(FR_WARPS * 32) route_fast_kernel(FastRouteArgs
     int *oid = reinterpret_cast<int *>(oval + E);       // [E]
     float *xs = reinterpret_cast<float *>(oid + E);     // [D]
     int *taken = reinterpret_cast<int *>(xs + D);       // [E]
+    __shared__ KeyIdx s_cand[32 * 17];
     __shared__ int s_top[17];
     __shared__ int s_mode;  // 0 certified, 1 candidate recompute, 2 full recompute
-    __shared__ float s_ex[16];
+    __shared__ float s_red[FR_WARPS];
+    __shared__ double s_hred[FR_WARPS];
+    __shared__ float s_w[16];
+    __shared__ int s_last;
 
-    const double2 *cd = a.cand + (size_t)t * (E + 1);
-    for (int e = threadIdx.x; e < E; e += blockDim.x) {
-        double2 v = __ldcg(cd + e);
+    pdl_wait();
+    const double2 *cd = a.cand + (size_t)t * E;
+    for (int e = tid; e < E; e += FR_THREADS) {
+        const double2 v = cd[e];
         Ls[e] = v.x;
         Bs[e] = v.y;
         taken[e] = 0;
     }
+    if (tid == 0) s_mode = 0;
     __syncthreads();
-
-    if (wid == 0) {
-        // top-k by L~ (ties: lower index first)
-        const int kk = K < E ? K + 1 : K;
-        for (int it = 0; it < kk; it++) {
-            double bv = -INFINITY;
-            int be = 0x7fffffff;
-            for (int e = lane; e < E; e += 32)
-                if (!taken[e] && (Ls[e] > bv || (Ls[e] == bv && e < be))) { bv = Ls[e]; be = e; }
+    // top K+1 by L~ (ties by index): per-32 chunk bitonic sort, then rank
+    // the chunk winners. Ranking key is float; the certificate uses L~, B.
+    const int kk = K < E ? K + 1 : K;
+    const int nchunks = (E + 31) / 32;
+    for (int c = wid; c < nchunks; c += FR_WARPS) {
+        const int e = c * 32 + lane;
+        KeyIdx v = (e < E) ? KeyIdx{(float)Ls[e], e} : KeyIdx{-INFINITY, 0x7fffffff};
+        v = warp_sort_desc(v, lane);
+        if (lane < kk) s_cand[c * kk + lane] = v;
+    }
+    __syncthreads();
+    const int ncand = nchunks * kk;
+    for (int i = tid; i < ncand; i += FR_THREADS) {
+        const KeyIdx v = s_cand[i];
+        int rank = 0;
+        for (int j = 0; j < ncand; j++) rank += better(s_cand[j], v);
+        if (rank < kk && v.i < E) s_top[rank] = v.i;
+    }
+    __syncthreads();
+    if (tid < K) taken[s_top[tid]] = 1;
+    __syncthreads();
+    // certificate: adjacent gaps inside the top-k, and top-k vs the rest
+    double hi_rest = -INFINITY;
+    for (int e = tid; e < E; e += FR_THREADS)
+        if (!taken[e]) hi_rest = fmax(hi_rest, Ls[e] + Bs[e]);
 #pragma unroll
-            for (int o = 16; o > 0; o >>= 1) {
-                double ov = __shfl_xor_sync(0xffffffffu, bv, o);
-                int oe = __shfl_xor_sync(0xffffffffu, be, o);
-                if (ov > bv || (ov == bv && oe < be)) { bv = ov; be = oe; }
-            }
-            if (it < K) {
-                if (lane == 0) { s_top[it] = be; taken[be] = 1; }
-            }
-            __syncwarp();
+    for (int o = 16; o > 0; o >>= 1) hi_rest = fmax(hi_rest, __shfl_xor_sync(0xffffffffu, hi_rest, o));
+    if (lane == 0) s_hred[wid] = hi_rest;
+    __syncthreads();
+    if (tid < K) {
+        const int e0 = s_top[tid];
+        double nxt;
+        if (tid + 1 < K) {
+            const int e1 = s_top[tid + 1];
+            nxt = Ls[e1] + Bs[e1];
+        } else {
+            nxt = -INFINITY;
+            for (int i = 0; i < FR_WARPS; i++) nxt = fmax(nxt, s_hred[i]);
         }
-        // largest upper bound outside the top-k
-        double hi_rest = -INFINITY;
-        for (int e = lane; e < E; e += 32)
-            if (!taken[e]) hi_rest = fmax(hi_rest, Ls[e] + Bs[e]);
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) hi_rest = fmax(hi_rest, __shfl_xor_sync(0xffffffffu, hi_rest, o));
-        if (lane == 0) {
-            bool ok = true;
-            for (int q = 0; q + 1 < K; q++) {
-                const int e0 = s_top[q], e1 = s_top[q + 1];
-                ok = ok && (Ls[e0] - Bs[e0] > Ls[e1] + Bs[e1] + FR_MARGIN);
-            }
-            const int el = s_top[K - 1];
-            ok = ok && (Ls[el] - Bs[el] > hi_rest + FR_MARGIN);
-            ok = ok && (Ls[el] - Ls[s_top[0]] > -80.0);
-            s_mode = ok ? 0 : 1;
-        }
-        __syncwarp();
+        bool ok = Ls[e0] - Bs[e0] > nxt + FR_MARGIN;
+        if (tid == K - 1) ok = ok && (Ls[e0] - Ls[s_top[0]] > -80.0);
+        if (!ok) s_mode = 1;
     }
     __syncthreads();
 
     if (s_mode != 0) {
         // ---- candidate recompute with the reference's exact chain --------
-        for (int d = threadIdx.x; d < D; d += blockDim.x) xs[d] = xt[d];
+        for (int d = tid; d < D; d += FR_THREADS) xs[d] = xt[d];
         double lo_min = INFINITY;
         for (int q = 0; q < K; q++) lo_min = fmin(lo_min, Ls[s_top[q]] - Bs[s_top[q]]);
         __syncthreads();
-        for (int e = threadIdx.x; e < E; e += blockDim.x) {
+        for (int e = tid; e < E; e += FR_THREADS) {
             const bool cand = (Ls[e] + Bs[e] >= lo_min - FR_MARGIN);
             val[e] = cand ? exact_logit(a.W + (size_t)e * D, xs, D) : -INFINITY;
             id[e] = e;
@@ -221,20 +307,19 @@ __global__ void __launch_bounds__(FR_WARPS * 32) route_fast_kernel(FastRouteArgs
             // probabilities are ordered like expf(l - max) unless two of them
             // are within a few ulps (then the division could tie them)
             __shared__ float s_max;
-            if (threadIdx.x == 0) {
+            __shared__ int s_unsafe;
+            if (tid == 0) {
                 float m = -INFINITY;
                 for (int e = 0; e < E; e++)
                     if (taken[e]) m = fmaxf(m, val[e]);
                 s_max = m;
+                s_unsafe = 0;
             }
             __syncthreads();
-            for (int e = threadIdx.x; e < E; e += blockDim.x)
+            for (int e = tid; e < E; e += FR_THREADS)
                 oval[e] = taken[e] ? ofb_exact_expf(__fsub_rn(val[e], s_max)) : -INFINITY;
             __syncthreads();
-            __shared__ int s_unsafe;
-            if (threadIdx.x == 0) s_unsafe = 0;
-            __syncthreads();
-            for (int e = threadIdx.x; e < E; e += blockDim.x) {
+            for (int e = tid; e < E; e += FR_THREADS) {
                 if (!taken[e]) continue;
                 for (int f = 0; f < E; f++)
                     if (f != e && taken[f] && close_ulps(oval[e], oval[f], 4)) s_unsafe = 1;
@@ -242,29 +327,28 @@ __global__ void __launch_bounds__(FR_WARPS * 32) route_fast_kernel(FastRouteArgs
             __syncthreads();
             if (s_unsafe) {
                 // ---- full recompute: every logit exact, softmax as the reference
-                for (int e = threadIdx.x; e < E; e += blockDim.x)
+                for (int e = tid; e < E; e += FR_THREADS)
                     val[e] = taken[e] ? val[e] : exact_logit(a.W + (size_t)e * D, xs, D);
                 __syncthreads();
-                if (threadIdx.x == 0) {
+                if (tid == 0) {
                     float m = val[0];
                     for (int e = 1; e < E; e++) if (val[e] > m) m = val[e];
                     s_max = m;
                 }
                 __syncthreads();
-                for (int e = threadIdx.x; e < E; e += blockDim.x)
-                    val[e] = ofb_exact_expf(__fsub_rn(val[e], s_max));
+                for (int e = tid; e < E; e += FR_THREADS) val[e] = ofb_exact_expf(__fsub_rn(val[e], s_max));
                 __syncthreads();
                 __shared__ float s_sum;
-                if (threadIdx.x == 0) {
+                if (tid == 0) {
                     float s = 0.0f;
                     for (int e = 0; e < E; e++) s = __fadd_rn(s, val[e]);
                     s_sum = s;
                     s_mode = 2;
                 }
                 __syncthreads();
-                for (int e = threadIdx.x; e < E; e += blockDim.x) val[e] = __fdiv_rn(val[e], s_sum);
+                for (int e = tid; e < E; e += FR_THREADS) val[e] = __fdiv_rn(val[e], s_sum);
             } else {
-                for (int e = threadIdx.x; e < E; e += blockDim.x) val[e] = oval[e];
+                for (int e = tid; e < E; e += FR_THREADS) val[e] = oval[e];
             }
             __syncthreads();
         }
@@ -277,65 +361,56 @@ __global__ void __launch_bounds__(FR_WARPS * 32) route_fast_kernel(FastRouteArgs
     }
 
     // ---- weights --------------------------------------------------------------
-    if (wid == 0) {
-        uint32_t *io = a.idx + (size_t)t * K;
-        float *wo = a.w + (size_t)t * K;
-        if (s_mode == 2) {
-            // bit-exact: val holds the reference's probabilities, id the order
-            if (lane == 0) {
-                float ssum = 0.0f;
-                for (int q = 0; q < K; q++) ssum = __fadd_rn(ssum, val[q]);
-                for (int q = 0; q < K; q++) {
-                    io[q] = (uint32_t)id[q];
-                    wo[q] = a.renorm ? __fdiv_rn(val[q], ssum) : val[q];
-                }
-            }
-        } else {
-            const float m = (float)Ls[s_top[0]];
-            if (a.routing == OFB_ROUTE_GET_ROUTING) {
-                if (lane < K) s_ex[lane] = expf((float)Ls[s_top[lane]] - m);
-                __syncwarp();
-                if (lane == 0) {
-                    float s = 0.0f;
-                    for (int q = 0; q < K; q++) s += s_ex[q];
-                    for (int q = 0; q < K; q++) { io[q] = (uint32_t)s_top[q]; wo[q] = s_ex[q] / s; }
-                }
-            } else {
-                float s = 0.0f;
-                for (int e = lane; e < E; e += 32) s += expf((float)Ls[e] - m);
-                s = warp_sum(s);
-                if (lane < K) s_ex[lane] = expf((float)Ls[s_top[lane]] - m) / s;
-                __syncwarp();
-                if (lane == 0) {
-                    float ss = 0.0f;
-                    for (int q = 0; q < K; q++) ss += s_ex[q];
-                    for (int q = 0; q < K; q++) {
-                        io[q] = (uint32_t)s_top[q];
-                        wo[q] = a.renorm ? s_ex[q] / ss : s_ex[q];
-                    }
-                }
+    uint32_t *io = a.idx + (size_t)t * K;
+    float *wo = a.w + (size_t)t * K;
+    if (s_mode == 2) {
+        // bit-exact: val holds the reference's probabilities, id the order
+        if (tid == 0) {
+            float ssum = 0.0f;
+            for (int q = 0; q < K; q++) ssum = __fadd_rn(ssum, val[q]);
+            for (int q = 0; q < K; q++) {
+                io[q] = (uint32_t)id[q];
+                wo[q] = a.renorm ? __fdiv_rn(val[q], ssum) : val[q];
             }
         }
-        if (lane == 0) {
-            if (a.stats) atomicAdd(&a.stats[s_mode], 1);
-            a.tok_cnt[t] = 0;
+    } else {
+        const float m = (float)Ls[s_top[0]];
+        float sum = 0.f;
+        if (a.routing == OFB_ROUTE_FORWARD) {
+            for (int e = tid; e < E; e += FR_THREADS) sum += expf((float)Ls[e] - m);
+        } else if (tid < K) {
+            sum = expf((float)Ls[s_top[tid]] - m);
+        }
+        sum = block_sum(sum, s_red);
+        if (tid < K) s_w[tid] = expf((float)Ls[s_top[tid]] - m) / sum;
+        __syncthreads();
+        if (tid < K) {
+            float ss = 0.f;
+            for (int q = 0; q < K; q++) ss += s_w[q];
+            io[tid] = (uint32_t)s_top[tid];
+            wo[tid] = (a.routing == OFB_ROUTE_FORWARD && a.renorm) ? s_w[tid] / ss : s_w[tid];
         }
     }
+    if (tid == 0 && a.stats) atomicAdd(&a.stats[s_mode], 1);
 
     // ---- the block finishing the last token builds the dispatch plan --------
-    __syncthreads();
-    if (threadIdx.x == 0) {
-        __threadfence();
-        s_last = (atomicAdd(a.all_cnt, 1) == a.T - 1);
+    if (a.T == 1) {
+        s_last = 1;
+    } else {
+        __syncthreads();
+        if (tid == 0) {
+            __threadfence();
+            s_last = (atomicAdd(a.all_cnt, 1) == a.T - 1);
+        }
     }
     __syncthreads();
     if (!s_last) return;
-    __threadfence();
+    if (a.T > 1) __threadfence();
     int *cnt = reinterpret_cast<int *>(smem);
     int *cursor = cnt + 1024;
     __shared__ int wsum[66];
     if (a.plan.n_slots) build_plan(a.plan, cnt, cursor, wsum);
-    if (threadIdx.x == 0) *a.all_cnt = 0;
+    if (tid == 0) *a.all_cnt = 0;
 }
 
 size_t route_fast_smem(int E, int D) {
@@ -345,25 +420,30 @@ size_t route_fast_smem(int E, int D) {
 }
 
 int launch_route_fast(const float *W, const float *x, const float *gate_v, int T, int D, int E, int K,
-                      int routing, int renorm, double2 *cand, int *tok_cnt, int *all_cnt, int *stats,
-                      uint32_t *idx, float *w, float *gsc, const PlanArgs *plan, cudaStream_t s) {
+                      int routing, int renorm, double2 *cand, int *all_cnt, int *stats,
+                      uint32_t *idx, float *w, float *gsc, unsigned char *xq, const PlanArgs *plan,
+                      cudaStream_t s) {
     FastRouteArgs a;
     a.W = W; a.x = x; a.gate_v = gate_v;
     a.T = T; a.D = D; a.E = E; a.K = K; a.routing = routing; a.renorm = renorm;
-    a.cand = cand; a.tok_cnt = tok_cnt; a.all_cnt = all_cnt; a.stats = stats;
-    a.idx = idx; a.w = w; a.gsc = gsc;
+    const double u = 0x1.0p-24, n = (double)D;
+    a.bound_scale = (1.0 + 0x1.0p-9) * u;
+    a.ngam = n * (n * u / (1.0 - n * u));
+    a.cand = cand; a.all_cnt = all_cnt; a.stats = stats;
+    a.idx = idx; a.w = w; a.gsc = gsc; a.xq = xq;
     if (plan) a.plan = *plan;
     else memset(&a.plan, 0, sizeof(a.plan));
     const size_t smem = route_fast_smem(E, D);
     static bool attr_set = false;
     if (!attr_set) {
-        cudaFuncSetAttribute(route_fast_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 64 * 1024);
+        cudaFuncSetAttribute(route_select_fast, cudaFuncAttributeMaxDynamicSharedMemorySize, 64 * 1024);
         attr_set = true;
     }
     if (smem > 64 * 1024) { set_error("route_fast: E/D too large for shared memory"); return OFB_EUNSUPPORTED; }
-    dim3 grid((E + 1 + FR_WARPS - 1) / FR_WARPS, T);
-    route_fast_kernel<<<grid, FR_WARPS * 32, smem, s>>>(a);
-    OFB_CHECK_LAUNCH("route_fast");
+    cudaError_t e = launch_pdl(route_rows_kernel, dim3((E + 1 + RR_WARPS - 1) / RR_WARPS, T),
+                               dim3(RR_WARPS * 32), 0, s, a);
+    if (e == cudaSuccess) e = launch_pdl(route_select_fast, dim3(T), dim3(FR_THREADS), smem, s, a);
+    if (e != cudaSuccess) return cuda_status(e, "route_fast launch");
     return OFB_OK;
 }
 
