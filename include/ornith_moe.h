@@ -162,6 +162,24 @@ int ofb_moe_forward_profiled(const ofb_moe_config *cfg, const ofb_moe_weights *w
  * every logit exactly. Synchronous. Diagnostic; no reference counterpart. */
 int ofb_workspace_route_stats(ofb_workspace *ws, int counts[3]);
 
+/* ofb_moe_forward without any device allocation, for callers that cannot call
+ * cudaMalloc: an engine whose device memory is reserved up front by its own
+ * pool or budget (a raw allocation could fail or take memory already
+ * promised elsewhere), or a per-token decode loop where allocating would
+ * synchronise the device. No counterpart in the reference (its CPU and Metal
+ * backends allocate per call).
+ * The scratch is one fixed array of ofb_noalloc_capacity() bytes (8 MiB) in
+ * device memory, held by every GPU that loads the library until exit; a call
+ * whose layer and token count need more returns OFB_ETOOLARGE. The first call
+ * on a device looks up the array's device address (make it before any stream
+ * capture). All calls share the array: calls whose GPU work overlaps (other
+ * streams or host threads) race; calls in one stream are safe. Arguments and
+ * results as ofb_moe_forward, without the workspace. */
+int ofb_moe_forward_noalloc(const ofb_moe_config *cfg, const ofb_moe_weights *w, const float *x,
+                            const float *resid, float *out, int n_tokens, uint32_t *idx_out,
+                            float *w_out, void *stream);
+size_t ofb_noalloc_capacity(void);
+
 /* ---- seeded synthetic inputs ---------------------------------------------- */
 
 /* Fills n_blocks Q4_K or Q6_K super-blocks on the device from a counter-based

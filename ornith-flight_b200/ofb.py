@@ -67,6 +67,8 @@ def _load() -> ctypes.CDLL:
         "ofb_moe_forward": (i32, [cfgp, wp, vp, vp, vp, i32, vp, vp, vp, vp]),
         "ofb_moe_forward_profiled": (i32, [cfgp, wp, vp, vp, vp, i32, vp, vp, vp]),
         "ofb_workspace_route_stats": (i32, [vp, ctypes.POINTER(ctypes.c_int * 3)]),
+        "ofb_moe_forward_noalloc": (i32, [cfgp, wp, vp, vp, vp, i32, vp, vp, vp]),
+        "ofb_noalloc_capacity": (sz, []),
         "ofb_synth_blocks": (i32, [vp, i32, u64, u64, u64, u64, vp]),
         "ofb_synth_blocks_host": (None, [vp, i32, u64, u64, u64, u64]),
         "ofb_synth_normal_host": (None, [vp, u64, u64, u64, ctypes.c_float]),
@@ -300,6 +302,17 @@ class MoeLayer:
                                             None, _ptr(out), x.shape[0], self.ws.handle,
                                             _stream(stream), ms))
         return list(ms)
+
+    def forward_noalloc(self, x: torch.Tensor, resid: torch.Tensor | None = None,
+                        out: torch.Tensor | None = None, idx: torch.Tensor | None = None,
+                        w: torch.Tensor | None = None, stream=None) -> torch.Tensor:
+        """forward() through ofb_moe_forward_noalloc (fixed in-library scratch)."""
+        if out is None:
+            out = torch.empty_like(x)
+        _check(lib.ofb_moe_forward_noalloc(ctypes.byref(self._cfg), ctypes.byref(self._w), _ptr(x),
+                                           _ptr(resid), _ptr(out), x.shape[0], _ptr(idx), _ptr(w),
+                                           _stream(stream)))
+        return out
 
     def route(self, x: torch.Tensor, stream=None):
         T = x.shape[0]
