@@ -2,25 +2,18 @@
 // weighted combine (the block engine/src/model.c:992-1143, batched).
 //
 // Pipeline for n tokens (all stream-ordered, no host synchronisation):
-//   1. routing (route.cu): idx[T][K], w[T][K], bit-exact.
-//   2. plan_kernel: device histogram of the kept assignments per expert,
-//      scan, and a CSR "slot" list: slot u = one used expert (ascending id)
-//      with its assignment ids; the shared expert is the last slot with every
-//      token. Assignment id a < T*K is (token a/K, rank a%K); a >= T*K is the
-//      shared expert of token a-T*K. Also the shared-expert sigmoid gates.
-//   3. expert_up_kernel: per (slot, hidden row) one warp streams the Q4_K
-//      gate and up rows (144-byte blocks, 16-byte vector loads, dequant fused
-//      into the dot product) and writes h = silu(x.G) * (x.U) per token.
-//   4. decode (T <= 32): expert_down_fused — per output row one warp walks
-//      every slot's Q6_K down row (staged through shared memory because the
-//      210-byte blocks are only 2-byte aligned), dots it with h and
-//      accumulates w * y per token; the combine and residual happen in the
-//      same pass, so y never reaches HBM.
-//      larger T: expert_down_rows writes y per assignment, combine_kernel sums
-//      them per token in the reference's order.
-// The interleaved (reference-slice) layout uses the element-wise kernels at
-// the end of the file; it touches every block of a tensor by construction and
-// is the correctness path for that layout.
+//   1. routing: certified fast kernels for decode batches (route_fast.cu),
+//      the exact kernels otherwise (route.cu); idx[T][K], w[T][K].
+//   2. dispatch plan (plan.cuh): device histogram of the kept assignments per
+//      expert, scan, and a CSR "slot" list: slot u = one used expert
+//      (ascending id) with its assignment ids; the shared expert is the last
+//      slot with every token. Assignment id a < T*K is (token a/K, rank a%K);
+//      a >= T*K is the shared expert of token a-T*K.
+//   3. experts: decode batches (T <= 32) use the dp4a GEMV kernels of
+//      decode.cu; larger batches the tcgen05 grouped GEMMs of prefill.cu.
+// The interleaved (reference-slice) layout uses the element-wise kernels
+// below; it touches every block of a tensor by construction and is the
+// correctness path for that layout.
 #include <cstdlib>
 #include <cstring>
 
@@ -31,8 +24,6 @@
 
 namespace ofb {
 
-
-
 __device__ __forceinline__ float silu_ref(float g) {
     // engine/src/model.c:340-344
     if (g < -50.0f) return 0.0f;
@@ -40,141 +31,12 @@ __device__ __forceinline__ float silu_ref(float g) {
     return g / (1.0f + expf(-g));
 }
 
+__device__ __forceinline__ int asg_token(int a, int TK, int K) { return a < TK ? a / K : a - TK; }
+
 __global__ void __launch_bounds__(1024) plan_kernel(PlanArgs p) {
     __shared__ int cnt[1024], cursor[1024], wsum[66];
     build_plan(p, cnt, cursor, wsum);
     if (p.has_shared && p.shared_gate) shared_gates(p);
-}
-
-// ---- contiguous layout: gate/up ------------------------------------------
-// Dot product of one 64-element chunk c of a Q4_K block with x[0..64):
-// sum_i (d*sc*q_i - dmin*m) x_i = d*sc * sum q_i x_i - dmin*m * sum x_i.
-__device__ __forceinline__ float q4k_chunk_dot(const uint8_t *blk, int c, const float *xs) {
-    const uint4 hdr = __ldg(reinterpret_cast<const uint4 *>(blk));
-    const uint4 qa = __ldg(reinterpret_cast<const uint4 *>(blk + 16 + c * 32));
-    const uint4 qb = __ldg(reinterpret_cast<const uint4 *>(blk + 32 + c * 32));
-    const uint32_t qw[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
-    const uint32_t s[3] = {hdr.y, hdr.z, hdr.w};
-    int sc0, m0, sc1, m1;
-    q4k_scale_min(s, 2 * c, sc0, m0);
-    q4k_scale_min(s, 2 * c + 1, sc1, m1);
-    const float d = half_bits_ref(hdr.x & 0xFFFFu), dmin = half_bits_ref(hdr.x >> 16);
-    float lo = 0.f, hi = 0.f, xl = 0.f, xh = 0.f;
-#pragma unroll
-    for (int w = 0; w < 8; w++) {
-        const float4 a = *reinterpret_cast<const float4 *>(xs + 4 * w);
-        const float4 b = *reinterpret_cast<const float4 *>(xs + 32 + 4 * w);
-        const uint32_t q = qw[w];
-        lo += (float)(q & 0xF) * a.x + (float)((q >> 8) & 0xF) * a.y +
-              (float)((q >> 16) & 0xF) * a.z + (float)((q >> 24) & 0xF) * a.w;
-        hi += (float)((q >> 4) & 0xF) * b.x + (float)((q >> 12) & 0xF) * b.y +
-              (float)((q >> 20) & 0xF) * b.z + (float)(q >> 28) * b.w;
-        xl += (a.x + a.y) + (a.z + a.w);
-        xh += (b.x + b.y) + (b.z + b.w);
-    }
-    return d * (float)sc0 * lo - dmin * (float)m0 * xl + d * (float)sc1 * hi - dmin * (float)m1 * xh;
-}
-
-__device__ __forceinline__ int asg_token(int a, int TK, int K) { return a < TK ? a / K : a - TK; }
-
-__global__ void __launch_bounds__(256) expert_up_kernel(LayerArgs a) {
-    const int lane = threadIdx.x & 31;
-    const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
-    const int nwarps = (gridDim.x * blockDim.x) >> 5;
-    const int nbr = a.D / QK, items = nbr * 4, TK = a.T * a.K;
-    const size_t row_bytes = (size_t)nbr * Q4K_BYTES;
-    const size_t exp_bytes = row_bytes * a.H;
-    const int units = *a.n_slots * a.H;
-    for (int unit = warp; unit < units; unit += nwarps) {
-        const int u = unit / a.H, m = unit - u * a.H;
-        const int e = a.slot_expert[u];
-        const uint8_t *G = (e == a.E ? a.gate_sh : a.gate + e * exp_bytes) + m * row_bytes;
-        const uint8_t *U = (e == a.E ? a.up_sh : a.up + e * exp_bytes) + m * row_bytes;
-        const int s1 = a.slot_start[u + 1];
-        for (int s = a.slot_start[u]; s < s1; s++) {
-            const int asg = a.assign[s];
-            const float *xt = a.x + (size_t)asg_token(asg, TK, a.K) * a.D;
-            float gp = 0.f, up = 0.f;
-            for (int j = lane; j < items; j += 32) {
-                const int b = j >> 2, c = j & 3;
-                const float *xs = xt + b * QK + c * 64;
-                gp += q4k_chunk_dot(G + b * Q4K_BYTES, c, xs);
-                up += q4k_chunk_dot(U + b * Q4K_BYTES, c, xs);
-            }
-            gp = warp_sum(gp);
-            up = warp_sum(up);
-            if (lane == 0) a.h[(size_t)asg * a.H + m] = silu_ref(gp) * up;
-        }
-    }
-}
-
-// ---- contiguous layout: down ---------------------------------------------
-// Lane item j of a staged Q6_K row: block b = j/16, half = (j/8)%2,
-// l = 4*(j%8) .. +3; the item covers quads 0..3 => 16 outputs.
-__device__ __forceinline__ float q6k_item_dot(const uint8_t *blk, int j, const float *hrow_blk) {
-    const int half = (j >> 3) & 1, l0 = (j & 7) * 4;
-    const uint8_t *ql = blk + half * 64;
-    const uint8_t *qh = blk + 128 + half * 32;
-    const int8_t *sc = reinterpret_cast<const int8_t *>(blk + 192 + half * 8 + (l0 >> 4));
-    const float d = half_bits_ref((uint32_t)blk[208] | ((uint32_t)blk[209] << 8));
-    const float *hb = hrow_blk + half * 128 + l0;
-    float acc = 0.f;
-#pragma unroll
-    for (int quad = 0; quad < 4; quad++) {
-        const float4 hv = *reinterpret_cast<const float4 *>(hb + quad * 32);
-        const float hh[4] = {hv.x, hv.y, hv.z, hv.w};
-        float part = 0.f;
-#pragma unroll
-        for (int i = 0; i < 4; i++) {
-            const int l = l0 + i;
-            const uint8_t lb = ql[(quad & 1) * 32 + l];
-            const int nib = (quad < 2) ? (lb & 0xF) : (lb >> 4);
-            const int top = (qh[l] >> (2 * quad)) & 3;
-            part += (float)((nib | (top << 4)) - 32) * hh[i];
-        }
-        acc += (float)sc[quad * 2] * part;
-    }
-    return d * acc;
-}
-
-__device__ __forceinline__ void stage_row(uint8_t *dst, const uint8_t *src, int bytes, int lane) {
-    const uint16_t *s2 = reinterpret_cast<const uint16_t *>(src);
-    uint16_t *d2 = reinterpret_cast<uint16_t *>(dst);
-    for (int i = lane; i < bytes / 2; i += 32) d2[i] = __ldg(s2 + i);
-}
-
-constexpr int DOWN_WARPS = 4;
-constexpr int MAX_ROW_BYTES = 16 * Q6K_BYTES;  // hidden <= 4096
-
-// Larger T: y[asg][n] for every assignment, one warp per (slot, row).
-__global__ void __launch_bounds__(DOWN_WARPS * 32) expert_down_rows(LayerArgs a) {
-    __shared__ __align__(16) uint8_t rowbuf[DOWN_WARPS][MAX_ROW_BYTES];
-    const int lane = threadIdx.x & 31, wib = threadIdx.x >> 5;
-    const int warp = blockIdx.x * DOWN_WARPS + wib;
-    const int nwarps = gridDim.x * DOWN_WARPS;
-    const int nbk = a.H / QK, items = nbk * 16;
-    const int row_bytes = nbk * Q6K_BYTES;
-    const size_t exp_bytes = (size_t)row_bytes * a.D;
-    const int units = *a.n_slots * a.D;
-    uint8_t *rb = rowbuf[wib];
-    for (int unit = warp; unit < units; unit += nwarps) {
-        const int u = unit / a.D, n = unit - u * a.D;
-        const int e = a.slot_expert[u];
-        const uint8_t *Dn = (e == a.E ? a.down_sh : a.down + e * exp_bytes) + (size_t)n * row_bytes;
-        __syncwarp();
-        stage_row(rb, Dn, row_bytes, lane);
-        __syncwarp();
-        const int s1 = a.slot_start[u + 1];
-        for (int s = a.slot_start[u]; s < s1; s++) {
-            const int asg = a.assign[s];
-            const float *hrow = a.h + (size_t)asg * a.H;
-            float part = 0.f;
-            for (int j = lane; j < items; j += 32)
-                part += q6k_item_dot(rb + (j >> 4) * Q6K_BYTES, j, hrow + (j >> 4) * QK);
-            part = warp_sum(part);
-            if (lane == 0) a.y[(size_t)asg * a.D + n] = part;
-        }
-    }
 }
 
 // out = resid + g*y_shared + sum_a w_a y_a (model.c:1007, :1090, :1142 order).
@@ -278,14 +140,23 @@ WorkspaceLayout workspace_layout(const ofb_moe_config *c, int max_tokens) {
     L.slot_expert = take((E + 1) * 4);
     L.slot_start = take((E + 2) * 4);
     L.assign = take(A * 4);
-    L.h = take(A * (size_t)c->hidden * 4);
-    // y per assignment is only needed beyond the fused decode path
-    L.y = take(A * (size_t)c->d_model * 4);
+    // h / y (f32) serve the decode kernels (T <= MAX_DECODE_T) and the
+    // interleaved path; the tensor-core prefill path uses bf16 x and h instead
+    const bool inter = c->layout == OFB_LAYOUT_INTERLEAVED;
+    const size_t Td = inter ? T : (T < (size_t)MAX_DECODE_T ? T : (size_t)MAX_DECODE_T);
+    const size_t Ad = Td * K + Td;
+    L.h = take(Ad * (size_t)c->hidden * 4);
+    L.y = take(Ad * (size_t)c->d_model * 4);
+    const bool prefill = !inter && (max_tokens > MAX_DECODE_T || c->hidden > MAX_DECODE_H);
+    L.xb = take(prefill ? T * (size_t)c->d_model * 2 : 0);
+    L.hb = take(prefill ? A * (size_t)c->hidden * 2 : 0);
+    L.tiles = take(prefill ? (1 + 3 * (size_t)prefill_max_tiles(max_tokens, K, E)) * 4 : 0);
     const size_t Tf = (size_t)(max_tokens < FAST_ROUTE_MAX_T ? max_tokens : FAST_ROUTE_MAX_T);
     L.cand = take(Tf * (E + 1) * 16);
     L.xq = take(Tf * xq_stride(c->d_model));
     // route tickets [64] + [1], route stats [3], pad [1], down-combine tickets [D/8]
-    L.counters_bytes = (FAST_ROUTE_MAX_T + 4 + c->d_model / 8) * 4;
+    // ... then the prefill error flag [1]
+    L.counters_bytes = (FAST_ROUTE_MAX_T + 4 + c->d_model / 8 + 1) * 4;
     L.counters = take(L.counters_bytes);
     L.total = off;
     return L;
@@ -396,13 +267,12 @@ int run_moe_layer(const ofb_moe_config *cfg, const ofb_moe_weights *wt, const fl
         mark(4);
         return OFB_OK;
     }
-    expert_up_kernel<<<grid_for((uint64_t)max_slots * H, 8, sms * 16), 256, 0, s>>>(a);
+    // prefill-sized batches: tcgen05 grouped GEMMs (prefill.cu)
+    int *err = (int *)(base + L.counters) + FAST_ROUTE_MAX_T + 4 + D / 8;
+    if ((st = launch_prefill(a, x, p.n_slots, (__nv_bfloat16 *)(base + L.xb), (__nv_bfloat16 *)(base + L.hb),
+                             (int *)(base + L.tiles), err, s)))
+        return st;
     mark(3);
-    {
-        expert_down_rows<<<grid_for((uint64_t)max_slots * D, DOWN_WARPS, sms * 16), DOWN_WARPS * 32, 0, s>>>(a);
-        combine_kernel<<<grid_for((uint64_t)T * D, 256, sms * 4), 256, 0, s>>>(a);
-    }
-    OFB_CHECK_LAUNCH("expert kernels");
     mark(4);
     return OFB_OK;
 }

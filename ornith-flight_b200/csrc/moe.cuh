@@ -37,6 +37,8 @@ struct WorkspaceLayout {
     size_t logits, idx, w, gsc, n_slots, slot_expert, slot_start, assign, h, y;
     size_t cand;      // fast routing: (approximate logit, bound) per (token, row)
     size_t xq;        // decode: quantised activations [T][xq_stride(D)]
+    size_t xb, hb;    // prefill: bf16 x [T][D], bf16 h [A][H] in slot order
+    size_t tiles;     // prefill: tile count + (slot, start, n) per tile
     size_t counters;  // fast routing tickets [T] + [1] and stats [3]; zero at creation
     size_t counters_bytes;
     size_t total;
@@ -49,6 +51,9 @@ constexpr int MAX_DECODE_T = 32;
 constexpr int MAX_DECODE_H = 1024;
 
 int launch_quantize_x(const float *x, int T, int D, unsigned char *xq, cudaStream_t s);
+int prefill_max_tiles(int T, int K, int E);
+int launch_prefill(const LayerArgs &la, const float *x, int *n_slots, __nv_bfloat16 *xb, __nv_bfloat16 *hb,
+                   int *tiles, int *err, cudaStream_t s);
 int launch_up_q(const LayerArgs &a, const unsigned char *xq, int max_slots, cudaStream_t s);
 int launch_down_q(const LayerArgs &a, int *tickets, int max_slots, cudaStream_t s);
 

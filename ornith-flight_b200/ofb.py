@@ -239,6 +239,17 @@ def make_layer(shape: LayerShape, seed: int, device="cuda", shared: bool = True,
     return LayerWeights(r, g, u, d, gs, us, ds, v)
 
 
+ZIPF_ALPHA = 0.15  # gives per-expert counts of ~60..600 at 4096 tokens, top-8 of 256
+
+
+def zipf_bias(n_experts: int, seed: int, alpha: float = ZIPF_ALPHA) -> torch.Tensor:
+    """Router logit bias alpha * log(r_e^-1.1) over a seeded expert ranking r
+    (the prefill configuration's Zipf(1.1) skew)."""
+    g = torch.Generator().manual_seed(seed)
+    rank = torch.randperm(n_experts, generator=g).double() + 1.0
+    return (alpha * (-1.1) * torch.log(rank)).float()
+
+
 def make_tokens(shape: LayerShape, n_tokens: int, seed: int, bias_coordinate: bool = False) -> torch.Tensor:
     """Host f32 [T][D] drawn N(0, 1); x[:, 0] = 1 when a router bias is used."""
     x = synth_normal(n_tokens * shape.d_model, seed, STREAM_X, 1.0).view(n_tokens, shape.d_model)
