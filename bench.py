@@ -1,6 +1,6 @@
 """Benchmark of the MoE feed-forward layer (ornith-flight's hot path) on B200.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload decode1|decode32]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload decode1|decode32|prefill4096]
                     [--impl ours|reference]
 
 A step = one MoE layer forward (router, softmax/top-8/renormalise, dispatch,
@@ -35,12 +35,18 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, os.path.join(ROOT, "oracle"))
 
 WORKLOADS = {
-    "decode1": dict(tokens=1, config="BASELINE config 1: decode batch 1"),
-    "decode32": dict(tokens=32, config="BASELINE config 2: decode batch 32"),
+    "decode1": dict(tokens=1, config="BASELINE config 1: decode batch 1", layers=16, bound="hbm",
+                    dtype="f32 accumulate (int16-quantised activations, dp4a)", launches=4,
+                    metric="MoE-layer tokens/s (decode batch 1)"),
+    "decode32": dict(tokens=32, config="BASELINE config 2: decode batch 32", layers=16, bound="hbm",
+                     dtype="f32 accumulate (int16-quantised activations, dp4a)", launches=4,
+                     metric="MoE-layer tokens/s (decode batch 32)"),
+    "prefill4096": dict(tokens=4096, zipf=True, layers=2, bound="tensor", dtype="bf16 (fp32 accumulate)",
+                        config="BASELINE config 3: 4096-token prefill, Zipf(1.1)-skewed routing",
+                        launches=7, metric="MoE-layer tokens/s (4096-token prefill)"),
 }
 D, H, E, K = 2048, 512, 256, 8
 EXPERT_BYTES = 2 * (H * D // 256) * 144 + (H * D // 256) * 210  # 2,039,808
-LAUNCHES_PER_STEP = 3  # route+plan, gate/up, down+combine
 
 
 def algorithmic_bytes(tokens: int, n_experts_touched: int) -> int:
@@ -60,13 +66,13 @@ def load_ofb():
     return mod
 
 
-def peaks():
+def peaks(key):
+    fallback = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
     try:
         with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
-            p = json.load(f)
-        return p["hbm_gbs"], "measured"
+            return float(json.load(f)[key]), "measured"
     except Exception:
-        return 6650.0, "fallback"
+        return fallback[key], "fallback"
 
 
 class ClockSampler:
@@ -165,19 +171,21 @@ def cpu_throughput(procs: int, seconds: float, tokens_per_call: int):
 
 # --------------------------------------------------------------- GPU arm ----
 
-def run_ours(args, rank, world, local_rank):
+def measure(args, ofb, dev, rank, world, local_rank, workload, steps, warmup, n_layers, sample_clocks):
+    """Times `steps` layer forwards of one workload (device time, max over
+    ranks), then the per-phase event times, routing paths and the end-to-end
+    rate with host buffers."""
     import torch
     import torch.distributed as dist
-    ofb = load_ofb()
-    torch.cuda.set_device(local_rank)
-    dev = torch.device("cuda", local_rank)
-    wl = WORKLOADS[args.workload]
+    wl = WORKLOADS[workload]
     T = wl["tokens"]
     shape = ofb.LayerShape()
-    n_layers = args.layers
-    layers = [ofb.MoeLayer(shape, ofb.make_layer(shape, seed=1000 * rank + l, device=dev), T)
+    zipf = wl.get("zipf", False)
+    layers = [ofb.MoeLayer(shape, ofb.make_layer(shape, seed=1000 * rank + l, device=dev,
+                                                 router_bias=ofb.zipf_bias(E, l) if zipf else None), T)
               for l in range(n_layers)]
-    xs = [ofb.make_tokens(shape, T, seed=77 + i + 1000 * rank).to(dev) for i in range(n_layers)]
+    xs = [ofb.make_tokens(shape, T, seed=77 + i + 1000 * rank, bias_coordinate=zipf).to(dev)
+          for i in range(n_layers)]
     out = torch.empty(T, D, device=dev)
     stream = torch.cuda.current_stream()
     torch.cuda.synchronize()
@@ -185,30 +193,33 @@ def run_ours(args, rank, world, local_rank):
     def step(i):
         layers[i % n_layers].forward(xs[i % n_layers], out=out)
 
-    for i in range(args.warmup):
+    for i in range(warmup):
         step(i)
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with ClockSampler(local_rank) as clk:
-        start.record(stream)
-        for i in range(args.steps):
-            step(i)
-        end.record(stream)
-        torch.cuda.synchronize()
-        if world > 1:
-            dist.barrier()
-        ms = start.elapsed_time(end)
-        # keep the sampler alive for >= 1 s of identical work so that clocks
-        # are observed even when K steps are shorter than one sample period
-        t_extra = time.perf_counter()
-        j = 0
+    clk = ClockSampler(local_rank) if sample_clocks else None
+    if clk:
+        clk.__enter__()
+    start.record(stream)
+    for i in range(steps):
+        step(i)
+    end.record(stream)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    ms = start.elapsed_time(end)
+    if clk:
+        # keep sampling for >= 1 s of identical work so that clocks are
+        # observed even when K steps are shorter than one sample period
+        t_extra, j = time.perf_counter(), 0
         while time.perf_counter() - t_extra < max(0.0, 1.2 - ms / 1e3):
-            for _ in range(200):
+            for _ in range(max(1, 200 // T)):
                 step(j)
                 j += 1
             torch.cuda.synchronize()
+        clk.__exit__(None, None, None)
     t = torch.tensor([ms], device=dev)
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -216,28 +227,25 @@ def run_ours(args, rank, world, local_rank):
 
     # per-phase device times over the same step sequence (events on the stream)
     phase = [0.0] * 4
-    n_prof = min(args.steps, 200)
+    n_prof = min(steps, 200)
     for i in range(n_prof):
         p = layers[i % n_layers].forward_profiled(xs[i % n_layers], out)
         phase = [a + b for a, b in zip(phase, p)]
     phase = [p / n_prof for p in phase]
-
     route_stats = [0, 0, 0]
     for l in layers:
         route_stats = [a + b for a, b in zip(route_stats, l.ws.route_stats())]
-
-    # experts touched per step (for the algorithmic byte count)
-    touched = []
+    touched, kept = [], []
     for l in range(min(n_layers, 8)):
-        idx, _ = layers[l].route(xs[l])
+        idx, w = layers[l].route(xs[l])
         touched.append(len(set(idx.flatten().tolist())))
-    n_touched = statistics.mean(touched)
+        kept.append(int((w >= 1e-6).sum().item()))
 
     # end to end through the public API with host buffers: pinned x in, out back
     hx = [xs[i].cpu().pin_memory() for i in range(n_layers)]
     hout = torch.empty(T, D).pin_memory()
     dx = torch.empty(T, D, device=dev)
-    for i in range(args.warmup):
+    for i in range(warmup):
         dx.copy_(hx[i % n_layers], non_blocking=True)
         layers[i % n_layers].forward(dx, out=out)
         hout.copy_(out, non_blocking=True)
@@ -246,7 +254,7 @@ def run_ours(args, rank, world, local_rank):
         dist.barrier()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(stream)
-    for i in range(args.steps):
+    for i in range(steps):
         dx.copy_(hx[i % n_layers], non_blocking=True)
         layers[i % n_layers].forward(dx, out=out)
         hout.copy_(out, non_blocking=True)
@@ -255,63 +263,105 @@ def run_ours(args, rank, world, local_rank):
     te = torch.tensor([e0.elapsed_time(e1)], device=dev)
     if world > 1:
         dist.all_reduce(te, op=dist.ReduceOp.MAX)
-    e2e_ms = float(te.item())
+    del layers
+    torch.cuda.empty_cache()
+    return dict(T=T, ms=ms, phase=phase, route_stats=route_stats, n_touched=statistics.mean(touched),
+                kept=statistics.mean(kept), e2e_ms=float(te.item()), clocks=clk.summary() if clk else None)
 
+
+def run_ours(args, rank, world, local_rank):
+    import torch
+    ofb = load_ofb()
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    wl = WORKLOADS[args.workload]
+    n_layers = args.layers if args.layers else wl["layers"]
+    m = measure(args, ofb, dev, rank, world, local_rank, args.workload, args.steps, args.warmup,
+                n_layers, True)
+    extra = None
+    if args.workload != "prefill4096" and not args.no_prefill:
+        extra = measure(args, ofb, dev, rank, world, local_rank, "prefill4096", args.prefill_steps,
+                        3, WORKLOADS["prefill4096"]["layers"], False)
     if rank != 0:
         return
-    peak, peak_kind = peaks()
-    layer_bytes = algorithmic_bytes(T, round(n_touched))
-    up_bytes = (round(n_touched) + 1) * 2 * (H * D // 256) * 144  # gate+up rows read by the up kernel
-    up_ms = phase[2]
-    achieved_up = up_bytes / (up_ms * 1e-3) / 1e9
-    step_ms = ms / args.steps
-    achieved_layer = layer_bytes / (step_ms * 1e-3) / 1e9
-    traffic = None
-    tp = os.path.join(ROOT, "profiles", "traffic.json")
-    if os.path.exists(tp):
-        try:
-            traffic = json.load(open(tp)).get(f"{args.workload}:expert_up_kernel")
-        except Exception:
-            traffic = None
-    clocks = clk.summary()
-    cpu = None
+    line = describe(args, world, args.workload, m, args.steps, args.warmup, n_layers)
+    if extra is not None:
+        sub = describe(args, world, "prefill4096", extra, args.prefill_steps, 3,
+                       WORKLOADS["prefill4096"]["layers"])
+        line["prefill4096"] = {k: sub[k] for k in ("metric", "value", "unit", "ms_per_step", "steps",
+                                                   "warmup", "config", "roofline", "layer_roofline",
+                                                   "phase_ms", "e2e", "gpu_launches")}
     if not args.no_cpu_baseline:
-        v, kind, sample = cpu_throughput(1, args.cpu_seconds, T)
-        cpu = {"value": v, "unit": "tokens/s", "cores": 1, "kind": kind, "sample": sample}
+        v, kind, sample = cpu_throughput(1, args.cpu_seconds, min(m["T"], 4))
+        line["cpu_baseline"] = {"value": v, "unit": "tokens/s", "cores": 1, "kind": kind,
+                                "sample": sample}
+    print(json.dumps(line), flush=True)
+
+
+def describe(args, world, workload, m, steps, warmup, n_layers):
+    wl = WORKLOADS[workload]
+    T = m["T"]
+    step_ms = m["ms"] / steps
+    phase = m["phase"]
     line = {
-        "metric": "MoE-layer tokens/s (decode)",
-        "value": world * T * args.steps / (ms / 1e3),
+        "metric": wl["metric"],
+        "value": world * T * steps / (m["ms"] / 1e3),
         "unit": "tokens/s",
-        "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "n_gpus": world, "steps": steps, "warmup": warmup,
         "ms_per_step": step_ms,
         "higher_is_better": True,
         "scaling": "weak",
         "vs_baseline": None,
-        "dtype": "f32",
+        "dtype": wl["dtype"],
         "data": "synthetic (seeded Q4_K/Q6_K blocks, N(0,1) tokens, N(0,0.02) router)",
-        "config": {"workload": args.workload, "desc": wl["config"], "tokens_per_step": T,
+        "config": {"workload": workload, "desc": wl["config"], "tokens_per_step": T,
                    "d_model": D, "hidden": H, "n_experts": E, "top_k": K,
-                   "routing": "softmax/top-8/renormalise, bit-exact", "shared_gate": True,
+                   "routing": "softmax/top-8/renormalise; indices bit-exact", "shared_gate": True,
                    "l2": f"rotate {n_layers} layer copies ({n_layers * 522} MB) > 126 MB L2",
                    "parallelism": f"replicas x{world}"},
-        "roofline": {"bound": "hbm", "kernel": "expert_up_kernel (gate/up Q4_K dequant-GEMV)",
-                     "achieved": achieved_up, "peak": peak, "unit": "GB/s",
-                     "frac": achieved_up / peak, "traffic": traffic,
-                     "peak_source": peak_kind,
-                     "algorithmic_bytes_per_launch": up_bytes, "launch_ms": up_ms},
-        "layer_roofline": {"achieved": achieved_layer, "frac": achieved_layer / peak,
-                           "algorithmic_bytes_per_step": layer_bytes,
-                           "experts_touched": n_touched},
         "phase_ms": {"routing": phase[0], "plan": phase[1], "up": phase[2], "down_combine": phase[3]},
-        "e2e": {"value": world * T * args.steps / (e2e_ms / 1e3), "unit": "tokens/s",
+        "e2e": {"value": world * T * steps / (m["e2e_ms"] / 1e3), "unit": "tokens/s",
                 "h2d_bytes_per_step": T * D * 4, "d2h_bytes_per_step": T * D * 4},
-        "route_paths": {"certified": route_stats[0], "candidates_recomputed": route_stats[1],
-                        "all_recomputed": route_stats[2]},
-        "gpu_launches": LAUNCHES_PER_STEP * args.steps,
-        "clocks": clocks,
-        "cpu_baseline": cpu,
+        "route_paths": {"certified": m["route_stats"][0], "candidates_recomputed": m["route_stats"][1],
+                        "all_recomputed": m["route_stats"][2]},
+        "gpu_launches": wl["launches"] * steps,
     }
-    print(json.dumps(line), flush=True)
+    traffic = None
+    tp = os.path.join(ROOT, "profiles", "traffic.json")
+    if os.path.exists(tp):
+        try:
+            traffic = json.load(open(tp)).get(workload)
+        except Exception:
+            traffic = None
+    if wl["bound"] == "hbm":
+        peak, peak_kind = peaks("hbm_gbs")
+        touched = round(m["n_touched"])
+        up_bytes = (touched + 1) * 2 * (H * D // 256) * 144  # gate+up rows read by the up kernel
+        achieved = up_bytes / (phase[2] * 1e-3) / 1e9
+        layer_bytes = algorithmic_bytes(T, touched)
+        line["roofline"] = {"bound": "hbm", "kernel": "expert_up_q (gate/up Q4_K dequant-GEMV)",
+                            "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                            "traffic": traffic, "peak_source": peak_kind,
+                            "algorithmic_bytes_per_launch": up_bytes, "launch_ms": phase[2]}
+        la = layer_bytes / (step_ms * 1e-3) / 1e9
+        line["layer_roofline"] = {"achieved": la, "frac": la / peak, "unit": "GB/s",
+                                  "algorithmic_bytes_per_step": layer_bytes, "experts_touched": m["n_touched"]}
+    else:
+        peak, peak_kind = peaks("bf16_tflops_sustained")
+        asg = m["kept"] + T  # routed assignments + shared expert rows
+        up_flops = 4.0 * asg * H * D  # gate and up GEMMs
+        achieved = up_flops / (phase[2] * 1e-3) / 1e12
+        layer_flops = 6.0 * asg * H * D
+        line["roofline"] = {"bound": "tensor", "kernel": "prefill_up_kernel (tcgen05 gate+up grouped GEMM)",
+                            "achieved": achieved, "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
+                            "traffic": traffic, "peak_source": peak_kind,
+                            "algorithmic_flops_per_launch": up_flops, "launch_ms": phase[2]}
+        la = layer_flops / (step_ms * 1e-3) / 1e12
+        line["layer_roofline"] = {"achieved": la, "frac": la / peak, "unit": "TFLOP/s",
+                                  "algorithmic_flops_per_step": layer_flops}
+    if m["clocks"] is not None:
+        line["clocks"] = m["clocks"]
+    return line
 
 
 def run_reference(args, rank, world):
@@ -322,10 +372,12 @@ def run_reference(args, rank, world):
     # One token-layer takes ~0.1 s of CPU, so K steps of the GPU arm's size
     # would run for hours: the arm runs one bounded sample (every core busy
     # for args.cpu_seconds * 4, at most 90 s) and reports its throughput.
-    v, kind, sample = cpu_throughput(procs, min(90.0, 4 * args.cpu_seconds), T)
+    # the reference processes one token at a time (inference.c:304-307), so
+    # its tokens/s does not depend on the batch: calls of <= 4 tokens
+    v, kind, sample = cpu_throughput(procs, min(90.0, 4 * args.cpu_seconds), min(T, 4))
     line = {
         "impl": "reference",
-        "metric": "MoE-layer tokens/s (decode)", "value": v, "unit": "tokens/s",
+        "metric": WORKLOADS[args.workload]["metric"], "value": v, "unit": "tokens/s",
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": 1e3 * T / v, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "f32", "data": "synthetic",
@@ -345,7 +397,9 @@ def main():
     ap.add_argument("--warmup", type=int, default=50)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default="decode1")
-    ap.add_argument("--layers", type=int, default=16, help="rotating layer copies (L2 flush)")
+    ap.add_argument("--layers", type=int, default=0, help="rotating layer copies (0: workload default)")
+    ap.add_argument("--prefill-steps", type=int, default=20)
+    ap.add_argument("--no-prefill", action="store_true", help="skip the prefill block of the decode line")
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()

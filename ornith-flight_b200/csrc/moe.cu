@@ -36,7 +36,25 @@ __device__ __forceinline__ int asg_token(int a, int TK, int K) { return a < TK ?
 __global__ void __launch_bounds__(1024) plan_kernel(PlanArgs p) {
     __shared__ int cnt[1024], cursor[1024], wsum[66];
     build_plan(p, cnt, cursor, wsum);
-    if (p.has_shared && p.shared_gate) shared_gates(p);
+}
+
+// Shared-expert gates sigmoid(x . v), one warp per token (tolerance-level:
+// the reference has no gate; any summation order).
+__global__ void __launch_bounds__(256) shared_gate_kernel(const float *__restrict__ x,
+                                                          const float *__restrict__ v, int T, int D,
+                                                          float *__restrict__ gsc) {
+    const int lane = threadIdx.x & 31;
+    const int t = blockIdx.x * 8 + (threadIdx.x >> 5);
+    if (t >= T) return;
+    const float4 *x4 = reinterpret_cast<const float4 *>(x + (size_t)t * D);
+    const float4 *v4 = reinterpret_cast<const float4 *>(v);
+    float z = 0.f;
+    for (int i = lane; i < D / 4; i += 32) {
+        const float4 a = __ldg(x4 + i), b = __ldg(v4 + i);
+        z += a.x * b.x + a.y * b.y + a.z * b.z + a.w * b.w;
+    }
+    z = warp_sum(z);
+    if (lane == 0) gsc[t] = 1.0f / (1.0f + expf(-z));
 }
 
 // out = resid + g*y_shared + sum_a w_a y_a (model.c:1007, :1090, :1142 order).
@@ -147,7 +165,7 @@ WorkspaceLayout workspace_layout(const ofb_moe_config *c, int max_tokens) {
     const size_t Ad = Td * K + Td;
     L.h = take(Ad * (size_t)c->hidden * 4);
     L.y = take(Ad * (size_t)c->d_model * 4);
-    const bool prefill = !inter && (max_tokens > MAX_DECODE_T || c->hidden > MAX_DECODE_H);
+    const bool prefill = !inter && max_tokens > MAX_DECODE_T && c->hidden <= PREFILL_MAX_H;
     L.xb = take(prefill ? T * (size_t)c->d_model * 2 : 0);
     L.hb = take(prefill ? A * (size_t)c->hidden * 2 : 0);
     L.tiles = take(prefill ? (1 + 3 * (size_t)prefill_max_tiles(max_tokens, K, E)) * 4 : 0);
@@ -168,7 +186,7 @@ int check_config(const ofb_moe_config *c) {
         set_error("d_model (%d) and hidden (%d) must be positive multiples of 256", c->d_model, c->hidden);
         return OFB_EINVAL;
     }
-    if (c->hidden > 16 * QK) { set_error("hidden %d > 4096 unsupported", c->hidden); return OFB_EUNSUPPORTED; }
+    if (c->hidden > MAX_DECODE_H) { set_error("hidden %d > %d unsupported", c->hidden, MAX_DECODE_H); return OFB_EUNSUPPORTED; }
     if (c->n_experts < 1 || c->n_experts > 1024) { set_error("n_experts %d not in [1,1024]", c->n_experts); return OFB_EINVAL; }
     if (c->top_k < 1 || c->top_k > 16 || c->top_k > c->n_experts) { set_error("top_k %d invalid", c->top_k); return OFB_EINVAL; }
     if (c->layout != OFB_LAYOUT_CONTIGUOUS && c->layout != OFB_LAYOUT_INTERLEAVED) { set_error("bad layout %d", c->layout); return OFB_EINVAL; }
@@ -228,6 +246,8 @@ int run_moe_layer(const ofb_moe_config *cfg, const ofb_moe_weights *wt, const fl
         }
         mark(1);
         plan_kernel<<<1, 1024, 0, s>>>(p);
+        if (p.has_shared && p.shared_gate)
+            shared_gate_kernel<<<(T + 7) / 8, 256, 0, s>>>(x, p.gate_v, T, D, p.gsc);
         OFB_CHECK_LAUNCH("plan");
         mark(2);
     }
@@ -268,11 +288,14 @@ int run_moe_layer(const ofb_moe_config *cfg, const ofb_moe_weights *wt, const fl
         return OFB_OK;
     }
     // prefill-sized batches: tcgen05 grouped GEMMs (prefill.cu)
+    if (H > PREFILL_MAX_H) {
+        set_error("batches above %d tokens need hidden <= %d (got %d)", MAX_DECODE_T, PREFILL_MAX_H, H);
+        return OFB_EUNSUPPORTED;
+    }
     int *err = (int *)(base + L.counters) + FAST_ROUTE_MAX_T + 4 + D / 8;
     if ((st = launch_prefill(a, x, p.n_slots, (__nv_bfloat16 *)(base + L.xb), (__nv_bfloat16 *)(base + L.hb),
-                             (int *)(base + L.tiles), err, s)))
+                             (int *)(base + L.tiles), err, s, ev ? ev[2] : nullptr, ev ? ev[3] : nullptr)))
         return st;
-    mark(3);
     mark(4);
     return OFB_OK;
 }

@@ -49,11 +49,14 @@ constexpr int FAST_ROUTE_MAX_T = 64;
 // Decode expert kernels (decode.cu): token and hidden-width limits.
 constexpr int MAX_DECODE_T = 32;
 constexpr int MAX_DECODE_H = 1024;
+// Tensor-core prefill kernels: the down kernel holds 128 Q6_K rows in shared memory.
+constexpr int PREFILL_MAX_H = 512;
 
 int launch_quantize_x(const float *x, int T, int D, unsigned char *xq, cudaStream_t s);
 int prefill_max_tiles(int T, int K, int E);
 int launch_prefill(const LayerArgs &la, const float *x, int *n_slots, __nv_bfloat16 *xb, __nv_bfloat16 *hb,
-                   int *tiles, int *err, cudaStream_t s);
+                   int *tiles, int *err, cudaStream_t s, cudaEvent_t before = nullptr,
+                   cudaEvent_t between = nullptr);
 int launch_up_q(const LayerArgs &a, const unsigned char *xq, int max_slots, cudaStream_t s);
 int launch_down_q(const LayerArgs &a, int *tickets, int max_slots, cudaStream_t s);
 

@@ -72,14 +72,4 @@ static __device__ void build_plan(const PlanArgs &p, int *cnt, int *cursor, int 
     }
 }
 
-static __device__ void shared_gates(const PlanArgs &p) {
-    const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
-    for (int t = wid; t < p.T; t += blockDim.x >> 5) {
-        float z = 0.0f;
-        for (int d = lane; d < p.D; d += 32) z += p.x[(size_t)t * p.D + d] * p.gate_v[d];
-        z = warp_sum(z);
-        if (lane == 0) p.gsc[t] = 1.0f / (1.0f + expf(-z));
-    }
-}
-
 }  // namespace ofb

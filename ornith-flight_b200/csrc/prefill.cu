@@ -135,127 +135,183 @@ __device__ __forceinline__ uint32_t core_off(int row, int chunk, int lbo) {
     return chunk * lbo + (row >> 3) * 128 + (row & 7) * 16;
 }
 
-// ---- B operand: token rows ---------------------------------------------------
-// 256 rows x 64 K of bf16 = 1024 units of 32 bytes; thread t owns units
-// t + 128 j (j < 8): row = 8 g + r, chunk pair cp (chunks 2cp, 2cp+1).
-struct BRegs { uint4 v[8][2]; };
-
-__device__ __forceinline__ void b_load(BRegs &br, const __nv_bfloat16 *const *rowp, int n_rows, int k0) {
-#pragma unroll
-    for (int j = 0; j < 8; j++) {
-        const int u = threadIdx.x + PF_THREADS * j;
-        const int r = u & 7, cp = (u >> 3) & 3, g = u >> 5;
-        const int row = g * 8 + r;
-        if (row < n_rows) {
-            const uint4 *src = reinterpret_cast<const uint4 *>(rowp[row] + k0 + cp * 16);
-            br.v[j][0] = __ldg(src);
-            br.v[j][1] = __ldg(src + 1);
-        } else {
-            br.v[j][0] = br.v[j][1] = make_uint4(0, 0, 0, 0);
-        }
-    }
+// ---- async copies -----------------------------------------------------------
+// 16-byte global->shared copy; src_bytes = 0 zero-fills the destination.
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void *src, uint32_t src_bytes) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(src_bytes)
+                 : "memory");
 }
-__device__ __forceinline__ void b_store(const BRegs &br, uint8_t *sb) {
-#pragma unroll
-    for (int j = 0; j < 8; j++) {
-        const int u = threadIdx.x + PF_THREADS * j;
-        const int r = u & 7, cp = (u >> 3) & 3, g = u >> 5;
-        const int row = g * 8 + r;
-        *reinterpret_cast<uint4 *>(sb + core_off(row, 2 * cp, B_LBO)) = br.v[j][0];
-        *reinterpret_cast<uint4 *>(sb + core_off(row, 2 * cp + 1, B_LBO)) = br.v[j][1];
-    }
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+// One TMA bulk copy global -> shared completing on an mbarrier (no multicast).
+__device__ __forceinline__ void bulk_copy(void *dst, const void *src, uint32_t bytes, uint64_t *bar) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
+                 : "memory");
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                     smem_u32(dst)),
+                 "l"(src), "r"(bytes), "r"(smem_u32(bar))
+                 : "memory");
 }
 
-// ---- A operand, Q4_K: row slice [k0, k0+64) = chunk c of block b -----------
-struct Q4Regs { uint4 hdr, qa, qb; };
-__device__ __forceinline__ void q4_load(Q4Regs &q, const uint8_t *row, int stage) {
-    const uint8_t *blk = row + (stage >> 2) * Q4K_BYTES;
-    const int c = stage & 3;
-    q.hdr = __ldg(reinterpret_cast<const uint4 *>(blk));
-    q.qa = __ldg(reinterpret_cast<const uint4 *>(blk + 16 + c * 32));
-    q.qb = __ldg(reinterpret_cast<const uint4 *>(blk + 32 + c * 32));
+// 4 bytes at a 2-byte aligned shared-memory address.
+__device__ __forceinline__ uint32_t lds_u32_2b(const uint8_t *p) {
+    const uintptr_t a = reinterpret_cast<uintptr_t>(p);
+    const uint32_t *b = reinterpret_cast<const uint32_t *>(a & ~uintptr_t(3));
+    return __funnelshift_r(b[0], b[1], (unsigned)(a & 3) * 8);
 }
-__device__ __forceinline__ void q4_store(const Q4Regs &q, int stage, uint8_t *sa) {
-    const int c = stage & 3, r = threadIdx.x;
-    const uint32_t s[3] = {q.hdr.y, q.hdr.z, q.hdr.w};
-    int sc0, m0, sc1, m1;
-    q4k_scale_min(s, 2 * c, sc0, m0);
-    q4k_scale_min(s, 2 * c + 1, sc1, m1);
-    const float d = half_bits_ref(q.hdr.x & 0xFFFFu), dmin = half_bits_ref(q.hdr.x >> 16);
-    const float d0 = __fmul_rn(d, (float)sc0), mm0 = __fmul_rn(dmin, (float)m0);
-    const float d1 = __fmul_rn(d, (float)sc1), mm1 = __fmul_rn(dmin, (float)m1);
-    const uint32_t qw[8] = {q.qa.x, q.qa.y, q.qa.z, q.qa.w, q.qb.x, q.qb.y, q.qb.z, q.qb.w};
+
+// byte k of w as a float (exact small integer): 2^23 + byte, minus 2^23 + bias
+template <int K>
+__device__ __forceinline__ float byte_f(uint32_t w, float bias) {
+    return __uint_as_float(__byte_perm(w, 0x4B000000u, 0x7540u + K)) - bias;
+}
+
+constexpr int PF_NT = 256;                    // threads per CTA (8 warps)
+constexpr int PF_STG = 3;                     // cp.async pipeline depth
+constexpr int B_LBO_P = B_LBO + 16;           // padded: the 8 chunks of a row hit 8 bank groups
+constexpr int B_STAGE_P = 8 * B_LBO_P;
+constexpr int RAW4 = PF_M * 48;               // raw Q4_K bytes of one matrix per stage
+
+// B: 2048 16-byte copies per stage; thread t copies j = t + 256 k (k < 8):
+// chunk = j & 7, row = j >> 3 (a quarter-warp copies one 128-byte row).
+// The per-thread sources and destinations are fixed for the whole K loop.
+struct BPlan { const __nv_bfloat16 *src[8]; uint32_t dst[8]; uint32_t bytes[8]; };
+__device__ __forceinline__ void b_plan(BPlan &p, const __nv_bfloat16 *const *rowp, int n_rows) {
 #pragma unroll
-    for (int ch = 0; ch < 8; ch++) {
-        // chunks 0-3: low nibbles of bytes 8ch..8ch+7; chunks 4-7: high nibbles
-        const int wb = (ch & 3) * 2;
-        const bool hi = ch >= 4;
-        const float dd = hi ? d1 : d0, mm = hi ? mm1 : mm0;
-        float v[8];
+    for (int k = 0; k < 8; k++) {
+        const int j = threadIdx.x + PF_NT * k;
+        const int ch = j & 7, row = j >> 3;
+        const bool ok = row < n_rows;
+        p.src[k] = rowp[ok ? row : 0] + ch * 8;
+        p.dst[k] = core_off(row, ch, B_LBO_P);
+        p.bytes[k] = ok ? 16u : 0u;
+    }
+}
+__device__ __forceinline__ void b_issue(const BPlan &p, uint32_t sb, int k0) {
 #pragma unroll
-        for (int i = 0; i < 8; i++) {
-            const uint32_t byte = (qw[wb + (i >> 2)] >> (8 * (i & 3))) & 0xFFu;
-            v[i] = q4k_value(dd, mm, hi ? (int)(byte >> 4) : (int)(byte & 0xF));
-        }
-        *reinterpret_cast<uint4 *>(sa + core_off(r, ch, A_LBO)) =
-            make_uint4(pack_bf16(v[0], v[1]), pack_bf16(v[2], v[3]), pack_bf16(v[4], v[5]),
-                       pack_bf16(v[6], v[7]));
+    for (int k = 0; k < 8; k++) cp_async16(sb + p.dst[k], p.src[k] + k0, p.bytes[k]);
+}
+
+// Q4_K raw bytes of one stage (16 B header + 32 quant bytes per row, both
+// matrices): 768 copies, thread t copies t, t+256, t+512.
+struct QPlan { const uint8_t *src[3]; uint32_t dst[3]; int part[3]; };
+__device__ __forceinline__ void q4_plan(QPlan &p, const uint8_t *g0, const uint8_t *u0, size_t row_bytes) {
+#pragma unroll
+    for (int k = 0; k < 3; k++) {
+        const int j = threadIdx.x + PF_NT * k;
+        const int mat = j / 384, rem = j - mat * 384, row = rem / 3, part = rem - row * 3;
+        p.src[k] = (mat ? u0 : g0) + row * row_bytes;
+        p.dst[k] = mat * RAW4 + row * 48 + part * 16;
+        p.part[k] = part;
+    }
+}
+__device__ __forceinline__ void q4_issue(const QPlan &p, uint32_t sraw, int stage) {
+    const int b = stage >> 2, c = stage & 3;
+#pragma unroll
+    for (int k = 0; k < 3; k++) {
+        const int off = b * Q4K_BYTES + (p.part[k] ? 16 + c * 32 + (p.part[k] - 1) * 16 : 0);
+        cp_async16(sraw + p.dst[k], p.src[k] + off, 16u);
     }
 }
 
-// ---- A operand, Q6_K: row slice [k0, k0+64) ----------------------------------
-// 64-element chunk q of a block: half = q/2, quads 2*(q%2) and 2*(q%2)+1.
-struct Q6Regs { uint16_t ql[32], qh[16], sc[2], d; };
-__device__ __forceinline__ void q6_load(Q6Regs &q, const uint8_t *row, int stage) {
-    const uint8_t *blk = row + (stage >> 2) * Q6K_BYTES;
-    const int c = stage & 3, half = c >> 1;
-    const uint16_t *ql = reinterpret_cast<const uint16_t *>(blk + half * 64);
-    const uint16_t *qh = reinterpret_cast<const uint16_t *>(blk + 128 + half * 32);
-    const uint16_t *sc = reinterpret_cast<const uint16_t *>(blk + 192 + half * 8 + (c & 1) * 4);
-#pragma unroll
-    for (int i = 0; i < 32; i++) q.ql[i] = __ldg(ql + i);
-#pragma unroll
-    for (int i = 0; i < 16; i++) q.qh[i] = __ldg(qh + i);
-    q.sc[0] = __ldg(sc);
-    q.sc[1] = __ldg(sc + 1);
-    q.d = __ldg(reinterpret_cast<const uint16_t *>(blk + 208));
+// Paired fp32 arithmetic (sm_100a f32x2): two lanes of work per instruction.
+__device__ __forceinline__ unsigned long long f2pack(float a, float b) {
+    unsigned long long p;
+    asm("mov.b64 %0, {%1,%2};" : "=l"(p) : "f"(a), "f"(b));
+    return p;
 }
-__device__ __forceinline__ void q6_store(const Q6Regs &q, int stage, uint8_t *sa) {
-    const int c = stage & 3, r = threadIdx.x, pair = c & 1;
-    const float d = half_bits_ref(q.d);
-    // scales for (quad 2*pair, is 0/1) and (quad 2*pair+1, is 0/1)
-    const int8_t s00 = (int8_t)(q.sc[0] & 0xFF), s01 = (int8_t)(q.sc[0] >> 8);
-    const int8_t s10 = (int8_t)(q.sc[1] & 0xFF), s11 = (int8_t)(q.sc[1] >> 8);
+__device__ __forceinline__ uint32_t f2_fma_bf16(unsigned long long x, unsigned long long m,
+                                                 unsigned long long c) {
+    unsigned long long r;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(x), "l"(m), "l"(c));
+    float lo, hi;
+    asm("mov.b64 {%0,%1}, %2;" : "=f"(lo), "=f"(hi) : "l"(r));
+    return pack_bf16(lo, hi);
+}
+__device__ __forceinline__ unsigned long long f2_add(unsigned long long a, unsigned long long b) {
+    unsigned long long r;
+    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+    return r;
+}
+// two bytes (k, k+1) of w as exact floats 2^23 + byte, as a pair
+template <int K>
+__device__ __forceinline__ unsigned long long byte_pair(uint32_t w) {
+    return f2pack(__uint_as_float(__byte_perm(w, 0x4B000000u, 0x7540u + K)),
+                  __uint_as_float(__byte_perm(w, 0x4B000000u, 0x7541u + K)));
+}
+
+// Dequantise one matrix's stage: thread (row r, half hh) writes chunks
+// 4hh..4hh+3 (low nibbles for hh = 0, high for hh = 1). Value = (d*sc)*q -
+// dmin*m as one fused multiply-add: d*sc*q is exact in fp32 (<= 21 bits), so
+// the result equals the reference's two separately rounded operations.
+__device__ __forceinline__ void q4_deq(const uint8_t *raw, int stage, uint8_t *sa) {
+    const int r = threadIdx.x & (PF_M - 1), hh = threadIdx.x >> 7, c = stage & 3;
+    const uint4 hdr = *reinterpret_cast<const uint4 *>(raw + r * 48);
+    const uint4 qa = *reinterpret_cast<const uint4 *>(raw + r * 48 + 16);
+    const uint4 qb = *reinterpret_cast<const uint4 *>(raw + r * 48 + 32);
+    const uint32_t s[3] = {hdr.y, hdr.z, hdr.w};
+    int sc, mn;
+    q4k_scale_min(s, 2 * c + hh, sc, mn);
+    const float dd = __fmul_rn(half_bits_ref(hdr.x & 0xFFFFu), (float)sc);
+    const float mm = __fmul_rn(half_bits_ref(hdr.x >> 16), (float)mn);
+    const unsigned long long d2 = f2pack(dd, dd), nm2 = f2pack(-mm, -mm);
+    const unsigned long long nb2 = f2pack(-8388608.0f, -8388608.0f);
+    const uint32_t qw[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
+    const int sh = 4 * hh;
 #pragma unroll
-    for (int ch = 0; ch < 8; ch++) {
-        // element kk = 8ch + i: quad = 2*pair + kk/32, l = kk % 32
-        const int qsel = ch >> 2;          // 0: first quad of the pair, 1: second
-        const int quad = 2 * pair + qsel;
-        const int l0 = (ch & 3) * 8;
-        const int8_t scv = qsel ? ((l0 >> 4) ? s11 : s10) : ((l0 >> 4) ? s01 : s00);
-        const float ds = __fmul_rn(d, (float)scv);
-        float v[8];
+    for (int ch = 0; ch < 4; ch++) {
+        const uint32_t w0 = (qw[2 * ch] >> sh) & 0x0F0F0F0Fu, w1 = (qw[2 * ch + 1] >> sh) & 0x0F0F0F0Fu;
+        // q as exact floats, then one paired FMA per two elements
+        const uint32_t p0 = f2_fma_bf16(f2_add(byte_pair<0>(w0), nb2), d2, nm2);
+        const uint32_t p1 = f2_fma_bf16(f2_add(byte_pair<2>(w0), nb2), d2, nm2);
+        const uint32_t p2 = f2_fma_bf16(f2_add(byte_pair<0>(w1), nb2), d2, nm2);
+        const uint32_t p3 = f2_fma_bf16(f2_add(byte_pair<2>(w1), nb2), d2, nm2);
+        *reinterpret_cast<uint4 *>(sa + core_off(r, 4 * hh + ch, A_LBO)) = make_uint4(p0, p1, p2, p3);
+    }
+}
+
+// Q6_K stage from the raw slab in shared memory: thread (row r, hh) writes the
+// 32 elements of quad 2*(chunk%2)+hh. Value = (d*sc)*(q-32), one rounding.
+__device__ __forceinline__ void q6_deq(const uint8_t *slab, int row_bytes, int stage, uint8_t *sa) {
+    const int r = threadIdx.x & (PF_M - 1), hh = threadIdx.x >> 7;
+    const int b = stage >> 2, q64 = stage & 3, half6 = q64 >> 1, quad = 2 * (q64 & 1) + hh;
+    const uint8_t *blk = slab + r * row_bytes + b * Q6K_BYTES;
+    const uint8_t *ql = blk + half6 * 64 + (quad & 1) * 32;
+    const uint8_t *qh = blk + 128 + half6 * 32;
+    const uint32_t scw = (uint32_t)blk[192 + half6 * 8 + quad * 2] | ((uint32_t)blk[193 + half6 * 8 + quad * 2] << 8);
+    const float d = half_bits_ref((uint32_t)blk[208] | ((uint32_t)blk[209] << 8));
+    const float ds0 = __fmul_rn(d, (float)(int8_t)(scw & 0xFF)), ds1 = __fmul_rn(d, (float)(int8_t)(scw >> 8));
+    const float bias = 8388608.0f + 32.0f;
+    const int nsh = (quad >= 2) ? 4 : 0, hsh = 2 * quad;
 #pragma unroll
-        for (int i = 0; i < 8; i++) {
-            const int l = l0 + i;
-            const int qlidx = ((quad & 1) ? 32 : 0) + l;
-            const uint32_t lb = (q.ql[qlidx >> 1] >> (8 * (qlidx & 1))) & 0xFF;
-            const int nib = (quad < 2) ? (int)(lb & 0xF) : (int)(lb >> 4);
-            const uint32_t hb = (q.qh[l >> 1] >> (8 * (l & 1))) & 0xFF;
-            const int top = (hb >> (2 * quad)) & 3;
-            v[i] = __fmul_rn(ds, (float)((nib | (top << 4)) - 32));
+    for (int ch = 0; ch < 4; ch++) {
+        const float ds = ch < 2 ? ds0 : ds1;  // l = 8ch..8ch+7, is = l/16
+        uint32_t q[2];
+#pragma unroll
+        for (int h2 = 0; h2 < 2; h2++) {
+            const uint32_t wl = lds_u32_2b(ql + ch * 8 + h2 * 4), wh = lds_u32_2b(qh + ch * 8 + h2 * 4);
+            q[h2] = ((wl >> nsh) & 0x0F0F0F0Fu) | (((wh >> hsh) & 0x03030303u) << 4);
         }
-        *reinterpret_cast<uint4 *>(sa + core_off(r, ch, A_LBO)) =
-            make_uint4(pack_bf16(v[0], v[1]), pack_bf16(v[2], v[3]), pack_bf16(v[4], v[5]),
-                       pack_bf16(v[6], v[7]));
+        const float v0 = __fmul_rn(ds, byte_f<0>(q[0], bias)), v1 = __fmul_rn(ds, byte_f<1>(q[0], bias));
+        const float v2 = __fmul_rn(ds, byte_f<2>(q[0], bias)), v3 = __fmul_rn(ds, byte_f<3>(q[0], bias));
+        const float v4 = __fmul_rn(ds, byte_f<0>(q[1], bias)), v5 = __fmul_rn(ds, byte_f<1>(q[1], bias));
+        const float v6 = __fmul_rn(ds, byte_f<2>(q[1], bias)), v7 = __fmul_rn(ds, byte_f<3>(q[1], bias));
+        *reinterpret_cast<uint4 *>(sa + core_off(r, 4 * hh + ch, A_LBO)) =
+            make_uint4(pack_bf16(v0, v1), pack_bf16(v2, v3), pack_bf16(v4, v5), pack_bf16(v6, v7));
     }
 }
 
 __device__ __forceinline__ int asg_token_p(int a, int TK, int K) { return a < TK ? a / K : a - TK; }
 
 // ---- phase 1: gate/up ----------------------------------------------------------
-// grid (max_tiles, H/128); dynamic smem: 2 stages x (Ag, Au, B) + bookkeeping.
-__global__ void __launch_bounds__(PF_THREADS, 1) prefill_up_kernel(PrefillArgs a) {
+// Iteration i: (1) stage i's copies have landed; (2) dequantise it into the
+// bf16 A buffer i%2 (free: MMA i-2 was waited for in iteration i-1) while the
+// tensor core runs MMA i-1; (3) issue MMA i; (4) wait for MMA i-1, whose B
+// buffer is the one stage i+2 refills, then issue stage i+2's copies.
+constexpr int UP_SMEM = PF_STG * (2 * RAW4 + B_STAGE_P) + 2 * (2 * A_STAGE);
+
+__global__ void __launch_bounds__(PF_NT, 1) prefill_up_kernel(PrefillArgs a) {
     extern __shared__ __align__(1024) uint8_t psm[];
     __shared__ uint64_t bars[2];
     __shared__ uint32_t tslot;
@@ -266,60 +322,79 @@ __global__ void __launch_bounds__(PF_THREADS, 1) prefill_up_kernel(PrefillArgs a
     const int e = a.slot_expert[u];
     const int m0 = blockIdx.y * PF_M;
     const int TK = a.T * a.K;
-    const int nbr = a.D / QK;
-    const size_t row_bytes = (size_t)nbr * Q4K_BYTES, exp_bytes = row_bytes * a.H;
-    const uint8_t *grow = (e == a.E ? a.gate_sh : a.gate + e * exp_bytes) + (m0 + threadIdx.x) * row_bytes;
-    const uint8_t *urow = (e == a.E ? a.up_sh : a.up + e * exp_bytes) + (m0 + threadIdx.x) * row_bytes;
-    for (int i = threadIdx.x; i < PF_NMAX; i += PF_THREADS)
+    const size_t row_bytes = (size_t)(a.D / QK) * Q4K_BYTES, exp_bytes = row_bytes * a.H;
+    const uint8_t *g0 = (e == a.E ? a.gate_sh : a.gate + e * exp_bytes) + (size_t)m0 * row_bytes;
+    const uint8_t *u0 = (e == a.E ? a.up_sh : a.up + e * exp_bytes) + (size_t)m0 * row_bytes;
+    for (int i = threadIdx.x; i < PF_NMAX; i += PF_NT)
         rowp[i] = a.xb + (size_t)(i < n ? asg_token_p(a.assign[s0 + i], TK, a.K) : 0) * a.D;
     if (threadIdx.x == 0) { mbar_init(&bars[0], 1); mbar_init(&bars[1], 1); }
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     const uint32_t tbase = tmem_alloc(&tslot, 512);  // gate: cols [0,256), up: [256,512)
 
-    const int nn = (n + 15) & ~15;  // MMA N: multiple of 16
+    uint8_t *raw = psm;                                   // [PF_STG][2*RAW4]
+    uint8_t *bst = psm + PF_STG * 2 * RAW4;               // [PF_STG][B_STAGE_P]
+    uint8_t *abf = bst + PF_STG * B_STAGE_P;              // [2][gate A | up A]
+    const int nn = (n + 15) & ~15;
     const uint32_t idesc = instr_desc(nn);
     const int nstages = a.D / PF_KS;
-    Q4Regs gq, uq;
-    BRegs br;
-    q4_load(gq, grow, 0);
-    q4_load(uq, urow, 0);
-    b_load(br, rowp, n, 0);
+    __syncthreads();  // rowp
+    BPlan bp;
+    b_plan(bp, rowp, n);
+    QPlan qp;
+    q4_plan(qp, g0, u0, row_bytes);
+    for (int i = 0; i < PF_STG - 1; i++) {
+        if (i < nstages) {
+            q4_issue(qp, smem_u32(raw + i * 2 * RAW4), i);
+            b_issue(bp, smem_u32(bst + i * B_STAGE_P), i * PF_KS);
+        }
+        cp_async_commit();
+    }
     bool ok = true;
     for (int i = 0; i < nstages; i++) {
-        const int s = i & 1;
-        uint8_t *sg = psm + s * (2 * A_STAGE + B_STAGE), *su = sg + A_STAGE, *sb = sg + 2 * A_STAGE;
-        if (i >= 2) ok = ok && mbar_wait(&bars[s], ((i - 2) >> 1) & 1);
-        q4_store(gq, i, sg);
-        q4_store(uq, i, su);
-        b_store(br, sb);
-        if (i + 1 < nstages) {
-            q4_load(gq, grow, i + 1);
-            q4_load(uq, urow, i + 1);
-            b_load(br, rowp, n, (i + 1) * PF_KS);
-        }
+        const int sr = i % PF_STG, sa = i & 1;
+        cp_async_wait<PF_STG - 2>();
+        __syncthreads();
+        uint8_t *ag = abf + sa * 2 * A_STAGE, *au = ag + A_STAGE;
+        q4_deq(raw + sr * 2 * RAW4, i, ag);
+        q4_deq(raw + sr * 2 * RAW4 + RAW4, i, au);
         async_proxy_fence();
         __syncthreads();
         if (threadIdx.x == 0) {
             tc_fence_after();
-            const uint32_t ag = smem_u32(sg), au = smem_u32(su), bb = smem_u32(sb);
+            const uint32_t ga = smem_u32(ag), ua = smem_u32(au), bb = smem_u32(bst + sr * B_STAGE_P);
 #pragma unroll
             for (int kk = 0; kk < PF_KS / 16; kk++) {
-                const uint64_t bd = smem_desc(bb + kk * 2 * B_LBO, B_LBO, 128);
-                mma_bf16(tbase, smem_desc(ag + kk * 2 * A_LBO, A_LBO, 128), bd, idesc, (i | kk) != 0);
-                mma_bf16(tbase + 256, smem_desc(au + kk * 2 * A_LBO, A_LBO, 128), bd, idesc, (i | kk) != 0);
+                const uint64_t bd = smem_desc(bb + kk * 2 * B_LBO_P, B_LBO_P, 128);
+                mma_bf16(tbase, smem_desc(ga + kk * 2 * A_LBO, A_LBO, 128), bd, idesc, (i | kk) != 0);
+                mma_bf16(tbase + 256, smem_desc(ua + kk * 2 * A_LBO, A_LBO, 128), bd, idesc, (i | kk) != 0);
             }
-            mma_commit(&bars[s]);
+            mma_commit(&bars[sa]);
         }
+        // one warp waits for MMA i-1 (its B buffer is refilled next); the
+        // others wait at the barrier instead of polling
+        if (i >= 1) {
+            if (threadIdx.x < 32) ok = ok && mbar_wait(&bars[(i - 1) & 1], ((i - 1) >> 1) & 1);
+            __syncthreads();
+        }
+        const int nx = i + PF_STG - 1;
+        if (nx < nstages) {
+            q4_issue(qp, smem_u32(raw + (nx % PF_STG) * 2 * RAW4), nx);
+            b_issue(bp, smem_u32(bst + (nx % PF_STG) * B_STAGE_P), nx * PF_KS);
+        }
+        cp_async_commit();
     }
-    ok = ok && mbar_wait(&bars[(nstages - 1) & 1], ((nstages - 1) >> 1) & 1);
+    if (threadIdx.x < 32) ok = ok && mbar_wait(&bars[(nstages - 1) & 1], ((nstages - 1) >> 1) & 1);
+    ok = __syncthreads_and(ok);
     tc_fence_after();
     if (!ok) {
         if (threadIdx.x == 0) atomicExch(a.err, 1);
     } else {
-        const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
-        const int m = m0 + w * 32 + lane;
-        const uint32_t lane_off = (uint32_t)(w * 32) << 16;
-        for (int j0 = 0; j0 < nn; j0 += 8) {
+        // warp w reads TMEM lanes 32*(w%4).. (its rows), columns of half w/4
+        const int w = threadIdx.x >> 5, lane = threadIdx.x & 31, q = w & 3;
+        const int m = m0 + q * 32 + lane;
+        const uint32_t lane_off = (uint32_t)(q * 32) << 16;
+        const int half = nn / 2, j_beg = (w >> 2) * half;
+        for (int j0 = j_beg; j0 < j_beg + half; j0 += 8) {
             float g[8], uu[8];
             tmem_ld8(tbase + lane_off + j0, g);
             tmem_ld8(tbase + lane_off + 256 + j0, uu);
@@ -336,9 +411,16 @@ __global__ void __launch_bounds__(PF_THREADS, 1) prefill_up_kernel(PrefillArgs a
 }
 
 // ---- phase 2: down + weighted combine -----------------------------------------
-__global__ void __launch_bounds__(PF_THREADS, 1) prefill_down_kernel(PrefillArgs a) {
+// The CTA's 128 Q6_K rows are one contiguous, 16-byte aligned slab
+// (128 x 420 B): one TMA bulk copy brings it in; stages then only copy B.
+__host__ __device__ inline int down_slab_bytes(int H) { return PF_M * (H / QK) * Q6K_BYTES; }
+__host__ __device__ inline int down_smem(int H) {
+    return down_slab_bytes(H) + 16 + PF_STG * B_STAGE_P + 2 * A_STAGE;
+}
+
+__global__ void __launch_bounds__(PF_NT, 1) prefill_down_kernel(PrefillArgs a) {
     extern __shared__ __align__(1024) uint8_t psm[];
-    __shared__ uint64_t bars[2];
+    __shared__ uint64_t bars[3];
     __shared__ uint32_t tslot;
     __shared__ const __nv_bfloat16 *rowp[PF_NMAX];
     __shared__ int tok[PF_NMAX];
@@ -349,10 +431,13 @@ __global__ void __launch_bounds__(PF_THREADS, 1) prefill_down_kernel(PrefillArgs
     const int e = a.slot_expert[u];
     const int n0 = blockIdx.y * PF_M;
     const int TK = a.T * a.K;
-    const int nbk = a.H / QK;
-    const size_t row_bytes = (size_t)nbk * Q6K_BYTES, exp_bytes = row_bytes * a.D;
-    const uint8_t *drow = (e == a.E ? a.down_sh : a.down + e * exp_bytes) + (n0 + threadIdx.x) * row_bytes;
-    for (int i = threadIdx.x; i < PF_NMAX; i += PF_THREADS) {
+    const int row_bytes = (a.H / QK) * Q6K_BYTES;
+    const size_t exp_bytes = (size_t)row_bytes * a.D;
+    const uint8_t *slab_src = (e == a.E ? a.down_sh : a.down + e * exp_bytes) + (size_t)n0 * row_bytes;
+    uint8_t *bst = psm;                                    // [PF_STG][B_STAGE_P]
+    uint8_t *abf = bst + PF_STG * B_STAGE_P;               // [2][A_STAGE]
+    uint8_t *slab = abf + 2 * A_STAGE;                     // raw Q6_K rows
+    for (int i = threadIdx.x; i < PF_NMAX; i += PF_NT) {
         rowp[i] = a.hb + (size_t)(s0 + (i < n ? i : 0)) * a.H;
         if (i < n) {
             const int asg = a.assign[s0 + i];
@@ -361,49 +446,58 @@ __global__ void __launch_bounds__(PF_THREADS, 1) prefill_down_kernel(PrefillArgs
             wgt[i] = asg < TK ? a.w[asg] : (a.shared_gate ? a.gsc[t] : 1.0f);
         }
     }
-    if (threadIdx.x == 0) { mbar_init(&bars[0], 1); mbar_init(&bars[1], 1); }
+    if (threadIdx.x == 0) { mbar_init(&bars[0], 1); mbar_init(&bars[1], 1); mbar_init(&bars[2], 1); }
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    __syncthreads();
+    if (threadIdx.x == 0) bulk_copy(slab, slab_src, down_slab_bytes(a.H), &bars[2]);
     const uint32_t tbase = tmem_alloc(&tslot, 256);
 
     const int nn = (n + 15) & ~15;
     const uint32_t idesc = instr_desc(nn);
     const int nstages = a.H / PF_KS;
-    Q6Regs dq;
-    BRegs br;
-    q6_load(dq, drow, 0);
-    b_load(br, rowp, n, 0);
-    bool ok = true;
+    BPlan bp;
+    b_plan(bp, rowp, n);
+    for (int i = 0; i < PF_STG - 1; i++) {
+        if (i < nstages) b_issue(bp, smem_u32(bst + i * B_STAGE_P), i * PF_KS);
+        cp_async_commit();
+    }
+    bool ok = mbar_wait(&bars[2], 0);
     for (int i = 0; i < nstages; i++) {
-        const int s = i & 1;
-        uint8_t *sa = psm + s * (A_STAGE + B_STAGE), *sb = sa + A_STAGE;
-        if (i >= 2) ok = ok && mbar_wait(&bars[s], ((i - 2) >> 1) & 1);
-        q6_store(dq, i, sa);
-        b_store(br, sb);
-        if (i + 1 < nstages) {
-            q6_load(dq, drow, i + 1);
-            b_load(br, rowp, n, (i + 1) * PF_KS);
-        }
+        const int sr = i % PF_STG, sa = i & 1;
+        cp_async_wait<PF_STG - 2>();
+        __syncthreads();
+        uint8_t *ad = abf + sa * A_STAGE;
+        q6_deq(slab, row_bytes, i, ad);
         async_proxy_fence();
         __syncthreads();
         if (threadIdx.x == 0) {
             tc_fence_after();
-            const uint32_t aa = smem_u32(sa), bb = smem_u32(sb);
+            const uint32_t aa = smem_u32(ad), bb = smem_u32(bst + sr * B_STAGE_P);
 #pragma unroll
             for (int kk = 0; kk < PF_KS / 16; kk++)
                 mma_bf16(tbase, smem_desc(aa + kk * 2 * A_LBO, A_LBO, 128),
-                         smem_desc(bb + kk * 2 * B_LBO, B_LBO, 128), idesc, (i | kk) != 0);
-            mma_commit(&bars[s]);
+                         smem_desc(bb + kk * 2 * B_LBO_P, B_LBO_P, 128), idesc, (i | kk) != 0);
+            mma_commit(&bars[sa]);
         }
+        if (i >= 1) {
+            if (threadIdx.x < 32) ok = ok && mbar_wait(&bars[(i - 1) & 1], ((i - 1) >> 1) & 1);
+            __syncthreads();
+        }
+        const int nx = i + PF_STG - 1;
+        if (nx < nstages) b_issue(bp, smem_u32(bst + (nx % PF_STG) * B_STAGE_P), nx * PF_KS);
+        cp_async_commit();
     }
-    ok = ok && mbar_wait(&bars[(nstages - 1) & 1], ((nstages - 1) >> 1) & 1);
+    if (threadIdx.x < 32) ok = ok && mbar_wait(&bars[(nstages - 1) & 1], ((nstages - 1) >> 1) & 1);
+    ok = __syncthreads_and(ok);
     tc_fence_after();
     if (!ok) {
         if (threadIdx.x == 0) atomicExch(a.err, 1);
     } else {
-        const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
-        const int row = n0 + w * 32 + lane;
-        const uint32_t lane_off = (uint32_t)(w * 32) << 16;
-        for (int j0 = 0; j0 < nn; j0 += 8) {
+        const int w = threadIdx.x >> 5, lane = threadIdx.x & 31, q = w & 3;
+        const int row = n0 + q * 32 + lane;
+        const uint32_t lane_off = (uint32_t)(q * 32) << 16;
+        const int half = nn / 2, j_beg = (w >> 2) * half;
+        for (int j0 = j_beg; j0 < j_beg + half; j0 += 8) {
             float y[8];
             tmem_ld8(tbase + lane_off + j0, y);
 #pragma unroll
@@ -461,7 +555,7 @@ int prefill_max_tiles(int T, int K, int E) {
 bool prefill_supported(int D, int H) { return D % 256 == 0 && H % 256 == 0 && H % PF_M == 0 && D % PF_M == 0; }
 
 int launch_prefill(const LayerArgs &la, const float *x, int *n_slots, __nv_bfloat16 *xb, __nv_bfloat16 *hb,
-                   int *tiles, int *err, cudaStream_t s) {
+                   int *tiles, int *err, cudaStream_t s, cudaEvent_t before, cudaEvent_t between) {
     const int T = la.T, D = la.D, H = la.H;
     const int max_tiles = prefill_max_tiles(T, la.K, la.E);
     int *n_tiles = tiles, *tile_slot = tiles + 1, *tile_start = tile_slot + max_tiles,
@@ -476,13 +570,13 @@ int launch_prefill(const LayerArgs &la, const float *x, int *n_slots, __nv_bfloa
     a.slot_expert = la.slot_expert; a.slot_start = la.slot_start; a.assign = la.assign;
     a.n_tiles = n_tiles; a.tile_slot = tile_slot; a.tile_start = tile_start; a.tile_n = tile_n;
     a.xb = xb; a.hb = hb; a.w = la.w; a.gsc = la.gsc; a.out = la.out; a.err = err;
-    const int smem_up = 2 * (2 * A_STAGE + B_STAGE);
-    const int smem_dn = 2 * (A_STAGE + B_STAGE);
-    static bool attr = false;
-    if (!attr) {
-        cudaFuncSetAttribute(prefill_up_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_up);
+    const int smem_up = UP_SMEM;
+    const int smem_dn = down_smem(H);
+    static int attr_dn = 0;
+    if (!attr_dn) cudaFuncSetAttribute(prefill_up_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_up);
+    if (smem_dn > attr_dn) {
         cudaFuncSetAttribute(prefill_down_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_dn);
-        attr = true;
+        attr_dn = smem_dn;
     }
     // out starts as the residual (or zero); the down kernel adds w * y into it
     cudaError_t e;
@@ -491,8 +585,10 @@ int launch_prefill(const LayerArgs &la, const float *x, int *n_slots, __nv_bfloa
         e = cudaMemcpyAsync(la.out, la.resid, (size_t)T * D * sizeof(float), cudaMemcpyDeviceToDevice, s);
     else e = cudaSuccess;
     if (e != cudaSuccess) return cuda_status(e, "prefill out init");
-    prefill_up_kernel<<<dim3(max_tiles, H / PF_M), PF_THREADS, smem_up, s>>>(a);
-    prefill_down_kernel<<<dim3(max_tiles, D / PF_M), PF_THREADS, smem_dn, s>>>(a);
+    if (before) cudaEventRecord(before, s);
+    prefill_up_kernel<<<dim3(max_tiles, H / PF_M), PF_NT, smem_up, s>>>(a);
+    if (between) cudaEventRecord(between, s);
+    prefill_down_kernel<<<dim3(max_tiles, D / PF_M), PF_NT, smem_dn, s>>>(a);
     OFB_CHECK_LAUNCH("prefill kernels");
     return OFB_OK;
 }
