@@ -1,29 +1,37 @@
 // prefill.cu — grouped expert GEMMs on the 5th-generation tensor cores
-// (tcgen05 + TMEM) for prefill-sized batches.
+// (tcgen05 + TMEM + TMA) for prefill-sized batches.
 //
 // Per expert e with n_e routed tokens (CSR slot from the dispatch plan), the
 // layer is two GEMMs:
-//   up:   H_e[n_e x 512]  = silu(X_e G_e^T) * (X_e U_e^T),  K = 2048
-//   down: Y_e[n_e x 2048] = H_e Dn_e^T,                     K = 512
+//   up:   H_e[n_e x H] = silu(X_e G_e^T) * (X_e U_e^T),  K = D
+//   down: Y_e[n_e x D] = H_e Dn_e^T,                     K = H
 // both computed transposed, D = A . B^T with A = dequantised weight rows
 // (M = 128 rows per CTA) and B = token rows (N <= 256 per tile), so the
 // ragged token dimension is the MMA's N and every CTA tile is a full 128-row
 // weight block.
-//  * A: each thread owns one weight row; the raw Q4_K / Q6_K bytes for the
-//    next 64-element K slice are loaded into registers while the tensor core
-//    works on the current one, then dequantised (the reference's exact fp32
-//    value, rounded to bf16) straight into shared memory in the canonical
-//    no-swizzle K-major layout (8x16-byte core matrices).
-//  * B: token rows are gathered from a bf16 copy of x (16.8 MB at 4096
-//    tokens: L2-resident) or from the bf16 h of phase 1, 32 bytes per load.
-//  * one elected thread issues tcgen05.mma (kind::f16, bf16 x bf16 -> f32)
-//    into TMEM; tcgen05.commit arrives on a per-stage mbarrier, which is what
-//    frees the stage for refilling (two stages in flight).
-//  * epilogue: tcgen05.ld of the accumulator (warp w reads TMEM lanes
-//    32w..32w+31 = its 32 weight rows); up writes h = silu(g)*u as bf16 in
+//  * B (token rows): TMA. The up GEMM gathers arbitrary token rows from a
+//    bf16 copy of x (L2-resident at 4096 tokens) with tile::gather4 loads
+//    (4 rows of 128 bytes each); the down GEMM's h rows are contiguous in slot
+//    order and come with one 2D tile load per stage. Both land in the 128-byte
+//    swizzled K-major layout and complete on a per-stage mbarrier.
+//  * A (weights): the raw Q4_K bytes a stage needs (the 16-byte header and
+//    two 16-byte quant chunks of each row's block) arrive by TMA through a 3D
+//    byte map (16-byte chunk x chunk index x row); the Q6_K rows of a CTA are
+//    one contiguous, 16-byte aligned slab (128 x 420 B) brought in by one bulk
+//    copy. 8 warps dequantise (the reference's exact fp32 value rounded to
+//    bf16; paired f32x2 arithmetic) into the same swizzled layout.
+//  * one thread issues tcgen05.mma (kind::f16, bf16 x bf16 -> f32) into TMEM;
+//    tcgen05.commit arrives on the mbarriers that free the stage's buffers.
+//  * warp-specialised: warp 0 produces (TMA), warp 1 issues the MMAs, warps
+//    4..11 dequantise; the roles meet only on full/empty mbarrier rings, so
+//    copies, dequantisation and tensor-core work of different stages overlap.
+//  * epilogue (warps 4..11): tcgen05.ld of the accumulator (warp w reads TMEM
+//    lanes 32*(w%4).. = its weight rows); up writes h = silu(g)*u as bf16 in
 //    slot order, down adds w * y into out with fp32 reductions.
-// Every mbarrier wait is bounded: on timeout the kernel records an error
-// flag, releases its TMEM and returns (the host reports OFB_ECUDA).
+// No TMA load here uses cluster multicast. Every mbarrier wait is bounded: on
+// timeout the kernel records an error flag, releases its TMEM and returns.
+#include <cuda.h>
+
 #include "common.cuh"
 #include "moe.cuh"
 
@@ -31,13 +39,16 @@ namespace ofb {
 
 constexpr int PF_M = 128;        // weight rows per CTA (MMA M)
 constexpr int PF_NMAX = 256;     // token rows per tile (MMA N, max)
-constexpr int PF_KS = 64;        // K elements per pipeline stage
-constexpr int PF_THREADS = 128;
-constexpr int A_LBO = (PF_M / 8) * 128;        // 2048 B between 8-element K chunks
-constexpr int B_LBO = (PF_NMAX / 8) * 128;     // 4096 B
-constexpr int A_STAGE = 8 * A_LBO;             // 16 KB
-constexpr int B_STAGE = 8 * B_LBO;             // 32 KB
-constexpr long long WAIT_LIMIT = 1ll << 26;    // try_wait polls before giving up
+constexpr int PF_KS = 64;        // K elements per pipeline stage (= one 128-byte swizzle row)
+constexpr int PF_NT = 384;       // threads per CTA: producer, MMA, 2 spare, 8 dequant/epilogue warps
+constexpr int PF_DQ0 = 128;      // first dequantising thread
+constexpr int PF_NDQW = 8;       // dequantising warps
+constexpr int PF_STG = 3;        // ring depth for B and raw A
+constexpr int PF_NA = 2;         // ring depth for dequantised A
+constexpr int A_STAGE = PF_M * 128;        // 16 KB: 128 rows x 128 B
+constexpr int B_STAGE = PF_NMAX * 128;     // 32 KB
+constexpr int RAW4 = PF_M * 48;            // raw Q4_K bytes of one matrix per stage
+constexpr long long WAIT_LIMIT = 1ll << 24;  // try_wait polls before giving up
 
 struct PrefillArgs {
     int T, D, H, E, K;
@@ -45,8 +56,7 @@ struct PrefillArgs {
     const uint8_t *gate, *up, *down, *gate_sh, *up_sh, *down_sh;
     const int *slot_expert, *slot_start, *assign;
     const int *n_tiles, *tile_slot, *tile_start, *tile_n;
-    const __nv_bfloat16 *xb;  // [T][D]
-    __nv_bfloat16 *hb;        // [A][H], slot order
+    __nv_bfloat16 *hb;  // [A][H], slot order
     const float *w, *gsc;
     float *out;
     int *err;
@@ -73,9 +83,18 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *b, uint32_t parity) {
     }
     return false;
 }
-__device__ __forceinline__ uint64_t smem_desc(uint32_t addr, uint32_t lbo, uint32_t sbo) {
-    return (uint64_t)((addr & 0x3FFFF) >> 4) | ((uint64_t)(lbo >> 4) << 16) |
-           ((uint64_t)(sbo >> 4) << 32) | (1ull << 46);
+__device__ __forceinline__ void mbar_arrive(uint64_t *b) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(b)) : "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(uint64_t *b, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(b)), "r"(bytes)
+                 : "memory");
+}
+// UMMA shared-memory descriptor, K-major, 128-byte swizzle: rows of 128 B,
+// 8-row atoms 1024 B apart (SBO), descriptor version 1.
+__device__ __forceinline__ uint64_t sw128_desc(uint32_t addr) {
+    return (uint64_t)((addr & 0x3FFFF) >> 4) | (1ull << 16) | ((uint64_t)(1024 >> 4) << 32) | (1ull << 46) |
+           (2ull << 61);
 }
 // bf16 x bf16 -> f32, both K-major, M = 128.
 __device__ __forceinline__ uint32_t instr_desc(int n) {
@@ -125,106 +144,59 @@ __device__ __forceinline__ void tmem_free(uint32_t base, uint32_t ncols) {
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(base), "r"(ncols));
 }
 
-__device__ __forceinline__ uint32_t pack_bf16(float a, float b) {
-    __nv_bfloat162 p = __floats2bfloat162_rn(a, b);
-    return *reinterpret_cast<uint32_t *>(&p);
-}
-
-// smem byte offset of (row, 8-element K chunk) in a no-swizzle K-major tile
-__device__ __forceinline__ uint32_t core_off(int row, int chunk, int lbo) {
-    return chunk * lbo + (row >> 3) * 128 + (row & 7) * 16;
-}
-
-// ---- async copies -----------------------------------------------------------
-// 16-byte global->shared copy; src_bytes = 0 zero-fills the destination.
-__device__ __forceinline__ void cp_async16(uint32_t dst, const void *src, uint32_t src_bytes) {
-    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(src_bytes)
-                 : "memory");
-}
-__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-template <int N>
-__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
-// One TMA bulk copy global -> shared completing on an mbarrier (no multicast).
+// ---- copies -----------------------------------------------------------------
+// TMA bulk copy global -> shared, completing on an mbarrier (no multicast).
 __device__ __forceinline__ void bulk_copy(void *dst, const void *src, uint32_t bytes, uint64_t *bar) {
-    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
-                 : "memory");
+    mbar_expect_tx(bar, bytes);
     asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
                      smem_u32(dst)),
                  "l"(src), "r"(bytes), "r"(smem_u32(bar))
                  : "memory");
 }
-
-// 4 bytes at a 2-byte aligned shared-memory address.
-__device__ __forceinline__ uint32_t lds_u32_2b(const uint8_t *p) {
-    const uintptr_t a = reinterpret_cast<uintptr_t>(p);
-    const uint32_t *b = reinterpret_cast<const uint32_t *>(a & ~uintptr_t(3));
-    return __funnelshift_r(b[0], b[1], (unsigned)(a & 3) * 8);
+// Four 64-element rows (y0..y3, starting at column x) of a 2D bf16 tensor:
+// 512 bytes, one-row box.
+__device__ __forceinline__ void tma_gather4(uint32_t dst, const CUtensorMap *map, int x, int y0, int y1, int y2,
+                                            int y3, uint64_t *bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile::gather4.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%2, %3, %4, %5, %6}], [%7];" ::"r"(dst),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y0), "r"(y1), "r"(y2), "r"(y3), "r"(smem_u32(bar))
+        : "memory");
+}
+// One 3D box at (c0, c1, c2).
+__device__ __forceinline__ void tma_load3d(uint32_t dst, const CUtensorMap *map, int c0, int c1, int c2,
+                                           uint64_t *bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%2, %3, %4}], [%5];" ::"r"(dst),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(smem_u32(bar))
+        : "memory");
+}
+// One 2D box (64 columns x 256 rows) at (x, y).
+__device__ __forceinline__ void tma_tile2d(uint32_t dst, const CUtensorMap *map, int x, int y, uint64_t *bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%2, %3}], [%4];" ::"r"(dst),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
+        : "memory");
 }
 
-// byte k of w as a float (exact small integer): 2^23 + byte, minus 2^23 + bias
-template <int K>
-__device__ __forceinline__ float byte_f(uint32_t w, float bias) {
-    return __uint_as_float(__byte_perm(w, 0x4B000000u, 0x7540u + K)) - bias;
-}
+// ---- layout and conversion helpers ----------------------------------------------
+// Byte offset of 16-byte chunk c of row r in a 128-byte swizzled K-major tile
+// (1024-byte aligned base): the TMA/UMMA SWIZZLE_128B pattern.
+__device__ __forceinline__ uint32_t sw_off(int r, int c) { return r * 128 + ((c ^ (r & 7)) << 4); }
 
-constexpr int PF_NT = 256;                    // threads per CTA (8 warps)
-constexpr int PF_STG = 3;                     // cp.async pipeline depth
-constexpr int B_LBO_P = B_LBO + 16;           // padded: the 8 chunks of a row hit 8 bank groups
-constexpr int B_STAGE_P = 8 * B_LBO_P;
-constexpr int RAW4 = PF_M * 48;               // raw Q4_K bytes of one matrix per stage
-
-// B: 2048 16-byte copies per stage; thread t copies j = t + 256 k (k < 8):
-// chunk = j & 7, row = j >> 3 (a quarter-warp copies one 128-byte row).
-// The per-thread sources and destinations are fixed for the whole K loop.
-struct BPlan { const __nv_bfloat16 *src[8]; uint32_t dst[8]; uint32_t bytes[8]; };
-__device__ __forceinline__ void b_plan(BPlan &p, const __nv_bfloat16 *const *rowp, int n_rows) {
-#pragma unroll
-    for (int k = 0; k < 8; k++) {
-        const int j = threadIdx.x + PF_NT * k;
-        const int ch = j & 7, row = j >> 3;
-        const bool ok = row < n_rows;
-        p.src[k] = rowp[ok ? row : 0] + ch * 8;
-        p.dst[k] = core_off(row, ch, B_LBO_P);
-        p.bytes[k] = ok ? 16u : 0u;
-    }
+__device__ __forceinline__ uint32_t pack_bf16(float a, float b) {
+    __nv_bfloat162 p = __floats2bfloat162_rn(a, b);
+    return *reinterpret_cast<uint32_t *>(&p);
 }
-__device__ __forceinline__ void b_issue(const BPlan &p, uint32_t sb, int k0) {
-#pragma unroll
-    for (int k = 0; k < 8; k++) cp_async16(sb + p.dst[k], p.src[k] + k0, p.bytes[k]);
-}
-
-// Q4_K raw bytes of one stage (16 B header + 32 quant bytes per row, both
-// matrices): 768 copies, thread t copies t, t+256, t+512.
-struct QPlan { const uint8_t *src[3]; uint32_t dst[3]; int part[3]; };
-__device__ __forceinline__ void q4_plan(QPlan &p, const uint8_t *g0, const uint8_t *u0, size_t row_bytes) {
-#pragma unroll
-    for (int k = 0; k < 3; k++) {
-        const int j = threadIdx.x + PF_NT * k;
-        const int mat = j / 384, rem = j - mat * 384, row = rem / 3, part = rem - row * 3;
-        p.src[k] = (mat ? u0 : g0) + row * row_bytes;
-        p.dst[k] = mat * RAW4 + row * 48 + part * 16;
-        p.part[k] = part;
-    }
-}
-__device__ __forceinline__ void q4_issue(const QPlan &p, uint32_t sraw, int stage) {
-    const int b = stage >> 2, c = stage & 3;
-#pragma unroll
-    for (int k = 0; k < 3; k++) {
-        const int off = b * Q4K_BYTES + (p.part[k] ? 16 + c * 32 + (p.part[k] - 1) * 16 : 0);
-        cp_async16(sraw + p.dst[k], p.src[k] + off, 16u);
-    }
-}
-
-// Paired fp32 arithmetic (sm_100a f32x2): two lanes of work per instruction.
+// Paired fp32 arithmetic (sm_100a f32x2): two elements per instruction.
 __device__ __forceinline__ unsigned long long f2pack(float a, float b) {
     unsigned long long p;
     asm("mov.b64 %0, {%1,%2};" : "=l"(p) : "f"(a), "f"(b));
     return p;
 }
-__device__ __forceinline__ uint32_t f2_fma_bf16(unsigned long long x, unsigned long long m,
-                                                 unsigned long long c) {
-    unsigned long long r;
-    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(x), "l"(m), "l"(c));
+__device__ __forceinline__ uint32_t f2_to_bf16(unsigned long long r) {
     float lo, hi;
     asm("mov.b64 {%0,%1}, %2;" : "=f"(lo), "=f"(hi) : "l"(r));
     return pack_bf16(lo, hi);
@@ -234,22 +206,50 @@ __device__ __forceinline__ unsigned long long f2_add(unsigned long long a, unsig
     asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
     return r;
 }
-// two bytes (k, k+1) of w as exact floats 2^23 + byte, as a pair
+__device__ __forceinline__ uint32_t f2_fma_bf16(unsigned long long x, unsigned long long m, unsigned long long c) {
+    unsigned long long r;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(x), "l"(m), "l"(c));
+    return f2_to_bf16(r);
+}
+__device__ __forceinline__ uint32_t f2_mul_bf16(unsigned long long x, unsigned long long m) {
+    unsigned long long r;
+    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(x), "l"(m));
+    return f2_to_bf16(r);
+}
+// bytes (k, k+1) of w as the exact floats 2^23 + byte, as a pair
 template <int K>
 __device__ __forceinline__ unsigned long long byte_pair(uint32_t w) {
     return f2pack(__uint_as_float(__byte_perm(w, 0x4B000000u, 0x7540u + K)),
                   __uint_as_float(__byte_perm(w, 0x4B000000u, 0x7541u + K)));
 }
+// 4 bytes at a 2-byte aligned shared-memory address.
+__device__ __forceinline__ uint32_t lds_u32_2b(const uint8_t *p) {
+    const uintptr_t a = reinterpret_cast<uintptr_t>(p);
+    const uint32_t *b = reinterpret_cast<const uint32_t *>(a & ~uintptr_t(3));
+    return __funnelshift_r(b[0], b[1], (unsigned)(a & 3) * 8);
+}
 
-// Dequantise one matrix's stage: thread (row r, half hh) writes chunks
-// 4hh..4hh+3 (low nibbles for hh = 0, high for hh = 1). Value = (d*sc)*q -
-// dmin*m as one fused multiply-add: d*sc*q is exact in fp32 (<= 21 bits), so
-// the result equals the reference's two separately rounded operations.
-__device__ __forceinline__ void q4_deq(const uint8_t *raw, int stage, uint8_t *sa) {
-    const int r = threadIdx.x & (PF_M - 1), hh = threadIdx.x >> 7, c = stage & 3;
-    const uint4 hdr = *reinterpret_cast<const uint4 *>(raw + r * 48);
-    const uint4 qa = *reinterpret_cast<const uint4 *>(raw + r * 48 + 16);
-    const uint4 qb = *reinterpret_cast<const uint4 *>(raw + r * 48 + 32);
+// ---- A operand, Q4_K ----------------------------------------------------------------
+// Raw bytes of one matrix for one stage, as three TMA boxes of 128 rows x 16
+// bytes: [header | quant chunk 2c | quant chunk 2c+1] (chunk c of block b:
+// elements 64c..64c+63, quant bytes 32c..32c+31).
+__device__ __forceinline__ void q4_issue(const CUtensorMap *map, int row0, uint32_t dst, int stage, uint64_t *bar) {
+    const int b = stage >> 2, c = stage & 3;
+    tma_load3d(dst, map, 0, b * 9, row0, bar);
+    tma_load3d(dst + 2048, map, 0, b * 9 + 1 + 2 * c, row0, bar);
+    tma_load3d(dst + 4096, map, 0, b * 9 + 2 + 2 * c, row0, bar);
+}
+
+// Dequantising thread t (row r = t%128, half hh = t/128) writes chunks
+// 4hh..4hh+3 of its row (low nibbles for hh = 0, high for hh = 1). Value =
+// (d*sc)*q - dmin*m as one fused multiply-add: d*sc*q is exact in fp32
+// (<= 21 significant bits), so the result equals the reference's two
+// separately rounded operations.
+__device__ __forceinline__ void q4_deq(const uint8_t *raw, int stage, int t, uint8_t *sa) {
+    const int r = t & (PF_M - 1), hh = t >> 7, c = stage & 3;
+    const uint4 hdr = *reinterpret_cast<const uint4 *>(raw + r * 16);
+    const uint4 qa = *reinterpret_cast<const uint4 *>(raw + 2048 + r * 16);
+    const uint4 qb = *reinterpret_cast<const uint4 *>(raw + 4096 + r * 16);
     const uint32_t s[3] = {hdr.y, hdr.z, hdr.w};
     int sc, mn;
     q4k_scale_min(s, 2 * c + hh, sc, mn);
@@ -262,138 +262,185 @@ __device__ __forceinline__ void q4_deq(const uint8_t *raw, int stage, uint8_t *s
 #pragma unroll
     for (int ch = 0; ch < 4; ch++) {
         const uint32_t w0 = (qw[2 * ch] >> sh) & 0x0F0F0F0Fu, w1 = (qw[2 * ch + 1] >> sh) & 0x0F0F0F0Fu;
-        // q as exact floats, then one paired FMA per two elements
         const uint32_t p0 = f2_fma_bf16(f2_add(byte_pair<0>(w0), nb2), d2, nm2);
         const uint32_t p1 = f2_fma_bf16(f2_add(byte_pair<2>(w0), nb2), d2, nm2);
         const uint32_t p2 = f2_fma_bf16(f2_add(byte_pair<0>(w1), nb2), d2, nm2);
         const uint32_t p3 = f2_fma_bf16(f2_add(byte_pair<2>(w1), nb2), d2, nm2);
-        *reinterpret_cast<uint4 *>(sa + core_off(r, 4 * hh + ch, A_LBO)) = make_uint4(p0, p1, p2, p3);
+        *reinterpret_cast<uint4 *>(sa + sw_off(r, 4 * hh + ch)) = make_uint4(p0, p1, p2, p3);
     }
 }
 
-// Q6_K stage from the raw slab in shared memory: thread (row r, hh) writes the
-// 32 elements of quad 2*(chunk%2)+hh. Value = (d*sc)*(q-32), one rounding.
-__device__ __forceinline__ void q6_deq(const uint8_t *slab, int row_bytes, int stage, uint8_t *sa) {
-    const int r = threadIdx.x & (PF_M - 1), hh = threadIdx.x >> 7;
+// ---- A operand, Q6_K (from the raw slab in shared memory) ----------------------------
+// 64-element chunk q of a block: half = q/2, quads 2*(q%2) and 2*(q%2)+1;
+// thread t (row r, hh) writes quad 2*(q%2)+hh. Value = (d*sc)*(q-32), one
+// rounding each, as the reference.
+__device__ __forceinline__ void q6_deq(const uint8_t *slab, int row_bytes, int stage, int t, uint8_t *sa) {
+    const int r = t & (PF_M - 1), hh = t >> 7;
     const int b = stage >> 2, q64 = stage & 3, half6 = q64 >> 1, quad = 2 * (q64 & 1) + hh;
     const uint8_t *blk = slab + r * row_bytes + b * Q6K_BYTES;
     const uint8_t *ql = blk + half6 * 64 + (quad & 1) * 32;
     const uint8_t *qh = blk + 128 + half6 * 32;
-    const uint32_t scw = (uint32_t)blk[192 + half6 * 8 + quad * 2] | ((uint32_t)blk[193 + half6 * 8 + quad * 2] << 8);
+    const int si = 192 + half6 * 8 + quad * 2;
     const float d = half_bits_ref((uint32_t)blk[208] | ((uint32_t)blk[209] << 8));
-    const float ds0 = __fmul_rn(d, (float)(int8_t)(scw & 0xFF)), ds1 = __fmul_rn(d, (float)(int8_t)(scw >> 8));
-    const float bias = 8388608.0f + 32.0f;
+    const float ds0 = __fmul_rn(d, (float)(int8_t)blk[si]), ds1 = __fmul_rn(d, (float)(int8_t)blk[si + 1]);
+    const unsigned long long nb2 = f2pack(-8388640.0f, -8388640.0f);  // -(2^23 + 32)
     const int nsh = (quad >= 2) ? 4 : 0, hsh = 2 * quad;
 #pragma unroll
     for (int ch = 0; ch < 4; ch++) {
-        const float ds = ch < 2 ? ds0 : ds1;  // l = 8ch..8ch+7, is = l/16
+        const float ds = ch < 2 ? ds0 : ds1;  // l = 8ch..8ch+7, scale index l/16
+        const unsigned long long d2 = f2pack(ds, ds);
         uint32_t q[2];
 #pragma unroll
         for (int h2 = 0; h2 < 2; h2++) {
             const uint32_t wl = lds_u32_2b(ql + ch * 8 + h2 * 4), wh = lds_u32_2b(qh + ch * 8 + h2 * 4);
             q[h2] = ((wl >> nsh) & 0x0F0F0F0Fu) | (((wh >> hsh) & 0x03030303u) << 4);
         }
-        const float v0 = __fmul_rn(ds, byte_f<0>(q[0], bias)), v1 = __fmul_rn(ds, byte_f<1>(q[0], bias));
-        const float v2 = __fmul_rn(ds, byte_f<2>(q[0], bias)), v3 = __fmul_rn(ds, byte_f<3>(q[0], bias));
-        const float v4 = __fmul_rn(ds, byte_f<0>(q[1], bias)), v5 = __fmul_rn(ds, byte_f<1>(q[1], bias));
-        const float v6 = __fmul_rn(ds, byte_f<2>(q[1], bias)), v7 = __fmul_rn(ds, byte_f<3>(q[1], bias));
-        *reinterpret_cast<uint4 *>(sa + core_off(r, 4 * hh + ch, A_LBO)) =
-            make_uint4(pack_bf16(v0, v1), pack_bf16(v2, v3), pack_bf16(v4, v5), pack_bf16(v6, v7));
+        const uint32_t p0 = f2_mul_bf16(f2_add(byte_pair<0>(q[0]), nb2), d2);
+        const uint32_t p1 = f2_mul_bf16(f2_add(byte_pair<2>(q[0]), nb2), d2);
+        const uint32_t p2 = f2_mul_bf16(f2_add(byte_pair<0>(q[1]), nb2), d2);
+        const uint32_t p3 = f2_mul_bf16(f2_add(byte_pair<2>(q[1]), nb2), d2);
+        *reinterpret_cast<uint4 *>(sa + sw_off(r, 4 * hh + ch)) = make_uint4(p0, p1, p2, p3);
     }
 }
 
 __device__ __forceinline__ int asg_token_p(int a, int TK, int K) { return a < TK ? a / K : a - TK; }
 
-// ---- phase 1: gate/up ----------------------------------------------------------
-// Iteration i: (1) stage i's copies have landed; (2) dequantise it into the
-// bf16 A buffer i%2 (free: MMA i-2 was waited for in iteration i-1) while the
-// tensor core runs MMA i-1; (3) issue MMA i; (4) wait for MMA i-1, whose B
-// buffer is the one stage i+2 refills, then issue stage i+2's copies.
-constexpr int UP_SMEM = PF_STG * (2 * RAW4 + B_STAGE_P) + 2 * (2 * A_STAGE);
+// Parity of the phase that completes the n-th use (n = 0, 1, ...) of a ring
+// slot is n & 1; a producer refilling a slot for use n >= 1 waits for the
+// consumer's release of use n-1, parity (n-1) & 1.
+struct Rings {
+    uint64_t bfull[PF_STG], bempty[PF_STG];   // B: TMA -> MMA
+    uint64_t rfull[PF_STG], rempty[PF_STG];   // raw A: TMA -> dequant
+    uint64_t afull[PF_NA], aempty[PF_NA];     // bf16 A: dequant -> MMA
+    uint64_t done;                            // all MMAs complete -> epilogue
+};
+__device__ __forceinline__ void rings_init(Rings &R) {
+    for (int i = 0; i < PF_STG; i++) {
+        mbar_init(&R.bfull[i], 1);
+        mbar_init(&R.bempty[i], 1);
+        mbar_init(&R.rfull[i], 1);
+        mbar_init(&R.rempty[i], PF_NDQW);
+    }
+    for (int i = 0; i < PF_NA; i++) {
+        mbar_init(&R.afull[i], PF_NDQW);
+        mbar_init(&R.aempty[i], 1);
+    }
+    mbar_init(&R.done, 1);
+}
 
-__global__ void __launch_bounds__(PF_NT, 1) prefill_up_kernel(PrefillArgs a) {
-    extern __shared__ __align__(1024) uint8_t psm[];
-    __shared__ uint64_t bars[2];
+// MMA role (one thread): per stage wait for A and B, issue the K = 64 slice
+// of the product into each accumulator, release both buffers.
+template <int NACC>
+__device__ __forceinline__ bool mma_role(Rings &R, int nstages, const uint8_t *abf, const uint8_t *bst,
+                                         uint32_t tbase, uint32_t idesc) {
+    bool ok = true;
+    for (int i = 0; i < nstages && ok; i++) {
+        const int sa = i % PF_NA, sb = i % PF_STG;
+        ok = mbar_wait(&R.afull[sa], (i / PF_NA) & 1) && mbar_wait(&R.bfull[sb], (i / PF_STG) & 1);
+        if (!ok) break;
+        tc_fence_after();
+        const uint32_t aa = smem_u32(abf + sa * NACC * A_STAGE), bb = smem_u32(bst + sb * B_STAGE);
+#pragma unroll
+        for (int kk = 0; kk < PF_KS / 16; kk++) {
+            const uint64_t bd = sw128_desc(bb + kk * 32);
+#pragma unroll
+            for (int m = 0; m < NACC; m++)
+                mma_bf16(tbase + m * 256, sw128_desc(aa + m * A_STAGE + kk * 32), bd, idesc, (i | kk) != 0);
+        }
+        mma_commit(&R.aempty[sa]);
+        mma_commit(&R.bempty[sb]);
+    }
+    mma_commit(&R.done);  // arrives once all issued MMAs complete
+    return ok;
+}
+
+// ---- phase 1: gate/up ----------------------------------------------------------------
+constexpr int UP_SMEM = 1024 + PF_STG * B_STAGE + PF_NA * 2 * A_STAGE + PF_STG * 2 * RAW4;
+
+__global__ void __launch_bounds__(PF_NT, 1)
+    prefill_up_kernel(PrefillArgs a, const __grid_constant__ CUtensorMap xmap,
+                      const __grid_constant__ CUtensorMap gmap, const __grid_constant__ CUtensorMap umap,
+                      const __grid_constant__ CUtensorMap gmap_sh, const __grid_constant__ CUtensorMap umap_sh) {
+    extern __shared__ uint8_t psm_raw[];
+    uint8_t *psm = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(psm_raw) + 1023) & ~uintptr_t(1023));
+    __shared__ Rings R;
     __shared__ uint32_t tslot;
-    __shared__ const __nv_bfloat16 *rowp[PF_NMAX];
+    __shared__ int trow[PF_NMAX];
     const int tile = blockIdx.x;
     if (tile >= *a.n_tiles) return;
     const int u = a.tile_slot[tile], s0 = a.tile_start[tile], n = a.tile_n[tile];
     const int e = a.slot_expert[u];
     const int m0 = blockIdx.y * PF_M;
     const int TK = a.T * a.K;
-    const size_t row_bytes = (size_t)(a.D / QK) * Q4K_BYTES, exp_bytes = row_bytes * a.H;
-    const uint8_t *g0 = (e == a.E ? a.gate_sh : a.gate + e * exp_bytes) + (size_t)m0 * row_bytes;
-    const uint8_t *u0 = (e == a.E ? a.up_sh : a.up + e * exp_bytes) + (size_t)m0 * row_bytes;
+    // token row of each tile row; padding rows repeat the first token (their
+    // accumulator columns are never read)
     for (int i = threadIdx.x; i < PF_NMAX; i += PF_NT)
-        rowp[i] = a.xb + (size_t)(i < n ? asg_token_p(a.assign[s0 + i], TK, a.K) : 0) * a.D;
-    if (threadIdx.x == 0) { mbar_init(&bars[0], 1); mbar_init(&bars[1], 1); }
+        trow[i] = asg_token_p(a.assign[s0 + (i < n ? i : 0)], TK, a.K);
+    if (threadIdx.x == 0) rings_init(R);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-    const uint32_t tbase = tmem_alloc(&tslot, 512);  // gate: cols [0,256), up: [256,512)
+    const uint32_t tbase = tmem_alloc(&tslot, 512);  // gate: cols [0,256), up: [256,512); syncs the CTA
 
-    uint8_t *raw = psm;                                   // [PF_STG][2*RAW4]
-    uint8_t *bst = psm + PF_STG * 2 * RAW4;               // [PF_STG][B_STAGE_P]
-    uint8_t *abf = bst + PF_STG * B_STAGE_P;              // [2][gate A | up A]
-    const int nn = (n + 15) & ~15;
-    const uint32_t idesc = instr_desc(nn);
+    uint8_t *bst = psm;                          // [PF_STG][B_STAGE]        1024-aligned
+    uint8_t *abf = bst + PF_STG * B_STAGE;       // [PF_NA][gate A | up A]   1024-aligned
+    uint8_t *raw = abf + PF_NA * 2 * A_STAGE;    // [PF_STG][gate raw | up raw]
+    const int nn = (n + 15) & ~15;               // MMA N and rows fetched per stage
     const int nstages = a.D / PF_KS;
-    __syncthreads();  // rowp
-    BPlan bp;
-    b_plan(bp, rowp, n);
-    QPlan qp;
-    q4_plan(qp, g0, u0, row_bytes);
-    for (int i = 0; i < PF_STG - 1; i++) {
-        if (i < nstages) {
-            q4_issue(qp, smem_u32(raw + i * 2 * RAW4), i);
-            b_issue(bp, smem_u32(bst + i * B_STAGE_P), i * PF_KS);
-        }
-        cp_async_commit();
-    }
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     bool ok = true;
-    for (int i = 0; i < nstages; i++) {
-        const int sr = i % PF_STG, sa = i & 1;
-        cp_async_wait<PF_STG - 2>();
-        __syncthreads();
-        uint8_t *ag = abf + sa * 2 * A_STAGE, *au = ag + A_STAGE;
-        q4_deq(raw + sr * 2 * RAW4, i, ag);
-        q4_deq(raw + sr * 2 * RAW4 + RAW4, i, au);
-        async_proxy_fence();
-        __syncthreads();
-        if (threadIdx.x == 0) {
-            tc_fence_after();
-            const uint32_t ga = smem_u32(ag), ua = smem_u32(au), bb = smem_u32(bst + sr * B_STAGE_P);
-#pragma unroll
-            for (int kk = 0; kk < PF_KS / 16; kk++) {
-                const uint64_t bd = smem_desc(bb + kk * 2 * B_LBO_P, B_LBO_P, 128);
-                mma_bf16(tbase, smem_desc(ga + kk * 2 * A_LBO, A_LBO, 128), bd, idesc, (i | kk) != 0);
-                mma_bf16(tbase + 256, smem_desc(ua + kk * 2 * A_LBO, A_LBO, 128), bd, idesc, (i | kk) != 0);
+    if (warp == 0) {
+        // producer: B by gather4 (lanes split the nn/4 gathers), raw A by lane 0
+        const CUtensorMap *gm = e == a.E ? &gmap_sh : &gmap, *um = e == a.E ? &umap_sh : &umap;
+        const int row0 = (e == a.E ? 0 : e * a.H) + m0;
+        for (int i = 0; i < nstages && ok; i++) {
+            const int sb = i % PF_STG, use = i / PF_STG;
+            if (use > 0) ok = mbar_wait(&R.bempty[sb], (use - 1) & 1);
+            if (!ok) break;
+            if (lane == 0) mbar_expect_tx(&R.bfull[sb], nn * 128);
+            __syncwarp();
+            const uint32_t dst = smem_u32(bst + sb * B_STAGE);
+            for (int g = lane; g < nn / 4; g += 32)
+                tma_gather4(dst + g * 512, &xmap, i * PF_KS, trow[4 * g], trow[4 * g + 1], trow[4 * g + 2],
+                            trow[4 * g + 3], &R.bfull[sb]);
+            if (use > 0) ok = mbar_wait(&R.rempty[sb], (use - 1) & 1);
+            if (!ok) break;
+            if (lane == 0) {
+                mbar_expect_tx(&R.rfull[sb], 2 * RAW4);
+                const uint32_t rd = smem_u32(raw + sb * 2 * RAW4);
+                q4_issue(gm, row0, rd, i, &R.rfull[sb]);
+                q4_issue(um, row0, rd + RAW4, i, &R.rfull[sb]);
             }
-            mma_commit(&bars[sa]);
         }
-        // one warp waits for MMA i-1 (its B buffer is refilled next); the
-        // others wait at the barrier instead of polling
-        if (i >= 1) {
-            if (threadIdx.x < 32) ok = ok && mbar_wait(&bars[(i - 1) & 1], ((i - 1) >> 1) & 1);
-            __syncthreads();
+    } else if (warp == 1) {
+        if (lane == 0) ok = mma_role<2>(R, nstages, abf, bst, tbase, instr_desc(nn));
+    } else if (warp >= PF_DQ0 / 32) {
+        const int t = threadIdx.x - PF_DQ0;
+        for (int i = 0; i < nstages && ok; i++) {
+            const int sr = i % PF_STG, sa = i % PF_NA;
+            ok = mbar_wait(&R.rfull[sr], (i / PF_STG) & 1);
+            if (ok && i >= PF_NA) ok = mbar_wait(&R.aempty[sa], (i / PF_NA - 1) & 1);
+            if (!ok) break;
+            uint8_t *ag = abf + sa * 2 * A_STAGE;
+            q4_deq(raw + sr * 2 * RAW4, i, t, ag);
+            q4_deq(raw + sr * 2 * RAW4 + RAW4, i, t, ag + A_STAGE);
+            async_proxy_fence();
+            __syncwarp();
+            if (lane == 0) {
+                mbar_arrive(&R.rempty[sr]);
+                mbar_arrive(&R.afull[sa]);
+            }
         }
-        const int nx = i + PF_STG - 1;
-        if (nx < nstages) {
-            q4_issue(qp, smem_u32(raw + (nx % PF_STG) * 2 * RAW4), nx);
-            b_issue(bp, smem_u32(bst + (nx % PF_STG) * B_STAGE_P), nx * PF_KS);
-        }
-        cp_async_commit();
+        if (ok) ok = mbar_wait(&R.done, 0);
     }
-    if (threadIdx.x < 32) ok = ok && mbar_wait(&bars[(nstages - 1) & 1], ((nstages - 1) >> 1) & 1);
     ok = __syncthreads_and(ok);
     tc_fence_after();
     if (!ok) {
         if (threadIdx.x == 0) atomicExch(a.err, 1);
-    } else {
-        // warp w reads TMEM lanes 32*(w%4).. (its rows), columns of half w/4
-        const int w = threadIdx.x >> 5, lane = threadIdx.x & 31, q = w & 3;
+    } else if (warp >= PF_DQ0 / 32) {
+        // warp w reads TMEM lanes 32*(w%4).. (its rows), columns of half (w-4)/4
+        const int q = warp & 3;
         const int m = m0 + q * 32 + lane;
         const uint32_t lane_off = (uint32_t)(q * 32) << 16;
-        const int half = nn / 2, j_beg = (w >> 2) * half;
+        const int half = nn / 2, j_beg = ((warp - PF_DQ0 / 32) >> 2) * half;
         for (int j0 = j_beg; j0 < j_beg + half; j0 += 8) {
             float g[8], uu[8];
             tmem_ld8(tbase + lane_off + j0, g);
@@ -412,17 +459,19 @@ __global__ void __launch_bounds__(PF_NT, 1) prefill_up_kernel(PrefillArgs a) {
 
 // ---- phase 2: down + weighted combine -----------------------------------------
 // The CTA's 128 Q6_K rows are one contiguous, 16-byte aligned slab
-// (128 x 420 B): one TMA bulk copy brings it in; stages then only copy B.
+// (128 x 420 B at H = 512): one bulk copy brings it in; stages copy only B.
 __host__ __device__ inline int down_slab_bytes(int H) { return PF_M * (H / QK) * Q6K_BYTES; }
 __host__ __device__ inline int down_smem(int H) {
-    return down_slab_bytes(H) + 16 + PF_STG * B_STAGE_P + 2 * A_STAGE;
+    return 1024 + PF_STG * B_STAGE + PF_NA * A_STAGE + down_slab_bytes(H);
 }
 
-__global__ void __launch_bounds__(PF_NT, 1) prefill_down_kernel(PrefillArgs a) {
-    extern __shared__ __align__(1024) uint8_t psm[];
-    __shared__ uint64_t bars[3];
+__global__ void __launch_bounds__(PF_NT, 1)
+    prefill_down_kernel(PrefillArgs a, const __grid_constant__ CUtensorMap hmap) {
+    extern __shared__ uint8_t psm_raw[];
+    uint8_t *psm = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(psm_raw) + 1023) & ~uintptr_t(1023));
+    __shared__ Rings R;
+    __shared__ uint64_t slab_bar;
     __shared__ uint32_t tslot;
-    __shared__ const __nv_bfloat16 *rowp[PF_NMAX];
     __shared__ int tok[PF_NMAX];
     __shared__ float wgt[PF_NMAX];
     const int tile = blockIdx.x;
@@ -434,69 +483,65 @@ __global__ void __launch_bounds__(PF_NT, 1) prefill_down_kernel(PrefillArgs a) {
     const int row_bytes = (a.H / QK) * Q6K_BYTES;
     const size_t exp_bytes = (size_t)row_bytes * a.D;
     const uint8_t *slab_src = (e == a.E ? a.down_sh : a.down + e * exp_bytes) + (size_t)n0 * row_bytes;
-    uint8_t *bst = psm;                                    // [PF_STG][B_STAGE_P]
-    uint8_t *abf = bst + PF_STG * B_STAGE_P;               // [2][A_STAGE]
-    uint8_t *slab = abf + 2 * A_STAGE;                     // raw Q6_K rows
-    for (int i = threadIdx.x; i < PF_NMAX; i += PF_NT) {
-        rowp[i] = a.hb + (size_t)(s0 + (i < n ? i : 0)) * a.H;
-        if (i < n) {
-            const int asg = a.assign[s0 + i];
-            const int t = asg_token_p(asg, TK, a.K);
-            tok[i] = t;
-            wgt[i] = asg < TK ? a.w[asg] : (a.shared_gate ? a.gsc[t] : 1.0f);
-        }
+    uint8_t *bst = psm;                        // [PF_STG][B_STAGE]
+    uint8_t *abf = bst + PF_STG * B_STAGE;     // [PF_NA][A_STAGE]
+    uint8_t *slab = abf + PF_NA * A_STAGE;     // raw Q6_K rows (16-byte aligned)
+    for (int i = threadIdx.x; i < n; i += PF_NT) {
+        const int asg = a.assign[s0 + i];
+        const int t = asg_token_p(asg, TK, a.K);
+        tok[i] = t;
+        wgt[i] = asg < TK ? a.w[asg] : (a.shared_gate ? a.gsc[t] : 1.0f);
     }
-    if (threadIdx.x == 0) { mbar_init(&bars[0], 1); mbar_init(&bars[1], 1); mbar_init(&bars[2], 1); }
+    if (threadIdx.x == 0) {
+        rings_init(R);
+        mbar_init(&slab_bar, 1);
+    }
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-    __syncthreads();
-    if (threadIdx.x == 0) bulk_copy(slab, slab_src, down_slab_bytes(a.H), &bars[2]);
-    const uint32_t tbase = tmem_alloc(&tslot, 256);
+    const uint32_t tbase = tmem_alloc(&tslot, 256);  // syncs the CTA
 
     const int nn = (n + 15) & ~15;
-    const uint32_t idesc = instr_desc(nn);
     const int nstages = a.H / PF_KS;
-    BPlan bp;
-    b_plan(bp, rowp, n);
-    for (int i = 0; i < PF_STG - 1; i++) {
-        if (i < nstages) b_issue(bp, smem_u32(bst + i * B_STAGE_P), i * PF_KS);
-        cp_async_commit();
-    }
-    bool ok = mbar_wait(&bars[2], 0);
-    for (int i = 0; i < nstages; i++) {
-        const int sr = i % PF_STG, sa = i & 1;
-        cp_async_wait<PF_STG - 2>();
-        __syncthreads();
-        uint8_t *ad = abf + sa * A_STAGE;
-        q6_deq(slab, row_bytes, i, ad);
-        async_proxy_fence();
-        __syncthreads();
-        if (threadIdx.x == 0) {
-            tc_fence_after();
-            const uint32_t aa = smem_u32(ad), bb = smem_u32(bst + sr * B_STAGE_P);
-#pragma unroll
-            for (int kk = 0; kk < PF_KS / 16; kk++)
-                mma_bf16(tbase, smem_desc(aa + kk * 2 * A_LBO, A_LBO, 128),
-                         smem_desc(bb + kk * 2 * B_LBO_P, B_LBO_P, 128), idesc, (i | kk) != 0);
-            mma_commit(&bars[sa]);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    bool ok = true;
+    if (warp == 0) {
+        // producer: the slab, then per stage one 64 x 256 box of h rows (rows
+        // past the tile are not used; rows past the tensor read as zero and
+        // still count toward the transaction bytes)
+        if (lane == 0) {
+            bulk_copy(slab, slab_src, down_slab_bytes(a.H), &slab_bar);
+            for (int i = 0; i < nstages && ok; i++) {
+                const int sb = i % PF_STG, use = i / PF_STG;
+                if (use > 0) ok = mbar_wait(&R.bempty[sb], (use - 1) & 1);
+                if (!ok) break;
+                mbar_expect_tx(&R.bfull[sb], B_STAGE);
+                tma_tile2d(smem_u32(bst + sb * B_STAGE), &hmap, i * PF_KS, s0, &R.bfull[sb]);
+            }
         }
-        if (i >= 1) {
-            if (threadIdx.x < 32) ok = ok && mbar_wait(&bars[(i - 1) & 1], ((i - 1) >> 1) & 1);
-            __syncthreads();
+    } else if (warp == 1) {
+        if (lane == 0) ok = mma_role<1>(R, nstages, abf, bst, tbase, instr_desc(nn));
+    } else if (warp >= PF_DQ0 / 32) {
+        const int t = threadIdx.x - PF_DQ0;
+        ok = mbar_wait(&slab_bar, 0);
+        for (int i = 0; i < nstages && ok; i++) {
+            const int sa = i % PF_NA;
+            if (i >= PF_NA) ok = mbar_wait(&R.aempty[sa], (i / PF_NA - 1) & 1);
+            if (!ok) break;
+            q6_deq(slab, row_bytes, i, t, abf + sa * A_STAGE);
+            async_proxy_fence();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&R.afull[sa]);
         }
-        const int nx = i + PF_STG - 1;
-        if (nx < nstages) b_issue(bp, smem_u32(bst + (nx % PF_STG) * B_STAGE_P), nx * PF_KS);
-        cp_async_commit();
+        if (ok) ok = mbar_wait(&R.done, 0);
     }
-    if (threadIdx.x < 32) ok = ok && mbar_wait(&bars[(nstages - 1) & 1], ((nstages - 1) >> 1) & 1);
     ok = __syncthreads_and(ok);
     tc_fence_after();
     if (!ok) {
         if (threadIdx.x == 0) atomicExch(a.err, 1);
-    } else {
-        const int w = threadIdx.x >> 5, lane = threadIdx.x & 31, q = w & 3;
+    } else if (warp >= PF_DQ0 / 32) {
+        const int q = warp & 3;
         const int row = n0 + q * 32 + lane;
         const uint32_t lane_off = (uint32_t)(q * 32) << 16;
-        const int half = nn / 2, j_beg = (w >> 2) * half;
+        const int half = nn / 2, j_beg = ((warp - PF_DQ0 / 32) >> 2) * half;
         for (int j0 = j_beg; j0 < j_beg + half; j0 += 8) {
             float y[8];
             tmem_ld8(tbase + lane_off + j0, y);
@@ -552,14 +597,92 @@ int prefill_max_tiles(int T, int K, int E) {
     return assignments / PF_NMAX + slots + 1;
 }
 
-bool prefill_supported(int D, int H) { return D % 256 == 0 && H % 256 == 0 && H % PF_M == 0 && D % PF_M == 0; }
+// cuTensorMapEncodeTiled through the runtime's driver entry point.
+typedef CUresult (*EncodeTiledFn)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
+                                  const cuuint64_t *, const cuuint32_t *, const cuuint32_t *,
+                                  CUtensorMapInterleave, CUtensorMapSwizzle, CUtensorMapL2promotion,
+                                  CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn encode_fn() {
+    static EncodeTiledFn fn = nullptr;
+    if (!fn) {
+        cudaDriverEntryPointQueryResult q;
+        void *p = nullptr;
+        cudaError_t e = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q);
+        if (e == cudaSuccess && q == cudaDriverEntryPointSuccess) fn = reinterpret_cast<EncodeTiledFn>(p);
+    }
+    return fn;
+}
+
+// Row-major [rows][cols] bf16 tensor, boxes of 64 columns x box_rows rows,
+// 128-byte swizzle.
+static int encode_bf16_2d(CUtensorMap *map, const void *base, uint64_t cols, uint64_t rows, uint32_t box_rows) {
+    EncodeTiledFn fn = encode_fn();
+    if (!fn) {
+        set_error("cuTensorMapEncodeTiled unavailable");
+        return OFB_ECUDA;
+    }
+    const cuuint64_t dims[2] = {cols, rows};
+    const cuuint64_t strides[1] = {cols * 2};
+    const cuuint32_t box[2] = {(cuuint32_t)PF_KS, box_rows};
+    const cuuint32_t estr[2] = {1, 1};
+    CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void *>(base), dims, strides, box, estr,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) {
+        set_error("cuTensorMapEncodeTiled (bf16) failed (%d)", (int)r);
+        return OFB_ECUDA;
+    }
+    return OFB_OK;
+}
+
+// Q4_K rows as a 3D byte tensor: 16-byte chunk x chunk index in the row x
+// row; boxes of one chunk x 128 rows.
+static int encode_q4_rows(CUtensorMap *map, const void *base, int D, uint64_t rows) {
+    EncodeTiledFn fn = encode_fn();
+    if (!fn) {
+        set_error("cuTensorMapEncodeTiled unavailable");
+        return OFB_ECUDA;
+    }
+    if (reinterpret_cast<uintptr_t>(base) & 15) {
+        set_error("Q4_K expert tensors must be 16-byte aligned for the prefill kernels");
+        return OFB_EINVAL;
+    }
+    const uint64_t row_bytes = (uint64_t)(D / QK) * Q4K_BYTES;
+    const cuuint64_t dims[3] = {16, row_bytes / 16, rows};
+    const cuuint64_t strides[2] = {16, row_bytes};
+    const cuuint32_t box[3] = {16, 1, (cuuint32_t)PF_M};
+    const cuuint32_t estr[3] = {1, 1, 1};
+    CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<void *>(base), dims, strides, box, estr,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) {
+        set_error("cuTensorMapEncodeTiled (Q4_K rows) failed (%d)", (int)r);
+        return OFB_ECUDA;
+    }
+    return OFB_OK;
+}
 
 int launch_prefill(const LayerArgs &la, const float *x, int *n_slots, __nv_bfloat16 *xb, __nv_bfloat16 *hb,
                    int *tiles, int *err, cudaStream_t s, cudaEvent_t before, cudaEvent_t between) {
     const int T = la.T, D = la.D, H = la.H;
     const int max_tiles = prefill_max_tiles(T, la.K, la.E);
+    const int n_asg = T * la.K + T;
     int *n_tiles = tiles, *tile_slot = tiles + 1, *tile_start = tile_slot + max_tiles,
         *tile_n = tile_start + max_tiles;
+    CUtensorMap xmap, hmap, gmap, umap, gmap_sh, umap_sh;
+    int st;
+    if ((st = encode_bf16_2d(&xmap, xb, D, T, 1))) return st;            // gather4 wants one-row boxes
+    if ((st = encode_bf16_2d(&hmap, hb, H, n_asg, PF_NMAX))) return st;  // 64 x 256 boxes
+    if ((st = encode_q4_rows(&gmap, la.gate, D, (uint64_t)la.E * H))) return st;
+    if ((st = encode_q4_rows(&umap, la.up, D, (uint64_t)la.E * H))) return st;
+    if (la.has_shared) {
+        if ((st = encode_q4_rows(&gmap_sh, la.gate_sh, D, H))) return st;
+        if ((st = encode_q4_rows(&umap_sh, la.up_sh, D, H))) return st;
+    } else {
+        gmap_sh = gmap;  // never read: no slot names the shared expert
+        umap_sh = umap;
+    }
     to_bf16_kernel<<<grid_for((size_t)T * D / 4, 256, 148 * 8), 256, 0, s>>>(x, (size_t)T * D, xb);
     tile_plan_kernel<<<1, 256, 0, s>>>(n_slots, la.slot_start, n_tiles, tile_slot, tile_start, tile_n);
     PrefillArgs a;
@@ -569,7 +692,7 @@ int launch_prefill(const LayerArgs &la, const float *x, int *n_slots, __nv_bfloa
     a.gate_sh = la.gate_sh; a.up_sh = la.up_sh; a.down_sh = la.down_sh;
     a.slot_expert = la.slot_expert; a.slot_start = la.slot_start; a.assign = la.assign;
     a.n_tiles = n_tiles; a.tile_slot = tile_slot; a.tile_start = tile_start; a.tile_n = tile_n;
-    a.xb = xb; a.hb = hb; a.w = la.w; a.gsc = la.gsc; a.out = la.out; a.err = err;
+    a.hb = hb; a.w = la.w; a.gsc = la.gsc; a.out = la.out; a.err = err;
     const int smem_up = UP_SMEM;
     const int smem_dn = down_smem(H);
     static int attr_dn = 0;
@@ -586,9 +709,9 @@ int launch_prefill(const LayerArgs &la, const float *x, int *n_slots, __nv_bfloa
     else e = cudaSuccess;
     if (e != cudaSuccess) return cuda_status(e, "prefill out init");
     if (before) cudaEventRecord(before, s);
-    prefill_up_kernel<<<dim3(max_tiles, H / PF_M), PF_NT, smem_up, s>>>(a);
+    prefill_up_kernel<<<dim3(max_tiles, H / PF_M), PF_NT, smem_up, s>>>(a, xmap, gmap, umap, gmap_sh, umap_sh);
     if (between) cudaEventRecord(between, s);
-    prefill_down_kernel<<<dim3(max_tiles, D / PF_M), PF_NT, smem_dn, s>>>(a);
+    prefill_down_kernel<<<dim3(max_tiles, D / PF_M), PF_NT, smem_dn, s>>>(a, hmap);
     OFB_CHECK_LAUNCH("prefill kernels");
     return OFB_OK;
 }
