@@ -39,7 +39,11 @@ __device__ __forceinline__ float half_bits_ref(uint32_t h) {
 // 6-bit (scale, min) of Q4_K sub-block j from the 12 packed bytes held as
 // three little-endian words s[0..2] (engine/src/gguf.c:31-40).
 __device__ __forceinline__ void q4k_scale_min(const uint32_t s[3], int j, int &sc, int &mn) {
-    auto byte = [&](int i) -> int { return (s[i >> 2] >> (8 * (i & 3))) & 0xFF; };
+    // selects, not s[i >> 2]: a runtime index would put s in local memory
+    auto byte = [&](int i) -> int {
+        const uint32_t w = i < 4 ? s[0] : (i < 8 ? s[1] : s[2]);
+        return (w >> (8 * (i & 3))) & 0xFF;
+    };
     if (j < 4) {
         sc = byte(j) & 63;
         mn = byte(j + 4) & 63;

@@ -166,7 +166,7 @@ WorkspaceLayout workspace_layout(const ofb_moe_config *c, int max_tokens) {
     L.h = take(Ad * (size_t)c->hidden * 4);
     L.y = take(Ad * (size_t)c->d_model * 4);
     const bool prefill = !inter && max_tokens > MAX_DECODE_T && c->hidden <= PREFILL_MAX_H;
-    L.xb = take(prefill ? T * (size_t)c->d_model * 2 : 0);
+    L.xb = take(prefill ? A * (size_t)c->d_model * 2 : 0);
     L.hb = take(prefill ? A * (size_t)c->hidden * 2 : 0);
     L.tiles = take(prefill ? (1 + 3 * (size_t)prefill_max_tiles(max_tokens, K, E)) * 4 : 0);
     const size_t Tf = (size_t)(max_tokens < FAST_ROUTE_MAX_T ? max_tokens : FAST_ROUTE_MAX_T);

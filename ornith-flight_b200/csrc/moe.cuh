@@ -37,7 +37,7 @@ struct WorkspaceLayout {
     size_t logits, idx, w, gsc, n_slots, slot_expert, slot_start, assign, h, y;
     size_t cand;      // fast routing: (approximate logit, bound) per (token, row)
     size_t xq;        // decode: quantised activations [T][xq_stride(D)]
-    size_t xb, hb;    // prefill: bf16 x [T][D], bf16 h [A][H] in slot order
+    size_t xb, hb;    // prefill: bf16 x rows [A][D] and h rows [A][H], both in slot order
     size_t tiles;     // prefill: tile count + (slot, start, n) per tile
     size_t counters;  // fast routing tickets [T] + [1] and stats [3]; zero at creation
     size_t counters_bytes;

@@ -9,25 +9,33 @@
 // (M = 128 rows per CTA) and B = token rows (N <= 256 per tile), so the
 // ragged token dimension is the MMA's N and every CTA tile is a full 128-row
 // weight block.
-//  * B (token rows): TMA. The up GEMM gathers arbitrary token rows from a
-//    bf16 copy of x (L2-resident at 4096 tokens) with tile::gather4 loads
-//    (4 rows of 128 bytes each); the down GEMM's h rows are contiguous in slot
-//    order and come with one 2D tile load per stage. Both land in the 128-byte
-//    swizzled K-major layout and complete on a per-stage mbarrier.
-//  * A (weights): the raw Q4_K bytes a stage needs (the 16-byte header and
-//    two 16-byte quant chunks of each row's block) arrive by TMA through a 3D
-//    byte map (16-byte chunk x chunk index x row); the Q6_K rows of a CTA are
-//    one contiguous, 16-byte aligned slab (128 x 420 B) brought in by one bulk
-//    copy. 8 warps dequantise (the reference's exact fp32 value rounded to
-//    bf16; paired f32x2 arithmetic) into the same swizzled layout.
-//  * one thread issues tcgen05.mma (kind::f16, bf16 x bf16 -> f32) into TMEM;
+//  * B (token rows): TMA tile loads of 64 columns x 16 rows, as many as the
+//    tile's rows need, per stage. A gather kernel first writes each
+//    assignment's token row as bf16 in slot order (x rows for the up GEMM);
+//    the up epilogue writes h in the same order, so every tile's B rows are
+//    contiguous. 128-byte swizzled K-major layout, one mbarrier per stage.
+//  * A (weights) lives in tensor memory: dequantising warps write their bf16
+//    pairs straight from registers with tcgen05.st and the MMA reads A from
+//    TMEM, so shared memory carries only B and the raw quant bytes. The raw
+//    Q4_K bytes a stage needs (16-byte header and two 16-byte quant chunks of
+//    each row's block) arrive by TMA through a 3D byte map (16-byte chunk x
+//    chunk index x row); the Q6_K rows of a CTA are one contiguous, 16-byte
+//    aligned slab (128 x 420 B) brought in by one bulk copy.
+//  * TMEM columns: up = gate accumulator [0,192), up accumulator [192,384),
+//    two A stages [384,512); down = accumulator [0,192), two A stages
+//    [192,256). Tiles hold at most 192 tokens (the MMA's N).
+//  * one thread issues tcgen05.mma (kind::f16, bf16 x bf16 -> f32);
 //    tcgen05.commit arrives on the mbarriers that free the stage's buffers.
-//  * warp-specialised: warp 0 produces (TMA), warp 1 issues the MMAs, warps
-//    4..11 dequantise; the roles meet only on full/empty mbarrier rings, so
-//    copies, dequantisation and tensor-core work of different stages overlap.
-//  * epilogue (warps 4..11): tcgen05.ld of the accumulator (warp w reads TMEM
-//    lanes 32*(w%4).. = its weight rows); up writes h = silu(g)*u as bf16 in
-//    slot order, down adds w * y into out with fp32 reductions.
+//  * warp-specialised: warp 0 produces B, warp 2 raw A (TMA), warp 1 issues
+//    the MMAs, warps 4..19 dequantise (warp w owns TMEM lanes 32*(w%4)..,
+//    i.e. weight rows 32*(w%4).. of the CTA); the roles meet only on
+//    full/empty mbarrier rings, so copies, dequantisation and tensor-core
+//    work of different stages overlap.
+//  * grid: (weight-row block, tile), so the CTAs sharing a tile's B rows run
+//    next to each other and read them from L2.
+//  * epilogue (warps 4..19): tcgen05.ld of the accumulator; up stages
+//    h = silu(g)*u as bf16 in shared memory and stores whole 16-byte pieces
+//    of each token's row, down adds w * y into out with fp32 reductions.
 // No TMA load here uses cluster multicast. Every mbarrier wait is bounded: on
 // timeout the kernel records an error flag, releases its TMEM and returns.
 #include <cuda.h>
@@ -38,16 +46,20 @@
 namespace ofb {
 
 constexpr int PF_M = 128;        // weight rows per CTA (MMA M)
-constexpr int PF_NMAX = 256;     // token rows per tile (MMA N, max)
+constexpr int PF_NMAX = 192;     // token rows per tile (MMA N, max; bounded by TMEM columns)
 constexpr int PF_KS = 64;        // K elements per pipeline stage (= one 128-byte swizzle row)
-constexpr int PF_NT = 384;       // threads per CTA: producer, MMA, 2 spare, 8 dequant/epilogue warps
+constexpr int PF_NT = 640;       // threads per CTA: B producer, MMA, A producer, spare, 16 dequant/epilogue warps
 constexpr int PF_DQ0 = 128;      // first dequantising thread
-constexpr int PF_NDQW = 8;       // dequantising warps
-constexpr int PF_STG = 3;        // ring depth for B and raw A
-constexpr int PF_NA = 2;         // ring depth for dequantised A
-constexpr int A_STAGE = PF_M * 128;        // 16 KB: 128 rows x 128 B
-constexpr int B_STAGE = PF_NMAX * 128;     // 32 KB
+constexpr int PF_NDQW = 16;      // dequantising warps
+constexpr int PF_STG = 4;        // ring depth for B
+constexpr int PF_RAW = 6;        // ring depth for raw Q4_K A (covers DRAM latency)
+constexpr int PF_NA = 2;         // A stages in TMEM
+constexpr int B_ROWS = 16;       // rows per B box
+constexpr int B_STAGE = PF_NMAX * 128;     // 24 KB: up to 192 rows x 128 B
 constexpr int RAW4 = PF_M * 48;            // raw Q4_K bytes of one matrix per stage
+constexpr int UP_ACC_U = PF_NMAX;          // TMEM column of the up accumulator
+constexpr int UP_A = 2 * PF_NMAX;          // up: A stage s, matrix m at UP_A + 64 s + 32 m
+constexpr int DN_A = PF_NMAX;              // down: A stage s at DN_A + 32 s
 constexpr long long WAIT_LIMIT = 1ll << 24;  // try_wait polls before giving up
 
 struct PrefillArgs {
@@ -61,6 +73,31 @@ struct PrefillArgs {
     float *out;
     int *err;
 };
+
+// Optional per-CTA timing of the roles' waits (build with -DOFB_PF_TRACE):
+// clock64 sums for the first 256 CTAs of each kernel, read back with
+// ofb_debug_prefill_trace.
+#ifdef OFB_PF_TRACE
+__device__ unsigned long long g_pf_trace[2][256][32];
+__device__ unsigned long long g_pf_span[2][8192][2];  // globaltimer start/end of every CTA
+__device__ __forceinline__ unsigned long long gtime() {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+    return t;
+}
+__device__ __forceinline__ unsigned long long *pf_tr(int kern) {
+    const int id = blockIdx.x + gridDim.x * blockIdx.y;
+    if (threadIdx.x == 0 && id < 8192) g_pf_span[kern][id][0] = gtime();
+    return id < 256 ? g_pf_trace[kern][id] : nullptr;
+}
+__device__ __forceinline__ void pf_end(int kern) {
+    const int id = blockIdx.x + gridDim.x * blockIdx.y;
+    if (threadIdx.x == 0 && id < 8192) g_pf_span[kern][id][1] = gtime();
+}
+#define PF_TR(...) __VA_ARGS__
+#else
+#define PF_TR(...)
+#endif
 
 // ---- PTX helpers ----------------------------------------------------------
 __device__ __forceinline__ uint32_t smem_u32(const void *p) {
@@ -100,16 +137,49 @@ __device__ __forceinline__ uint64_t sw128_desc(uint32_t addr) {
 __device__ __forceinline__ uint32_t instr_desc(int n) {
     return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(PF_M >> 4) << 24);
 }
-__device__ __forceinline__ void mma_bf16(uint32_t tmem_d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
+// D (TMEM) (+)= A (TMEM, 128 lanes x 16 bf16 in 8 columns) . B^T (shared memory)
+__device__ __forceinline__ void mma_bf16_ta(uint32_t tmem_d, uint32_t tmem_a, uint64_t b, uint32_t idesc,
+                                            uint32_t acc) {
     asm volatile(
         "{ .reg .pred p; setp.ne.b32 p, %4, 0;\n\t"
-        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p; }" ::"r"(tmem_d),
-        "l"(a), "l"(b), "r"(idesc), "r"(acc));
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p; }" ::"r"(tmem_d),
+        "r"(tmem_a), "l"(b), "r"(idesc), "r"(acc));
 }
+// This warp's 32 TMEM lanes, 16 / 8 consecutive 32-bit columns from registers.
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t v[16]) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(
+            taddr),
+        "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]),
+        "r"(v[9]), "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15])
+        : "memory");
+}
+__device__ __forceinline__ void tmem_st8(uint32_t taddr, const uint32_t v[8]) {
+    asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"r"(taddr), "r"(v[0]),
+                 "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7])
+                 : "memory");
+}
+__device__ __forceinline__ void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 __device__ __forceinline__ void mma_commit(uint64_t *bar) {
     asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
         smem_u32(bar))
                  : "memory");
+}
+// 32 consecutive columns of this warp's 32 TMEM lanes (one per thread).
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float v[32]) {
+    uint32_t r[32];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+        "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];\n\t"
+        "tcgen05.wait::ld.sync.aligned;"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+          "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+          "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+        : "r"(taddr)
+        : "memory");
+#pragma unroll
+    for (int i = 0; i < 32; i++) v[i] = __uint_as_float(r[i]);
 }
 __device__ __forceinline__ void tmem_ld8(uint32_t taddr, float v[8]) {
     uint32_t r[8];
@@ -153,16 +223,6 @@ __device__ __forceinline__ void bulk_copy(void *dst, const void *src, uint32_t b
                  "l"(src), "r"(bytes), "r"(smem_u32(bar))
                  : "memory");
 }
-// Four 64-element rows (y0..y3, starting at column x) of a 2D bf16 tensor:
-// 512 bytes, one-row box.
-__device__ __forceinline__ void tma_gather4(uint32_t dst, const CUtensorMap *map, int x, int y0, int y1, int y2,
-                                            int y3, uint64_t *bar) {
-    asm volatile(
-        "cp.async.bulk.tensor.2d.shared::cluster.global.tile::gather4.mbarrier::complete_tx::bytes"
-        " [%0], [%1, {%2, %3, %4, %5, %6}], [%7];" ::"r"(dst),
-        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y0), "r"(y1), "r"(y2), "r"(y3), "r"(smem_u32(bar))
-        : "memory");
-}
 // One 3D box at (c0, c1, c2).
 __device__ __forceinline__ void tma_load3d(uint32_t dst, const CUtensorMap *map, int c0, int c1, int c2,
                                            uint64_t *bar) {
@@ -182,46 +242,19 @@ __device__ __forceinline__ void tma_tile2d(uint32_t dst, const CUtensorMap *map,
 }
 
 // ---- layout and conversion helpers ----------------------------------------------
-// Byte offset of 16-byte chunk c of row r in a 128-byte swizzled K-major tile
-// (1024-byte aligned base): the TMA/UMMA SWIZZLE_128B pattern.
-__device__ __forceinline__ uint32_t sw_off(int r, int c) { return r * 128 + ((c ^ (r & 7)) << 4); }
 
 __device__ __forceinline__ uint32_t pack_bf16(float a, float b) {
     __nv_bfloat162 p = __floats2bfloat162_rn(a, b);
     return *reinterpret_cast<uint32_t *>(&p);
 }
-// Paired fp32 arithmetic (sm_100a f32x2): two elements per instruction.
-__device__ __forceinline__ unsigned long long f2pack(float a, float b) {
-    unsigned long long p;
-    asm("mov.b64 %0, {%1,%2};" : "=l"(p) : "f"(a), "f"(b));
-    return p;
-}
-__device__ __forceinline__ uint32_t f2_to_bf16(unsigned long long r) {
-    float lo, hi;
-    asm("mov.b64 {%0,%1}, %2;" : "=f"(lo), "=f"(hi) : "l"(r));
-    return pack_bf16(lo, hi);
-}
-__device__ __forceinline__ unsigned long long f2_add(unsigned long long a, unsigned long long b) {
-    unsigned long long r;
-    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
-    return r;
-}
-__device__ __forceinline__ uint32_t f2_fma_bf16(unsigned long long x, unsigned long long m, unsigned long long c) {
-    unsigned long long r;
-    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(x), "l"(m), "l"(c));
-    return f2_to_bf16(r);
-}
-__device__ __forceinline__ uint32_t f2_mul_bf16(unsigned long long x, unsigned long long m) {
-    unsigned long long r;
-    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(x), "l"(m));
-    return f2_to_bf16(r);
-}
-// bytes (k, k+1) of w as the exact floats 2^23 + byte, as a pair
+// Two quant bytes (k, k+1 of w, each < 128) as the bf16 pair (128 + q_k,
+// 128 + q_k+1): 0x43 is the high byte of bf16 128, the quant is the mantissa.
 template <int K>
-__device__ __forceinline__ unsigned long long byte_pair(uint32_t w) {
-    return f2pack(__uint_as_float(__byte_perm(w, 0x4B000000u, 0x7540u + K)),
-                  __uint_as_float(__byte_perm(w, 0x4B000000u, 0x7541u + K)));
+__device__ __forceinline__ __nv_bfloat162 q_pair128(uint32_t w) {
+    const uint32_t v = __byte_perm(w, 0x43434343u, K == 0 ? 0x4140u : 0x4342u);
+    return *reinterpret_cast<const __nv_bfloat162 *>(&v);
 }
+__device__ __forceinline__ uint32_t bf2_bits(__nv_bfloat162 v) { return *reinterpret_cast<uint32_t *>(&v); }
 // 4 bytes at a 2-byte aligned shared-memory address.
 __device__ __forceinline__ uint32_t lds_u32_2b(const uint8_t *p) {
     const uintptr_t a = reinterpret_cast<uintptr_t>(p);
@@ -240,84 +273,101 @@ __device__ __forceinline__ void q4_issue(const CUtensorMap *map, int row0, uint3
     tma_load3d(dst + 4096, map, 0, b * 9 + 2 + 2 * c, row0, bar);
 }
 
-// Dequantising thread t (row r = t%128, half hh = t/128) writes chunks
-// 4hh..4hh+3 of its row (low nibbles for hh = 0, high for hh = 1). Value =
-// (d*sc)*q - dmin*m as one fused multiply-add: d*sc*q is exact in fp32
-// (<= 21 significant bits), so the result equals the reference's two
-// separately rounded operations.
-__device__ __forceinline__ void q4_deq(const uint8_t *raw, int stage, int t, uint8_t *sa) {
-    const int r = t & (PF_M - 1), hh = t >> 7, c = stage & 3;
+// A dequantising thread owns one (row r, nibble half hh) of one matrix: in
+// every stage it produces K elements 32hh..32hh+31 of row r (low nibbles for
+// hh = 0, high for hh = 1), TMEM columns 16hh..16hh+15 of the stage.
+// Arithmetic is bf16 pairs: q exactly (bf16(128+q) - 128), then one fused
+// q*bf16(d*sc) - bf16(dmin*m) rounded once to bf16. d*sc and dmin*m are the
+// reference's fp32 products; rounding them to bf16 adds at most 2^-9 of
+// |q*d*sc| + |dmin*m| to the bf16 operand's own rounding (2^-9 of |value|).
+struct Q4Scales { uint32_t d2[4], nm2[4]; };  // bf16 pairs, sub-block 2c+hh for c = 0..3
+
+// Decodes the row's block header (at the block's first stage) into the four
+// scale pairs this thread uses in the block's four stages.
+__device__ __forceinline__ void q4_scales(const uint8_t *raw, int r, int hh, Q4Scales &S) {
     const uint4 hdr = *reinterpret_cast<const uint4 *>(raw + r * 16);
+    const uint32_t s[3] = {hdr.y, hdr.z, hdr.w};
+    const float d = half_bits_ref(hdr.x & 0xFFFFu), dmin = half_bits_ref(hdr.x >> 16);
+#pragma unroll
+    for (int c = 0; c < 4; c++) {
+        int sc, mn;
+        q4k_scale_min(s, 2 * c + hh, sc, mn);
+        S.d2[c] = bf2_bits(__float2bfloat162_rn(__fmul_rn(d, (float)sc)));
+        S.nm2[c] = bf2_bits(__float2bfloat162_rn(-__fmul_rn(dmin, (float)mn)));
+    }
+}
+
+__device__ __forceinline__ __nv_bfloat162 as_bf2(uint32_t v) { return *reinterpret_cast<const __nv_bfloat162 *>(&v); }
+
+__device__ __forceinline__ void q4_deq(const uint8_t *raw, int c, int r, int hh, const Q4Scales &S,
+                                       uint32_t out[16]) {
     const uint4 qa = *reinterpret_cast<const uint4 *>(raw + 2048 + r * 16);
     const uint4 qb = *reinterpret_cast<const uint4 *>(raw + 4096 + r * 16);
-    const uint32_t s[3] = {hdr.y, hdr.z, hdr.w};
-    int sc, mn;
-    q4k_scale_min(s, 2 * c + hh, sc, mn);
-    const float dd = __fmul_rn(half_bits_ref(hdr.x & 0xFFFFu), (float)sc);
-    const float mm = __fmul_rn(half_bits_ref(hdr.x >> 16), (float)mn);
-    const unsigned long long d2 = f2pack(dd, dd), nm2 = f2pack(-mm, -mm);
-    const unsigned long long nb2 = f2pack(-8388608.0f, -8388608.0f);
+    // selects, not S.d2[c]: a runtime index would put S in local memory
+    const __nv_bfloat162 d2 = as_bf2(c == 0 ? S.d2[0] : c == 1 ? S.d2[1] : c == 2 ? S.d2[2] : S.d2[3]);
+    const __nv_bfloat162 nm2 = as_bf2(c == 0 ? S.nm2[0] : c == 1 ? S.nm2[1] : c == 2 ? S.nm2[2] : S.nm2[3]);
+    const __nv_bfloat162 c128 = __float2bfloat162_rn(128.f);
     const uint32_t qw[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
     const int sh = 4 * hh;
 #pragma unroll
-    for (int ch = 0; ch < 4; ch++) {
-        const uint32_t w0 = (qw[2 * ch] >> sh) & 0x0F0F0F0Fu, w1 = (qw[2 * ch + 1] >> sh) & 0x0F0F0F0Fu;
-        const uint32_t p0 = f2_fma_bf16(f2_add(byte_pair<0>(w0), nb2), d2, nm2);
-        const uint32_t p1 = f2_fma_bf16(f2_add(byte_pair<2>(w0), nb2), d2, nm2);
-        const uint32_t p2 = f2_fma_bf16(f2_add(byte_pair<0>(w1), nb2), d2, nm2);
-        const uint32_t p3 = f2_fma_bf16(f2_add(byte_pair<2>(w1), nb2), d2, nm2);
-        *reinterpret_cast<uint4 *>(sa + sw_off(r, 4 * hh + ch)) = make_uint4(p0, p1, p2, p3);
+    for (int k = 0; k < 8; k++) {
+        const uint32_t w = (qw[k] >> sh) & 0x0F0F0F0Fu;
+        out[2 * k] = bf2_bits(__hfma2(__hsub2(q_pair128<0>(w), c128), d2, nm2));
+        out[2 * k + 1] = bf2_bits(__hfma2(__hsub2(q_pair128<2>(w), c128), d2, nm2));
     }
 }
 
 // ---- A operand, Q6_K (from the raw slab in shared memory) ----------------------------
-// 64-element chunk q of a block: half = q/2, quads 2*(q%2) and 2*(q%2)+1;
-// thread t (row r, hh) writes quad 2*(q%2)+hh. Value = (d*sc)*(q-32), one
-// rounding each, as the reference.
-__device__ __forceinline__ void q6_deq(const uint8_t *slab, int row_bytes, int stage, int t, uint8_t *sa) {
-    const int r = t & (PF_M - 1), hh = t >> 7;
+// 64-element chunk q of a block: half = q/2, quads 2*(q%2) and 2*(q%2)+1
+// (32 elements each). Four threads per row: thread (r, hh, g) produces
+// elements 16g..16g+15 of quad 2*(q%2)+hh (one scale), TMEM columns
+// 16hh+8g..16hh+8g+7 of the stage. Value = (q-32) exactly
+// (bf16(128+q) - 160) times bf16(d*sc), rounded once to bf16; d*sc is the
+// reference's fp32 product.
+__device__ __forceinline__ void q6_deq(const uint8_t *slab, int row_bytes, int stage, int r, int hh, int g,
+                                       uint32_t out[8]) {
     const int b = stage >> 2, q64 = stage & 3, half6 = q64 >> 1, quad = 2 * (q64 & 1) + hh;
     const uint8_t *blk = slab + r * row_bytes + b * Q6K_BYTES;
-    const uint8_t *ql = blk + half6 * 64 + (quad & 1) * 32;
-    const uint8_t *qh = blk + 128 + half6 * 32;
-    const int si = 192 + half6 * 8 + quad * 2;
+    const uint8_t *ql = blk + half6 * 64 + (quad & 1) * 32 + g * 16;
+    const uint8_t *qh = blk + 128 + half6 * 32 + g * 16;
     const float d = half_bits_ref((uint32_t)blk[208] | ((uint32_t)blk[209] << 8));
-    const float ds0 = __fmul_rn(d, (float)(int8_t)blk[si]), ds1 = __fmul_rn(d, (float)(int8_t)blk[si + 1]);
-    const unsigned long long nb2 = f2pack(-8388640.0f, -8388640.0f);  // -(2^23 + 32)
+    const __nv_bfloat162 d2 =
+        __float2bfloat162_rn(__fmul_rn(d, (float)(int8_t)blk[192 + half6 * 8 + quad * 2 + g]));
+    const __nv_bfloat162 c160 = __float2bfloat162_rn(160.f);
     const int nsh = (quad >= 2) ? 4 : 0, hsh = 2 * quad;
 #pragma unroll
-    for (int ch = 0; ch < 4; ch++) {
-        const float ds = ch < 2 ? ds0 : ds1;  // l = 8ch..8ch+7, scale index l/16
-        const unsigned long long d2 = f2pack(ds, ds);
-        uint32_t q[2];
-#pragma unroll
-        for (int h2 = 0; h2 < 2; h2++) {
-            const uint32_t wl = lds_u32_2b(ql + ch * 8 + h2 * 4), wh = lds_u32_2b(qh + ch * 8 + h2 * 4);
-            q[h2] = ((wl >> nsh) & 0x0F0F0F0Fu) | (((wh >> hsh) & 0x03030303u) << 4);
-        }
-        const uint32_t p0 = f2_mul_bf16(f2_add(byte_pair<0>(q[0]), nb2), d2);
-        const uint32_t p1 = f2_mul_bf16(f2_add(byte_pair<2>(q[0]), nb2), d2);
-        const uint32_t p2 = f2_mul_bf16(f2_add(byte_pair<0>(q[1]), nb2), d2);
-        const uint32_t p3 = f2_mul_bf16(f2_add(byte_pair<2>(q[1]), nb2), d2);
-        *reinterpret_cast<uint4 *>(sa + sw_off(r, 4 * hh + ch)) = make_uint4(p0, p1, p2, p3);
+    for (int k = 0; k < 4; k++) {
+        const uint32_t wl = lds_u32_2b(ql + 4 * k), wh = lds_u32_2b(qh + 4 * k);
+        const uint32_t q = ((wl >> nsh) & 0x0F0F0F0Fu) | (((wh >> hsh) & 0x03030303u) << 4);
+        out[2 * k] = bf2_bits(__hmul2(__hsub2(q_pair128<0>(q), c160), d2));
+        out[2 * k + 1] = bf2_bits(__hmul2(__hsub2(q_pair128<2>(q), c160), d2));
     }
 }
 
 __device__ __forceinline__ int asg_token_p(int a, int TK, int K) { return a < TK ? a / K : a - TK; }
+
+// silu(g) * u; the product is rounded to bf16 next, so the fast exponential
+// and division (relative error ~1e-6) are below that rounding.
+__device__ __forceinline__ float silu_mul(float g, float u) {
+    const float sl = g < -50.f ? 0.f : (g > 50.f ? g : __fdividef(g, 1.f + __expf(-g)));
+    return sl * u;
+}
 
 // Parity of the phase that completes the n-th use (n = 0, 1, ...) of a ring
 // slot is n & 1; a producer refilling a slot for use n >= 1 waits for the
 // consumer's release of use n-1, parity (n-1) & 1.
 struct Rings {
     uint64_t bfull[PF_STG], bempty[PF_STG];   // B: TMA -> MMA
-    uint64_t rfull[PF_STG], rempty[PF_STG];   // raw A: TMA -> dequant
-    uint64_t afull[PF_NA], aempty[PF_NA];     // bf16 A: dequant -> MMA
+    uint64_t rfull[PF_RAW], rempty[PF_RAW];   // raw A: TMA -> dequant
+    uint64_t afull[PF_NA], aempty[PF_NA];     // A in TMEM: dequant -> MMA
     uint64_t done;                            // all MMAs complete -> epilogue
 };
 __device__ __forceinline__ void rings_init(Rings &R) {
     for (int i = 0; i < PF_STG; i++) {
         mbar_init(&R.bfull[i], 1);
         mbar_init(&R.bempty[i], 1);
+    }
+    for (int i = 0; i < PF_RAW; i++) {
         mbar_init(&R.rfull[i], 1);
         mbar_init(&R.rempty[i], PF_NDQW);
     }
@@ -328,34 +378,60 @@ __device__ __forceinline__ void rings_init(Rings &R) {
     mbar_init(&R.done, 1);
 }
 
-// MMA role (one thread): per stage wait for A and B, issue the K = 64 slice
-// of the product into each accumulator, release both buffers.
+// B producer (one thread): per stage the tile's nn rows of a [rows][K] bf16
+// tensor, in 16-row boxes (rows past the tensor read as zero and count
+// toward the transaction bytes).
+__device__ __forceinline__ bool b_producer(Rings &R, const CUtensorMap *map, uint8_t *bst, int nstages, int s0,
+                                           int nn PF_TR(, unsigned long long *acc)) {
+    bool ok = true;
+    for (int i = 0; i < nstages && ok; i++) {
+        const int sb = i % PF_STG, use = i / PF_STG;
+        PF_TR(unsigned long long tc = clock64();)
+        if (use > 0) ok = mbar_wait(&R.bempty[sb], (use - 1) & 1);
+        PF_TR(if (acc) acc[4] += clock64() - tc;)
+        if (!ok) break;
+        mbar_expect_tx(&R.bfull[sb], nn * 128);
+        const uint32_t dst = smem_u32(bst + sb * B_STAGE);
+        for (int k = 0; k < nn / B_ROWS; k++)
+            tma_tile2d(dst + k * B_ROWS * 128, map, i * PF_KS, s0 + k * B_ROWS, &R.bfull[sb]);
+    }
+    return ok;
+}
+
+// MMA role (one thread): per stage wait for A (TMEM) and B (shared memory),
+// issue the stage's K = 64 slice into each accumulator, release both.
 template <int NACC>
-__device__ __forceinline__ bool mma_role(Rings &R, int nstages, const uint8_t *abf, const uint8_t *bst,
-                                         uint32_t tbase, uint32_t idesc) {
+__device__ __forceinline__ bool mma_role(Rings &R, int nstages, uint32_t a_col0, int acc_stride, const uint8_t *bst,
+                                         uint32_t tbase, uint32_t idesc PF_TR(, unsigned long long *acc)) {
     bool ok = true;
     for (int i = 0; i < nstages && ok; i++) {
         const int sa = i % PF_NA, sb = i % PF_STG;
-        ok = mbar_wait(&R.afull[sa], (i / PF_NA) & 1) && mbar_wait(&R.bfull[sb], (i / PF_STG) & 1);
+        PF_TR(unsigned long long tc = clock64();)
+        ok = mbar_wait(&R.afull[sa], (i / PF_NA) & 1);
+        PF_TR(if (acc) acc[6] += clock64() - tc; tc = clock64();)
+        ok = ok && mbar_wait(&R.bfull[sb], (i / PF_STG) & 1);
+        PF_TR(if (acc) acc[7] += clock64() - tc; tc = clock64();)
         if (!ok) break;
         tc_fence_after();
-        const uint32_t aa = smem_u32(abf + sa * NACC * A_STAGE), bb = smem_u32(bst + sb * B_STAGE);
+        const uint32_t bb = smem_u32(bst + sb * B_STAGE);
+        const uint32_t ta = tbase + a_col0 + sa * 32 * NACC;
 #pragma unroll
         for (int kk = 0; kk < PF_KS / 16; kk++) {
             const uint64_t bd = sw128_desc(bb + kk * 32);
 #pragma unroll
             for (int m = 0; m < NACC; m++)
-                mma_bf16(tbase + m * 256, sw128_desc(aa + m * A_STAGE + kk * 32), bd, idesc, (i | kk) != 0);
+                mma_bf16_ta(tbase + m * acc_stride, ta + m * 32 + kk * 8, bd, idesc, (i | kk) != 0);
         }
         mma_commit(&R.aempty[sa]);
         mma_commit(&R.bempty[sb]);
+        PF_TR(if (acc) acc[16] += clock64() - tc;)
     }
     mma_commit(&R.done);  // arrives once all issued MMAs complete
     return ok;
 }
 
 // ---- phase 1: gate/up ----------------------------------------------------------------
-constexpr int UP_SMEM = 1024 + PF_STG * B_STAGE + PF_NA * 2 * A_STAGE + PF_STG * 2 * RAW4;
+constexpr int UP_SMEM = 1024 + PF_STG * B_STAGE + PF_RAW * 2 * RAW4;
 
 __global__ void __launch_bounds__(PF_NT, 1)
     prefill_up_kernel(PrefillArgs a, const __grid_constant__ CUtensorMap xmap,
@@ -365,105 +441,133 @@ __global__ void __launch_bounds__(PF_NT, 1)
     uint8_t *psm = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(psm_raw) + 1023) & ~uintptr_t(1023));
     __shared__ Rings R;
     __shared__ uint32_t tslot;
-    __shared__ int trow[PF_NMAX];
-    const int tile = blockIdx.x;
+    const int tile = blockIdx.y;
     if (tile >= *a.n_tiles) return;
+    PF_TR(unsigned long long *tr = pf_tr(0); const unsigned long long tc0 = clock64(); unsigned long long tc;
+          unsigned long long acc[18] = {};)
     const int u = a.tile_slot[tile], s0 = a.tile_start[tile], n = a.tile_n[tile];
     const int e = a.slot_expert[u];
-    const int m0 = blockIdx.y * PF_M;
-    const int TK = a.T * a.K;
-    // token row of each tile row; padding rows repeat the first token (their
-    // accumulator columns are never read)
-    for (int i = threadIdx.x; i < PF_NMAX; i += PF_NT)
-        trow[i] = asg_token_p(a.assign[s0 + (i < n ? i : 0)], TK, a.K);
+    const int m0 = blockIdx.x * PF_M;
     if (threadIdx.x == 0) rings_init(R);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-    const uint32_t tbase = tmem_alloc(&tslot, 512);  // gate: cols [0,256), up: [256,512); syncs the CTA
+    const uint32_t tbase = tmem_alloc(&tslot, 512);  // syncs the CTA
+    PF_TR(if (tr && threadIdx.x == 0) tr[1] = clock64() - tc0;)
 
-    uint8_t *bst = psm;                          // [PF_STG][B_STAGE]        1024-aligned
-    uint8_t *abf = bst + PF_STG * B_STAGE;       // [PF_NA][gate A | up A]   1024-aligned
-    uint8_t *raw = abf + PF_NA * 2 * A_STAGE;    // [PF_STG][gate raw | up raw]
-    const int nn = (n + 15) & ~15;               // MMA N and rows fetched per stage
+    uint8_t *bst = psm;                          // [PF_STG][B_STAGE]   1024-aligned
+    uint8_t *raw = bst + PF_STG * B_STAGE;       // [PF_RAW][gate raw | up raw]
+    const int nn = (n + 15) & ~15;               // MMA N
     const int nstages = a.D / PF_KS;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     bool ok = true;
     if (warp == 0) {
-        // producer: B by gather4 (lanes split the nn/4 gathers), raw A by lane 0
-        const CUtensorMap *gm = e == a.E ? &gmap_sh : &gmap, *um = e == a.E ? &umap_sh : &umap;
-        const int row0 = (e == a.E ? 0 : e * a.H) + m0;
-        for (int i = 0; i < nstages && ok; i++) {
-            const int sb = i % PF_STG, use = i / PF_STG;
-            if (use > 0) ok = mbar_wait(&R.bempty[sb], (use - 1) & 1);
-            if (!ok) break;
-            if (lane == 0) mbar_expect_tx(&R.bfull[sb], nn * 128);
-            __syncwarp();
-            const uint32_t dst = smem_u32(bst + sb * B_STAGE);
-            for (int g = lane; g < nn / 4; g += 32)
-                tma_gather4(dst + g * 512, &xmap, i * PF_KS, trow[4 * g], trow[4 * g + 1], trow[4 * g + 2],
-                            trow[4 * g + 3], &R.bfull[sb]);
-            if (use > 0) ok = mbar_wait(&R.rempty[sb], (use - 1) & 1);
-            if (!ok) break;
-            if (lane == 0) {
-                mbar_expect_tx(&R.rfull[sb], 2 * RAW4);
-                const uint32_t rd = smem_u32(raw + sb * 2 * RAW4);
-                q4_issue(gm, row0, rd, i, &R.rfull[sb]);
-                q4_issue(um, row0, rd + RAW4, i, &R.rfull[sb]);
+        if (lane == 0) ok = b_producer(R, &xmap, bst, nstages, s0, nn PF_TR(, tr ? acc : nullptr));
+    } else if (warp == 2) {
+        // raw A producer (one thread): runs up to PF_RAW stages ahead
+        if (lane == 0) {
+            const CUtensorMap *gm = e == a.E ? &gmap_sh : &gmap, *um = e == a.E ? &umap_sh : &umap;
+            const int row0 = (e == a.E ? 0 : e * a.H) + m0;
+            for (int i = 0; i < nstages && ok; i++) {
+                const int sr = i % PF_RAW, use = i / PF_RAW;
+                PF_TR(tc = clock64();)
+                if (use > 0) ok = mbar_wait(&R.rempty[sr], (use - 1) & 1);
+                PF_TR(if (tr) acc[5] += clock64() - tc;)
+                if (!ok) break;
+                mbar_expect_tx(&R.rfull[sr], 2 * RAW4);
+                const uint32_t rd = smem_u32(raw + sr * 2 * RAW4);
+                q4_issue(gm, row0, rd, i, &R.rfull[sr]);
+                q4_issue(um, row0, rd + RAW4, i, &R.rfull[sr]);
             }
         }
     } else if (warp == 1) {
-        if (lane == 0) ok = mma_role<2>(R, nstages, abf, bst, tbase, instr_desc(nn));
+        if (lane == 0)
+            ok = mma_role<2>(R, nstages, UP_A, UP_ACC_U, bst, tbase, instr_desc(nn) PF_TR(, tr ? acc : nullptr));
     } else if (warp >= PF_DQ0 / 32) {
-        const int t = threadIdx.x - PF_DQ0;
+        // warp w: TMEM lanes (= weight rows) 32*(w%4).., matrix and nibble
+        // half from (w-4)/4
+        const int grp = (warp - PF_DQ0 / 32) >> 2, mat = grp >> 1, hh = grp & 1;
+        const int r = (warp & 3) * 32 + lane;
+        const uint32_t t_st = tbase + ((uint32_t)((warp & 3) * 32) << 16) + UP_A + mat * 32 + hh * 16;
+        Q4Scales S;
         for (int i = 0; i < nstages && ok; i++) {
-            const int sr = i % PF_STG, sa = i % PF_NA;
-            ok = mbar_wait(&R.rfull[sr], (i / PF_STG) & 1);
+            const int sr = i % PF_RAW, sa = i % PF_NA;
+            PF_TR(tc = clock64();)
+            ok = mbar_wait(&R.rfull[sr], (i / PF_RAW) & 1);
+            PF_TR(if (tr && threadIdx.x == PF_DQ0) acc[8] += clock64() - tc; tc = clock64();)
             if (ok && i >= PF_NA) ok = mbar_wait(&R.aempty[sa], (i / PF_NA - 1) & 1);
+            PF_TR(if (tr && threadIdx.x == PF_DQ0) acc[9] += clock64() - tc; tc = clock64();)
             if (!ok) break;
-            uint8_t *ag = abf + sa * 2 * A_STAGE;
-            q4_deq(raw + sr * 2 * RAW4, i, t, ag);
-            q4_deq(raw + sr * 2 * RAW4 + RAW4, i, t, ag + A_STAGE);
-            async_proxy_fence();
+            tc_fence_after();
+            const uint8_t *rw = raw + sr * 2 * RAW4 + mat * RAW4;
+            if ((i & 3) == 0) q4_scales(rw, r, hh, S);
+            uint32_t v[16];
+            q4_deq(rw, i & 3, r, hh, S, v);
+            tmem_st16(t_st + sa * 64, v);
+            tmem_st_wait();
+            PF_TR(if (tr && threadIdx.x == PF_DQ0) acc[10] += clock64() - tc; tc = clock64();)
+            tc_fence_before();
             __syncwarp();
             if (lane == 0) {
                 mbar_arrive(&R.rempty[sr]);
                 mbar_arrive(&R.afull[sa]);
             }
+            PF_TR(if (tr && threadIdx.x == PF_DQ0) acc[11] += clock64() - tc;)
         }
+        PF_TR(tc = clock64();)
         if (ok) ok = mbar_wait(&R.done, 0);
+        PF_TR(if (tr && threadIdx.x == PF_DQ0) acc[12] += clock64() - tc;)
     }
+    PF_TR(if (tr) {
+        _Pragma("unroll") for (int k = 4; k < 17; k++) if (acc[k]) atomicAdd(&tr[k], acc[k]);
+    })
     ok = __syncthreads_and(ok);
+    PF_TR(if (tr && threadIdx.x == 0) { tr[2] = clock64() - tc0; tr[13] = nn; })
     tc_fence_after();
     if (!ok) {
         if (threadIdx.x == 0) atomicExch(a.err, 1);
     } else if (warp >= PF_DQ0 / 32) {
-        // warp w reads TMEM lanes 32*(w%4).. (its rows), columns of half (w-4)/4
-        const int q = warp & 3;
-        const int m = m0 + q * 32 + lane;
+        // h tile through shared memory (the B ring is free now): the four
+        // warps of lane quarter q write rows m0+32q.. of every fourth
+        // 32-token chunk as stage[token][row], then all 16 warps store whole
+        // 16-byte pieces of each token's 128-row slice of h.
+        PF_TR(const unsigned long long te0 = clock64();)
+        const int q = warp & 3, r = q * 32 + lane;
         const uint32_t lane_off = (uint32_t)(q * 32) << 16;
-        const int half = nn / 2, j_beg = ((warp - PF_DQ0 / 32) >> 2) * half;
-        for (int j0 = j_beg; j0 < j_beg + half; j0 += 8) {
-            float g[8], uu[8];
-            tmem_ld8(tbase + lane_off + j0, g);
-            tmem_ld8(tbase + lane_off + 256 + j0, uu);
+        __nv_bfloat16 *stage = reinterpret_cast<__nv_bfloat16 *>(bst);  // [PF_NMAX][PF_M]
+        for (int j0 = ((warp - PF_DQ0 / 32) >> 2) * 32; j0 < n; j0 += 128) {
+            if (j0 + 32 <= nn) {
+                float g[32], uu[32];
+                tmem_ld32(tbase + lane_off + j0, g);
+                tmem_ld32(tbase + lane_off + UP_ACC_U + j0, uu);
 #pragma unroll
-            for (int j = 0; j < 8; j++) {
-                if (j0 + j >= n) break;
-                const float gv = g[j];
-                const float sl = gv < -50.f ? 0.f : (gv > 50.f ? gv : gv / (1.f + expf(-gv)));
-                a.hb[(size_t)(s0 + j0 + j) * a.H + m] = __float2bfloat16_rn(sl * uu[j]);
+                for (int j = 0; j < 32; j++) stage[(j0 + j) * PF_M + r] = __float2bfloat16_rn(silu_mul(g[j], uu[j]));
+            } else {
+                for (int j1 = j0; j1 < nn; j1 += 8) {
+                    float g[8], uu[8];
+                    tmem_ld8(tbase + lane_off + j1, g);
+                    tmem_ld8(tbase + lane_off + UP_ACC_U + j1, uu);
+#pragma unroll
+                    for (int j = 0; j < 8; j++) stage[(j1 + j) * PF_M + r] = __float2bfloat16_rn(silu_mul(g[j], uu[j]));
+                }
             }
         }
+        asm volatile("bar.sync 1, %0;" ::"n"(PF_NDQW * 32) : "memory");
+        const int t = threadIdx.x - PF_DQ0;
+        for (int k = t; k < n * (PF_M / 8); k += PF_NDQW * 32) {
+            const int j = k / (PF_M / 8), part = k % (PF_M / 8);
+            *reinterpret_cast<uint4 *>(a.hb + (size_t)(s0 + j) * a.H + m0 + part * 8) =
+                *reinterpret_cast<const uint4 *>(stage + j * PF_M + part * 8);
+        }
+        PF_TR(if (tr && threadIdx.x == PF_DQ0) tr[30] = clock64() - te0;)
     }
     tmem_free(tbase, 512);
+    PF_TR(if (tr && threadIdx.x == 0) tr[3] = clock64() - tc0; pf_end(0);)
 }
 
 // ---- phase 2: down + weighted combine -----------------------------------------
 // The CTA's 128 Q6_K rows are one contiguous, 16-byte aligned slab
 // (128 x 420 B at H = 512): one bulk copy brings it in; stages copy only B.
 __host__ __device__ inline int down_slab_bytes(int H) { return PF_M * (H / QK) * Q6K_BYTES; }
-__host__ __device__ inline int down_smem(int H) {
-    return 1024 + PF_STG * B_STAGE + PF_NA * A_STAGE + down_slab_bytes(H);
-}
+__host__ __device__ inline int down_smem(int H) { return 1024 + PF_STG * B_STAGE + down_slab_bytes(H); }
 
 __global__ void __launch_bounds__(PF_NT, 1)
     prefill_down_kernel(PrefillArgs a, const __grid_constant__ CUtensorMap hmap) {
@@ -474,18 +578,19 @@ __global__ void __launch_bounds__(PF_NT, 1)
     __shared__ uint32_t tslot;
     __shared__ int tok[PF_NMAX];
     __shared__ float wgt[PF_NMAX];
-    const int tile = blockIdx.x;
+    const int tile = blockIdx.y;
     if (tile >= *a.n_tiles) return;
+    PF_TR(unsigned long long *tr = pf_tr(1); const unsigned long long tc0 = clock64(); unsigned long long tc;
+          unsigned long long acc[18] = {};)
     const int u = a.tile_slot[tile], s0 = a.tile_start[tile], n = a.tile_n[tile];
     const int e = a.slot_expert[u];
-    const int n0 = blockIdx.y * PF_M;
+    const int n0 = blockIdx.x * PF_M;
     const int TK = a.T * a.K;
     const int row_bytes = (a.H / QK) * Q6K_BYTES;
     const size_t exp_bytes = (size_t)row_bytes * a.D;
     const uint8_t *slab_src = (e == a.E ? a.down_sh : a.down + e * exp_bytes) + (size_t)n0 * row_bytes;
     uint8_t *bst = psm;                        // [PF_STG][B_STAGE]
-    uint8_t *abf = bst + PF_STG * B_STAGE;     // [PF_NA][A_STAGE]
-    uint8_t *slab = abf + PF_NA * A_STAGE;     // raw Q6_K rows (16-byte aligned)
+    uint8_t *slab = bst + PF_STG * B_STAGE;    // raw Q6_K rows (16-byte aligned)
     for (int i = threadIdx.x; i < n; i += PF_NT) {
         const int asg = a.assign[s0 + i];
         const int t = asg_token_p(asg, TK, a.K);
@@ -498,70 +603,98 @@ __global__ void __launch_bounds__(PF_NT, 1)
     }
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     const uint32_t tbase = tmem_alloc(&tslot, 256);  // syncs the CTA
+    PF_TR(if (tr && threadIdx.x == 0) tr[1] = clock64() - tc0;)
 
     const int nn = (n + 15) & ~15;
     const int nstages = a.H / PF_KS;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     bool ok = true;
     if (warp == 0) {
-        // producer: the slab, then per stage one 64 x 256 box of h rows (rows
-        // past the tile are not used; rows past the tensor read as zero and
-        // still count toward the transaction bytes)
         if (lane == 0) {
             bulk_copy(slab, slab_src, down_slab_bytes(a.H), &slab_bar);
-            for (int i = 0; i < nstages && ok; i++) {
-                const int sb = i % PF_STG, use = i / PF_STG;
-                if (use > 0) ok = mbar_wait(&R.bempty[sb], (use - 1) & 1);
-                if (!ok) break;
-                mbar_expect_tx(&R.bfull[sb], B_STAGE);
-                tma_tile2d(smem_u32(bst + sb * B_STAGE), &hmap, i * PF_KS, s0, &R.bfull[sb]);
-            }
+            ok = b_producer(R, &hmap, bst, nstages, s0, nn PF_TR(, tr ? acc : nullptr));
         }
     } else if (warp == 1) {
-        if (lane == 0) ok = mma_role<1>(R, nstages, abf, bst, tbase, instr_desc(nn));
+        if (lane == 0) ok = mma_role<1>(R, nstages, DN_A, 0, bst, tbase, instr_desc(nn) PF_TR(, tr ? acc : nullptr));
     } else if (warp >= PF_DQ0 / 32) {
-        const int t = threadIdx.x - PF_DQ0;
+        const int grp = (warp - PF_DQ0 / 32) >> 2, hh = grp & 1, g = grp >> 1;
+        const int r = (warp & 3) * 32 + lane;
+        const uint32_t t_st = tbase + ((uint32_t)((warp & 3) * 32) << 16) + DN_A + hh * 16 + g * 8;
+        PF_TR(tc = clock64();)
         ok = mbar_wait(&slab_bar, 0);
+        PF_TR(if (tr && threadIdx.x == PF_DQ0) acc[8] += clock64() - tc;)
         for (int i = 0; i < nstages && ok; i++) {
             const int sa = i % PF_NA;
+            PF_TR(tc = clock64();)
             if (i >= PF_NA) ok = mbar_wait(&R.aempty[sa], (i / PF_NA - 1) & 1);
+            PF_TR(if (tr && threadIdx.x == PF_DQ0) acc[9] += clock64() - tc; tc = clock64();)
             if (!ok) break;
-            q6_deq(slab, row_bytes, i, t, abf + sa * A_STAGE);
-            async_proxy_fence();
+            tc_fence_after();
+            uint32_t v[8];
+            q6_deq(slab, row_bytes, i, r, hh, g, v);
+            tmem_st8(t_st + sa * 32, v);
+            tmem_st_wait();
+            PF_TR(if (tr && threadIdx.x == PF_DQ0) acc[10] += clock64() - tc; tc = clock64();)
+            tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(&R.afull[sa]);
+            PF_TR(if (tr && threadIdx.x == PF_DQ0) acc[11] += clock64() - tc;)
         }
+        PF_TR(tc = clock64();)
         if (ok) ok = mbar_wait(&R.done, 0);
+        PF_TR(if (tr && threadIdx.x == PF_DQ0) acc[12] += clock64() - tc;)
     }
+    PF_TR(if (tr) {
+        _Pragma("unroll") for (int k = 4; k < 17; k++) if (acc[k]) atomicAdd(&tr[k], acc[k]);
+    })
     ok = __syncthreads_and(ok);
+    PF_TR(if (tr && threadIdx.x == 0) { tr[2] = clock64() - tc0; tr[13] = nn; })
     tc_fence_after();
     if (!ok) {
         if (threadIdx.x == 0) atomicExch(a.err, 1);
     } else if (warp >= PF_DQ0 / 32) {
+        // the four warps of lane quarter q take every fourth 32-token chunk
         const int q = warp & 3;
         const int row = n0 + q * 32 + lane;
         const uint32_t lane_off = (uint32_t)(q * 32) << 16;
-        const int half = nn / 2, j_beg = ((warp - PF_DQ0 / 32) >> 2) * half;
-        for (int j0 = j_beg; j0 < j_beg + half; j0 += 8) {
-            float y[8];
-            tmem_ld8(tbase + lane_off + j0, y);
+        float *ocol = a.out + row;
+        for (int j0 = ((warp - PF_DQ0 / 32) >> 2) * 32; j0 < n; j0 += 128) {
+            if (j0 + 32 <= nn) {
+                float y[32];
+                tmem_ld32(tbase + lane_off + j0, y);
 #pragma unroll
-            for (int j = 0; j < 8; j++) {
-                if (j0 + j >= n) break;
-                atomicAdd(a.out + (size_t)tok[j0 + j] * a.D + row, wgt[j0 + j] * y[j]);
+                for (int j = 0; j < 32; j++)
+                    if (j0 + j < n) atomicAdd(ocol + (size_t)tok[j0 + j] * a.D, wgt[j0 + j] * y[j]);
+            } else {
+                for (int j1 = j0; j1 < n; j1 += 8) {
+                    float y[8];
+                    tmem_ld8(tbase + lane_off + j1, y);
+#pragma unroll
+                    for (int j = 0; j < 8; j++)
+                        if (j1 + j < n) atomicAdd(ocol + (size_t)tok[j1 + j] * a.D, wgt[j1 + j] * y[j]);
+                }
             }
         }
     }
     tmem_free(tbase, 256);
+    PF_TR(if (tr && threadIdx.x == 0) tr[3] = clock64() - tc0; pf_end(1);)
 }
 
 // ---- helpers: x to bf16, tile list ---------------------------------------------
-__global__ void to_bf16_kernel(const float *__restrict__ x, size_t n, __nv_bfloat16 *__restrict__ y) {
-    for (size_t i = (blockIdx.x * (size_t)blockDim.x + threadIdx.x) * 4; i < n;
-         i += (size_t)gridDim.x * blockDim.x * 4) {
-        const float4 v = *reinterpret_cast<const float4 *>(x + i);
-        uint2 o = make_uint2(pack_bf16(v.x, v.y), pack_bf16(v.z, v.w));
-        *reinterpret_cast<uint2 *>(y + i) = o;
+// x rows of every assignment, as bf16, in slot order: xg[p] = bf16(x[token of
+// assign[p]]). One warp per row.
+__global__ void gather_rows_kernel(const float *__restrict__ x, const int *__restrict__ assign,
+                                   const int *n_slots, const int *slot_start, int TK, int K, int D,
+                                   __nv_bfloat16 *__restrict__ xg) {
+    const int rows = slot_start[*n_slots];
+    const int lane = threadIdx.x & 31;
+    for (int p = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; p < rows; p += (gridDim.x * blockDim.x) >> 5) {
+        const float4 *src = reinterpret_cast<const float4 *>(x + (size_t)asg_token_p(assign[p], TK, K) * D);
+        uint2 *dst = reinterpret_cast<uint2 *>(xg + (size_t)p * D);
+        for (int c = lane; c < D / 4; c += 32) {
+            const float4 v = __ldg(src + c);
+            dst[c] = make_uint2(pack_bf16(v.x, v.y), pack_bf16(v.z, v.w));
+        }
     }
 }
 
@@ -672,8 +805,8 @@ int launch_prefill(const LayerArgs &la, const float *x, int *n_slots, __nv_bfloa
         *tile_n = tile_start + max_tiles;
     CUtensorMap xmap, hmap, gmap, umap, gmap_sh, umap_sh;
     int st;
-    if ((st = encode_bf16_2d(&xmap, xb, D, T, 1))) return st;            // gather4 wants one-row boxes
-    if ((st = encode_bf16_2d(&hmap, hb, H, n_asg, PF_NMAX))) return st;  // 64 x 256 boxes
+    if ((st = encode_bf16_2d(&xmap, xb, D, n_asg, B_ROWS))) return st;  // 64 x 16 boxes
+    if ((st = encode_bf16_2d(&hmap, hb, H, n_asg, B_ROWS))) return st;
     if ((st = encode_q4_rows(&gmap, la.gate, D, (uint64_t)la.E * H))) return st;
     if ((st = encode_q4_rows(&umap, la.up, D, (uint64_t)la.E * H))) return st;
     if (la.has_shared) {
@@ -683,7 +816,7 @@ int launch_prefill(const LayerArgs &la, const float *x, int *n_slots, __nv_bfloa
         gmap_sh = gmap;  // never read: no slot names the shared expert
         umap_sh = umap;
     }
-    to_bf16_kernel<<<grid_for((size_t)T * D / 4, 256, 148 * 8), 256, 0, s>>>(x, (size_t)T * D, xb);
+    gather_rows_kernel<<<148 * 8, 256, 0, s>>>(x, la.assign, n_slots, la.slot_start, T * la.K, la.K, D, xb);
     tile_plan_kernel<<<1, 256, 0, s>>>(n_slots, la.slot_start, n_tiles, tile_slot, tile_start, tile_n);
     PrefillArgs a;
     a.T = T; a.D = D; a.H = H; a.E = la.E; a.K = la.K;
@@ -709,11 +842,18 @@ int launch_prefill(const LayerArgs &la, const float *x, int *n_slots, __nv_bfloa
     else e = cudaSuccess;
     if (e != cudaSuccess) return cuda_status(e, "prefill out init");
     if (before) cudaEventRecord(before, s);
-    prefill_up_kernel<<<dim3(max_tiles, H / PF_M), PF_NT, smem_up, s>>>(a, xmap, gmap, umap, gmap_sh, umap_sh);
+    prefill_up_kernel<<<dim3(H / PF_M, max_tiles), PF_NT, smem_up, s>>>(a, xmap, gmap, umap, gmap_sh, umap_sh);
     if (between) cudaEventRecord(between, s);
-    prefill_down_kernel<<<dim3(max_tiles, D / PF_M), PF_NT, smem_dn, s>>>(a, hmap);
+    prefill_down_kernel<<<dim3(D / PF_M, max_tiles), PF_NT, smem_dn, s>>>(a, hmap);
     OFB_CHECK_LAUNCH("prefill kernels");
     return OFB_OK;
 }
 
 }  // namespace ofb
+
+#ifdef OFB_PF_TRACE
+extern "C" int ofb_debug_prefill_trace(unsigned long long *host, unsigned long long *span) {
+    if (cudaMemcpyFromSymbol(host, ofb::g_pf_trace, sizeof(ofb::g_pf_trace)) != cudaSuccess) return 1;
+    return cudaMemcpyFromSymbol(span, ofb::g_pf_span, sizeof(ofb::g_pf_span)) == cudaSuccess ? 0 : 1;
+}
+#endif
