@@ -180,6 +180,53 @@ int ofb_moe_forward_noalloc(const ofb_moe_config *cfg, const ofb_moe_weights *w,
                             float *w_out, void *stream);
 size_t ofb_noalloc_capacity(void);
 
+/* ---- expert parallelism (experts sharded over GPUs) ------------------------
+ * Building blocks for one MoE layer whose routed experts are split over
+ * n_ranks GPUs, experts_per_rank = n_experts / n_ranks each (rank r owns
+ * experts [r*experts_per_rank, (r+1)*experts_per_rank), stored as the
+ * CONTIGUOUS layout's expert range); tokens are split too, each rank routing
+ * its own. Per layer: ofb_route on own tokens -> ofb_ep_plan + ofb_ep_pack ->
+ * all-to-all of rows and metadata (NCCL, by the caller) -> ofb_moe_experts ->
+ * all-to-all back -> ofb_moe_shared + ofb_ep_combine. The reference runs its
+ * MoE block on one CPU (engine/src/model.c:992-1143) and has no counterpart;
+ * the arithmetic per (token, expert) pair is that block's. */
+#define OFB_EP_MAX_RANKS 16
+
+/* Dispatch order of a rank's T*K assignments (a = t*K + k, expert idx[a]):
+ * grouped by destination rank idx[a] / experts_per_rank, assignment order
+ * kept inside a group. Writes send_counts[n_ranks] (int32),
+ * slot_of_assignment[T*K] and assignment_of_slot[T*K]. One block; device. */
+int ofb_ep_plan(const uint32_t *idx, int n_tokens, int top_k, int experts_per_rank, int n_ranks,
+                int32_t *send_counts, int32_t *slot_of_assignment, int32_t *assignment_of_slot,
+                void *stream);
+/* Send buffers in slot order: send_x[s] = x[token of a] (f32 [d_model]) and
+ * send_meta[s] = {expert - dest*experts_per_rank, float bits of w[a]}
+ * (int32 pairs), a = assignment_of_slot[s]. */
+int ofb_ep_pack(const float *x, const uint32_t *idx, const float *w, int n_tokens, int top_k,
+                int d_model, int experts_per_rank, const int32_t *assignment_of_slot, float *send_x,
+                int32_t *send_meta, void *stream);
+/* out_rows[r] = weight * SwiGLU_e(x_rows[r]) for the row's {local expert e,
+ * weight} pair in row_meta (the format ofb_ep_pack writes); routed experts
+ * only, cfg->n_experts = experts_per_rank, cfg->top_k = 1, ws created for
+ * that cfg with max_tokens >= n_rows. */
+int ofb_moe_experts(const ofb_moe_config *cfg, const ofb_moe_weights *w, const float *x_rows,
+                    int n_rows, const int32_t *row_meta, float *out_rows, ofb_workspace *ws,
+                    void *stream);
+/* out[t] = resid[t] (or 0 when resid is NULL) + g_t * SwiGLU_shared(x[t]),
+ * g_t = sigmoid(x[t] . shexp_gate) when cfg->shared_gate and the gate vector
+ * is set, else 1. ws: any workspace of this d_model/hidden (contiguous
+ * layout) with max_tokens >= n_tokens, e.g. the one ofb_route uses. */
+int ofb_moe_shared(const ofb_moe_config *cfg, const ofb_moe_weights *w, const float *x,
+                   const float *resid, float *out, int n_tokens, ofb_workspace *ws, void *stream);
+/* out[t] += r, r = the sum over k = 0..K-1 (in order) of
+ * y_back[slot_of_assignment[t*K+k]] (model.c:1090, :1142 order). */
+int ofb_ep_combine(const float *y_back, const int32_t *slot_of_assignment, int n_tokens, int top_k,
+                   int d_model, float *out, void *stream);
+/* out[t] = x[t] / sqrt(mean(x[t]^2) + eps): the unit-weight RMSNorm that
+ * feeds each layer of a layer stack (cpu_rmsnorm, engine/src/model.c:333,
+ * with every per-channel weight 1). out may alias x. */
+int ofb_rmsnorm(const float *x, int n_tokens, int d_model, float eps, float *out, void *stream);
+
 /* ---- seeded synthetic inputs ---------------------------------------------- */
 
 /* Fills n_blocks Q4_K or Q6_K super-blocks on the device from a counter-based

@@ -207,13 +207,14 @@ static int sm_count() {
 
 int run_moe_layer(const ofb_moe_config *cfg, const ofb_moe_weights *wt, const float *x,
                   const float *resid, float *out, int T, uint32_t *idx_out, float *w_out,
-                  uint8_t *base, const WorkspaceLayout &L, cudaStream_t s, cudaEvent_t *ev) {
+                  uint8_t *base, const WorkspaceLayout &L, cudaStream_t s, cudaEvent_t *ev,
+                  const uint32_t *given_idx, const float *given_w) {
     const int D = cfg->d_model, H = cfg->hidden, E = cfg->n_experts, K = cfg->top_k;
     auto mark = [&](int i) { if (ev) cudaEventRecord(ev[i], s); };
     mark(0);
     float *logits = (float *)(base + L.logits);
-    uint32_t *idx = idx_out ? idx_out : (uint32_t *)(base + L.idx);
-    float *w = w_out ? w_out : (float *)(base + L.w);
+    uint32_t *idx = given_idx ? const_cast<uint32_t *>(given_idx) : idx_out ? idx_out : (uint32_t *)(base + L.idx);
+    float *w = given_w ? const_cast<float *>(given_w) : w_out ? w_out : (float *)(base + L.w);
     const bool has_shared = wt->gate_shexp && wt->up_shexp && wt->down_shexp;
     PlanArgs p;
     p.idx = idx; p.w = w; p.T = T; p.K = K; p.E = E; p.D = D;
@@ -225,7 +226,7 @@ int run_moe_layer(const ofb_moe_config *cfg, const ofb_moe_weights *wt, const fl
     p.slot_start = (int *)(base + L.slot_start);
     p.assign = (int *)(base + L.assign);
     int st;
-    const bool fast = wt->router && cfg->layout == OFB_LAYOUT_CONTIGUOUS && T <= FAST_ROUTE_MAX_T;
+    const bool fast = !given_idx && wt->router && cfg->layout == OFB_LAYOUT_CONTIGUOUS && T <= FAST_ROUTE_MAX_T;
     if (fast) {
         // one launch: certified routing, shared-expert gates, dispatch plan
         int *ctr = (int *)(base + L.counters);
@@ -238,7 +239,9 @@ int run_moe_layer(const ofb_moe_config *cfg, const ofb_moe_weights *wt, const fl
         mark(1);
         mark(2);
     } else {
-        if (wt->router) {
+        if (given_idx) {
+            // routing supplied by the caller
+        } else if (wt->router) {
             if ((st = launch_router_logits(cfg->layout, wt->router, x, T, D, E, logits, s))) return st;
             if ((st = launch_route_select(logits, T, E, K, cfg->routing, cfg->renorm, idx, w, s))) return st;
         } else if ((st = launch_route_uniform(T, K, idx, w, s))) {
@@ -408,6 +411,106 @@ extern "C" int ofb_moe_forward_profiled(const ofb_moe_config *cfg, const ofb_moe
     }
     for (int i = 0; i < 5; i++) cudaEventDestroy(ev[i]);
     return st;
+}
+
+// Row metadata {local expert, float bits of weight} -> idx / w arrays.
+__global__ void unpack_meta_kernel(const int32_t *__restrict__ meta, int n, uint32_t *__restrict__ idx,
+                                   float *__restrict__ w) {
+    for (int r = blockIdx.x * blockDim.x + threadIdx.x; r < n; r += gridDim.x * blockDim.x) {
+        idx[r] = (uint32_t)meta[2 * r];
+        w[r] = __int_as_float(meta[2 * r + 1]);
+    }
+}
+
+__global__ void fill_kernel(float *__restrict__ p, int n, float v) {
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) p[i] = v;
+}
+
+static bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
+extern "C" int ofb_moe_experts(const ofb_moe_config *cfg, const ofb_moe_weights *w, const float *x_rows,
+                               int n_rows, const int32_t *row_meta, float *out_rows, ofb_workspace *ws,
+                               void *stream) {
+    int st = check_config(cfg);
+    if (st) return st;
+    if (!w || n_rows < 0) { set_error("ofb_moe_experts: bad arguments"); return OFB_EINVAL; }
+    if (cfg->top_k != 1 || cfg->layout != OFB_LAYOUT_CONTIGUOUS) {
+        set_error("ofb_moe_experts: needs top_k = 1 and the contiguous layout");
+        return OFB_EINVAL;
+    }
+    if ((st = check_ws(cfg, ws, n_rows))) return st;
+    if (n_rows == 0) return OFB_OK;
+    if (!x_rows || !row_meta || !out_rows || !w->gate_exps || !w->up_exps || !w->down_exps) {
+        set_error("ofb_moe_experts: NULL pointer");
+        return OFB_EINVAL;
+    }
+    if (!aligned16(x_rows) || !aligned16(w->gate_exps) || !aligned16(w->up_exps) || !aligned16(w->down_exps)) {
+        set_error("ofb_moe_experts: tensors must be 16-byte aligned");
+        return OFB_EINVAL;
+    }
+    ofb_moe_weights routed = *w;  // routed experts only
+    routed.router = nullptr;
+    routed.gate_shexp = routed.up_shexp = routed.down_shexp = nullptr;
+    routed.shexp_gate = nullptr;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    uint32_t *idx = (uint32_t *)(ws->base + ws->layout.idx);
+    float *wt = (float *)(ws->base + ws->layout.w);
+    unpack_meta_kernel<<<grid_for((size_t)n_rows, 256, 148 * 4), 256, 0, s>>>(row_meta, n_rows, idx, wt);
+    OFB_CHECK_LAUNCH("unpack row metadata");
+    // rows whose weight is below the skip threshold get no expert term; on
+    // the decode-sized path the combine writes rows only when some row has
+    // one, so start from zeros (the tensor-core path initialises out itself)
+    if (n_rows <= MAX_DECODE_T) {
+        cudaError_t e = cudaMemsetAsync(out_rows, 0, (size_t)n_rows * cfg->d_model * sizeof(float), s);
+        if (e != cudaSuccess) return cuda_status(e, "ofb_moe_experts memset");
+    }
+    return run_moe_layer(cfg, &routed, x_rows, nullptr, out_rows, n_rows, nullptr, nullptr, ws->base, ws->layout,
+                         s, nullptr, idx, wt);
+}
+
+extern "C" int ofb_moe_shared(const ofb_moe_config *cfg, const ofb_moe_weights *w, const float *x,
+                              const float *resid, float *out, int n_tokens, ofb_workspace *ws, void *stream) {
+    int st = check_config(cfg);
+    if (st) return st;
+    if (!w || !ws || n_tokens < 0) { set_error("ofb_moe_shared: bad arguments"); return OFB_EINVAL; }
+    if (n_tokens == 0) return OFB_OK;
+    if (!x || !out || !w->gate_shexp || !w->up_shexp || !w->down_shexp) {
+        set_error("ofb_moe_shared: NULL pointer");
+        return OFB_EINVAL;
+    }
+    const ofb_moe_config &wc = ws->cfg;
+    if (wc.d_model != cfg->d_model || wc.hidden != cfg->hidden || wc.layout != OFB_LAYOUT_CONTIGUOUS ||
+        cfg->layout != OFB_LAYOUT_CONTIGUOUS || n_tokens > ws->max_tokens) {
+        set_error("ofb_moe_shared: workspace does not fit (shape, contiguous layout, max_tokens)");
+        return OFB_EINVAL;
+    }
+    if (!aligned16(x) || !aligned16(w->gate_shexp) || !aligned16(w->up_shexp) || !aligned16(w->down_shexp)) {
+        set_error("ofb_moe_shared: tensors must be 16-byte aligned");
+        return OFB_EINVAL;
+    }
+    // the shared expert as a one-expert layer: every token routed to it with
+    // weight g_t (a workspace of any expert count / top_k >= 1 holds this);
+    // the routed skip rule then drops a term whose gate is below 1e-6, a
+    // change below 1e-6 of |y|
+    ofb_moe_config one = *cfg;
+    one.n_experts = 1;
+    one.top_k = 1;
+    ofb_moe_weights sw = {};
+    sw.gate_exps = w->gate_shexp;
+    sw.up_exps = w->up_shexp;
+    sw.down_exps = w->down_shexp;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    uint32_t *idx = (uint32_t *)(ws->base + ws->layout.idx);
+    float *g = (float *)(ws->base + ws->layout.w);
+    cudaError_t e = cudaMemsetAsync(idx, 0, (size_t)n_tokens * sizeof(uint32_t), s);
+    if (e != cudaSuccess) return cuda_status(e, "ofb_moe_shared memset");
+    if (cfg->shared_gate && w->shexp_gate)
+        shared_gate_kernel<<<(n_tokens + 7) / 8, 256, 0, s>>>(x, w->shexp_gate, n_tokens, cfg->d_model, g);
+    else
+        fill_kernel<<<grid_for((size_t)n_tokens, 256, 148), 256, 0, s>>>(g, n_tokens, 1.0f);
+    OFB_CHECK_LAUNCH("shared gates");
+    return run_moe_layer(&one, &sw, x, resid, out, n_tokens, nullptr, nullptr, ws->base, ws->layout, s, nullptr,
+                         idx, g);
 }
 
 extern "C" int ofb_workspace_route_stats(ofb_workspace *ws, int counts[3]) {

@@ -71,9 +71,12 @@ __host__ __device__ inline size_t xq_stride(int D) { return (size_t)2 * D + (siz
 
 WorkspaceLayout workspace_layout(const ofb_moe_config *c, int max_tokens);
 int check_config(const ofb_moe_config *c);
+// given_idx / given_w (device, [T][top_k]): routing supplied by the caller;
+// the router is skipped and the layer runs from the dispatch plan on.
 int run_moe_layer(const ofb_moe_config *cfg, const ofb_moe_weights *wt, const float *x,
                   const float *resid, float *out, int T, uint32_t *idx_out, float *w_out,
                   uint8_t *base, const WorkspaceLayout &L, cudaStream_t s,
-                  cudaEvent_t *phase_events /* 5 events or NULL */);
+                  cudaEvent_t *phase_events /* 5 events or NULL */,
+                  const uint32_t *given_idx = nullptr, const float *given_w = nullptr);
 
 }  // namespace ofb

@@ -36,7 +36,7 @@
 //  * epilogue (warps 4..19): tcgen05.ld of the accumulator; up stages
 //    h = silu(g)*u as bf16 in shared memory and stores whole 16-byte pieces
 //    of each token's row, down adds w * y into out with fp32 reductions.
-// No TMA load here uses cluster multicast. Every mbarrier wait is bounded: on
+// Every TMA load here reads this GPU's own memory into this CTA only. Every mbarrier wait is bounded: on
 // timeout the kernel records an error flag, releases its TMEM and returns.
 #include <cuda.h>
 
@@ -215,7 +215,7 @@ __device__ __forceinline__ void tmem_free(uint32_t base, uint32_t ncols) {
 }
 
 // ---- copies -----------------------------------------------------------------
-// TMA bulk copy global -> shared, completing on an mbarrier (no multicast).
+// TMA bulk copy global -> shared, completing on an mbarrier (this CTA only).
 __device__ __forceinline__ void bulk_copy(void *dst, const void *src, uint32_t bytes, uint64_t *bar) {
     mbar_expect_tx(bar, bytes);
     asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(

@@ -72,6 +72,12 @@ def _load() -> ctypes.CDLL:
         "ofb_synth_blocks": (i32, [vp, i32, u64, u64, u64, u64, vp]),
         "ofb_synth_blocks_host": (None, [vp, i32, u64, u64, u64, u64]),
         "ofb_synth_normal_host": (None, [vp, u64, u64, u64, ctypes.c_float]),
+        "ofb_ep_plan": (i32, [vp, i32, i32, i32, i32, vp, vp, vp, vp]),
+        "ofb_ep_pack": (i32, [vp, vp, vp, i32, i32, i32, i32, vp, vp, vp, vp]),
+        "ofb_moe_experts": (i32, [cfgp, wp, vp, i32, vp, vp, vp, vp]),
+        "ofb_moe_shared": (i32, [cfgp, wp, vp, vp, vp, i32, vp, vp]),
+        "ofb_ep_combine": (i32, [vp, vp, i32, i32, i32, vp, vp]),
+        "ofb_rmsnorm": (i32, [vp, i32, i32, ctypes.c_float, vp, vp]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(lib, name)
@@ -203,6 +209,17 @@ class LayerWeights:
             self.up_shexp, self.down_shexp, self.shexp_gate)))
 
 
+def make_router(shape: LayerShape, seed: int, router_bias: torch.Tensor | None = None) -> torch.Tensor:
+    """Host f32 router of make_layer (flat, laid out per `shape.layout`)."""
+    E, D = shape.n_experts, shape.d_model
+    r = synth_normal(E * D, seed, STREAM_ROUTER, 0.02).view(E, D)
+    if router_bias is not None:
+        r[:, 0] = router_bias.float()
+    if shape.layout == LAYOUT_INTERLEAVED:
+        r = r.t().contiguous()
+    return r.reshape(-1)
+
+
 def make_layer(shape: LayerShape, seed: int, device="cuda", shared: bool = True,
                router: bool = True, router_bias: torch.Tensor | None = None) -> LayerWeights:
     """Seeded synthetic layer with the benchmark's distributions.
@@ -219,14 +236,7 @@ def make_layer(shape: LayerShape, seed: int, device="cuda", shared: bool = True,
     nb = shape.q4k_blocks_per_expert
     gen = (lambda q, n, s: synth_blocks_host(q, n, seed, s)) if str(device) == "cpu" else \
           (lambda q, n, s: synth_blocks(q, n, seed, s, device=device))
-    r = None
-    if router:
-        r = synth_normal(E * D, seed, STREAM_ROUTER, 0.02).view(E, D)
-        if router_bias is not None:
-            r[:, 0] = router_bias.float()
-        if shape.layout == LAYOUT_INTERLEAVED:
-            r = r.t().contiguous()
-        r = r.reshape(-1).to(device)
+    r = make_router(shape, seed, router_bias).to(device) if router else None
     g = gen(TYPE_Q4_K, E * nb, STREAM_GATE)
     u = gen(TYPE_Q4_K, E * nb, STREAM_UP)
     d = gen(TYPE_Q6_K, E * nb, STREAM_DOWN)
@@ -237,6 +247,28 @@ def make_layer(shape: LayerShape, seed: int, device="cuda", shared: bool = True,
         ds = gen(TYPE_Q6_K, nb, STREAM_DOWN_SH)
         v = synth_normal(D, seed, STREAM_GATE_V, 0.02).to(device)
     return LayerWeights(r, g, u, d, gs, us, ds, v)
+
+
+def make_layer_slice(shape: LayerShape, seed: int, e0: int, e1: int, device="cuda",
+                     shared: bool = True, router: bool = True) -> LayerWeights:
+    """The tensors of make_layer(shape, seed) that one expert-parallel rank
+    holds: routed experts [e0, e1) (the same bytes as those experts of the
+    whole layer), the full router, the shared expert and its gate vector."""
+    nb = shape.q4k_blocks_per_expert
+    n = (e1 - e0) * nb
+    if str(device) == "cpu":
+        gen = lambda q, s: synth_blocks_host(q, n, seed, s, first_block=e0 * nb)
+    else:
+        gen = lambda q, s: synth_blocks(q, n, seed, s, device=device, first_block=e0 * nb)
+    r = make_router(shape, seed).to(device) if router else None
+    gs = us = ds = v = None
+    if shared:
+        sgen = (lambda q, s: synth_blocks_host(q, nb, seed, s)) if str(device) == "cpu" else \
+               (lambda q, s: synth_blocks(q, nb, seed, s, device=device))
+        gs, us, ds = sgen(TYPE_Q4_K, STREAM_GATE_SH), sgen(TYPE_Q4_K, STREAM_UP_SH), sgen(TYPE_Q6_K, STREAM_DOWN_SH)
+        v = synth_normal(shape.d_model, seed, STREAM_GATE_V, 0.02).to(device)
+    return LayerWeights(r, gen(TYPE_Q4_K, STREAM_GATE), gen(TYPE_Q4_K, STREAM_UP),
+                        gen(TYPE_Q6_K, STREAM_DOWN), gs, us, ds, v)
 
 
 ZIPF_ALPHA = 0.15  # gives per-expert counts of ~60..600 at 4096 tokens, top-8 of 256

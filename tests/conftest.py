@@ -30,6 +30,18 @@ def ofb():
     return load_ofb()
 
 
+def load_ep():
+    """The expert-parallel host module (ornith-flight_b200/ep.py)."""
+    load_ofb()
+    if "ornith_flight_b200.ep" in sys.modules:
+        return sys.modules["ornith_flight_b200.ep"]
+    spec = importlib.util.spec_from_file_location("ornith_flight_b200.ep", os.path.join(PKG_DIR, "ep.py"))
+    mod = importlib.util.module_from_spec(spec)
+    sys.modules["ornith_flight_b200.ep"] = mod
+    spec.loader.exec_module(mod)
+    return mod
+
+
 @pytest.fixture(scope="session")
 def oracle():
     import binding

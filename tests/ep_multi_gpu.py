@@ -1,0 +1,70 @@
+"""Expert-parallel check on N GPUs (run by tests/test_gpu_ep.py under torchrun).
+
+Every rank holds experts [r*E/N, (r+1)*E/N) and tokens [r*T/N, ...) of seeded
+layers; the expert-parallel result must match the single-GPU layer
+(ofb_moe_forward of the whole layer on the same rank) on the rank's tokens,
+one layer and a 3-layer stack, at a decode-sized and a tensor-core-sized
+batch. Rank 0 also checks a few tokens against the oracle."""
+import os
+import sys
+
+import numpy as np
+import torch
+import torch.distributed as dist
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, HERE)
+from conftest import load_ep, load_ofb  # noqa: E402
+from test_gpu_moe import TOL, TOL_BF16, oracle_layer, rel_err  # noqa: E402
+
+
+def main():
+    rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
+    torch.cuda.set_device(int(os.environ["LOCAL_RANK"]))
+    dev = torch.device("cuda", int(os.environ["LOCAL_RANK"]))
+    dist.init_process_group("nccl", device_id=dev)
+    ofb, ep = load_ofb(), load_ep()
+    shape = ofb.LayerShape(d_model=512, hidden=256, n_experts=16, top_k=4)
+    epr = shape.n_experts // world
+    fails = []
+    for T_global in (4 * world, 40 * world):
+        tpr = T_global // world
+        ops = ep.EPOps(shape, world, max_tokens=tpr)
+        seeds = [31 + l for l in range(3)]
+        layers = [ep.EPLayer(shape, ofb.make_layer_slice(shape, s, rank * epr, (rank + 1) * epr, device=dev), ops, tpr,
+                             dev) for s in seeds]
+        x_all = ofb.make_tokens(shape, T_global, seed=5).to(dev)
+        x = x_all[rank * tpr:(rank + 1) * tpr].contiguous()
+        # single-GPU reference on this rank: the whole layers, all tokens
+        full = [ofb.MoeLayer(shape, ofb.make_layer(shape, s, device=dev), T_global) for s in seeds]
+        tol = TOL if tpr * shape.top_k <= 32 and T_global <= 32 else TOL_BF16
+        out = torch.empty_like(x)
+        layers[0].forward(x, x, out)
+        ref = full[0].forward(x_all, x_all)[rank * tpr:(rank + 1) * tpr]
+        e1 = rel_err((out - x).cpu().numpy(), (ref - x).cpu().numpy())
+        got = ep.EPStack(layers, ops, tpr, dev).forward(x)
+        cur = x_all.clone()
+        for f in full:
+            xn = torch.empty_like(cur)
+            ops.rmsnorm(cur, xn)
+            cur = f.forward(xn, cur)
+        e2 = rel_err(got.cpu().numpy(), cur[rank * tpr:(rank + 1) * tpr].cpu().numpy())
+        if rank == 0:
+            want, _, _ = oracle_layer(__import__("binding"), shape, ofb.make_layer(shape, seeds[0], device="cpu"),
+                                      x[:3].cpu().numpy(), x[:3].cpu().numpy())
+            e3 = rel_err((out[:3] - x[:3]).cpu().numpy(), want - x[:3].cpu().numpy())
+        else:
+            e3 = 0.0
+        print(f"rank {rank} T={T_global}: layer {e1:.2e} stack {e2:.2e} oracle {e3:.2e} (tol {tol})", flush=True)
+        if not (e1 <= tol and e2 <= tol and e3 <= tol):
+            fails.append(T_global)
+    ok = torch.tensor([0 if fails else 1], device=dev)
+    dist.all_reduce(ok, op=dist.ReduceOp.MIN)
+    dist.destroy_process_group()
+    if rank == 0 and ok.item() == 1:
+        print("ep_multi_gpu: ok", flush=True)
+    sys.exit(0 if ok.item() == 1 else 1)
+
+
+if __name__ == "__main__":
+    main()
