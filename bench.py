@@ -1,7 +1,7 @@
 """Benchmark of the MoE feed-forward layer (ornith-flight's hot path) on B200.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload decode1|decode32|prefill4096]
-                    [--impl ours|reference]
+    python bench.py [--gpus N] [--steps K] [--warmup W]
+                    [--workload decode1|decode32|prefill4096|stack40] [--impl ours|reference]
 
 A step = one MoE layer forward (router, softmax/top-8/renormalise, dispatch,
 Q4_K/Q6_K expert SwiGLU, sigmoid-gated shared expert, weighted combine) over
@@ -14,6 +14,11 @@ max over ranks. Step i runs layer copy i % L: L seeded layer copies (each
 522 MB of expert weights, > 8 GB in total) rotate so that no step finds its
 experts in the 126 MB L2 ("rotate" in config). Multi-GPU: one independent
 replica per GPU (weak scaling; the decode layer has no exchange step).
+
+The default line also carries "prefill4096" (config 3) and "stack40"
+(config 4: 40 layers at batch 256, routed experts split over all N ranks,
+NCCL all-to-all dispatch and combine; strong scaling, tokens/s of the whole
+job) blocks measured in the same run.
 
 --impl reference times the reference's CPU implementation of the same layer:
 the reference's own engine/src/gguf.c (compiled unmodified into oracle/_ref)
@@ -44,6 +49,11 @@ WORKLOADS = {
     "prefill4096": dict(tokens=4096, zipf=True, layers=2, bound="tensor", dtype="bf16 (fp32 accumulate)",
                         config="BASELINE config 3: 4096-token prefill, Zipf(1.1)-skewed routing",
                         launches=7, metric="MoE-layer tokens/s (4096-token prefill)"),
+    "stack40": dict(tokens=256, layers=40, bound="hbm", ep=True,
+                    dtype="bf16 tensor-core / f32 dp4a experts (fp32 accumulate), f32 rows exchanged",
+                    config="BASELINE config 4: 40-layer MoE stack, batch 256, experts sharded over the GPUs, "
+                           "NCCL all-to-all dispatch/combine",
+                    metric="MoE-stack tokens/s (40 layers, batch 256, expert parallel)"),
 }
 D, H, E, K = 2048, 512, 256, 8
 EXPERT_BYTES = 2 * (H * D // 256) * 144 + (H * D // 256) * 210  # 2,039,808
@@ -269,6 +279,149 @@ def measure(args, ofb, dev, rank, world, local_rank, workload, steps, warmup, n_
                 kept=statistics.mean(kept), e2e_ms=float(te.item()), clocks=clk.summary() if clk else None)
 
 
+def load_ep():
+    import importlib.util
+    load_ofb() if "ornith_flight_b200.ofb" not in sys.modules else None
+    spec = importlib.util.spec_from_file_location(
+        "ornith_flight_b200.ep", os.path.join(ROOT, "ornith-flight_b200", "ep.py"))
+    mod = importlib.util.module_from_spec(spec)
+    sys.modules[spec.name] = mod
+    spec.loader.exec_module(mod)
+    return mod
+
+
+def layer_launches(rows: int, tokens: int) -> int:
+    """Kernels of this library one expert-parallel layer launches (the
+    dispatch logic of moe.cu: <= 32 rows take the dp4a decode kernels, more
+    the tensor-core prefill kernels)."""
+    def grouped(n):  # plan + expert kernels of one run_moe_layer with given routing
+        return 1 + (3 if n <= 32 else 4)  # plan; quantize, up, down | gather, tiles, up, down
+    route = 2  # router logits, select
+    experts = (1 + grouped(rows)) if rows else 0  # unpack + grouped
+    shared = 1 + grouped(tokens)  # gate (or fill) + grouped
+    return route + 2 + experts + shared + 1 + 1  # + plan, pack, combine, rmsnorm
+
+
+def measure_stack(args, ofb, dev, rank, world, local_rank, steps, warmup):
+    """Config 4: a 40-layer stack at batch 256 with the routed experts split
+    over the `world` ranks (EPStack). Device time of K stack steps, max over
+    ranks; then the same with host buffers (end to end)."""
+    import torch
+    import torch.distributed as dist
+    ep = load_ep()
+    own_group = not dist.is_initialized()
+    if own_group:  # one rank: a single-member NCCL group for the exchange calls
+        import socket
+        sk = socket.socket()
+        sk.bind(("127.0.0.1", 0))
+        port = sk.getsockname()[1]
+        sk.close()
+        dist.init_process_group("nccl", init_method=f"tcp://127.0.0.1:{port}", rank=0, world_size=1,
+                                device_id=dev)
+    try:
+        return _measure_stack(ofb, ep, dev, rank, world, steps, warmup)
+    finally:
+        if own_group:
+            dist.destroy_process_group()
+
+
+def _measure_stack(ofb, ep, dev, rank, world, steps, warmup):
+    import torch
+    import torch.distributed as dist
+    wl = WORKLOADS["stack40"]
+    shape = ofb.LayerShape()
+    T, L = wl["tokens"], wl["layers"]
+    if E % world or T % world:
+        raise SystemExit(f"stack40 needs the world size to divide {E} experts and {T} tokens")
+    epr, tpr = E // world, T // world
+    ops = ep.EPOps(shape, world, tpr)
+    layers = [ep.EPLayer(shape, ofb.make_layer_slice(shape, 5000 + l, rank * epr, (rank + 1) * epr, device=dev),
+                         ops, tpr, dev) for l in range(L)]
+    stack = ep.EPStack(layers, ops, tpr, dev)
+    x = ofb.make_tokens(shape, T, seed=99)[rank * tpr:(rank + 1) * tpr].contiguous().to(dev)
+    stream = torch.cuda.current_stream()
+    for _ in range(warmup):
+        stack.forward(x)
+    rows = [sum(l.last_counts[1]) for l in layers]  # rows each layer's experts received here
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(steps):
+        stack.forward(x)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    t = torch.tensor([e0.elapsed_time(e1)], device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = float(t.item())
+    # end to end: pinned host tokens in, final stream back, every step
+    hx = x.cpu().pin_memory()
+    hout = torch.empty_like(hx).pin_memory()
+    dx = torch.empty_like(x)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    e0.record(stream)
+    for _ in range(steps):
+        dx.copy_(hx, non_blocking=True)
+        hout.copy_(stack.forward(dx), non_blocking=True)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    te = torch.tensor([e0.elapsed_time(e1)], device=dev)
+    if world > 1:
+        dist.all_reduce(te, op=dist.ReduceOp.MAX)
+    # experts this rank's slice had rows for, per layer (for the HBM bytes)
+    touched = []
+    for l in layers:
+        idx = l.idx[:tpr]
+        touched.append(idx)
+    all_idx = torch.cat([i.reshape(-1) for i in touched]).to(torch.int64)
+    if world > 1:
+        g = [torch.empty_like(all_idx) for _ in range(world)]
+        dist.all_gather(g, all_idx)
+        all_idx = torch.cat(g)
+    per_layer = all_idx.view(world, L, tpr * K).permute(1, 0, 2).reshape(L, -1)
+    local = [((pl // epr) == rank) for pl in per_layer]
+    n_local = [len(set(pl[m].tolist())) for pl, m in zip(per_layer, local)]
+    launches = sum(layer_launches(r, tpr) for r in rows)
+    del layers, stack
+    torch.cuda.empty_cache()
+    return dict(T=T, ms=ms, e2e_ms=float(te.item()), n_local=n_local, rows=rows, launches=launches)
+
+
+def describe_stack(world, m, steps, warmup):
+    wl = WORKLOADS["stack40"]
+    T, L = m["T"], wl["layers"]
+    step_ms = m["ms"] / steps
+    peak, peak_kind = peaks("hbm_gbs")
+    # per GPU and step: the touched local experts' weights, the replicated
+    # router, shared expert and gate vector, of every layer
+    gpu_bytes = sum(n * EXPERT_BYTES + EXPERT_BYTES + E * D * 4 + D * 4 for n in m["n_local"])
+    achieved = gpu_bytes / (step_ms * 1e-3) / 1e9
+    nvlink = L * 2 * (T // world) * K * D * 4 * (world - 1) / world  # rows out and back, per GPU
+    return {
+        "metric": wl["metric"], "value": T * steps / (m["ms"] / 1e3), "unit": "tokens/s",
+        "n_gpus": world, "steps": steps, "warmup": warmup, "ms_per_step": step_ms,
+        "higher_is_better": True, "scaling": "strong", "dtype": wl["dtype"],
+        "data": "synthetic (seeded Q4_K/Q6_K blocks, N(0,1) tokens, N(0,0.02) router)",
+        "config": {"workload": "stack40", "desc": wl["config"], "tokens_per_step": T, "layers": L,
+                   "d_model": D, "hidden": H, "n_experts": E, "top_k": K, "experts_per_gpu": E // world,
+                   "tokens_per_gpu": T // world, "between_layers": "unit-weight RMSNorm, residual add",
+                   "l2": f"{L} distinct layers per step ({L * 522 // world} MB of experts per GPU) > 126 MB L2",
+                   "parallelism": f"ep{world}"},
+        "roofline": {"bound": "hbm", "kernel": "whole stack step (per GPU)", "achieved": achieved, "peak": peak,
+                     "unit": "GB/s", "frac": achieved / peak, "traffic": None, "peak_source": peak_kind,
+                     "algorithmic_bytes_per_gpu_step": gpu_bytes},
+        "nvlink_bytes_per_gpu_step": nvlink,
+        "rows_received_per_layer": statistics.mean(m["rows"]),
+        "e2e": {"value": T * steps / (m["e2e_ms"] / 1e3), "unit": "tokens/s",
+                "h2d_bytes_per_step": (T // world) * D * 4, "d2h_bytes_per_step": (T // world) * D * 4},
+        "gpu_launches": m["launches"] * steps,
+    }
+
+
 def run_ours(args, rank, world, local_rank):
     import torch
     ofb = load_ofb()
@@ -276,12 +429,23 @@ def run_ours(args, rank, world, local_rank):
     dev = torch.device("cuda", local_rank)
     wl = WORKLOADS[args.workload]
     n_layers = args.layers if args.layers else wl["layers"]
+    if wl.get("ep"):
+        with ClockSampler(local_rank) as clk:
+            m = measure_stack(args, ofb, dev, rank, world, local_rank, args.steps, args.warmup)
+        if rank == 0:
+            line = describe_stack(world, m, args.steps, args.warmup)
+            line["clocks"] = clk.summary()
+            print(json.dumps(line), flush=True)
+        return
     m = measure(args, ofb, dev, rank, world, local_rank, args.workload, args.steps, args.warmup,
                 n_layers, True)
     extra = None
     if args.workload != "prefill4096" and not args.no_prefill:
         extra = measure(args, ofb, dev, rank, world, local_rank, "prefill4096", args.prefill_steps,
                         3, WORKLOADS["prefill4096"]["layers"], False)
+    stack = None
+    if not args.no_stack:
+        stack = measure_stack(args, ofb, dev, rank, world, local_rank, args.stack_steps, 3)
     if rank != 0:
         return
     line = describe(args, world, args.workload, m, args.steps, args.warmup, n_layers)
@@ -291,6 +455,8 @@ def run_ours(args, rank, world, local_rank):
         line["prefill4096"] = {k: sub[k] for k in ("metric", "value", "unit", "ms_per_step", "steps",
                                                    "warmup", "config", "roofline", "layer_roofline",
                                                    "phase_ms", "e2e", "gpu_launches")}
+    if stack is not None:
+        line["stack40"] = describe_stack(world, stack, args.stack_steps, 3)
     if not args.no_cpu_baseline:
         v, kind, sample = cpu_throughput(1, args.cpu_seconds, min(m["T"], 4))
         line["cpu_baseline"] = {"value": v, "unit": "tokens/s", "cores": 1, "kind": kind,
@@ -400,6 +566,8 @@ def main():
     ap.add_argument("--layers", type=int, default=0, help="rotating layer copies (0: workload default)")
     ap.add_argument("--prefill-steps", type=int, default=20)
     ap.add_argument("--no-prefill", action="store_true", help="skip the prefill block of the decode line")
+    ap.add_argument("--stack-steps", type=int, default=5)
+    ap.add_argument("--no-stack", action="store_true", help="skip the expert-parallel stack block")
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()

@@ -158,25 +158,33 @@ WorkspaceLayout workspace_layout(const ofb_moe_config *c, int max_tokens) {
     L.slot_expert = take((E + 1) * 4);
     L.slot_start = take((E + 2) * 4);
     L.assign = take(A * 4);
-    // h / y (f32) serve the decode kernels (T <= MAX_DECODE_T) and the
+    // h / y (f32) serve the decode kernels (T <= gemv_max_tokens) and the
     // interleaved path; the tensor-core prefill path uses bf16 x and h instead
     const bool inter = c->layout == OFB_LAYOUT_INTERLEAVED;
-    const size_t Td = inter ? T : (T < (size_t)MAX_DECODE_T ? T : (size_t)MAX_DECODE_T);
+    const size_t Tg = (size_t)gemv_max_tokens((int)K, (int)E);
+    const size_t Td = inter ? T : (T < Tg ? T : Tg);
     const size_t Ad = Td * K + Td;
     L.h = take(Ad * (size_t)c->hidden * 4);
     L.y = take(Ad * (size_t)c->d_model * 4);
+    // tensor-core buffers whenever a call may exceed the fixed decode size:
+    // the layer itself above gemv_max_tokens, and one-expert runs over the
+    // same tokens (ofb_moe_shared) above MAX_DECODE_T
     const bool prefill = !inter && max_tokens > MAX_DECODE_T && c->hidden <= PREFILL_MAX_H;
     L.xb = take(prefill ? A * (size_t)c->d_model * 2 : 0);
     L.hb = take(prefill ? A * (size_t)c->hidden * 2 : 0);
     L.tiles = take(prefill ? (1 + 3 * (size_t)prefill_max_tiles(max_tokens, K, E)) * 4 : 0);
     const size_t Tf = (size_t)(max_tokens < FAST_ROUTE_MAX_T ? max_tokens : FAST_ROUTE_MAX_T);
     L.cand = take(Tf * (E + 1) * 16);
-    L.xq = take(Tf * xq_stride(c->d_model));
+    L.xq = take((Tf > Td ? Tf : Td) * xq_stride(c->d_model));
     // route tickets [64] + [1], route stats [3], pad [1], down-combine tickets [D/8]
     // ... then the prefill error flag [1]
     L.counters_bytes = (FAST_ROUTE_MAX_T + 4 + c->d_model / 8 + 1) * 4;
     L.counters = take(L.counters_bytes);
     L.total = off;
+    L.gemv_tokens = Td;
+    L.gemv_rows = Ad;
+    L.prefill_rows = prefill ? A : 0;
+    L.prefill_tiles = prefill ? (size_t)prefill_max_tiles(max_tokens, K, E) : 0;
     return L;
 }
 
@@ -233,7 +241,7 @@ int run_moe_layer(const ofb_moe_config *cfg, const ofb_moe_weights *wt, const fl
         if ((st = launch_route_fast(wt->router, x, p.shared_gate ? wt->shexp_gate : nullptr, T, D, E, K,
                                     cfg->routing, cfg->renorm, (double2 *)(base + L.cand),
                                     ctr + FAST_ROUTE_MAX_T, ctr + FAST_ROUTE_MAX_T + 1, idx, w, p.gsc,
-                                    (T <= MAX_DECODE_T && H <= MAX_DECODE_H) ? base + L.xq : nullptr,
+                                    use_gemv(T, K, E, H) ? base + L.xq : nullptr,
                                     &p, s)))
             return st;
         mark(1);
@@ -280,7 +288,11 @@ int run_moe_layer(const ofb_moe_config *cfg, const ofb_moe_weights *wt, const fl
         mark(4);
         return OFB_OK;
     }
-    if (T <= MAX_DECODE_T && H <= MAX_DECODE_H) {
+    if (use_gemv(T, K, E, H)) {
+        if ((size_t)T > L.gemv_tokens || (size_t)T * K + (has_shared ? T : 0) > L.gemv_rows) {
+            set_error("workspace holds %zu decode-path tokens; call needs %d", L.gemv_tokens, T);
+            return OFB_ETOOLARGE;
+        }
         unsigned char *xq = base + L.xq;
         if (!fast && (st = launch_quantize_x(x, T, D, xq, s))) return st;
         if ((st = launch_up_q(a, xq, max_slots, s))) return st;
@@ -292,8 +304,13 @@ int run_moe_layer(const ofb_moe_config *cfg, const ofb_moe_weights *wt, const fl
     }
     // prefill-sized batches: tcgen05 grouped GEMMs (prefill.cu)
     if (H > PREFILL_MAX_H) {
-        set_error("batches above %d tokens need hidden <= %d (got %d)", MAX_DECODE_T, PREFILL_MAX_H, H);
+        set_error("batches above %d tokens need hidden <= %d (got %d)", gemv_max_tokens(K, E), PREFILL_MAX_H, H);
         return OFB_EUNSUPPORTED;
+    }
+    if ((size_t)T * K + T > L.prefill_rows || (size_t)prefill_max_tiles(T, K, E) > L.prefill_tiles) {
+        set_error("workspace has no tensor-core buffers for %d tokens (rows %zu, tiles %zu)", T, L.prefill_rows,
+                  L.prefill_tiles);
+        return OFB_ETOOLARGE;
     }
     int *err = (int *)(base + L.counters) + FAST_ROUTE_MAX_T + 4 + D / 8;
     if ((st = launch_prefill(a, x, p.n_slots, (__nv_bfloat16 *)(base + L.xb), (__nv_bfloat16 *)(base + L.hb),
@@ -460,7 +477,7 @@ extern "C" int ofb_moe_experts(const ofb_moe_config *cfg, const ofb_moe_weights 
     // rows whose weight is below the skip threshold get no expert term; on
     // the decode-sized path the combine writes rows only when some row has
     // one, so start from zeros (the tensor-core path initialises out itself)
-    if (n_rows <= MAX_DECODE_T) {
+    if (use_gemv(n_rows, 1, cfg->n_experts, cfg->hidden)) {
         cudaError_t e = cudaMemsetAsync(out_rows, 0, (size_t)n_rows * cfg->d_model * sizeof(float), s);
         if (e != cudaSuccess) return cuda_status(e, "ofb_moe_experts memset");
     }

@@ -42,6 +42,11 @@ struct WorkspaceLayout {
     size_t counters;  // fast routing tickets [T] + [1] and stats [3]; zero at creation
     size_t counters_bytes;
     size_t total;
+    // capacities the regions were sized for (checked before every launch)
+    size_t gemv_tokens;    // tokens h / y / xq hold on the decode-kernel path
+    size_t gemv_rows;      // assignments (incl. shared) h / y hold
+    size_t prefill_rows;   // assignments xb / hb hold (0: no tensor-core path)
+    size_t prefill_tiles;  // tile-list entries
 };
 
 // Token counts up to which routing uses the certified fast kernel.
@@ -51,6 +56,13 @@ constexpr int MAX_DECODE_T = 32;
 constexpr int MAX_DECODE_H = 1024;
 // Tensor-core prefill kernels: the down kernel holds 128 Q6_K rows in shared memory.
 constexpr int PREFILL_MAX_H = 512;
+// Batches the dp4a decode kernels take. Above 32 tokens the tensor-core
+// kernels win even at a few rows per expert (measured: a 2048-row,
+// 8-rows-per-expert batch ran 2.5x slower on the decode kernels).
+__host__ __device__ inline int gemv_max_tokens(int, int) { return MAX_DECODE_T; }
+__host__ __device__ inline bool use_gemv(int T, int K, int E, int H) {
+    return H <= MAX_DECODE_H && T <= gemv_max_tokens(K, E);
+}
 
 int launch_quantize_x(const float *x, int T, int D, unsigned char *xq, cudaStream_t s);
 int prefill_max_tiles(int T, int K, int E);
