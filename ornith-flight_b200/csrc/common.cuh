@@ -137,6 +137,57 @@ inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, s
 }
 
 // L2 prefetch of [p, p + bytes) spread over the calling threads.
+// Optional launch timeline of the decode kernels (build with
+// -DOFB_DECODE_TRACE): per launch, block 0 takes a ring slot and records
+// globaltimer at start and after griddepcontrol.wait; every block raises the
+// slot's end time. Each translation unit keeps its own ring (DTRACE_DEFINE).
+#ifdef OFB_DECODE_TRACE
+#define DTRACE_DEFINE(tag)                                                                        \
+    __device__ unsigned long long g_dtr_##tag[4][64][6];                                          \
+    __device__ unsigned int g_dtn_##tag[4], g_dtc_##tag[4];                                        \
+    extern "C" int ofb_debug_dtrace_##tag(unsigned long long *host, int reset) {                   \
+        if (reset) {                                                                              \
+            static unsigned long long z[4 * 64 * 6];                                              \
+            static unsigned int zn[4];                                                            \
+            cudaMemcpyToSymbol(g_dtr_##tag, z, sizeof(z));                                        \
+            return cudaMemcpyToSymbol(g_dtn_##tag, zn, sizeof(zn)) == cudaSuccess ? 0 : 1;        \
+        }                                                                                         \
+        return cudaMemcpyFromSymbol(host, g_dtr_##tag, sizeof(g_dtr_##tag)) == cudaSuccess ? 0 : 1; \
+    }
+#define DTRACE_START(tag, k)                                                                      \
+    if (threadIdx.x == 0 && blockIdx.x == 0 && blockIdx.y == 0) {                                 \
+        unsigned long long t_;                                                                    \
+        asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t_));                                     \
+        const unsigned s_ = atomicAdd(&g_dtn_##tag[k], 1) & 63;                                    \
+        g_dtc_##tag[k] = s_;                                                                      \
+        g_dtr_##tag[k][s_][0] = t_;                                                               \
+    }
+#define DTRACE_WAITED(tag, k)                                                                     \
+    if (threadIdx.x == 0 && blockIdx.x == 0 && blockIdx.y == 0) {                                 \
+        unsigned long long t_;                                                                    \
+        asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t_));                                     \
+        g_dtr_##tag[k][g_dtc_##tag[k]][1] = t_;                                                   \
+    }
+#define DTRACE_MARK(tag, k, f)                                                                    \
+    if (threadIdx.x == 0 && blockIdx.x == 0 && blockIdx.y == 0) {                                 \
+        unsigned long long t_;                                                                    \
+        asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t_));                                     \
+        g_dtr_##tag[k][g_dtc_##tag[k]][f] = t_;                                                   \
+    }
+#define DTRACE_END(tag, k)                                                                        \
+    if (threadIdx.x == 0) {                                                                       \
+        unsigned long long t_;                                                                    \
+        asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t_));                                     \
+        atomicMax(&g_dtr_##tag[k][*(volatile unsigned *)&g_dtc_##tag[k]][2], t_);                 \
+    }
+#else
+#define DTRACE_DEFINE(tag)
+#define DTRACE_START(tag, k)
+#define DTRACE_WAITED(tag, k)
+#define DTRACE_MARK(tag, k, f)
+#define DTRACE_END(tag, k)
+#endif
+
 __device__ __forceinline__ void prefetch_l2(const void *p, size_t bytes, int tid, int nthreads) {
     const char *c = static_cast<const char *>(p);
     for (size_t o = (size_t)tid * 128; o < bytes; o += (size_t)nthreads * 128)

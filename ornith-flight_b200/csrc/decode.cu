@@ -12,9 +12,12 @@
 //  * expert_up_q: one warp per (slot, 2 hidden rows) streams the Q4_K gate
 //    and up rows (lane = one 64-element chunk: 16 B header + 32 B quants),
 //    writes h = silu(x.G) * (x.U) per token.
-//  * expert_down_q: one warp per (slot, 8 output rows) stages the 8 Q6_K rows
-//    (3360 B, 16-byte aligned) through shared memory, writes y per
-//    assignment; the last warp to finish a group of 8 rows (atomic ticket)
+//    Once routing is known it also prefetches the routed experts' down rows
+//    into L2 for the next kernel.
+//  * expert_down_q: one CTA per (slot, 64 output rows) stages the 64 Q6_K
+//    rows (26,880 B, 16-byte aligned) in shared memory and quantises each
+//    token's h once per CTA; warp w computes rows 4w..4w+3 and writes y per
+//    assignment; the last warp to finish a group of 4 rows (atomic ticket)
 //    adds resid + gate*shared + sum_a w_a*y_a in the reference's order
 //    (model.c:1007, :1090, :1142), so the combine is deterministic and
 //    needs no extra launch.
@@ -22,6 +25,8 @@
 #include "moe.cuh"
 
 namespace ofb {
+
+DTRACE_DEFINE(dc)
 
 __device__ __forceinline__ float silu_ref_d(float g) {
     // engine/src/model.c:340-344
@@ -69,6 +74,7 @@ __device__ __forceinline__ int asg_token_d(int a, int TK, int K) { return a < TK
 constexpr int UP_R = 2;  // hidden rows per warp
 
 __global__ void __launch_bounds__(256) expert_up_q(LayerArgs a, const unsigned char *__restrict__ xq) {
+    DTRACE_START(dc, 0)
     pdl_trigger();
     const int lane = threadIdx.x & 31;
     const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
@@ -82,6 +88,18 @@ __global__ void __launch_bounds__(256) expert_up_q(LayerArgs a, const unsigned c
         prefetch_l2(a.up_sh, exp_bytes, gt, nt);
     }
     pdl_wait();
+    DTRACE_WAITED(dc, 0)
+    {
+        // routing is known: pull the routed experts' down rows into L2 so
+        // that expert_down_q (next in the stream) reads them from there
+        const size_t dbytes = (size_t)(a.H / QK) * Q6K_BYTES * D, lines = dbytes / 128;
+        const int ns = *a.n_slots;
+        const size_t gt = blockIdx.x * (size_t)blockDim.x + threadIdx.x, nt = (size_t)gridDim.x * blockDim.x;
+        for (size_t i = gt; i < (size_t)ns * lines; i += nt) {
+            const int e = a.slot_expert[i / lines];
+            if (e < a.E) asm volatile("prefetch.global.L2 [%0];" ::"l"(a.down + e * dbytes + (i % lines) * 128));
+        }
+    }
     const size_t xs = xq_stride(D);
     const int groups = a.H / UP_R;
     const int units = *a.n_slots * groups;
@@ -134,12 +152,15 @@ __global__ void __launch_bounds__(256) expert_up_q(LayerArgs a, const unsigned c
             }
         }
     }
+    DTRACE_END(dc, 0)
 }
 
 // ---- down ------------------------------------------------------------------
 
-constexpr int DG = 8;  // output rows per warp
-constexpr int DOWN_Q_WARPS = 4;
+constexpr int DG = DOWN_TICKET_ROWS;  // output rows per warp (one ticket each)
+constexpr int DQ_WARPS = 16;  // warps per CTA
+constexpr int DQ_ROWS = DG * DQ_WARPS;  // output rows per CTA
+constexpr int DQ_TOK = 8;     // tokens whose quantised h is staged at once
 
 // 4 bytes at a 2-byte aligned shared-memory address.
 __device__ __forceinline__ uint32_t lds_u32_2(const uint8_t *p) {
@@ -148,103 +169,125 @@ __device__ __forceinline__ uint32_t lds_u32_2(const uint8_t *p) {
     return __funnelshift_r(b[0], b[1], (unsigned)(a & 3) * 8);
 }
 
-__global__ void __launch_bounds__(DOWN_Q_WARPS * 32) expert_down_q(LayerArgs a, int *__restrict__ tickets) {
+// Quantised h of one item (16 values: 4 quads x 4) of one token, as the
+// dp4a loop consumes it: int8 high / uint8 low planes, the element sum, and
+// the scale, per quad.
+struct HQuad { uint32_t hh, hl; int xs; float sq; };
+
+// One CTA per (slot, 64 output rows): stage the 64 Q6_K rows in shared memory
+// (read from L2: expert_up_q prefetched the routed experts' down rows),
+// quantise each token's h once per CTA (per 16-element Q6_K scale group),
+// then warp w computes rows 4w..4w+3 for every token of the slot.
+__global__ void __launch_bounds__(DQ_WARPS * 32) expert_down_q(LayerArgs a, int *__restrict__ tickets) {
     extern __shared__ __align__(16) uint8_t dsm[];
-    const int lane = threadIdx.x & 31, wib = threadIdx.x >> 5;
-    const int warp = blockIdx.x * DOWN_Q_WARPS + wib;
-    const int nwarps = gridDim.x * DOWN_Q_WARPS;
+    const int lane = threadIdx.x & 31, wib = threadIdx.x >> 5, tid = threadIdx.x;
     const int D = a.D, H = a.H, nbk = H / QK, items = nbk * 16, TK = a.T * a.K;
-    const int row_bytes = nbk * Q6K_BYTES, grp_bytes = DG * row_bytes;
+    const int row_bytes = nbk * Q6K_BYTES;
     const size_t exp_bytes = (size_t)row_bytes * D;
-    const int ngroups = D / DG;
+    const int nblk = D / DQ_ROWS;
+    DTRACE_START(dc, 1)
     pdl_trigger();
     if (a.has_shared) {
         const int gt = blockIdx.x * blockDim.x + threadIdx.x, nt = gridDim.x * blockDim.x;
         prefetch_l2(a.down_sh, exp_bytes, gt, nt);
     }
     pdl_wait();
+    DTRACE_WAITED(dc, 1)
+    uint8_t *slab = dsm;                                                        // [64][row_bytes]
+    HQuad *hq = reinterpret_cast<HQuad *>(dsm + DQ_ROWS * row_bytes + 16);     // [DQ_TOK][items][4]
     const int nslots = *a.n_slots;
-    const int units = nslots * ngroups;
-    uint8_t *st = dsm + (size_t)wib * (grp_bytes + 16);
-    for (int unit = warp; unit < units; unit += nwarps) {
-        const int u = unit / ngroups, g = unit - u * ngroups, n0 = g * DG;
+    const int units = nslots * nblk;
+    for (int unit = blockIdx.x; unit < units; unit += gridDim.x) {
+        const int u = unit / nblk, n0 = (unit - u * nblk) * DQ_ROWS;
         const int e = a.slot_expert[u];
         const uint8_t *src = (e == a.E ? a.down_sh : a.down + e * exp_bytes) + (size_t)n0 * row_bytes;
-        __syncwarp();
-        for (int i = lane; i < grp_bytes / 16; i += 32)
-            reinterpret_cast<uint4 *>(st)[i] = __ldg(reinterpret_cast<const uint4 *>(src) + i);
-        __syncwarp();
-        const int s1 = a.slot_start[u + 1];
-        for (int s = a.slot_start[u]; s < s1; s++) {
-            const int asg = a.assign[s];
-            const float *hrow = a.h + (size_t)asg * H;
-            float yp[DG];
+        __syncthreads();  // previous unit done with the slab and hq
+        for (int i = tid; i < DQ_ROWS * row_bytes / 16; i += DQ_WARPS * 32)
+            reinterpret_cast<uint4 *>(slab)[i] = __ldg(reinterpret_cast<const uint4 *>(src) + i);
+        const int s0 = a.slot_start[u], s1 = a.slot_start[u + 1];
+        for (int c0 = s0; c0 < s1; c0 += DQ_TOK) {
+            const int nc = min(DQ_TOK, s1 - c0);
+            if (c0 > s0) __syncthreads();  // previous chunk's hq consumed
+            // quantise h: thread p = (token, quad, item); the 4 items of a
+            // scale group are adjacent lanes
+            for (int p = tid; p < nc * 4 * items; p += DQ_WARPS * 32) {
+                const int tk = p / (4 * items), rem = p - tk * 4 * items, quad = rem / items, j = rem - quad * items;
+                const float *hrow = a.h + (size_t)a.assign[c0 + tk] * H;
+                const int b = j >> 4, half = (j >> 3) & 1, l0 = (j & 7) * 4;
+                const float4 hv = *reinterpret_cast<const float4 *>(hrow + b * QK + half * 128 + l0 + quad * 32);
+                float m = fmaxf(fmaxf(fabsf(hv.x), fabsf(hv.y)), fmaxf(fabsf(hv.z), fabsf(hv.w)));
+                m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 1));
+                m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 2));
+                const float sc = m / 32767.0f;
+                const float inv = (m > 0.f) ? 32767.0f / m : 0.f;
+                const int i0 = __float2int_rn(hv.x * inv), i1 = __float2int_rn(hv.y * inv);
+                const int i2 = __float2int_rn(hv.z * inv), i3 = __float2int_rn(hv.w * inv);
+                HQuad q;
+                q.hh = ((uint32_t)(i0 >> 8) & 0xFF) | (((uint32_t)(i1 >> 8) & 0xFF) << 8) |
+                       (((uint32_t)(i2 >> 8) & 0xFF) << 16) | (((uint32_t)(i3 >> 8) & 0xFF) << 24);
+                q.hl = (uint32_t)(i0 & 255) | ((uint32_t)(i1 & 255) << 8) | ((uint32_t)(i2 & 255) << 16) |
+                       ((uint32_t)(i3 & 255) << 24);
+                q.xs = i0 + i1 + i2 + i3;
+                q.sq = sc;
+                hq[(tk * items + j) * 4 + quad] = q;
+            }
+            __syncthreads();
+            for (int tk = 0; tk < nc; tk++) {
+                const int asg = a.assign[c0 + tk];
+                float yp[DG];
 #pragma unroll
-            for (int r = 0; r < DG; r++) yp[r] = 0.f;
-            for (int j0 = 0; j0 < items; j0 += 32) {
-                // all lanes run every iteration (the shuffles below need them)
-                const int j = j0 + lane;
-                const bool valid = j < items;
-                const int b = valid ? j >> 4 : 0, half = (j >> 3) & 1, l0 = (j & 7) * 4;
-                // the item's 16 h values (4 quads x 4), quantised per 16-element
-                // Q6_K scale group; the 4 lanes sharing a group exchange maxima
-                const float *hb = hrow + b * QK + half * 128 + l0;
-                uint32_t HH[4], HL[4];
-                int XS[4];
-                float sq[4];
+                for (int r = 0; r < DG; r++) yp[r] = 0.f;
+                for (int j = lane; j < items; j += 32) {
+                    const int b = j >> 4, half = (j >> 3) & 1, l0 = (j & 7) * 4;
+                    const HQuad *hp = hq + (tk * items + j) * 4;
+                    uint32_t HH[4], HL[4];
+                    int XS[4];
+                    float sq[4];
 #pragma unroll
-                for (int quad = 0; quad < 4; quad++) {
-                    const float4 hv = valid ? *reinterpret_cast<const float4 *>(hb + quad * 32)
-                                            : make_float4(0.f, 0.f, 0.f, 0.f);
-                    float m = fmaxf(fmaxf(fabsf(hv.x), fabsf(hv.y)), fmaxf(fabsf(hv.z), fabsf(hv.w)));
-                    m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 1));
-                    m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 2));
-                    const float sc = m / 32767.0f;
-                    const float inv = (m > 0.f) ? 32767.0f / m : 0.f;
-                    const int i0 = __float2int_rn(hv.x * inv), i1 = __float2int_rn(hv.y * inv);
-                    const int i2 = __float2int_rn(hv.z * inv), i3 = __float2int_rn(hv.w * inv);
-                    HH[quad] = ((uint32_t)(i0 >> 8) & 0xFF) | (((uint32_t)(i1 >> 8) & 0xFF) << 8) |
-                               (((uint32_t)(i2 >> 8) & 0xFF) << 16) | (((uint32_t)(i3 >> 8) & 0xFF) << 24);
-                    HL[quad] = (uint32_t)(i0 & 255) | ((uint32_t)(i1 & 255) << 8) |
-                               ((uint32_t)(i2 & 255) << 16) | ((uint32_t)(i3 & 255) << 24);
-                    XS[quad] = i0 + i1 + i2 + i3;
-                    sq[quad] = sc;
+                    for (int quad = 0; quad < 4; quad++) {
+                        const uint4 v = *reinterpret_cast<const uint4 *>(hp + quad);
+                        HH[quad] = v.x;
+                        HL[quad] = v.y;
+                        XS[quad] = (int)v.z;
+                        sq[quad] = __uint_as_float(v.w);
+                    }
+#pragma unroll
+                    for (int r = 0; r < DG; r++) {
+                        const uint8_t *blk = slab + (wib * DG + r) * row_bytes + b * Q6K_BYTES;
+                        const uint32_t W1 = lds_u32_2(blk + half * 64 + l0);
+                        const uint32_t W2 = lds_u32_2(blk + half * 64 + 32 + l0);
+                        const uint32_t Qh = lds_u32_2(blk + 128 + half * 32 + l0);
+                        const uint32_t SC0 = lds_u32_2(blk + 192 + half * 8);
+                        const uint32_t SC1 = lds_u32_2(blk + 192 + half * 8 + 4);
+                        const uint32_t DW = lds_u32_2(blk + 208);
+                        const uint32_t qv[4] = {
+                            (W1 & 0x0F0F0F0Fu) | ((Qh << 4) & 0x30303030u),
+                            (W2 & 0x0F0F0F0Fu) | ((Qh << 2) & 0x30303030u),
+                            ((W1 >> 4) & 0x0F0F0F0Fu) | (Qh & 0x30303030u),
+                            ((W2 >> 4) & 0x0F0F0F0Fu) | ((Qh >> 2) & 0x30303030u)};
+                        const int is = l0 >> 4;
+                        float acc = 0.f;
+#pragma unroll
+                        for (int quad = 0; quad < 4; quad++) {
+                            const int sidx = quad * 2 + is;  // scales[half*8 + 2*quad + is]
+                            const uint32_t scw = sidx < 4 ? SC0 : SC1;
+                            const int scale = (int)(int8_t)(scw >> (8 * (sidx & 3)));
+                            const int S = dp4a_s((int)qv[quad], (int)HH[quad], 0) * 256 +
+                                          dp4a_u(qv[quad], HL[quad], 0) - 32 * XS[quad];
+                            acc += (float)scale * sq[quad] * (float)S;
+                        }
+                        yp[r] += half_bits_ref(DW & 0xFFFFu) * acc;
+                    }
                 }
 #pragma unroll
                 for (int r = 0; r < DG; r++) {
-                    const uint8_t *blk = st + r * row_bytes + b * Q6K_BYTES;
-                    const uint32_t W1 = lds_u32_2(blk + half * 64 + l0);
-                    const uint32_t W2 = lds_u32_2(blk + half * 64 + 32 + l0);
-                    const uint32_t Qh = lds_u32_2(blk + 128 + half * 32 + l0);
-                    const uint32_t SC0 = lds_u32_2(blk + 192 + half * 8);
-                    const uint32_t SC1 = lds_u32_2(blk + 192 + half * 8 + 4);
-                    const uint32_t DW = lds_u32_2(blk + 208);
-                    const uint32_t qv[4] = {
-                        (W1 & 0x0F0F0F0Fu) | ((Qh << 4) & 0x30303030u),
-                        (W2 & 0x0F0F0F0Fu) | ((Qh << 2) & 0x30303030u),
-                        ((W1 >> 4) & 0x0F0F0F0Fu) | (Qh & 0x30303030u),
-                        ((W2 >> 4) & 0x0F0F0F0Fu) | ((Qh >> 2) & 0x30303030u)};
-                    const int is = l0 >> 4;
-                    float acc = 0.f;
-#pragma unroll
-                    for (int quad = 0; quad < 4; quad++) {
-                        const int sidx = quad * 2 + is;  // scales[half*8 + 2*quad + is]
-                        const uint32_t scw = sidx < 4 ? SC0 : SC1;
-                        const int scale = (int)(int8_t)(scw >> (8 * (sidx & 3)));
-                        const int S = dp4a_s((int)qv[quad], (int)HH[quad], 0) * 256 +
-                                      dp4a_u(qv[quad], HL[quad], 0) - 32 * XS[quad];
-                        acc += (float)scale * sq[quad] * (float)S;
-                    }
-                    if (valid) yp[r] += half_bits_ref(DW & 0xFFFFu) * acc;
+                    const float v = warp_sum(yp[r]);
+                    if (lane == 0) a.y[(size_t)asg * D + n0 + wib * DG + r] = v;
                 }
             }
-#pragma unroll
-            for (int r = 0; r < DG; r++) {
-                const float v = warp_sum(yp[r]);
-                if (lane == 0) a.y[(size_t)asg * D + n0 + r] = v;
-            }
         }
-        // the last slot to finish these 8 rows combines them
+        // the last slot to finish a group of 4 rows combines them
+        const int g = n0 / DG + wib;
         int last = 0;
         if (lane == 0) {
             __threadfence();
@@ -253,8 +296,9 @@ __global__ void __launch_bounds__(DOWN_Q_WARPS * 32) expert_down_q(LayerArgs a, 
         last = __shfl_sync(0xffffffffu, last, 0);
         if (last) {
             __threadfence();
+            const int m0 = n0 + wib * DG;
             for (int p = lane; p < a.T * DG; p += 32) {
-                const int t = p / DG, n = n0 + (p - t * DG);
+                const int t = p / DG, n = m0 + (p - t * DG);
                 const size_t o = (size_t)t * D + n;
                 float acc = a.resid ? a.resid[o] : 0.f;
                 if (a.has_shared) {
@@ -273,6 +317,7 @@ __global__ void __launch_bounds__(DOWN_Q_WARPS * 32) expert_down_q(LayerArgs a, 
             if (lane == 0) tickets[g] = 0;
         }
     }
+    DTRACE_END(dc, 1)
 }
 
 __global__ void quantize_x_kernel(const float *__restrict__ x, int D, unsigned char *__restrict__ xq) {
@@ -318,21 +363,21 @@ int launch_quantize_x(const float *x, int T, int D, unsigned char *xq, cudaStrea
 
 int launch_up_q(const LayerArgs &a, const unsigned char *xq, int max_slots, cudaStream_t s) {
     const uint64_t up_units = (uint64_t)max_slots * (a.H / UP_R);
-    cudaError_t e = launch_pdl(expert_up_q, dim3(grid_for(up_units, 8, sms() * 16)), dim3(256), 0, s, a, xq);
+    cudaError_t e = launch_pdl(expert_up_q, dim3(grid_for(up_units, 8, sms() * 32)), dim3(256), 0, s, a, xq);
     return e == cudaSuccess ? OFB_OK : cuda_status(e, "expert_up_q launch");
 }
 
 int launch_down_q(const LayerArgs &a, int *tickets, int max_slots, cudaStream_t s) {
     const int n = sms();
-    const size_t smem = (size_t)DOWN_Q_WARPS * (DG * (a.H / QK) * Q6K_BYTES + 16);
+    const size_t smem = (size_t)DQ_ROWS * (a.H / QK) * Q6K_BYTES + 16 + (size_t)DQ_TOK * (a.H / QK) * 16 * 4 * sizeof(HQuad);
     static size_t attr = 0;
     if (smem > 48 * 1024 && smem > attr) {
         cudaFuncSetAttribute(expert_down_q, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
         attr = smem;
     }
-    const uint64_t dn_units = (uint64_t)max_slots * (a.D / DG);
-    cudaError_t e = launch_pdl(expert_down_q, dim3(grid_for(dn_units, DOWN_Q_WARPS, n * 16)),
-                               dim3(DOWN_Q_WARPS * 32), smem, s, a, tickets);
+    const uint64_t dn_units = (uint64_t)max_slots * (a.D / DQ_ROWS);
+    const int grid = (int)(dn_units < (uint64_t)n * 4 ? dn_units : (uint64_t)n * 4);
+    cudaError_t e = launch_pdl(expert_down_q, dim3(grid), dim3(DQ_WARPS * 32), smem, s, a, tickets);
     return e == cudaSuccess ? OFB_OK : cuda_status(e, "expert_down_q launch");
 }
 

@@ -176,9 +176,9 @@ WorkspaceLayout workspace_layout(const ofb_moe_config *c, int max_tokens) {
     const size_t Tf = (size_t)(max_tokens < FAST_ROUTE_MAX_T ? max_tokens : FAST_ROUTE_MAX_T);
     L.cand = take(Tf * (E + 1) * 16);
     L.xq = take((Tf > Td ? Tf : Td) * xq_stride(c->d_model));
-    // route tickets [64] + [1], route stats [3], pad [1], down-combine tickets [D/8]
+    // route tickets [64] + [1], route stats [3], pad [1], down-combine tickets [D/4]
     // ... then the prefill error flag [1]
-    L.counters_bytes = (FAST_ROUTE_MAX_T + 4 + c->d_model / 8 + 1) * 4;
+    L.counters_bytes = (FAST_ROUTE_MAX_T + 4 + c->d_model / DOWN_TICKET_ROWS + 1) * 4;
     L.counters = take(L.counters_bytes);
     L.total = off;
     L.gemv_tokens = Td;
@@ -312,7 +312,7 @@ int run_moe_layer(const ofb_moe_config *cfg, const ofb_moe_weights *wt, const fl
                   L.prefill_tiles);
         return OFB_ETOOLARGE;
     }
-    int *err = (int *)(base + L.counters) + FAST_ROUTE_MAX_T + 4 + D / 8;
+    int *err = (int *)(base + L.counters) + FAST_ROUTE_MAX_T + 4 + D / DOWN_TICKET_ROWS;
     if ((st = launch_prefill(a, x, p.n_slots, (__nv_bfloat16 *)(base + L.xb), (__nv_bfloat16 *)(base + L.hb),
                              (int *)(base + L.tiles), err, s, ev ? ev[2] : nullptr, ev ? ev[3] : nullptr)))
         return st;

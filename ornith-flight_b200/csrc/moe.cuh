@@ -54,6 +54,8 @@ constexpr int FAST_ROUTE_MAX_T = 64;
 // Decode expert kernels (decode.cu): token and hidden-width limits.
 constexpr int MAX_DECODE_T = 32;
 constexpr int MAX_DECODE_H = 1024;
+// Output rows per completion ticket of the decode down kernel.
+constexpr int DOWN_TICKET_ROWS = 4;
 // Tensor-core prefill kernels: the down kernel holds 128 Q6_K rows in shared memory.
 constexpr int PREFILL_MAX_H = 512;
 // Batches the dp4a decode kernels take. Above 32 tokens the tensor-core

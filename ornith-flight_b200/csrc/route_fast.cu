@@ -47,10 +47,13 @@
 
 namespace ofb {
 
+DTRACE_DEFINE(rf)
+
 constexpr int RR_WARPS = 2;  // router rows per block in the row kernel
 constexpr int FR_WARPS = 8;
 constexpr int FR_THREADS = FR_WARPS * 32;
 constexpr double FR_MARGIN = 0x1.0p-14;
+constexpr int FW_PER_LANE = 8;  // warp top-k path: experts per lane (E <= 256)
 
 struct FastRouteArgs {
     const float *W, *x, *gate_v;
@@ -111,6 +114,7 @@ __device__ __forceinline__ void quantize_subblock(float v, unsigned char *q, int
 
 // ---- kernel 1: router rows ---------------------------------------------------
 __global__ void __launch_bounds__(RR_WARPS * 32) route_rows_kernel(FastRouteArgs a) {
+    DTRACE_START(rf, 0)
     pdl_trigger();
     const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
     const int t = blockIdx.y;
@@ -131,6 +135,7 @@ __global__ void __launch_bounds__(RR_WARPS * 32) route_rows_kernel(FastRouteArgs
             if (j < seg / 4) wv[j] = __ldg(w4 + j);
     }
     pdl_wait();
+    DTRACE_WAITED(rf, 0)
     if (has_row) {
 #pragma unroll
         for (int j = 0; j < PF; j++)
@@ -141,7 +146,10 @@ __global__ void __launch_bounds__(RR_WARPS * 32) route_rows_kernel(FastRouteArgs
         for (int sb = r; sb < D / 32; sb += gridDim.x * RR_WARPS)
             quantize_subblock(__ldg(xt + sb * 32 + lane), q, D, sb, lane);
     }
-    if (!has_row) return;
+    if (!has_row) {
+        DTRACE_END(rf, 0)
+        return;
+    }
     double P = 0.0, SP = 0.0, A = 0.0;
     for (int i0 = 0; i0 < seg / 4; i0 += PF) {
         if (i0) {
@@ -178,6 +186,7 @@ __global__ void __launch_bounds__(RR_WARPS * 32) route_rows_kernel(FastRouteArgs
         else
             a.gsc[t] = 1.0f / (1.0f + expf(-(float)L));
     }
+    DTRACE_END(rf, 0)
 }
 
 // ---- kernel 2: selection, one block per token ---------------------------------
@@ -212,6 +221,7 @@ __device__ __forceinline__ float block_sum(float v, float *red) {
 }
 
 __global__ void __launch_bounds__(FR_THREADS) route_select_fast(FastRouteArgs a) {
+    DTRACE_START(rf, 1)
     pdl_trigger();
     const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5, tid = threadIdx.x;
     const int t = blockIdx.x;
@@ -236,7 +246,137 @@ __global__ void __launch_bounds__(FR_THREADS) route_select_fast(FastRouteArgs a)
     __shared__ int s_last;
 
     pdl_wait();
+    DTRACE_WAITED(rf, 1)
     const double2 *cd = a.cand + (size_t)t * E;
+    if (E <= 32 * FW_PER_LANE) {
+        // ---- warp 0: top-k, certificate and (when certified) weights from
+        // registers; the block steps below run only for uncertain tokens
+        if (wid == 0) {
+            double L[FW_PER_LANE], B[FW_PER_LANE];
+            bool top[FW_PER_LANE];
+#pragma unroll
+            for (int j = 0; j < FW_PER_LANE; j++) {
+                const int e = lane + 32 * j;
+                top[j] = false;
+                if (e < E) {
+                    const double2 v = cd[e];
+                    L[j] = v.x;
+                    B[j] = v.y;
+                    Ls[e] = v.x;
+                    Bs[e] = v.y;
+                } else {
+                    L[j] = -INFINITY;
+                    B[j] = 0.0;
+                }
+            }
+            DTRACE_MARK(rf, 1, 3)
+            // top K by float(L~) (ties by index): K rounds of a warp argmax
+            // on order-preserving 32-bit keys. A mis-order between logits
+            // that round to the same float cannot pass the certificate,
+            // which checks every adjacent gap on the double values.
+            uint32_t key[FW_PER_LANE];
+#pragma unroll
+            for (int j = 0; j < FW_PER_LANE; j++) {
+                const uint32_t u = __float_as_uint((float)L[j]);
+                key[j] = (lane + 32 * j < E) ? ((u & 0x80000000u) ? ~u : (u | 0x80000000u)) : 0u;
+            }
+            for (int q = 0; q < K; q++) {
+                uint32_t lb = 0;
+                int le = 0x7fffffff;
+#pragma unroll
+                for (int j = 0; j < FW_PER_LANE; j++)
+                    if (!top[j] && key[j] > lb) {  // strict: the smallest index wins a tie
+                        lb = key[j];
+                        le = lane + 32 * j;
+                    }
+                const uint32_t wb = __reduce_max_sync(0xffffffffu, lb);
+                const int bi = (int)__reduce_min_sync(0xffffffffu, lb == wb ? (uint32_t)le : 0x7fffffffu);
+#pragma unroll
+                for (int j = 0; j < FW_PER_LANE; j++)
+                    if (lane + 32 * j == bi) top[j] = true;
+                if (lane == 0) s_top[q] = bi;
+            }
+            DTRACE_MARK(rf, 1, 4)
+            // certificate: adjacent gaps in the top-k, the last against the rest
+            double hi_rest = -INFINITY;
+#pragma unroll
+            for (int j = 0; j < FW_PER_LANE; j++)
+                if (lane + 32 * j < E && !top[j]) hi_rest = fmax(hi_rest, L[j] + B[j]);
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) hi_rest = fmax(hi_rest, __shfl_xor_sync(0xffffffffu, hi_rest, o));
+            __syncwarp();
+            bool ok = true;
+            if (lane < K) {
+                const int e0 = s_top[lane];
+                const double nxt = lane + 1 < K ? Ls[s_top[lane + 1]] + Bs[s_top[lane + 1]] : hi_rest;
+                ok = Ls[e0] - Bs[e0] > nxt + FR_MARGIN;
+                if (lane == K - 1) ok = ok && (Ls[e0] - Ls[s_top[0]] > -80.0);
+            }
+            ok = __all_sync(0xffffffffu, ok);
+            if (lane == 0) s_mode = ok ? 0 : 1;
+            DTRACE_MARK(rf, 1, 5)
+            if (ok) {
+                // weights: fp32 softmax of L~ (model.c:1027-1049 / :300-316 forms)
+                const float m = (float)Ls[s_top[0]];
+                float sum = 0.f;
+                if (a.routing == OFB_ROUTE_FORWARD) {
+#pragma unroll
+                    for (int j = 0; j < FW_PER_LANE; j++)
+                        if (lane + 32 * j < E) sum += expf((float)L[j] - m);
+                } else if (lane < K) {
+                    sum = expf((float)Ls[s_top[lane]] - m);
+                }
+                sum = warp_sum(sum);
+                if (lane < K) s_w[lane] = expf((float)Ls[s_top[lane]] - m) / sum;
+                __syncwarp();
+                uint32_t *io = a.idx + (size_t)t * K;
+                float *wo = a.w + (size_t)t * K;
+                float wq = 0.f;
+                int eq = 0;
+                if (lane < K) {
+                    float ss = 0.f;
+                    for (int q = 0; q < K; q++) ss += s_w[q];
+                    eq = s_top[lane];
+                    wq = (a.routing == OFB_ROUTE_FORWARD && a.renorm) ? s_w[lane] / ss : s_w[lane];
+                    io[lane] = (uint32_t)eq;
+                    wo[lane] = wq;
+                }
+                if (lane == 0 && a.stats) atomicAdd(&a.stats[0], 1);
+                if (a.T == 1 && a.plan.n_slots) {
+                    // the dispatch plan of one token (what build_plan makes):
+                    // kept experts in ascending id order, then the shared slot
+                    const bool kept = lane < K && !(wq < 1e-6f);
+                    const unsigned km = __ballot_sync(0xffffffffu, kept);
+                    int rank = 0;
+                    for (int q = 0; q < K; q++) rank += ((km >> q) & 1) && s_top[q] < eq;
+                    const PlanArgs &p = a.plan;
+                    if (kept) {
+                        p.slot_expert[rank] = eq;
+                        p.slot_start[rank] = rank;
+                        p.assign[rank] = lane;
+                    }
+                    if (lane == 0) {
+                        const int nk = __popc(km);
+                        if (p.has_shared) {
+                            p.slot_expert[nk] = E;
+                            p.slot_start[nk] = nk;
+                            p.slot_start[nk + 1] = nk + 1;
+                            p.assign[nk] = K;
+                            *p.n_slots = nk + 1;
+                        } else {
+                            p.slot_start[nk] = nk;
+                            *p.n_slots = nk;
+                        }
+                    }
+                }
+            }
+        }
+        __syncthreads();
+        if (s_mode == 0 && a.T == 1) {
+            DTRACE_END(rf, 1)
+            return;
+        }
+    } else {
     for (int e = tid; e < E; e += FR_THREADS) {
         const double2 v = cd[e];
         Ls[e] = v.x;
@@ -289,6 +429,8 @@ __global__ void __launch_bounds__(FR_THREADS) route_select_fast(FastRouteArgs a)
         if (!ok) s_mode = 1;
     }
     __syncthreads();
+    }
+    const bool warp_done = (E <= 32 * FW_PER_LANE) && s_mode == 0;  // weights already written
 
     if (s_mode != 0) {
         // ---- candidate recompute with the reference's exact chain --------
@@ -363,7 +505,9 @@ __global__ void __launch_bounds__(FR_THREADS) route_select_fast(FastRouteArgs a)
     // ---- weights --------------------------------------------------------------
     uint32_t *io = a.idx + (size_t)t * K;
     float *wo = a.w + (size_t)t * K;
-    if (s_mode == 2) {
+    if (warp_done) {
+        // written by warp 0 above
+    } else if (s_mode == 2) {
         // bit-exact: val holds the reference's probabilities, id the order
         if (tid == 0) {
             float ssum = 0.0f;
@@ -391,7 +535,7 @@ __global__ void __launch_bounds__(FR_THREADS) route_select_fast(FastRouteArgs a)
             wo[tid] = (a.routing == OFB_ROUTE_FORWARD && a.renorm) ? s_w[tid] / ss : s_w[tid];
         }
     }
-    if (tid == 0 && a.stats) atomicAdd(&a.stats[s_mode], 1);
+    if (tid == 0 && a.stats && !warp_done) atomicAdd(&a.stats[s_mode], 1);
 
     // ---- the block finishing the last token builds the dispatch plan --------
     if (a.T == 1) {
@@ -404,13 +548,17 @@ __global__ void __launch_bounds__(FR_THREADS) route_select_fast(FastRouteArgs a)
         }
     }
     __syncthreads();
-    if (!s_last) return;
+    if (!s_last) {
+        DTRACE_END(rf, 1)
+        return;
+    }
     if (a.T > 1) __threadfence();
     int *cnt = reinterpret_cast<int *>(smem);
     int *cursor = cnt + 1024;
     __shared__ int wsum[66];
     if (a.plan.n_slots) build_plan(a.plan, cnt, cursor, wsum);
     if (tid == 0) *a.all_cnt = 0;
+    DTRACE_END(rf, 1)
 }
 
 size_t route_fast_smem(int E, int D) {
