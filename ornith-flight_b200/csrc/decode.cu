@@ -205,6 +205,7 @@ __global__ void __launch_bounds__(DQ_WARPS * 32) expert_down_q(LayerArgs a, int 
         for (int i = tid; i < DQ_ROWS * row_bytes / 16; i += DQ_WARPS * 32)
             reinterpret_cast<uint4 *>(slab)[i] = __ldg(reinterpret_cast<const uint4 *>(src) + i);
         const int s0 = a.slot_start[u], s1 = a.slot_start[u + 1];
+        DTRACE_MARK(dc, 1, 3)
         for (int c0 = s0; c0 < s1; c0 += DQ_TOK) {
             const int nc = min(DQ_TOK, s1 - c0);
             if (c0 > s0) __syncthreads();  // previous chunk's hq consumed
@@ -232,6 +233,7 @@ __global__ void __launch_bounds__(DQ_WARPS * 32) expert_down_q(LayerArgs a, int 
                 hq[(tk * items + j) * 4 + quad] = q;
             }
             __syncthreads();
+            DTRACE_MARK(dc, 1, 4)
             for (int tk = 0; tk < nc; tk++) {
                 const int asg = a.assign[c0 + tk];
                 float yp[DG];
@@ -286,6 +288,7 @@ __global__ void __launch_bounds__(DQ_WARPS * 32) expert_down_q(LayerArgs a, int 
                 }
             }
         }
+        DTRACE_MARK(dc, 1, 5)
         // the last slot to finish a group of 4 rows combines them
         const int g = n0 / DG + wib;
         int last = 0;

@@ -174,7 +174,10 @@ WorkspaceLayout workspace_layout(const ofb_moe_config *c, int max_tokens) {
     L.hb = take(prefill ? A * (size_t)c->hidden * 2 : 0);
     L.tiles = take(prefill ? (1 + 3 * (size_t)prefill_max_tiles(max_tokens, K, E)) * 4 : 0);
     const size_t Tf = (size_t)(max_tokens < FAST_ROUTE_MAX_T ? max_tokens : FAST_ROUTE_MAX_T);
-    L.cand = take(Tf * (E + 1) * 16);
+    // certified routing holds (L~, B) per (token, expert): every token on the
+    // contiguous layout (the large-batch router too), else the decode sizes
+    L.cand = take((inter ? Tf : T) * (E + 1) * 16);
+    L.norms = take(inter ? 0 : (T + E) * (size_t)(c->d_model / 64) * 4);
     L.xq = take((Tf > Td ? Tf : Td) * xq_stride(c->d_model));
     // route tickets [64] + [1], route stats [3], pad [1], down-combine tickets [D/4]
     // ... then the prefill error flag [1]
@@ -245,6 +248,20 @@ int run_moe_layer(const ofb_moe_config *cfg, const ofb_moe_weights *wt, const fl
                                     &p, s)))
             return st;
         mark(1);
+        mark(2);
+    } else if (!given_idx && wt->router && cfg->layout == OFB_LAYOUT_CONTIGUOUS && E <= 256) {
+        // large batches: certified routing from a bounded fp32 GEMM; the last
+        // selection block builds the plan
+        int *ctr = (int *)(base + L.counters);
+        if ((st = launch_route_fast_large(wt->router, x, T, D, E, K, cfg->routing, cfg->renorm,
+                                          (double2 *)(base + L.cand), (float *)(base + L.norms),
+                                          (int *)(base + L.logits), ctr, ctr + FAST_ROUTE_MAX_T + 1, idx, w, s)))
+            return st;
+        mark(1);
+        plan_kernel<<<1, 1024, 0, s>>>(p);
+        if (p.has_shared && p.shared_gate)
+            shared_gate_kernel<<<(T + 7) / 8, 256, 0, s>>>(x, p.gate_v, T, D, p.gsc);
+        OFB_CHECK_LAUNCH("plan");
         mark(2);
     } else {
         if (given_idx) {

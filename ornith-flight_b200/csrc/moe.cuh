@@ -36,6 +36,7 @@ struct LayerArgs {
 struct WorkspaceLayout {
     size_t logits, idx, w, gsc, n_slots, slot_expert, slot_start, assign, h, y;
     size_t cand;      // fast routing: (approximate logit, bound) per (token, row)
+    size_t norms;     // large-batch routing: segment norms of x rows and router rows
     size_t xq;        // decode: quantised activations [T][xq_stride(D)]
     size_t xb, hb;    // prefill: bf16 x rows [A][D] and h rows [A][H], both in slot order
     size_t tiles;     // prefill: tile count + (slot, start, n) per tile
@@ -74,6 +75,13 @@ int launch_prefill(const LayerArgs &la, const float *x, int *n_slots, __nv_bfloa
 int launch_up_q(const LayerArgs &a, const unsigned char *xq, int max_slots, cudaStream_t s);
 int launch_down_q(const LayerArgs &a, int *tickets, int max_slots, cudaStream_t s);
 
+// Certified routing for batches above FAST_ROUTE_MAX_T: fp32 GEMM logits with
+// rigorous bounds, the same per-token certificate (one warp per token), exact
+// fallback for the tokens it leaves (flagged list, T ints; *n_flagged is
+// scratch). norms: scratch of (T + E) * d_model / 64 floats.
+int launch_route_fast_large(const float *W, const float *x, int T, int D, int E, int K, int routing, int renorm,
+                            double2 *cand, float *norms, int *flagged, int *n_flagged, int *stats, uint32_t *idx,
+                            float *w, cudaStream_t s);
 int launch_route_fast(const float *W, const float *x, const float *gate_v, int T, int D, int E, int K,
                       int routing, int renorm, double2 *cand, int *all_cnt, int *stats,
                       uint32_t *idx, float *w, float *gsc, unsigned char *xq, const PlanArgs *plan,

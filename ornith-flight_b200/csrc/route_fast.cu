@@ -67,6 +67,8 @@ struct FastRouteArgs {
     float *w, *gsc;
     unsigned char *xq;  // [T][xq_stride(D)] quantised activations, or NULL
     PlanArgs plan;
+    const int *flagged;    // large batches: tokens the warp certificate left (or NULL)
+    const int *n_flagged;
 };
 
 __device__ __forceinline__ double warp_sum_d(double v) {
@@ -76,16 +78,31 @@ __device__ __forceinline__ double warp_sum_d(double v) {
 }
 
 // Reference-order logit: sequential fp32, product then add, d = 0..D-1.
+// The router row streams through registers in 64-element chunks, the next
+// chunk loading while the chain runs over the current one (the 2048-step
+// add chain is the latency floor).
 __device__ float exact_logit(const float *wrow, const float *xs, int D) {
-    float s = 0.0f;
+    constexpr int C = 16;  // float4 per chunk
     const float4 *w4 = reinterpret_cast<const float4 *>(wrow);
-#pragma unroll 4
-    for (int i = 0; i < D / 4; i++) {
-        float4 w = __ldg(w4 + i);
-        s = __fadd_rn(s, __fmul_rn(xs[4 * i + 0], w.x));
-        s = __fadd_rn(s, __fmul_rn(xs[4 * i + 1], w.y));
-        s = __fadd_rn(s, __fmul_rn(xs[4 * i + 2], w.z));
-        s = __fadd_rn(s, __fmul_rn(xs[4 * i + 3], w.w));
+    float4 cur[C], nxt[C];
+#pragma unroll
+    for (int j = 0; j < C; j++) cur[j] = __ldg(w4 + j);
+    float s = 0.0f;
+    for (int c0 = 0; c0 < D / 4; c0 += C) {
+        if (c0 + C < D / 4) {
+#pragma unroll
+            for (int j = 0; j < C; j++) nxt[j] = __ldg(w4 + c0 + C + j);
+        }
+#pragma unroll
+        for (int j = 0; j < C; j++) {
+            const float4 x4 = *reinterpret_cast<const float4 *>(xs + 4 * (c0 + j));
+            s = __fadd_rn(s, __fmul_rn(x4.x, cur[j].x));
+            s = __fadd_rn(s, __fmul_rn(x4.y, cur[j].y));
+            s = __fadd_rn(s, __fmul_rn(x4.z, cur[j].z));
+            s = __fadd_rn(s, __fmul_rn(x4.w, cur[j].w));
+        }
+#pragma unroll
+        for (int j = 0; j < C; j++) cur[j] = nxt[j];
     }
     return s;
 }
@@ -220,13 +237,150 @@ __device__ __forceinline__ float block_sum(float v, float *red) {
     return r;
 }
 
+// Per-warp scratch of the certified selection (top_k <= 16).
+struct WarpSel { int top[16]; double L[16], B[16]; float w[16]; };
+
+// Certified top-k of token t by one warp (E <= 32 * FW_PER_LANE): K rounds of
+// a warp argmax on order-preserving 32-bit keys of float(L~) (a mis-order
+// between logits that round to the same float cannot pass the certificate,
+// which checks every adjacent gap on the double values), then the
+// certificate, then - when it holds - the weights (fp32 softmax of L~,
+// model.c:1027-1049 / :300-316 forms) written to idx / w. Ls / Bs, when
+// given, receive every (L~, B) of the token for a block fallback.
+__device__ bool certify_token_warp(const FastRouteArgs &a, int t, WarpSel &ws, double *Ls, double *Bs) {
+    const int lane = threadIdx.x & 31, E = a.E, K = a.K;
+    const double2 *cd = a.cand + (size_t)t * E;
+    double L[FW_PER_LANE], B[FW_PER_LANE];
+    uint32_t key[FW_PER_LANE];
+    bool top[FW_PER_LANE];
+#pragma unroll
+    for (int j = 0; j < FW_PER_LANE; j++) {
+        const int e = lane + 32 * j;
+        top[j] = false;
+        L[j] = -INFINITY;
+        B[j] = 0.0;
+        if (e < E) {
+            const double2 v = cd[e];
+            L[j] = v.x;
+            B[j] = v.y;
+            if (Ls) {
+                Ls[e] = v.x;
+                Bs[e] = v.y;
+            }
+        }
+        const uint32_t u = __float_as_uint((float)L[j]);
+        key[j] = (e < E) ? ((u & 0x80000000u) ? ~u : (u | 0x80000000u)) : 0u;
+    }
+    for (int q = 0; q < K; q++) {
+        uint32_t lb = 0;
+        int le = 0x7fffffff;
+#pragma unroll
+        for (int j = 0; j < FW_PER_LANE; j++)
+            if (!top[j] && key[j] > lb) {  // strict: the smallest index wins a tie
+                lb = key[j];
+                le = lane + 32 * j;
+            }
+        const uint32_t wb = __reduce_max_sync(0xffffffffu, lb);
+        const int bi = (int)__reduce_min_sync(0xffffffffu, lb == wb ? (uint32_t)le : 0x7fffffffu);
+#pragma unroll
+        for (int j = 0; j < FW_PER_LANE; j++)
+            if (lane + 32 * j == bi) {
+                top[j] = true;
+                ws.L[q] = L[j];
+                ws.B[q] = B[j];
+            }
+        if (lane == 0) ws.top[q] = bi;
+    }
+    // certificate: adjacent gaps in the top-k, the last against the rest
+    double hi_rest = -INFINITY;
+#pragma unroll
+    for (int j = 0; j < FW_PER_LANE; j++)
+        if (lane + 32 * j < E && !top[j]) hi_rest = fmax(hi_rest, L[j] + B[j]);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) hi_rest = fmax(hi_rest, __shfl_xor_sync(0xffffffffu, hi_rest, o));
+    __syncwarp();
+    bool ok = true;
+    if (lane < K) {
+        const double nxt = lane + 1 < K ? ws.L[lane + 1] + ws.B[lane + 1] : hi_rest;
+        ok = ws.L[lane] - ws.B[lane] > nxt + FR_MARGIN;
+        if (lane == K - 1) ok = ok && (ws.L[lane] - ws.L[0] > -80.0);
+    }
+    ok = __all_sync(0xffffffffu, ok);
+    if (!ok) return false;
+    const float m = (float)ws.L[0];
+    float sum = 0.f;
+    if (a.routing == OFB_ROUTE_FORWARD) {
+#pragma unroll
+        for (int j = 0; j < FW_PER_LANE; j++)
+            if (lane + 32 * j < E) sum += expf((float)L[j] - m);
+    } else if (lane < K) {
+        sum = expf((float)ws.L[lane] - m);
+    }
+    sum = warp_sum(sum);
+    float wq = 0.f;
+    if (lane < K) wq = expf((float)ws.L[lane] - m) / sum;
+    if (lane < K) ws.w[lane] = wq;
+    __syncwarp();
+    if (lane < K) {
+        float ss = 0.f;
+        for (int q = 0; q < K; q++) ss += ws.w[q];
+        if (a.routing == OFB_ROUTE_FORWARD && a.renorm) wq = wq / ss;
+        a.idx[(size_t)t * K + lane] = (uint32_t)ws.top[lane];
+        a.w[(size_t)t * K + lane] = wq;
+    }
+    __syncwarp();
+    if (lane < K) ws.w[lane] = wq;
+    if (lane == 0 && a.stats) atomicAdd(&a.stats[0], 1);
+    __syncwarp();
+    return true;
+}
+
+// The dispatch plan of one token (what build_plan makes for T = 1): kept
+// experts in ascending id order, then the shared slot. One warp.
+__device__ void one_token_plan(const FastRouteArgs &a, const WarpSel &ws) {
+    const int lane = threadIdx.x & 31, K = a.K;
+    const bool kept = lane < K && !(ws.w[lane] < 1e-6f);
+    const unsigned km = __ballot_sync(0xffffffffu, kept);
+    const int eq = lane < K ? ws.top[lane] : 0;
+    int rank = 0;
+    for (int q = 0; q < K; q++) rank += ((km >> q) & 1) && ws.top[q] < eq;
+    const PlanArgs &p = a.plan;
+    if (kept) {
+        p.slot_expert[rank] = eq;
+        p.slot_start[rank] = rank;
+        p.assign[rank] = lane;
+    }
+    if (lane == 0) {
+        const int nk = __popc(km);
+        if (p.has_shared) {
+            p.slot_expert[nk] = a.E;
+            p.slot_start[nk] = nk;
+            p.slot_start[nk + 1] = nk + 1;
+            p.assign[nk] = K;
+            *p.n_slots = nk + 1;
+        } else {
+            p.slot_start[nk] = nk;
+            *p.n_slots = nk;
+        }
+    }
+}
+
+// Large batches: one warp per token; tokens whose certificate fails go to the
+// flagged list for the block fallback (route_select_fast in list mode).
+__global__ void __launch_bounds__(256) route_certify_warps(FastRouteArgs a, int *flagged, int *n_flagged) {
+    __shared__ WarpSel sel[8];
+    const int wid = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int t = blockIdx.x * 8 + wid;
+    if (t >= a.T) return;
+    const bool ok = certify_token_warp(a, t, sel[wid], nullptr, nullptr);
+    if (!ok && lane == 0) flagged[atomicAdd(n_flagged, 1)] = t;
+}
+
 __global__ void __launch_bounds__(FR_THREADS) route_select_fast(FastRouteArgs a) {
     DTRACE_START(rf, 1)
     pdl_trigger();
     const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5, tid = threadIdx.x;
-    const int t = blockIdx.x;
     const int E = a.E, D = a.D, K = a.K;
-    const float *xt = a.x + (size_t)t * D;
 
     extern __shared__ __align__(16) unsigned char smem[];
     double *Ls = reinterpret_cast<double *>(smem);     // [E]
@@ -244,132 +398,26 @@ __global__ void __launch_bounds__(FR_THREADS) route_select_fast(FastRouteArgs a)
     __shared__ double s_hred[FR_WARPS];
     __shared__ float s_w[16];
     __shared__ int s_last;
+    __shared__ WarpSel sel;
+    __shared__ int s_clist[FW_PER_LANE * 32 * 4];  // candidate experts of a fallback
+    __shared__ int s_nc;
 
     pdl_wait();
     DTRACE_WAITED(rf, 1)
+    // one token per block, or (list mode, large batches) every flagged token
+    const int n_tok = a.flagged ? *a.n_flagged : 1;
+    for (int it = a.flagged ? blockIdx.x : 0; it < n_tok; it += a.flagged ? gridDim.x : 1) {
+    const int t = a.flagged ? a.flagged[it] : blockIdx.x;
+    const float *xt = a.x + (size_t)t * D;
     const double2 *cd = a.cand + (size_t)t * E;
-    if (E <= 32 * FW_PER_LANE) {
+    if (E <= 32 * FW_PER_LANE && !a.flagged) {
         // ---- warp 0: top-k, certificate and (when certified) weights from
         // registers; the block steps below run only for uncertain tokens
         if (wid == 0) {
-            double L[FW_PER_LANE], B[FW_PER_LANE];
-            bool top[FW_PER_LANE];
-#pragma unroll
-            for (int j = 0; j < FW_PER_LANE; j++) {
-                const int e = lane + 32 * j;
-                top[j] = false;
-                if (e < E) {
-                    const double2 v = cd[e];
-                    L[j] = v.x;
-                    B[j] = v.y;
-                    Ls[e] = v.x;
-                    Bs[e] = v.y;
-                } else {
-                    L[j] = -INFINITY;
-                    B[j] = 0.0;
-                }
-            }
-            DTRACE_MARK(rf, 1, 3)
-            // top K by float(L~) (ties by index): K rounds of a warp argmax
-            // on order-preserving 32-bit keys. A mis-order between logits
-            // that round to the same float cannot pass the certificate,
-            // which checks every adjacent gap on the double values.
-            uint32_t key[FW_PER_LANE];
-#pragma unroll
-            for (int j = 0; j < FW_PER_LANE; j++) {
-                const uint32_t u = __float_as_uint((float)L[j]);
-                key[j] = (lane + 32 * j < E) ? ((u & 0x80000000u) ? ~u : (u | 0x80000000u)) : 0u;
-            }
-            for (int q = 0; q < K; q++) {
-                uint32_t lb = 0;
-                int le = 0x7fffffff;
-#pragma unroll
-                for (int j = 0; j < FW_PER_LANE; j++)
-                    if (!top[j] && key[j] > lb) {  // strict: the smallest index wins a tie
-                        lb = key[j];
-                        le = lane + 32 * j;
-                    }
-                const uint32_t wb = __reduce_max_sync(0xffffffffu, lb);
-                const int bi = (int)__reduce_min_sync(0xffffffffu, lb == wb ? (uint32_t)le : 0x7fffffffu);
-#pragma unroll
-                for (int j = 0; j < FW_PER_LANE; j++)
-                    if (lane + 32 * j == bi) top[j] = true;
-                if (lane == 0) s_top[q] = bi;
-            }
-            DTRACE_MARK(rf, 1, 4)
-            // certificate: adjacent gaps in the top-k, the last against the rest
-            double hi_rest = -INFINITY;
-#pragma unroll
-            for (int j = 0; j < FW_PER_LANE; j++)
-                if (lane + 32 * j < E && !top[j]) hi_rest = fmax(hi_rest, L[j] + B[j]);
-#pragma unroll
-            for (int o = 16; o > 0; o >>= 1) hi_rest = fmax(hi_rest, __shfl_xor_sync(0xffffffffu, hi_rest, o));
-            __syncwarp();
-            bool ok = true;
-            if (lane < K) {
-                const int e0 = s_top[lane];
-                const double nxt = lane + 1 < K ? Ls[s_top[lane + 1]] + Bs[s_top[lane + 1]] : hi_rest;
-                ok = Ls[e0] - Bs[e0] > nxt + FR_MARGIN;
-                if (lane == K - 1) ok = ok && (Ls[e0] - Ls[s_top[0]] > -80.0);
-            }
-            ok = __all_sync(0xffffffffu, ok);
+            const bool ok = certify_token_warp(a, t, sel, Ls, Bs);
             if (lane == 0) s_mode = ok ? 0 : 1;
-            DTRACE_MARK(rf, 1, 5)
-            if (ok) {
-                // weights: fp32 softmax of L~ (model.c:1027-1049 / :300-316 forms)
-                const float m = (float)Ls[s_top[0]];
-                float sum = 0.f;
-                if (a.routing == OFB_ROUTE_FORWARD) {
-#pragma unroll
-                    for (int j = 0; j < FW_PER_LANE; j++)
-                        if (lane + 32 * j < E) sum += expf((float)L[j] - m);
-                } else if (lane < K) {
-                    sum = expf((float)Ls[s_top[lane]] - m);
-                }
-                sum = warp_sum(sum);
-                if (lane < K) s_w[lane] = expf((float)Ls[s_top[lane]] - m) / sum;
-                __syncwarp();
-                uint32_t *io = a.idx + (size_t)t * K;
-                float *wo = a.w + (size_t)t * K;
-                float wq = 0.f;
-                int eq = 0;
-                if (lane < K) {
-                    float ss = 0.f;
-                    for (int q = 0; q < K; q++) ss += s_w[q];
-                    eq = s_top[lane];
-                    wq = (a.routing == OFB_ROUTE_FORWARD && a.renorm) ? s_w[lane] / ss : s_w[lane];
-                    io[lane] = (uint32_t)eq;
-                    wo[lane] = wq;
-                }
-                if (lane == 0 && a.stats) atomicAdd(&a.stats[0], 1);
-                if (a.T == 1 && a.plan.n_slots) {
-                    // the dispatch plan of one token (what build_plan makes):
-                    // kept experts in ascending id order, then the shared slot
-                    const bool kept = lane < K && !(wq < 1e-6f);
-                    const unsigned km = __ballot_sync(0xffffffffu, kept);
-                    int rank = 0;
-                    for (int q = 0; q < K; q++) rank += ((km >> q) & 1) && s_top[q] < eq;
-                    const PlanArgs &p = a.plan;
-                    if (kept) {
-                        p.slot_expert[rank] = eq;
-                        p.slot_start[rank] = rank;
-                        p.assign[rank] = lane;
-                    }
-                    if (lane == 0) {
-                        const int nk = __popc(km);
-                        if (p.has_shared) {
-                            p.slot_expert[nk] = E;
-                            p.slot_start[nk] = nk;
-                            p.slot_start[nk + 1] = nk + 1;
-                            p.assign[nk] = K;
-                            *p.n_slots = nk + 1;
-                        } else {
-                            p.slot_start[nk] = nk;
-                            *p.n_slots = nk;
-                        }
-                    }
-                }
-            }
+            if (lane < K) s_top[lane] = sel.top[lane];
+            if (ok && a.T == 1 && a.plan.n_slots) one_token_plan(a, sel);
         }
         __syncthreads();
         if (s_mode == 0 && a.T == 1) {
@@ -430,7 +478,7 @@ __global__ void __launch_bounds__(FR_THREADS) route_select_fast(FastRouteArgs a)
     }
     __syncthreads();
     }
-    const bool warp_done = (E <= 32 * FW_PER_LANE) && s_mode == 0;  // weights already written
+    const bool warp_done = (E <= 32 * FW_PER_LANE) && !a.flagged && s_mode == 0;  // weights already written
 
     if (s_mode != 0) {
         // ---- candidate recompute with the reference's exact chain --------
@@ -438,11 +486,22 @@ __global__ void __launch_bounds__(FR_THREADS) route_select_fast(FastRouteArgs a)
         double lo_min = INFINITY;
         for (int q = 0; q < K; q++) lo_min = fmin(lo_min, Ls[s_top[q]] - Bs[s_top[q]]);
         __syncthreads();
+        // candidates into a compact list, so that their exact chains occupy
+        // the first threads (one warp for up to 32) instead of every warp
+        if (tid == 0) s_nc = 0;
+        __syncthreads();
         for (int e = tid; e < E; e += FR_THREADS) {
             const bool cand = (Ls[e] + Bs[e] >= lo_min - FR_MARGIN);
-            val[e] = cand ? exact_logit(a.W + (size_t)e * D, xs, D) : -INFINITY;
+            val[e] = -INFINITY;
             id[e] = e;
             taken[e] = cand;
+            if (cand) s_clist[atomicAdd(&s_nc, 1)] = e;
+        }
+        __syncthreads();
+        const int nc = s_nc;
+        for (int c = tid; c < nc; c += FR_THREADS) {
+            const int e = s_clist[c];
+            val[e] = exact_logit(a.W + (size_t)e * D, xs, D);
         }
         __syncthreads();
         if (a.routing == OFB_ROUTE_FORWARD) {
@@ -461,10 +520,10 @@ __global__ void __launch_bounds__(FR_THREADS) route_select_fast(FastRouteArgs a)
             for (int e = tid; e < E; e += FR_THREADS)
                 oval[e] = taken[e] ? ofb_exact_expf(__fsub_rn(val[e], s_max)) : -INFINITY;
             __syncthreads();
-            for (int e = tid; e < E; e += FR_THREADS) {
-                if (!taken[e]) continue;
-                for (int f = 0; f < E; f++)
-                    if (f != e && taken[f] && close_ulps(oval[e], oval[f], 4)) s_unsafe = 1;
+            for (int c = tid; c < nc; c += FR_THREADS) {
+                const int e = s_clist[c];
+                for (int c2 = 0; c2 < nc; c2++)
+                    if (c2 != c && close_ulps(oval[e], oval[s_clist[c2]], 4)) s_unsafe = 1;
             }
             __syncthreads();
             if (s_unsafe) {
@@ -536,6 +595,12 @@ __global__ void __launch_bounds__(FR_THREADS) route_select_fast(FastRouteArgs a)
         }
     }
     if (tid == 0 && a.stats && !warp_done) atomicAdd(&a.stats[s_mode], 1);
+    __syncthreads();  // the next token reuses the shared arrays
+    }
+    if (a.flagged) {
+        DTRACE_END(rf, 1)
+        return;
+    }
 
     // ---- the block finishing the last token builds the dispatch plan --------
     if (a.T == 1) {
@@ -561,6 +626,151 @@ __global__ void __launch_bounds__(FR_THREADS) route_select_fast(FastRouteArgs a)
     DTRACE_END(rf, 1)
 }
 
+// ---- large batches: logits and bounds as a tiled fp32 GEMM ---------------------
+// For batches above FAST_ROUTE_MAX_T tokens the per-row fp64 dots of
+// route_rows_kernel are replaced by a SIMT fp32 GEMM with the same output
+// (L~, B) per (token, expert), so route_select_fast certifies the top-k the
+// same way:
+//  * K runs in 64-element segments; inside a segment the sum is one fp32 FMA
+//    chain (each step rounds once), so |c_s - sum_s p| <= gamma_64 * A_s,
+//    A_s = sum_s |x w|; segment sums accumulate in fp64: L~ = sum_s c_s.
+//  * A_s <= ||x_s|| ||w_s|| (Cauchy-Schwarz) from per-segment norms.
+//  * the reference's sequential prefixes P_i (i in segment s) satisfy
+//    |P_i| <= |P(64s)| + A_s and |P(64s)| <= |L~ before s| + gamma_64 *
+//    (A before s), which bounds S_P = sum |P_i| segment by segment.
+//  * B = (1+2^-9) u (A + S_P + n gamma_n A) + (1+2^-9) gamma_64 A + 2^-60,
+//    A, S_P accumulated in fp32 rounding up; the norms carry a 2^-16
+//    inflation for their own rounding.
+constexpr int RG_T = 64, RG_E = 64, RG_SEG = 64;
+
+// Norm of every 64-element segment of `rows` rows: one half-warp per segment.
+__global__ void segment_norms_kernel(const float *__restrict__ m, int rows, int D, float *__restrict__ nrm) {
+    const int nseg = D / RG_SEG;
+    const int lane = threadIdx.x & 31, half = lane >> 4, l16 = lane & 15;
+    const int total = rows * nseg;
+    for (int w = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; 2 * w < total; w += (gridDim.x * blockDim.x) >> 5) {
+        const int i = 2 * w + half;
+        float ss = 0.f;
+        if (i < total) {
+            const int r = i / nseg, sg = i - r * nseg;
+            const float4 v = __ldg(reinterpret_cast<const float4 *>(m + (size_t)r * D + sg * RG_SEG) + l16);
+            ss = v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
+        }
+#pragma unroll
+        for (int o = 8; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+        if (i < total && l16 == 0) nrm[i] = sqrtf(ss) * (1.0f + 0x1.0p-16f);
+    }
+}
+
+constexpr int RG_LD = RG_SEG + 4;  // smem row stride (floats): 16-byte rows, conflict-free float4 reads
+constexpr int RG_SMEM = 2 * (RG_T + RG_E) * RG_LD * 4;
+
+__device__ __forceinline__ void rg_cp16(float *dst, const float *src, bool valid) {
+    const uint32_t d = (uint32_t)__cvta_generic_to_shared(dst);
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(d), "l"(src), "r"(valid ? 16 : 0) : "memory");
+}
+
+// Two-stage cp.async pipeline over the 64-element segments; thread (ty, tx)
+// owns tokens t0 + ty + 16i and experts e0 + tx + 16j (i, j < 4), reading
+// float4s along K from [row][k] tiles.
+__global__ void __launch_bounds__(256) router_bound_gemm(const float *__restrict__ W, const float *__restrict__ x,
+                                                         const float *__restrict__ nx,
+                                                         const float *__restrict__ nw, int T, int D, int E,
+                                                         double bound_scale, double ngam, double gam64,
+                                                         double2 *__restrict__ cand) {
+    extern __shared__ __align__(16) float rg_sm[];
+    float *xs = rg_sm;                       // [2][RG_T][RG_LD]
+    float *ws = rg_sm + 2 * RG_T * RG_LD;    // [2][RG_E][RG_LD]
+    const int tid = threadIdx.x, ty = tid >> 4, tx = tid & 15;
+    const int t0 = blockIdx.x * RG_T, e0 = blockIdx.y * RG_E;
+    const int nseg = D / RG_SEG;
+    const float g64 = (float)gam64;
+    auto issue = [&](int sg, int buf) {
+#pragma unroll
+        for (int q = 0; q < 4; q++) {
+            const int c = tid + 256 * q, r = c >> 4, kq = c & 15;  // 16 chunks of 16 B per row
+            const int tr = min(t0 + r, T - 1), er = min(e0 + r, E - 1);
+            rg_cp16(xs + (buf * RG_T + r) * RG_LD + 4 * kq, x + (size_t)tr * D + sg * RG_SEG + 4 * kq, t0 + r < T);
+            rg_cp16(ws + (buf * RG_E + r) * RG_LD + 4 * kq, W + (size_t)er * D + sg * RG_SEG + 4 * kq, e0 + r < E);
+        }
+        asm volatile("cp.async.commit_group;" ::: "memory");
+    };
+    double P[4][4];
+    float SP[4][4], Ab[4][4];
+#pragma unroll
+    for (int i = 0; i < 4; i++)
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+            P[i][j] = 0.0;
+            SP[i][j] = 0.f;
+            Ab[i][j] = 0.f;
+        }
+    issue(0, 0);
+    for (int sg = 0; sg < nseg; sg++) {
+        const int buf = sg & 1;
+        if (sg + 1 < nseg) {
+            issue(sg + 1, buf ^ 1);
+            asm volatile("cp.async.wait_group 1;" ::: "memory");
+        } else {
+            asm volatile("cp.async.wait_group 0;" ::: "memory");
+        }
+        __syncthreads();
+        float acc[4][4];
+#pragma unroll
+        for (int i = 0; i < 4; i++)
+#pragma unroll
+            for (int j = 0; j < 4; j++) acc[i][j] = 0.f;
+        const float *xb = xs + (buf * RG_T + ty) * RG_LD, *wb = ws + (buf * RG_E + tx) * RG_LD;
+#pragma unroll 4
+        for (int k = 0; k < RG_SEG; k += 4) {
+            float4 a[4], b[4];
+#pragma unroll
+            for (int i = 0; i < 4; i++) a[i] = *reinterpret_cast<const float4 *>(xb + 16 * i * RG_LD + k);
+#pragma unroll
+            for (int j = 0; j < 4; j++) b[j] = *reinterpret_cast<const float4 *>(wb + 16 * j * RG_LD + k);
+            // the segment's chain runs in k order: one FMA per step and output
+#pragma unroll
+            for (int i = 0; i < 4; i++)
+#pragma unroll
+                for (int j = 0; j < 4; j++) {
+                    acc[i][j] = fmaf(a[i].x, b[j].x, acc[i][j]);
+                    acc[i][j] = fmaf(a[i].y, b[j].y, acc[i][j]);
+                    acc[i][j] = fmaf(a[i].z, b[j].z, acc[i][j]);
+                    acc[i][j] = fmaf(a[i].w, b[j].w, acc[i][j]);
+                }
+        }
+        // fold the segment: prefix bound with the sums before it, then the sum
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            const int t = min(t0 + ty + 16 * i, T - 1);
+            const float xn = nx[(size_t)t * nseg + sg];
+#pragma unroll
+            for (int j = 0; j < 4; j++) {
+                const int e = min(e0 + tx + 16 * j, E - 1);
+                const float as = __fmul_ru(xn, nw[(size_t)e * nseg + sg]);
+                const float pb = __fmaf_ru(g64, Ab[i][j], __double2float_ru(fabs(P[i][j])));
+                SP[i][j] = __fmaf_ru(64.f, __fadd_ru(pb, as), SP[i][j]);
+                Ab[i][j] = __fadd_ru(Ab[i][j], as);
+                P[i][j] += (double)acc[i][j];
+            }
+        }
+        __syncthreads();  // this buffer is refilled two segments on
+    }
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+        const int t = t0 + ty + 16 * i;
+        if (t >= T) continue;
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+            const int e = e0 + tx + 16 * j;
+            if (e >= E) continue;
+            const double A = Ab[i][j];
+            const double B = bound_scale * (A + (double)SP[i][j] + ngam * A) + (1.0 + 0x1.0p-9) * gam64 * A + 0x1.0p-60;
+            cand[(size_t)t * E + e] = make_double2(P[i][j], B);
+        }
+    }
+}
+
 size_t route_fast_smem(int E, int D) {
     size_t sel = (size_t)E * (8 + 8 + 4 + 4 + 4 + 4 + 4) + (size_t)D * 4;
     size_t plan = 2 * 1024 * sizeof(int);
@@ -581,6 +791,8 @@ int launch_route_fast(const float *W, const float *x, const float *gate_v, int T
     a.idx = idx; a.w = w; a.gsc = gsc; a.xq = xq;
     if (plan) a.plan = *plan;
     else memset(&a.plan, 0, sizeof(a.plan));
+    a.flagged = nullptr;
+    a.n_flagged = nullptr;
     const size_t smem = route_fast_smem(E, D);
     static bool attr_set = false;
     if (!attr_set) {
@@ -592,6 +804,41 @@ int launch_route_fast(const float *W, const float *x, const float *gate_v, int T
                                dim3(RR_WARPS * 32), 0, s, a);
     if (e == cudaSuccess) e = launch_pdl(route_select_fast, dim3(T), dim3(FR_THREADS), smem, s, a);
     if (e != cudaSuccess) return cuda_status(e, "route_fast launch");
+    return OFB_OK;
+}
+
+int launch_route_fast_large(const float *W, const float *x, int T, int D, int E, int K, int routing, int renorm,
+                            double2 *cand, float *norms, int *flagged, int *n_flagged, int *stats, uint32_t *idx,
+                            float *w, cudaStream_t s) {
+    if (D % RG_SEG) { set_error("route_fast_large: d_model must be a multiple of %d", RG_SEG); return OFB_EUNSUPPORTED; }
+    FastRouteArgs a;
+    a.W = W; a.x = x; a.gate_v = nullptr;
+    a.T = T; a.D = D; a.E = E; a.K = K; a.routing = routing; a.renorm = renorm;
+    const double u = 0x1.0p-24, n = (double)D;
+    a.bound_scale = (1.0 + 0x1.0p-9) * u;
+    a.ngam = n * (n * u / (1.0 - n * u));
+    const double gam64 = 64.0 * u / (1.0 - 64.0 * u);
+    a.cand = cand; a.all_cnt = nullptr; a.stats = stats;
+    a.idx = idx; a.w = w; a.gsc = nullptr; a.xq = nullptr;
+    memset(&a.plan, 0, sizeof(a.plan));
+    a.flagged = flagged;
+    a.n_flagged = n_flagged;
+    const size_t smem = route_fast_smem(E, D);
+    if (smem > 64 * 1024) { set_error("route_fast: E/D too large for shared memory"); return OFB_EUNSUPPORTED; }
+    cudaFuncSetAttribute(route_select_fast, cudaFuncAttributeMaxDynamicSharedMemorySize, 64 * 1024);
+    float *nx = norms, *nw = norms + (size_t)T * (D / RG_SEG);
+    const int nseg = D / RG_SEG;
+    segment_norms_kernel<<<grid_for((uint64_t)T * nseg / 2, 8, 148 * 16), 256, 0, s>>>(x, T, D, nx);
+    segment_norms_kernel<<<grid_for((uint64_t)E * nseg / 2, 8, 148 * 16), 256, 0, s>>>(W, E, D, nw);
+    cudaFuncSetAttribute(router_bound_gemm, cudaFuncAttributeMaxDynamicSharedMemorySize, RG_SMEM);
+    router_bound_gemm<<<dim3((T + RG_T - 1) / RG_T, (E + RG_E - 1) / RG_E), 256, RG_SMEM, s>>>(
+        W, x, nx, nw, T, D, E, a.bound_scale, a.ngam, gam64, cand);
+    if (E > 32 * FW_PER_LANE) { set_error("route_fast_large: at most %d experts", 32 * FW_PER_LANE); return OFB_EUNSUPPORTED; }
+    cudaError_t e = cudaMemsetAsync(n_flagged, 0, sizeof(int), s);
+    if (e != cudaSuccess) return cuda_status(e, "route_fast_large memset");
+    route_certify_warps<<<(T + 7) / 8, 256, 0, s>>>(a, flagged, n_flagged);
+    route_select_fast<<<T < 148 ? T : 148, FR_THREADS, smem, s>>>(a);  // flagged tokens only
+    OFB_CHECK_LAUNCH("route_fast_large");
     return OFB_OK;
 }
 
