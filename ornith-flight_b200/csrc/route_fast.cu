@@ -399,8 +399,10 @@ __global__ void __launch_bounds__(FR_THREADS) route_select_fast(FastRouteArgs a)
     __shared__ float s_w[16];
     __shared__ int s_last;
     __shared__ WarpSel sel;
-    __shared__ int s_clist[FW_PER_LANE * 32 * 4];  // candidate experts of a fallback
-    __shared__ int s_nc;
+    // fallback: candidate experts in expert order, their values, sort scratch
+    __shared__ int s_clist[1024], s_cid[1024], s_coid[1024];
+    __shared__ float s_cv[1024], s_cov[1024];
+    __shared__ int s_nc, s_full, s_wcnt[FR_WARPS];
 
     pdl_wait();
     DTRACE_WAITED(rf, 1)
@@ -486,47 +488,61 @@ __global__ void __launch_bounds__(FR_THREADS) route_select_fast(FastRouteArgs a)
         double lo_min = INFINITY;
         for (int q = 0; q < K; q++) lo_min = fmin(lo_min, Ls[s_top[q]] - Bs[s_top[q]]);
         __syncthreads();
-        // candidates into a compact list, so that their exact chains occupy
-        // the first threads (one warp for up to 32) instead of every warp
+        // candidates in ascending expert order (a ballot prefix per round of
+        // 256 experts): their exact chains occupy the first threads, and the
+        // exchange sort runs over them alone - experts outside the list hold
+        // -inf, never win a strict comparison, and so leave the candidates'
+        // relative order as the full sort would.
         if (tid == 0) s_nc = 0;
         __syncthreads();
-        for (int e = tid; e < E; e += FR_THREADS) {
-            const bool cand = (Ls[e] + Bs[e] >= lo_min - FR_MARGIN);
-            val[e] = -INFINITY;
-            id[e] = e;
-            taken[e] = cand;
-            if (cand) s_clist[atomicAdd(&s_nc, 1)] = e;
+        for (int e0 = 0; e0 < E; e0 += FR_THREADS) {
+            const int e = e0 + tid;
+            const bool cand = e < E && (Ls[e] + Bs[e] >= lo_min - FR_MARGIN);
+            if (e < E) {
+                val[e] = -INFINITY;
+                id[e] = e;
+                taken[e] = cand;
+            }
+            const unsigned bal = __ballot_sync(0xffffffffu, cand);
+            if (lane == 0) s_wcnt[wid] = __popc(bal);
+            __syncthreads();
+            int off = s_nc;
+            for (int q = 0; q < wid; q++) off += s_wcnt[q];
+            if (cand) s_clist[off + __popc(bal & ((1u << lane) - 1u))] = e;
+            __syncthreads();
+            if (tid == 0)
+                for (int q = 0; q < FR_WARPS; q++) s_nc += s_wcnt[q];
+            __syncthreads();
         }
-        __syncthreads();
         const int nc = s_nc;
         for (int c = tid; c < nc; c += FR_THREADS) {
             const int e = s_clist[c];
-            val[e] = exact_logit(a.W + (size_t)e * D, xs, D);
+            const float l = exact_logit(a.W + (size_t)e * D, xs, D);
+            val[e] = l;
+            s_cv[c] = l;
+            s_cid[c] = e;
         }
+        if (tid == 0) s_full = 0;
         __syncthreads();
         if (a.routing == OFB_ROUTE_FORWARD) {
             // probabilities are ordered like expf(l - max) unless two of them
             // are within a few ulps (then the division could tie them)
             __shared__ float s_max;
-            __shared__ int s_unsafe;
-            if (tid == 0) {
+            if (wid == 0) {
                 float m = -INFINITY;
-                for (int e = 0; e < E; e++)
-                    if (taken[e]) m = fmaxf(m, val[e]);
-                s_max = m;
-                s_unsafe = 0;
+                for (int c = lane; c < nc; c += 32) m = fmaxf(m, s_cv[c]);
+#pragma unroll
+                for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+                if (lane == 0) s_max = m;
             }
             __syncthreads();
-            for (int e = tid; e < E; e += FR_THREADS)
-                oval[e] = taken[e] ? ofb_exact_expf(__fsub_rn(val[e], s_max)) : -INFINITY;
+            for (int c = tid; c < nc; c += FR_THREADS) s_cv[c] = ofb_exact_expf(__fsub_rn(s_cv[c], s_max));
             __syncthreads();
-            for (int c = tid; c < nc; c += FR_THREADS) {
-                const int e = s_clist[c];
+            for (int c = tid; c < nc; c += FR_THREADS)
                 for (int c2 = 0; c2 < nc; c2++)
-                    if (c2 != c && close_ulps(oval[e], oval[s_clist[c2]], 4)) s_unsafe = 1;
-            }
+                    if (c2 != c && close_ulps(s_cv[c], s_cv[c2], 4)) s_full = 1;
             __syncthreads();
-            if (s_unsafe) {
+            if (s_full) {
                 // ---- full recompute: every logit exact, softmax as the reference
                 for (int e = tid; e < E; e += FR_THREADS)
                     val[e] = taken[e] ? val[e] : exact_logit(a.W + (size_t)e * D, xs, D);
@@ -548,15 +564,19 @@ __global__ void __launch_bounds__(FR_THREADS) route_select_fast(FastRouteArgs a)
                 }
                 __syncthreads();
                 for (int e = tid; e < E; e += FR_THREADS) val[e] = __fdiv_rn(val[e], s_sum);
-            } else {
-                for (int e = tid; e < E; e += FR_THREADS) val[e] = oval[e];
+                __syncthreads();
             }
-            __syncthreads();
         }
         if (wid == 0) {
-            for (int i = 0; i < K; i++) exchange_pass(val, id, oval, oid, E, i, lane);
-            if (lane == 0)
-                for (int q = 0; q < K; q++) s_top[q] = id[q];
+            if (s_full) {
+                for (int i = 0; i < K; i++) exchange_pass(val, id, oval, oid, E, i, lane);
+                if (lane == 0)
+                    for (int q = 0; q < K; q++) s_top[q] = id[q];
+            } else {
+                for (int i = 0; i < K; i++) exchange_pass(s_cv, s_cid, s_cov, s_coid, nc, i, lane);
+                if (lane == 0)
+                    for (int q = 0; q < K; q++) s_top[q] = s_cid[q];
+            }
         }
         __syncthreads();
     }
