@@ -22,8 +22,10 @@
 //    chunk index x row); the Q6_K rows of a CTA are one contiguous, 16-byte
 //    aligned slab (128 x 420 B) brought in by one bulk copy.
 //  * TMEM columns: up = gate accumulator [0,192), up accumulator [192,384),
-//    two A stages [384,512); down = accumulator [0,192), two A stages
-//    [192,256). Tiles hold at most 192 tokens (the MMA's N).
+//    two A stages [384,512); down (persistent, two accumulators so that one
+//    unit's epilogue overlaps the next unit's MMAs) = accumulators [0,192)
+//    and [192,384), two A stages [384,448). Tiles hold at most 192 tokens
+//    (the MMA's N).
 //  * one thread issues tcgen05.mma (kind::f16, bf16 x bf16 -> f32);
 //    tcgen05.commit arrives on the mbarriers that free the stage's buffers.
 //  * warp-specialised: warp 0 produces B, warp 2 raw A (TMA), warp 1 issues
@@ -59,7 +61,6 @@ constexpr int B_STAGE = PF_NMAX * 128;     // 24 KB: up to 192 rows x 128 B
 constexpr int RAW4 = PF_M * 48;            // raw Q4_K bytes of one matrix per stage
 constexpr int UP_ACC_U = PF_NMAX;          // TMEM column of the up accumulator
 constexpr int UP_A = 2 * PF_NMAX;          // up: A stage s, matrix m at UP_A + 64 s + 32 m
-constexpr int DN_A = PF_NMAX;              // down: A stage s at DN_A + 32 s
 constexpr long long WAIT_LIMIT = 1ll << 24;  // try_wait polls before giving up
 
 struct PrefillArgs {
@@ -119,6 +120,16 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *b, uint32_t parity) {
         if (done) return true;
     }
     return false;
+}
+// Named barrier `id` over n threads returning the AND of their `v`.
+__device__ __forceinline__ bool bar_and(int id, int n, bool v) {
+    uint32_t r;
+    asm volatile(
+        "{ .reg .pred p, q; setp.ne.u32 p, %1, 0; barrier.red.and.pred q, %2, %3, p; selp.u32 %0, 1, 0, q; }"
+        : "=r"(r)
+        : "r"((uint32_t)v), "r"(id), "r"(n)
+        : "memory");
+    return r != 0;
 }
 __device__ __forceinline__ void mbar_arrive(uint64_t *b) {
     asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(b)) : "memory");
@@ -563,120 +574,206 @@ __global__ void __launch_bounds__(PF_NT, 1)
     PF_TR(if (tr && threadIdx.x == 0) tr[3] = clock64() - tc0; pf_end(0);)
 }
 
-// ---- phase 2: down + weighted combine -----------------------------------------
-// The CTA's 128 Q6_K rows are one contiguous, 16-byte aligned slab
-// (128 x 420 B at H = 512): one bulk copy brings it in; stages copy only B.
-__host__ __device__ inline int down_slab_bytes(int H) { return PF_M * (H / QK) * Q6K_BYTES; }
-__host__ __device__ inline int down_smem(int H) { return 1024 + PF_STG * B_STAGE + down_slab_bytes(H); }
+// ---- phase 2: down + weighted combine (persistent) -----------------------------
+// One CTA per SM loops over units (tile, 128 output rows), output-row block
+// fastest, so the CTAs running at the same time share a tile's h rows in L2.
+// The unit's 128 Q6_K rows (one contiguous, 16-byte aligned slab, 128 x 420 B
+// at H = 512) come in one bulk copy into one of two slab buffers while the
+// previous unit computes; the tensor core accumulates into one of two TMEM
+// accumulators while 8 epilogue warps add the other one's w * y into out.
+// TMEM: accumulators [0,192) and [192,384), A stages [384,448).
+constexpr int DN_EPI0 = 20;                 // first epilogue warp
+constexpr int DN_NEPI = 8;                  // epilogue warps (2 per TMEM lane quarter)
+constexpr int DN_THREADS = (DN_EPI0 + DN_NEPI) * 32;
+constexpr int DN_ACC1 = PF_NMAX;            // TMEM column of the second accumulator
+constexpr int DN_A = 2 * PF_NMAX;           // TMEM column of A stage 0 (32 columns each)
 
-__global__ void __launch_bounds__(PF_NT, 1)
+__host__ __device__ inline int down_slab_bytes(int H) { return PF_M * (H / QK) * Q6K_BYTES; }
+__host__ __device__ inline int down_smem(int H) { return 1024 + PF_STG * B_STAGE + 2 * down_slab_bytes(H); }
+
+struct DownBars {
+    uint64_t bfull[PF_STG], bempty[PF_STG];  // B: TMA -> MMA
+    uint64_t afull[PF_NA], aempty[PF_NA];    // A in TMEM: dequant -> MMA
+    uint64_t sfull[2], sempty[2];            // Q6_K slabs: bulk copy -> dequant
+    uint64_t cfull[2], cempty[2];            // accumulators: MMA -> epilogue
+};
+
+__global__ void __launch_bounds__(DN_THREADS, 1)
     prefill_down_kernel(PrefillArgs a, const __grid_constant__ CUtensorMap hmap) {
     extern __shared__ uint8_t psm_raw[];
     uint8_t *psm = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(psm_raw) + 1023) & ~uintptr_t(1023));
-    __shared__ Rings R;
-    __shared__ uint64_t slab_bar;
+    __shared__ DownBars R;
     __shared__ uint32_t tslot;
-    __shared__ int tok[PF_NMAX];
-    __shared__ float wgt[PF_NMAX];
-    const int tile = blockIdx.y;
-    if (tile >= *a.n_tiles) return;
-    PF_TR(unsigned long long *tr = pf_tr(1); const unsigned long long tc0 = clock64(); unsigned long long tc;
-          unsigned long long acc[18] = {};)
-    const int u = a.tile_slot[tile], s0 = a.tile_start[tile], n = a.tile_n[tile];
-    const int e = a.slot_expert[u];
-    const int n0 = blockIdx.x * PF_M;
+    __shared__ float epi_tile[DN_NEPI * 16 * 33];     // per epilogue warp: 16 tokens x 32 rows
+    __shared__ int epi_tok[PF_NMAX];                  // the unit's tokens
+    __shared__ float epi_w[PF_NMAX];                  // and their weights
+    const int nblk = a.D / PF_M;
+    const int n_units = *a.n_tiles * nblk;
+    if ((int)blockIdx.x >= n_units) return;
+    const int n_my = (n_units - (int)blockIdx.x + (int)gridDim.x - 1) / (int)gridDim.x;
+    PF_TR(unsigned long long *tr = pf_tr(1); const unsigned long long tc0 = clock64();)
     const int TK = a.T * a.K;
-    const int row_bytes = (a.H / QK) * Q6K_BYTES;
+    const int row_bytes = (a.H / QK) * Q6K_BYTES, slab_bytes = PF_M * row_bytes;
     const size_t exp_bytes = (size_t)row_bytes * a.D;
-    const uint8_t *slab_src = (e == a.E ? a.down_sh : a.down + e * exp_bytes) + (size_t)n0 * row_bytes;
+    const int nstages = a.H / PF_KS;
     uint8_t *bst = psm;                        // [PF_STG][B_STAGE]
-    uint8_t *slab = bst + PF_STG * B_STAGE;    // raw Q6_K rows (16-byte aligned)
-    for (int i = threadIdx.x; i < n; i += PF_NT) {
-        const int asg = a.assign[s0 + i];
-        const int t = asg_token_p(asg, TK, a.K);
-        tok[i] = t;
-        wgt[i] = asg < TK ? a.w[asg] : (a.shared_gate ? a.gsc[t] : 1.0f);
-    }
+    uint8_t *slab = bst + PF_STG * B_STAGE;    // [2][slab_bytes], 16-byte aligned
     if (threadIdx.x == 0) {
-        rings_init(R);
-        mbar_init(&slab_bar, 1);
+        for (int i = 0; i < PF_STG; i++) {
+            mbar_init(&R.bfull[i], 1);
+            mbar_init(&R.bempty[i], 1);
+        }
+        for (int i = 0; i < PF_NA; i++) {
+            mbar_init(&R.afull[i], PF_NDQW);
+            mbar_init(&R.aempty[i], 1);
+        }
+        for (int i = 0; i < 2; i++) {
+            mbar_init(&R.sfull[i], 1);
+            mbar_init(&R.sempty[i], PF_NDQW);
+            mbar_init(&R.cfull[i], 1);
+            mbar_init(&R.cempty[i], DN_NEPI);
+        }
     }
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-    const uint32_t tbase = tmem_alloc(&tslot, 256);  // syncs the CTA
-    PF_TR(if (tr && threadIdx.x == 0) tr[1] = clock64() - tc0;)
-
-    const int nn = (n + 15) & ~15;
-    const int nstages = a.H / PF_KS;
+    const uint32_t tbase = tmem_alloc(&tslot, 512);  // syncs the CTA
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     bool ok = true;
     if (warp == 0) {
+        // producer: the unit's slab (one bulk copy), then its h rows per stage
         if (lane == 0) {
-            bulk_copy(slab, slab_src, down_slab_bytes(a.H), &slab_bar);
-            ok = b_producer(R, &hmap, bst, nstages, s0, nn PF_TR(, tr ? acc : nullptr));
-        }
-    } else if (warp == 1) {
-        if (lane == 0) ok = mma_role<1>(R, nstages, DN_A, 0, bst, tbase, instr_desc(nn) PF_TR(, tr ? acc : nullptr));
-    } else if (warp >= PF_DQ0 / 32) {
-        const int grp = (warp - PF_DQ0 / 32) >> 2, hh = grp & 1, g = grp >> 1;
-        const int r = (warp & 3) * 32 + lane;
-        const uint32_t t_st = tbase + ((uint32_t)((warp & 3) * 32) << 16) + DN_A + hh * 16 + g * 8;
-        PF_TR(tc = clock64();)
-        ok = mbar_wait(&slab_bar, 0);
-        PF_TR(if (tr && threadIdx.x == PF_DQ0) acc[8] += clock64() - tc;)
-        for (int i = 0; i < nstages && ok; i++) {
-            const int sa = i % PF_NA;
-            PF_TR(tc = clock64();)
-            if (i >= PF_NA) ok = mbar_wait(&R.aempty[sa], (i / PF_NA - 1) & 1);
-            PF_TR(if (tr && threadIdx.x == PF_DQ0) acc[9] += clock64() - tc; tc = clock64();)
-            if (!ok) break;
-            tc_fence_after();
-            uint32_t v[8];
-            q6_deq(slab, row_bytes, i, r, hh, g, v);
-            tmem_st8(t_st + sa * 32, v);
-            tmem_st_wait();
-            PF_TR(if (tr && threadIdx.x == PF_DQ0) acc[10] += clock64() - tc; tc = clock64();)
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&R.afull[sa]);
-            PF_TR(if (tr && threadIdx.x == PF_DQ0) acc[11] += clock64() - tc;)
-        }
-        PF_TR(tc = clock64();)
-        if (ok) ok = mbar_wait(&R.done, 0);
-        PF_TR(if (tr && threadIdx.x == PF_DQ0) acc[12] += clock64() - tc;)
-    }
-    PF_TR(if (tr) {
-        _Pragma("unroll") for (int k = 4; k < 17; k++) if (acc[k]) atomicAdd(&tr[k], acc[k]);
-    })
-    ok = __syncthreads_and(ok);
-    PF_TR(if (tr && threadIdx.x == 0) { tr[2] = clock64() - tc0; tr[13] = nn; })
-    tc_fence_after();
-    if (!ok) {
-        if (threadIdx.x == 0) atomicExch(a.err, 1);
-    } else if (warp >= PF_DQ0 / 32) {
-        // the four warps of lane quarter q take every fourth 32-token chunk
-        const int q = warp & 3;
-        const int row = n0 + q * 32 + lane;
-        const uint32_t lane_off = (uint32_t)(q * 32) << 16;
-        float *ocol = a.out + row;
-        for (int j0 = ((warp - PF_DQ0 / 32) >> 2) * 32; j0 < n; j0 += 128) {
-            if (j0 + 32 <= nn) {
-                float y[32];
-                tmem_ld32(tbase + lane_off + j0, y);
-#pragma unroll
-                for (int j = 0; j < 32; j++)
-                    if (j0 + j < n) atomicAdd(ocol + (size_t)tok[j0 + j] * a.D, wgt[j0 + j] * y[j]);
-            } else {
-                for (int j1 = j0; j1 < n; j1 += 8) {
-                    float y[8];
-                    tmem_ld8(tbase + lane_off + j1, y);
-#pragma unroll
-                    for (int j = 0; j < 8; j++)
-                        if (j1 + j < n) atomicAdd(ocol + (size_t)tok[j1 + j] * a.D, wgt[j1 + j] * y[j]);
+            int g = 0;  // stage counter across units
+            for (int k = 0; k < n_my && ok; k++) {
+                const int u = (int)blockIdx.x + k * (int)gridDim.x, tile = u / nblk, n0 = (u - tile * nblk) * PF_M;
+                const int e = a.slot_expert[a.tile_slot[tile]], s0 = a.tile_start[tile];
+                const int nn = (a.tile_n[tile] + 15) & ~15;
+                const int sb = k & 1;
+                if (k >= 2) ok = mbar_wait(&R.sempty[sb], ((k >> 1) - 1) & 1);
+                if (!ok) break;
+                bulk_copy(slab + sb * slab_bytes, (e == a.E ? a.down_sh : a.down + e * exp_bytes) + (size_t)n0 * row_bytes,
+                          slab_bytes, &R.sfull[sb]);
+                for (int i = 0; i < nstages && ok; i++, g++) {
+                    const int rb = g % PF_STG, use = g / PF_STG;
+                    if (use > 0) ok = mbar_wait(&R.bempty[rb], (use - 1) & 1);
+                    if (!ok) break;
+                    mbar_expect_tx(&R.bfull[rb], nn * 128);
+                    const uint32_t dst = smem_u32(bst + rb * B_STAGE);
+                    for (int q = 0; q < nn / B_ROWS; q++)
+                        tma_tile2d(dst + q * B_ROWS * 128, &hmap, i * PF_KS, s0 + q * B_ROWS, &R.bfull[rb]);
                 }
             }
         }
+    } else if (warp == 1) {
+        // MMA issuer: unit k accumulates into TMEM accumulator k % 2
+        if (lane == 0) {
+            int g = 0;
+            for (int k = 0; k < n_my && ok; k++) {
+                const int tile = ((int)blockIdx.x + k * (int)gridDim.x) / nblk;
+                const uint32_t idesc = instr_desc((a.tile_n[tile] + 15) & ~15);
+                const int ab = k & 1;
+                if (k >= 2) ok = mbar_wait(&R.cempty[ab], ((k >> 1) - 1) & 1);
+                if (!ok) break;
+                tc_fence_after();
+                const uint32_t dacc = tbase + ab * DN_ACC1;
+                for (int i = 0; i < nstages && ok; i++, g++) {
+                    const int sa = g % PF_NA, sb = g % PF_STG;
+                    ok = mbar_wait(&R.afull[sa], (g / PF_NA) & 1) && mbar_wait(&R.bfull[sb], (g / PF_STG) & 1);
+                    if (!ok) break;
+                    tc_fence_after();
+                    const uint32_t bb = smem_u32(bst + sb * B_STAGE), ta = tbase + DN_A + sa * 32;
+#pragma unroll
+                    for (int kk = 0; kk < PF_KS / 16; kk++)
+                        mma_bf16_ta(dacc, ta + kk * 8, sw128_desc(bb + kk * 32), idesc, (i | kk) != 0);
+                    mma_commit(&R.aempty[sa]);
+                    mma_commit(&R.bempty[sb]);
+                }
+                mma_commit(&R.cfull[ab]);  // arrives once the unit's MMAs complete
+            }
+        }
+    } else if (warp >= PF_DQ0 / 32 && warp < DN_EPI0) {
+        // dequantisers: warp w owns TMEM lanes (= rows) 32*(w%4).. of A
+        const int grp = (warp - PF_DQ0 / 32) >> 2, hh = grp & 1, gq = grp >> 1;
+        const int r = (warp & 3) * 32 + lane;
+        const uint32_t t_st = tbase + ((uint32_t)((warp & 3) * 32) << 16) + DN_A + hh * 16 + gq * 8;
+        int g = 0;
+        for (int k = 0; k < n_my && ok; k++) {
+            const int sb = k & 1;
+            ok = mbar_wait(&R.sfull[sb], (k >> 1) & 1);
+            const uint8_t *sl = slab + sb * slab_bytes;
+            for (int i = 0; i < nstages && ok; i++, g++) {
+                const int sa = g % PF_NA;
+                if (g >= PF_NA) ok = mbar_wait(&R.aempty[sa], (g / PF_NA - 1) & 1);
+                if (!ok) break;
+                tc_fence_after();
+                uint32_t v[8];
+                q6_deq(sl, row_bytes, i, r, hh, gq, v);
+                tmem_st8(t_st + sa * 32, v);
+                tmem_st_wait();
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&R.afull[sa]);
+            }
+            __syncwarp();
+            if (ok && lane == 0) mbar_arrive(&R.sempty[sb]);  // done reading this slab
+        }
+    } else if (warp >= DN_EPI0) {
+        // epilogue: out[token] += w * y for the 128 rows of the unit. Warp
+        // (q, half) reads TMEM lanes 32q.. and alternate 16-token chunks,
+        // turns each 32-row x 16-token block around in shared memory and
+        // adds whole 16-byte row pieces (red.global.add.v4.f32).
+        const int q = warp & 3, half = (warp - DN_EPI0) >> 2, ew = warp - DN_EPI0;
+        const uint32_t lane_off = (uint32_t)(q * 32) << 16;
+        float *blk = epi_tile + ew * 16 * 33;  // [16 tokens][32 rows + 1]
+        for (int k = 0; k < n_my && ok; k++) {
+            const int u = (int)blockIdx.x + k * (int)gridDim.x, tile = u / nblk, n0 = (u - tile * nblk) * PF_M;
+            const int s0 = a.tile_start[tile], n = a.tile_n[tile], nn = (n + 15) & ~15;
+            const int ab = k & 1;
+            // every epilogue warp reaches this barrier (its wait is bounded),
+            // so they leave together on a timeout; it also marks the
+            // previous unit's readers done
+            ok = bar_and(2, DN_NEPI * 32, mbar_wait(&R.cfull[ab], (k >> 1) & 1));
+            if (!ok) break;
+            tc_fence_after();
+            // token and weight of each tile row, shared by the epilogue warps
+            for (int j = ew * 32 + lane; j < n; j += DN_NEPI * 32) {
+                const int asg = __ldg(a.assign + s0 + j);
+                const int t = asg_token_p(asg, TK, a.K);
+                epi_tok[j] = t;
+                epi_w[j] = asg < TK ? __ldg(a.w + asg) : (a.shared_gate ? __ldg(a.gsc + t) : 1.0f);
+            }
+            asm volatile("bar.sync 2, %0;" ::"n"(DN_NEPI * 32) : "memory");
+            const uint32_t tacc = tbase + lane_off + ab * DN_ACC1;
+            float *orow = a.out + n0 + q * 32 + 4 * (lane & 7);
+            for (int j0 = half * 16; j0 < n; j0 += 32) {
+                float y[16];
+                tmem_ld8(tacc + j0, y);
+                if (j0 + 8 < nn) tmem_ld8(tacc + j0 + 8, y + 8);
+#pragma unroll
+                for (int j = 0; j < 16; j++) blk[j * 33 + lane] = y[j];
+                __syncwarp();
+                // lane: token j0 + (lane >> 3) + 4 it, rows 4*(lane & 7)..+3
+#pragma unroll
+                for (int it = 0; it < 4; it++) {
+                    const int jj = (lane >> 3) + 4 * it;
+                    if (j0 + jj < n) {
+                        const float wv = epi_w[j0 + jj];
+                        const float *src = blk + jj * 33 + 4 * (lane & 7);
+                        float *dst = orow + (size_t)epi_tok[j0 + jj] * a.D;
+                        asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(dst), "f"(wv * src[0]),
+                                     "f"(wv * src[1]), "f"(wv * src[2]), "f"(wv * src[3])
+                                     : "memory");
+                    }
+                }
+                __syncwarp();
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&R.cempty[ab]);
+        }
     }
-    tmem_free(tbase, 256);
+    ok = __syncthreads_and(ok);
+    if (!ok && threadIdx.x == 0) atomicExch(a.err, 1);
+    PF_TR(if (tr && threadIdx.x == 0) { tr[2] = clock64() - tc0; tr[13] = n_my; })
+    tmem_free(tbase, 512);
     PF_TR(if (tr && threadIdx.x == 0) tr[3] = clock64() - tc0; pf_end(1);)
 }
 
@@ -844,7 +941,11 @@ int launch_prefill(const LayerArgs &la, const float *x, int *n_slots, __nv_bfloa
     if (before) cudaEventRecord(before, s);
     prefill_up_kernel<<<dim3(H / PF_M, max_tiles), PF_NT, smem_up, s>>>(a, xmap, gmap, umap, gmap_sh, umap_sh);
     if (between) cudaEventRecord(between, s);
-    prefill_down_kernel<<<dim3(D / PF_M, max_tiles), PF_NT, smem_dn, s>>>(a, hmap);
+    int dev = 0, sms = 148;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    const int dn_units = max_tiles * (D / PF_M);
+    prefill_down_kernel<<<dn_units < sms ? dn_units : sms, DN_THREADS, smem_dn, s>>>(a, hmap);
     OFB_CHECK_LAUNCH("prefill kernels");
     return OFB_OK;
 }
