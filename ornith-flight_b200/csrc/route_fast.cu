@@ -683,21 +683,25 @@ __global__ void segment_norms_kernel(const float *__restrict__ m, int rows, int 
 }
 
 constexpr int RG_LD = RG_SEG + 4;  // smem row stride (floats): 16-byte rows, conflict-free float4 reads
-constexpr int RG_SMEM = 2 * (RG_T + RG_E) * RG_LD * 4;
+constexpr int RG_SMEM_OPS = 2 * (RG_T + RG_E) * RG_LD * 4;
+constexpr int RG_SMEM = RG_SMEM_OPS + 2 * 32 * 128 * 4;  // + per-thread bound sums (S_P, A) of 32 outputs
 
 __device__ __forceinline__ void rg_cp16(float *dst, const float *src, bool valid) {
     const uint32_t d = (uint32_t)__cvta_generic_to_shared(dst);
     asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(d), "l"(src), "r"(valid ? 16 : 0) : "memory");
 }
 
+constexpr int RG_THREADS = 128;
+
 // Two-stage cp.async pipeline over the 64-element segments; thread (ty, tx)
-// owns tokens t0 + ty + 16i and experts e0 + tx + 16j (i, j < 4), reading
-// float4s along K from [row][k] tiles.
-__global__ void __launch_bounds__(256) router_bound_gemm(const float *__restrict__ W, const float *__restrict__ x,
-                                                         const float *__restrict__ nx,
-                                                         const float *__restrict__ nw, int T, int D, int E,
-                                                         double bound_scale, double ngam, double gam64,
-                                                         double2 *__restrict__ cand) {
+// owns tokens t0 + ty + 8i (i < 8) and experts e0 + tx + 16j (j < 4), reading
+// float4s along K from [row][k] tiles: 12 shared loads per 128 FMAs.
+__global__ void __launch_bounds__(RG_THREADS) router_bound_gemm(const float *__restrict__ W,
+                                                                const float *__restrict__ x,
+                                                                const float *__restrict__ nx,
+                                                                const float *__restrict__ nw, int T, int D, int E,
+                                                                double bound_scale, double ngam, double gam64,
+                                                                double2 *__restrict__ cand) {
     extern __shared__ __align__(16) float rg_sm[];
     float *xs = rg_sm;                       // [2][RG_T][RG_LD]
     float *ws = rg_sm + 2 * RG_T * RG_LD;    // [2][RG_E][RG_LD]
@@ -707,23 +711,24 @@ __global__ void __launch_bounds__(256) router_bound_gemm(const float *__restrict
     const float g64 = (float)gam64;
     auto issue = [&](int sg, int buf) {
 #pragma unroll
-        for (int q = 0; q < 4; q++) {
-            const int c = tid + 256 * q, r = c >> 4, kq = c & 15;  // 16 chunks of 16 B per row
+        for (int q = 0; q < 8; q++) {
+            const int c = tid + RG_THREADS * q, r = c >> 4, kq = c & 15;  // 16 chunks of 16 B per row
             const int tr = min(t0 + r, T - 1), er = min(e0 + r, E - 1);
             rg_cp16(xs + (buf * RG_T + r) * RG_LD + 4 * kq, x + (size_t)tr * D + sg * RG_SEG + 4 * kq, t0 + r < T);
             rg_cp16(ws + (buf * RG_E + r) * RG_LD + 4 * kq, W + (size_t)er * D + sg * RG_SEG + 4 * kq, e0 + r < E);
         }
         asm volatile("cp.async.commit_group;" ::: "memory");
     };
-    double P[4][4];
-    float SP[4][4], Ab[4][4];
+    // bound sums in shared memory, [output slot][thread] (conflict-free)
+    float *SPs = rg_sm + RG_SMEM_OPS / 4, *Abs = SPs + 32 * RG_THREADS;
+    double P[8][4];
 #pragma unroll
-    for (int i = 0; i < 4; i++)
+    for (int i = 0; i < 8; i++)
 #pragma unroll
         for (int j = 0; j < 4; j++) {
             P[i][j] = 0.0;
-            SP[i][j] = 0.f;
-            Ab[i][j] = 0.f;
+            SPs[(i * 4 + j) * RG_THREADS + tid] = 0.f;
+            Abs[(i * 4 + j) * RG_THREADS + tid] = 0.f;
         }
     issue(0, 0);
     for (int sg = 0; sg < nseg; sg++) {
@@ -735,57 +740,60 @@ __global__ void __launch_bounds__(256) router_bound_gemm(const float *__restrict
             asm volatile("cp.async.wait_group 0;" ::: "memory");
         }
         __syncthreads();
-        float acc[4][4];
+        float acc[8][4];
 #pragma unroll
-        for (int i = 0; i < 4; i++)
+        for (int i = 0; i < 8; i++)
 #pragma unroll
             for (int j = 0; j < 4; j++) acc[i][j] = 0.f;
         const float *xb = xs + (buf * RG_T + ty) * RG_LD, *wb = ws + (buf * RG_E + tx) * RG_LD;
-#pragma unroll 4
+#pragma unroll 2
         for (int k = 0; k < RG_SEG; k += 4) {
-            float4 a[4], b[4];
-#pragma unroll
-            for (int i = 0; i < 4; i++) a[i] = *reinterpret_cast<const float4 *>(xb + 16 * i * RG_LD + k);
+            float4 b[4];
 #pragma unroll
             for (int j = 0; j < 4; j++) b[j] = *reinterpret_cast<const float4 *>(wb + 16 * j * RG_LD + k);
             // the segment's chain runs in k order: one FMA per step and output
 #pragma unroll
-            for (int i = 0; i < 4; i++)
+            for (int i = 0; i < 8; i++) {
+                const float4 av = *reinterpret_cast<const float4 *>(xb + 8 * i * RG_LD + k);
 #pragma unroll
                 for (int j = 0; j < 4; j++) {
-                    acc[i][j] = fmaf(a[i].x, b[j].x, acc[i][j]);
-                    acc[i][j] = fmaf(a[i].y, b[j].y, acc[i][j]);
-                    acc[i][j] = fmaf(a[i].z, b[j].z, acc[i][j]);
-                    acc[i][j] = fmaf(a[i].w, b[j].w, acc[i][j]);
+                    acc[i][j] = fmaf(av.x, b[j].x, acc[i][j]);
+                    acc[i][j] = fmaf(av.y, b[j].y, acc[i][j]);
+                    acc[i][j] = fmaf(av.z, b[j].z, acc[i][j]);
+                    acc[i][j] = fmaf(av.w, b[j].w, acc[i][j]);
                 }
+            }
         }
         // fold the segment: prefix bound with the sums before it, then the sum
+        float wn[4];
 #pragma unroll
-        for (int i = 0; i < 4; i++) {
-            const int t = min(t0 + ty + 16 * i, T - 1);
-            const float xn = nx[(size_t)t * nseg + sg];
+        for (int j = 0; j < 4; j++) wn[j] = nw[(size_t)min(e0 + tx + 16 * j, E - 1) * nseg + sg];
+#pragma unroll
+        for (int i = 0; i < 8; i++) {
+            const float xn = nx[(size_t)min(t0 + ty + 8 * i, T - 1) * nseg + sg];
 #pragma unroll
             for (int j = 0; j < 4; j++) {
-                const int e = min(e0 + tx + 16 * j, E - 1);
-                const float as = __fmul_ru(xn, nw[(size_t)e * nseg + sg]);
-                const float pb = __fmaf_ru(g64, Ab[i][j], __double2float_ru(fabs(P[i][j])));
-                SP[i][j] = __fmaf_ru(64.f, __fadd_ru(pb, as), SP[i][j]);
-                Ab[i][j] = __fadd_ru(Ab[i][j], as);
+                float *sp = SPs + (i * 4 + j) * RG_THREADS + tid, *ab = Abs + (i * 4 + j) * RG_THREADS + tid;
+                const float as = __fmul_ru(xn, wn[j]), a0 = *ab;
+                const float pb = __fmaf_ru(g64, a0, __double2float_ru(fabs(P[i][j])));
+                *sp = __fmaf_ru(64.f, __fadd_ru(pb, as), *sp);
+                *ab = __fadd_ru(a0, as);
                 P[i][j] += (double)acc[i][j];
             }
         }
         __syncthreads();  // this buffer is refilled two segments on
     }
 #pragma unroll
-    for (int i = 0; i < 4; i++) {
-        const int t = t0 + ty + 16 * i;
+    for (int i = 0; i < 8; i++) {
+        const int t = t0 + ty + 8 * i;
         if (t >= T) continue;
 #pragma unroll
         for (int j = 0; j < 4; j++) {
             const int e = e0 + tx + 16 * j;
             if (e >= E) continue;
-            const double A = Ab[i][j];
-            const double B = bound_scale * (A + (double)SP[i][j] + ngam * A) + (1.0 + 0x1.0p-9) * gam64 * A + 0x1.0p-60;
+            const double A = Abs[(i * 4 + j) * RG_THREADS + tid];
+            const double B = bound_scale * (A + (double)SPs[(i * 4 + j) * RG_THREADS + tid] + ngam * A) +
+                             (1.0 + 0x1.0p-9) * gam64 * A + 0x1.0p-60;
             cand[(size_t)t * E + e] = make_double2(P[i][j], B);
         }
     }
@@ -851,7 +859,7 @@ int launch_route_fast_large(const float *W, const float *x, int T, int D, int E,
     segment_norms_kernel<<<grid_for((uint64_t)T * nseg / 2, 8, 148 * 16), 256, 0, s>>>(x, T, D, nx);
     segment_norms_kernel<<<grid_for((uint64_t)E * nseg / 2, 8, 148 * 16), 256, 0, s>>>(W, E, D, nw);
     cudaFuncSetAttribute(router_bound_gemm, cudaFuncAttributeMaxDynamicSharedMemorySize, RG_SMEM);
-    router_bound_gemm<<<dim3((T + RG_T - 1) / RG_T, (E + RG_E - 1) / RG_E), 256, RG_SMEM, s>>>(
+    router_bound_gemm<<<dim3((T + RG_T - 1) / RG_T, (E + RG_E - 1) / RG_E), RG_THREADS, RG_SMEM, s>>>(
         W, x, nx, nw, T, D, E, a.bound_scale, a.ngam, gam64, cand);
     if (E > 32 * FW_PER_LANE) { set_error("route_fast_large: at most %d experts", 32 * FW_PER_LANE); return OFB_EUNSUPPORTED; }
     cudaError_t e = cudaMemsetAsync(n_flagged, 0, sizeof(int), s);
