@@ -123,6 +123,17 @@ typedef struct ofb_workspace ofb_workspace;
 int ofb_route(const ofb_moe_config *cfg, const float *router, const float *x, int n_tokens,
               uint32_t *idx, float *w, ofb_workspace *ws, void *stream);
 
+/* The routing ofb_moe_forward uses: top-k indices bit-identical to the
+ * reference's, weights within 1e-5 relative of its (an fp32 softmax of logits
+ * known to within a rigorous bound of the reference's sequential fp32 sums;
+ * tokens whose top-k order the bound cannot certify are recomputed with the
+ * reference's exact chain). Contiguous layout with at most 256 experts; other
+ * configurations take ofb_route's exact path. Same arguments as ofb_route.
+ * Matches model_get_routing / model_forward's router (engine/src/model.c) as
+ * stated above. */
+int ofb_route_certified(const ofb_moe_config *cfg, const float *router, const float *x, int n_tokens,
+                        uint32_t *idx, float *w, ofb_workspace *ws, void *stream);
+
 /* ---- MoE layer --------------------------------------------------------- */
 
 /* Bytes of device scratch one ofb_moe_forward call needs for up to
@@ -142,7 +153,9 @@ int ofb_workspace_destroy(ofb_workspace *ws);
  * . Dn with silu clamped at +-50 (model.c:340-344); experts whose weight is
  * below 1e-6 are skipped (model.c:1066). Stream-ordered, no host sync.
  * Accumulation is fp32 (decode) or bf16 tensor-core with fp32 accumulate
- * (prefill); routing is always bit-exact. */
+ * (prefill). Routing indices are always bit-exact; weights are bit-exact on
+ * the exact path (interleaved layout, no router) and within 1e-5 relative on
+ * the certified path (ofb_route_certified, contiguous layout). */
 int ofb_moe_forward(const ofb_moe_config *cfg, const ofb_moe_weights *w, const float *x,
                     const float *resid, float *out, int n_tokens, uint32_t *idx_out,
                     float *w_out, ofb_workspace *ws, void *stream);

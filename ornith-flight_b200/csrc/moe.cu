@@ -404,6 +404,32 @@ extern "C" int ofb_route(const ofb_moe_config *cfg, const float *router, const f
     return launch_route_select(logits, n_tokens, cfg->n_experts, cfg->top_k, cfg->routing, cfg->renorm, idx, w, s);
 }
 
+extern "C" int ofb_route_certified(const ofb_moe_config *cfg, const float *router, const float *x,
+                                   int n_tokens, uint32_t *idx, float *w, ofb_workspace *ws, void *stream) {
+    int st = check_config(cfg);
+    if (st) return st;
+    if (!x || !idx || !w || n_tokens < 0) { set_error("ofb_route_certified: bad arguments"); return OFB_EINVAL; }
+    if ((st = check_ws(cfg, ws, n_tokens))) return st;
+    if (n_tokens == 0) return OFB_OK;
+    if (!router || cfg->layout != OFB_LAYOUT_CONTIGUOUS || cfg->n_experts > 256)
+        return ofb_route(cfg, router, x, n_tokens, idx, w, ws, stream);
+    if ((reinterpret_cast<uintptr_t>(router) | reinterpret_cast<uintptr_t>(x)) & 15) {
+        set_error("ofb_route_certified: router and x must be 16-byte aligned");
+        return OFB_EINVAL;
+    }
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    const WorkspaceLayout &L = ws->layout;
+    int *ctr = (int *)(ws->base + L.counters);
+    const int D = cfg->d_model, E = cfg->n_experts, K = cfg->top_k;
+    if (n_tokens <= FAST_ROUTE_MAX_T)
+        return launch_route_fast(router, x, nullptr, n_tokens, D, E, K, cfg->routing, cfg->renorm,
+                                 (double2 *)(ws->base + L.cand), ctr + FAST_ROUTE_MAX_T, ctr + FAST_ROUTE_MAX_T + 1,
+                                 idx, w, (float *)(ws->base + L.gsc), nullptr, nullptr, s);
+    return launch_route_fast_large(router, x, n_tokens, D, E, K, cfg->routing, cfg->renorm,
+                                   (double2 *)(ws->base + L.cand), (float *)(ws->base + L.norms),
+                                   (int *)(ws->base + L.logits), ctr, ctr + FAST_ROUTE_MAX_T + 1, idx, w, s);
+}
+
 extern "C" int ofb_moe_forward(const ofb_moe_config *cfg, const ofb_moe_weights *w,
                                const float *x, const float *resid, float *out, int n_tokens,
                                uint32_t *idx_out, float *w_out, ofb_workspace *ws, void *stream) {

@@ -4,7 +4,7 @@ Rank r of n owns the routed experts [r*E/n, (r+1)*E/n) of every layer (the
 contiguous layout's expert range) and the tokens [r*T/n, (r+1)*T/n) of a step;
 the router and the shared expert are replicated. One layer, on every rank:
 
-  1. route own tokens (softmax / top-k over all E experts), ofb_route;
+  1. route own tokens (softmax / top-k over all E experts), ofb_route_certified;
   2. dispatch plan: slots grouped by destination rank, ofb_ep_plan, and the
      send buffers (x rows, {local expert, weight} pairs), ofb_ep_pack;
   3. all-to-all of the per-rank counts, then of rows and pairs;
@@ -71,8 +71,10 @@ class EPOps:
         return s
 
     def route(self, lw: ofb.LayerWeights, x, idx, w):
-        ofb._check(ofb.lib.ofb_route(ctypes.byref(self.full_cfg), ofb._ptr(lw.router), ofb._ptr(x), x.shape[0],
-                                     ofb._ptr(idx), ofb._ptr(w), self.ws_full.handle, ofb._stream()))
+        # the layer's certified routing: indices bit-exact, weights within 1e-5
+        ofb._check(ofb.lib.ofb_route_certified(ctypes.byref(self.full_cfg), ofb._ptr(lw.router), ofb._ptr(x),
+                                               x.shape[0], ofb._ptr(idx), ofb._ptr(w), self.ws_full.handle,
+                                               ofb._stream()))
 
     def plan(self, idx, send_counts, slot_of, asg_of):
         T, K = idx.shape

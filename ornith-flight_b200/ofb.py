@@ -61,6 +61,7 @@ def _load() -> ctypes.CDLL:
         "ofb_dequantize": (i32, [vp, i32, u64, vp, i32, vp]),
         "ofb_dequantize_expert_slice": (i32, [vp, i32, u64, u64, i32, vp, i32, vp]),
         "ofb_route": (i32, [cfgp, vp, vp, i32, vp, vp, vp, vp]),
+        "ofb_route_certified": (i32, [cfgp, vp, vp, i32, vp, vp, vp, vp]),
         "ofb_workspace_size": (sz, [cfgp, i32]),
         "ofb_workspace_create": (i32, [cfgp, i32, ctypes.POINTER(vp)]),
         "ofb_workspace_destroy": (i32, [vp]),

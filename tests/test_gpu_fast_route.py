@@ -64,3 +64,27 @@ def test_exact_ties_full_recompute(ofb, oracle, cuda, routing):
     np.testing.assert_allclose(gw, ow, rtol=1e-5)
     if routing == 0:
         assert stats[2] > 0  # probabilities tie -> every logit recomputed
+
+
+@pytest.mark.parametrize("T,routing,bias", [(1, 0, False), (17, 1, False), (64, 0, True), (65, 0, False),
+                                            (300, 1, False), (1000, 0, True)])
+def test_route_certified_entry(ofb, cuda, T, routing, bias):
+    """ofb_route_certified (decode-size and large-batch certified paths)
+    against ofb_route (the exact reference routing): indices identical,
+    weights within 1e-5 relative; the Zipf-biased router pushes near-ties."""
+    import ctypes
+    shape = ofb.LayerShape(routing=routing)
+    r = ofb.make_router(shape, 5, ofb.zipf_bias(shape.n_experts, 5) if bias else None).to(cuda)
+    x = ofb.make_tokens(shape, T, seed=T, bias_coordinate=bias).to(cuda)
+    ws = ofb.Workspace(shape, T)
+    cfg = shape.config()
+    res = []
+    for fn in (ofb.lib.ofb_route, ofb.lib.ofb_route_certified):
+        idx = torch.empty(T, shape.top_k, dtype=torch.int32, device=cuda)
+        w = torch.empty(T, shape.top_k, dtype=torch.float32, device=cuda)
+        ofb._check(fn(ctypes.byref(cfg), ofb._ptr(r), ofb._ptr(x), T, ofb._ptr(idx), ofb._ptr(w), ws.handle,
+                      ofb._stream()))
+        torch.cuda.synchronize()
+        res.append((idx.cpu().numpy(), w.cpu().numpy()))
+    assert np.array_equal(res[0][0], res[1][0])
+    np.testing.assert_allclose(res[1][1], res[0][1], rtol=1e-5)
