@@ -50,17 +50,14 @@ namespace ofb {
 constexpr int PF_M = 128;        // weight rows per CTA (MMA M)
 constexpr int PF_NMAX = 192;     // token rows per tile (MMA N, max; bounded by TMEM columns)
 constexpr int PF_KS = 64;        // K elements per pipeline stage (= one 128-byte swizzle row)
-constexpr int PF_NT = 640;       // threads per CTA: B producer, MMA, A producer, spare, 16 dequant/epilogue warps
 constexpr int PF_DQ0 = 128;      // first dequantising thread
 constexpr int PF_NDQW = 16;      // dequantising warps
 constexpr int PF_STG = 4;        // ring depth for B
-constexpr int PF_RAW = 6;        // ring depth for raw Q4_K A (covers DRAM latency)
+constexpr int PF_RAW = 3;        // raw Q4_K blocks in flight (108 KB of gate + up rows)
 constexpr int PF_NA = 2;         // A stages in TMEM
 constexpr int B_ROWS = 16;       // rows per B box
 constexpr int B_STAGE = PF_NMAX * 128;     // 24 KB: up to 192 rows x 128 B
-constexpr int RAW4 = PF_M * 48;            // raw Q4_K bytes of one matrix per stage
-constexpr int UP_ACC_U = PF_NMAX;          // TMEM column of the up accumulator
-constexpr int UP_A = 2 * PF_NMAX;          // up: A stage s, matrix m at UP_A + 64 s + 32 m
+constexpr int RAW4 = PF_M * Q4K_BYTES;      // raw Q4_K bytes of one matrix per raw stage (one block)
 constexpr long long WAIT_LIMIT = 1ll << 24;  // try_wait polls before giving up
 
 struct PrefillArgs {
@@ -243,7 +240,7 @@ __device__ __forceinline__ void tma_load3d(uint32_t dst, const CUtensorMap *map,
         "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(smem_u32(bar))
         : "memory");
 }
-// One 2D box (64 columns x 256 rows) at (x, y).
+// One 2D box of the map at (x, y).
 __device__ __forceinline__ void tma_tile2d(uint32_t dst, const CUtensorMap *map, int x, int y, uint64_t *bar) {
     asm volatile(
         "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes"
@@ -274,19 +271,17 @@ __device__ __forceinline__ uint32_t lds_u32_2b(const uint8_t *p) {
 }
 
 // ---- A operand, Q4_K ----------------------------------------------------------------
-// Raw bytes of one matrix for one stage, as three TMA boxes of 128 rows x 16
-// bytes: [header | quant chunk 2c | quant chunk 2c+1] (chunk c of block b:
-// elements 64c..64c+63, quant bytes 32c..32c+31).
-__device__ __forceinline__ void q4_issue(const CUtensorMap *map, int row0, uint32_t dst, int stage, uint64_t *bar) {
-    const int b = stage >> 2, c = stage & 3;
-    tma_load3d(dst, map, 0, b * 9, row0, bar);
-    tma_load3d(dst + 2048, map, 0, b * 9 + 1 + 2 * c, row0, bar);
-    tma_load3d(dst + 4096, map, 0, b * 9 + 2 + 2 * c, row0, bar);
+// Raw bytes of one matrix for one raw stage: Q4_K block b of 128 rows, one
+// 2D TMA box of 128 rows x 144 bytes, [row][144] in shared memory (header at
+// 0, quant chunk c of the block at 16 + 32c: elements 64c..64c+63).
+__device__ __forceinline__ void q4_issue(const CUtensorMap *map, int row0, uint32_t dst, int b, uint64_t *bar) {
+    tma_tile2d(dst, map, b * Q4K_BYTES, row0, bar);
 }
 
 // A dequantising thread owns one (row r, nibble half hh) of one matrix: in
 // every stage it produces K elements 32hh..32hh+31 of row r (low nibbles for
-// hh = 0, high for hh = 1), TMEM columns 16hh..16hh+15 of the stage.
+// hh = 0, high for hh = 1) of chunk c, TMEM columns 16hh..16hh+15 of the
+// A stage.
 // Arithmetic is bf16 pairs: q exactly (bf16(128+q) - 128), then one fused
 // q*bf16(d*sc) - bf16(dmin*m) rounded once to bf16. d*sc and dmin*m are the
 // reference's fp32 products; rounding them to bf16 adds at most 2^-9 of
@@ -296,7 +291,7 @@ struct Q4Scales { uint32_t d2[4], nm2[4]; };  // bf16 pairs, sub-block 2c+hh for
 // Decodes the row's block header (at the block's first stage) into the four
 // scale pairs this thread uses in the block's four stages.
 __device__ __forceinline__ void q4_scales(const uint8_t *raw, int r, int hh, Q4Scales &S) {
-    const uint4 hdr = *reinterpret_cast<const uint4 *>(raw + r * 16);
+    const uint4 hdr = *reinterpret_cast<const uint4 *>(raw + r * Q4K_BYTES);
     const uint32_t s[3] = {hdr.y, hdr.z, hdr.w};
     const float d = half_bits_ref(hdr.x & 0xFFFFu), dmin = half_bits_ref(hdr.x >> 16);
 #pragma unroll
@@ -312,8 +307,8 @@ __device__ __forceinline__ __nv_bfloat162 as_bf2(uint32_t v) { return *reinterpr
 
 __device__ __forceinline__ void q4_deq(const uint8_t *raw, int c, int r, int hh, const Q4Scales &S,
                                        uint32_t out[16]) {
-    const uint4 qa = *reinterpret_cast<const uint4 *>(raw + 2048 + r * 16);
-    const uint4 qb = *reinterpret_cast<const uint4 *>(raw + 4096 + r * 16);
+    const uint4 qa = *reinterpret_cast<const uint4 *>(raw + r * Q4K_BYTES + 16 + 32 * c);
+    const uint4 qb = *reinterpret_cast<const uint4 *>(raw + r * Q4K_BYTES + 32 + 32 * c);
     // selects, not S.d2[c]: a runtime index would put S in local memory
     const __nv_bfloat162 d2 = as_bf2(c == 0 ? S.d2[0] : c == 1 ? S.d2[1] : c == 2 ? S.d2[2] : S.d2[3]);
     const __nv_bfloat162 nm2 = as_bf2(c == 0 ? S.nm2[0] : c == 1 ? S.nm2[1] : c == 2 ? S.nm2[2] : S.nm2[3]);
@@ -367,209 +362,308 @@ __device__ __forceinline__ float silu_mul(float g, float u) {
 // Parity of the phase that completes the n-th use (n = 0, 1, ...) of a ring
 // slot is n & 1; a producer refilling a slot for use n >= 1 waits for the
 // consumer's release of use n-1, parity (n-1) & 1.
-struct Rings {
-    uint64_t bfull[PF_STG], bempty[PF_STG];   // B: TMA -> MMA
-    uint64_t rfull[PF_RAW], rempty[PF_RAW];   // raw A: TMA -> dequant
-    uint64_t afull[PF_NA], aempty[PF_NA];     // A in TMEM: dequant -> MMA
-    uint64_t done;                            // all MMAs complete -> epilogue
-};
-__device__ __forceinline__ void rings_init(Rings &R) {
-    for (int i = 0; i < PF_STG; i++) {
-        mbar_init(&R.bfull[i], 1);
-        mbar_init(&R.bempty[i], 1);
-    }
-    for (int i = 0; i < PF_RAW; i++) {
-        mbar_init(&R.rfull[i], 1);
-        mbar_init(&R.rempty[i], PF_NDQW);
-    }
-    for (int i = 0; i < PF_NA; i++) {
-        mbar_init(&R.afull[i], PF_NDQW);
-        mbar_init(&R.aempty[i], 1);
-    }
-    mbar_init(&R.done, 1);
-}
 
-// B producer (one thread): per stage the tile's nn rows of a [rows][K] bf16
-// tensor, in 16-row boxes (rows past the tensor read as zero and count
-// toward the transaction bytes).
-__device__ __forceinline__ bool b_producer(Rings &R, const CUtensorMap *map, uint8_t *bst, int nstages, int s0,
-                                           int nn PF_TR(, unsigned long long *acc)) {
-    bool ok = true;
-    for (int i = 0; i < nstages && ok; i++) {
-        const int sb = i % PF_STG, use = i / PF_STG;
-        PF_TR(unsigned long long tc = clock64();)
-        if (use > 0) ok = mbar_wait(&R.bempty[sb], (use - 1) & 1);
-        PF_TR(if (acc) acc[4] += clock64() - tc;)
-        if (!ok) break;
-        mbar_expect_tx(&R.bfull[sb], nn * 128);
-        const uint32_t dst = smem_u32(bst + sb * B_STAGE);
-        for (int k = 0; k < nn / B_ROWS; k++)
-            tma_tile2d(dst + k * B_ROWS * 128, map, i * PF_KS, s0 + k * B_ROWS, &R.bfull[sb]);
-    }
-    return ok;
-}
-
-// MMA role (one thread): per stage wait for A (TMEM) and B (shared memory),
-// issue the stage's K = 64 slice into each accumulator, release both.
-template <int NACC>
-__device__ __forceinline__ bool mma_role(Rings &R, int nstages, uint32_t a_col0, int acc_stride, const uint8_t *bst,
-                                         uint32_t tbase, uint32_t idesc PF_TR(, unsigned long long *acc)) {
-    bool ok = true;
-    for (int i = 0; i < nstages && ok; i++) {
-        const int sa = i % PF_NA, sb = i % PF_STG;
-        PF_TR(unsigned long long tc = clock64();)
-        ok = mbar_wait(&R.afull[sa], (i / PF_NA) & 1);
-        PF_TR(if (acc) acc[6] += clock64() - tc; tc = clock64();)
-        ok = ok && mbar_wait(&R.bfull[sb], (i / PF_STG) & 1);
-        PF_TR(if (acc) acc[7] += clock64() - tc; tc = clock64();)
-        if (!ok) break;
-        tc_fence_after();
-        const uint32_t bb = smem_u32(bst + sb * B_STAGE);
-        const uint32_t ta = tbase + a_col0 + sa * 32 * NACC;
-#pragma unroll
-        for (int kk = 0; kk < PF_KS / 16; kk++) {
-            const uint64_t bd = sw128_desc(bb + kk * 32);
-#pragma unroll
-            for (int m = 0; m < NACC; m++)
-                mma_bf16_ta(tbase + m * acc_stride, ta + m * 32 + kk * 8, bd, idesc, (i | kk) != 0);
-        }
-        mma_commit(&R.aempty[sa]);
-        mma_commit(&R.bempty[sb]);
-        PF_TR(if (acc) acc[16] += clock64() - tc;)
-    }
-    mma_commit(&R.done);  // arrives once all issued MMAs complete
-    return ok;
-}
-
-// ---- phase 1: gate/up ----------------------------------------------------------------
+// ---- phase 1: gate/up (persistent) -----------------------------------------------------
+// One CTA per SM loops over units (tile, 128 hidden rows), row block fastest,
+// so CTAs running at the same time share a tile's x rows in L2. The raw
+// Q4_K, x and A rings run on across unit boundaries, so the DRAM stream and
+// the tensor core never drain between units.
+//
+// A thread waits about a hundred cycles on every tcgen05.mma it issues, so
+// four threads issue them: issuer (m, p) the products of matrix m (gate,
+// up) in the stages of parity p, into an accumulator of its own; the
+// epilogue adds the two parities (a fixed order: deterministic). Units wider
+// than 96 tokens have no room for four accumulators and use issuers (m, 0).
+// TMEM (512 columns): two accumulator buffers of 192 columns. A unit of N <=
+// 48 takes one buffer (accumulator (m, p) at 48 (2m + p)) and alternates with
+// the next; N <= 96 takes both (at 96 (2m + p)); wider units take both
+// without the parity split (gate at 0, up at 192). A stages at 384 + 64 s,
+// matrix m at +32 m. 8 epilogue warps turn a finished unit's accumulators
+// into h while the next unit accumulates.
+constexpr int UP_EPI0 = 20;                  // first epilogue warp
+constexpr int UP_NEPI = 8;                   // epilogue warps (2 per TMEM lane quarter)
+constexpr int UP_ISS2 = UP_EPI0 + UP_NEPI;   // issuers (m, 1): warps 28, 29; (m, 0): warps 1, 3
+constexpr int UP_THREADS = (UP_ISS2 + 2) * 32;
+constexpr int UP_BUF = PF_NMAX;              // columns per accumulator buffer
+constexpr int UP_NARROW = UP_BUF / 4;        // widest unit that fits one buffer (four accumulators)
+constexpr int UP_SPLIT = UP_BUF / 2;         // widest unit with the parity split
+constexpr int UP_A = 2 * UP_BUF;             // TMEM column of A stage 0 (64 columns each)
 constexpr int UP_SMEM = 1024 + PF_STG * B_STAGE + PF_RAW * 2 * RAW4;
 
-__global__ void __launch_bounds__(PF_NT, 1)
+struct UpBars {
+    uint64_t bfull[PF_STG], bempty[PF_STG];   // x: TMA -> MMA
+    uint64_t rfull[PF_RAW], rempty[PF_RAW];   // raw Q4_K: TMA -> dequant
+    uint64_t afull[PF_NA], aempty[PF_NA];     // A in TMEM: dequant -> MMA
+    uint64_t cfull[2], cempty[2];             // accumulator buffers: MMA -> epilogue
+};
+
+// Accumulators of a unit: mask bit b set = buffer b used, split = parity
+// split, col(m, p) = TMEM column of accumulator (m, p). `cur` is the buffer
+// the next narrow unit takes. Every role walks the same unit sequence and so
+// makes the same choices.
+struct UpAcc {
+    int mask, split, base, step;
+    __device__ __forceinline__ uint32_t col(int m, int p) const { return base + (2 * m + p) * step; }
+};
+__device__ __forceinline__ UpAcc up_acc(int nn, int &cur) {
+    UpAcc u;
+    if (nn <= UP_NARROW) {
+        u.mask = 1 << cur;
+        u.split = 1;
+        u.base = cur * UP_BUF;
+        u.step = UP_NARROW;
+        cur ^= 1;
+        return u;
+    }
+    cur = 0;
+    u.mask = 3;
+    u.base = 0;
+    u.split = nn <= UP_SPLIT;
+    u.step = u.split ? UP_SPLIT : UP_BUF / 2;  // unsplit: (m, 0) at 192 m
+    return u;
+}
+
+__global__ void __launch_bounds__(UP_THREADS, 1)
     prefill_up_kernel(PrefillArgs a, const __grid_constant__ CUtensorMap xmap,
                       const __grid_constant__ CUtensorMap gmap, const __grid_constant__ CUtensorMap umap,
                       const __grid_constant__ CUtensorMap gmap_sh, const __grid_constant__ CUtensorMap umap_sh) {
     extern __shared__ uint8_t psm_raw[];
     uint8_t *psm = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(psm_raw) + 1023) & ~uintptr_t(1023));
-    __shared__ Rings R;
+    __shared__ UpBars R;
     __shared__ uint32_t tslot;
-    const int tile = blockIdx.y;
-    if (tile >= *a.n_tiles) return;
+    __shared__ __align__(16) __nv_bfloat16 epi_tile[UP_NEPI][16 * 40];  // per warp: 16 tokens x 32 rows (+pad)
+    const int nblk = a.H / PF_M;
+    const int n_units = *a.n_tiles * nblk;
+    if ((int)blockIdx.x >= n_units) return;
+    const int n_my = (n_units - (int)blockIdx.x + (int)gridDim.x - 1) / (int)gridDim.x;
     PF_TR(unsigned long long *tr = pf_tr(0); const unsigned long long tc0 = clock64(); unsigned long long tc;
-          unsigned long long acc[18] = {};)
-    const int u = a.tile_slot[tile], s0 = a.tile_start[tile], n = a.tile_n[tile];
-    const int e = a.slot_expert[u];
-    const int m0 = blockIdx.x * PF_M;
-    if (threadIdx.x == 0) rings_init(R);
+          unsigned long long acc[20] = {};)
+    const int nstages = a.D / PF_KS, nblocks = a.D / QK;
+    uint8_t *bst = psm;                       // [PF_STG][B_STAGE]   1024-aligned
+    uint8_t *raw = bst + PF_STG * B_STAGE;    // [PF_RAW][gate raw | up raw]
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < PF_STG; i++) {
+            mbar_init(&R.bfull[i], 1);
+            mbar_init(&R.bempty[i], 2);
+        }
+        for (int i = 0; i < PF_RAW; i++) {
+            mbar_init(&R.rfull[i], 1);
+            mbar_init(&R.rempty[i], PF_NDQW);
+        }
+        for (int i = 0; i < PF_NA; i++) {
+            mbar_init(&R.afull[i], PF_NDQW);
+            mbar_init(&R.aempty[i], 2);
+        }
+        for (int i = 0; i < 2; i++) {
+            mbar_init(&R.cfull[i], 4);
+            mbar_init(&R.cempty[i], UP_NEPI);
+        }
+    }
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     const uint32_t tbase = tmem_alloc(&tslot, 512);  // syncs the CTA
-    PF_TR(if (tr && threadIdx.x == 0) tr[1] = clock64() - tc0;)
-
-    uint8_t *bst = psm;                          // [PF_STG][B_STAGE]   1024-aligned
-    uint8_t *raw = bst + PF_STG * B_STAGE;       // [PF_RAW][gate raw | up raw]
-    const int nn = (n + 15) & ~15;               // MMA N
-    const int nstages = a.D / PF_KS;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     bool ok = true;
     if (warp == 0) {
-        if (lane == 0) ok = b_producer(R, &xmap, bst, nstages, s0, nn PF_TR(, tr ? acc : nullptr));
-    } else if (warp == 2) {
-        // raw A producer (one thread): runs up to PF_RAW stages ahead
+        // x producer: per stage the unit's nn rows of xg, in 16-row boxes
         if (lane == 0) {
-            const CUtensorMap *gm = e == a.E ? &gmap_sh : &gmap, *um = e == a.E ? &umap_sh : &umap;
-            const int row0 = (e == a.E ? 0 : e * a.H) + m0;
-            for (int i = 0; i < nstages && ok; i++) {
-                const int sr = i % PF_RAW, use = i / PF_RAW;
-                PF_TR(tc = clock64();)
-                if (use > 0) ok = mbar_wait(&R.rempty[sr], (use - 1) & 1);
-                PF_TR(if (tr) acc[5] += clock64() - tc;)
-                if (!ok) break;
-                mbar_expect_tx(&R.rfull[sr], 2 * RAW4);
-                const uint32_t rd = smem_u32(raw + sr * 2 * RAW4);
-                q4_issue(gm, row0, rd, i, &R.rfull[sr]);
-                q4_issue(um, row0, rd + RAW4, i, &R.rfull[sr]);
+            int g = 0;
+            for (int k = 0; k < n_my && ok; k++) {
+                const int tile = ((int)blockIdx.x + k * (int)gridDim.x) / nblk;
+                const int s0 = a.tile_start[tile], nn = (a.tile_n[tile] + 15) & ~15;
+                for (int i = 0; i < nstages && ok; i++, g++) {
+                    const int sb = g % PF_STG, use = g / PF_STG;
+                    PF_TR(tc = clock64();)
+                    if (use > 0) ok = mbar_wait(&R.bempty[sb], (use - 1) & 1);
+                    PF_TR(acc[4] += clock64() - tc;)
+                    if (!ok) break;
+                    mbar_expect_tx(&R.bfull[sb], nn * 128);
+                    const uint32_t dst = smem_u32(bst + sb * B_STAGE);
+                    for (int q = 0; q < nn / B_ROWS; q++)
+                        tma_tile2d(dst + q * B_ROWS * 128, &xmap, i * PF_KS, s0 + q * B_ROWS, &R.bfull[sb]);
+                }
             }
         }
-    } else if (warp == 1) {
-        if (lane == 0)
-            ok = mma_role<2>(R, nstages, UP_A, UP_ACC_U, bst, tbase, instr_desc(nn) PF_TR(, tr ? acc : nullptr));
-    } else if (warp >= PF_DQ0 / 32) {
-        // warp w: TMEM lanes (= weight rows) 32*(w%4).., matrix and nibble
-        // half from (w-4)/4
+    } else if (warp == 2) {
+        // raw Q4_K producer: gate and up block i of the unit's 128 rows, up
+        // to PF_RAW blocks ahead
+        if (lane == 0) {
+            int g = 0;
+            for (int k = 0; k < n_my && ok; k++) {
+                const int u = (int)blockIdx.x + k * (int)gridDim.x, tile = u / nblk, m0 = (u - tile * nblk) * PF_M;
+                const int e = a.slot_expert[a.tile_slot[tile]];
+                const CUtensorMap *gm = e == a.E ? &gmap_sh : &gmap, *um = e == a.E ? &umap_sh : &umap;
+                const int row0 = (e == a.E ? 0 : e * a.H) + m0;
+                for (int i = 0; i < nblocks && ok; i++, g++) {
+                    const int sr = g % PF_RAW, use = g / PF_RAW;
+                    PF_TR(tc = clock64();)
+                    if (use > 0) ok = mbar_wait(&R.rempty[sr], (use - 1) & 1);
+                    PF_TR(acc[5] += clock64() - tc;)
+                    if (!ok) break;
+                    mbar_expect_tx(&R.rfull[sr], 2 * RAW4);
+                    const uint32_t rd = smem_u32(raw + sr * 2 * RAW4);
+                    q4_issue(gm, row0, rd, i, &R.rfull[sr]);
+                    q4_issue(um, row0, rd + RAW4, i, &R.rfull[sr]);
+                }
+            }
+        }
+    } else if (warp == 1 || warp == 3 || warp >= UP_ISS2) {
+        // MMA issuer (m, p); every issuer waits for the buffers' release
+        // before committing to their cfull, so no arrival lands in an
+        // earlier phase
+        const int mat = warp == 3 || warp == UP_ISS2 + 1, par = warp >= UP_ISS2;
+        if (lane == 0) {
+            int g = 0, cur = 0, uses[2] = {0, 0};
+            for (int k = 0; k < n_my && ok; k++) {
+                const int tile = ((int)blockIdx.x + k * (int)gridDim.x) / nblk;
+                const int nn = (a.tile_n[tile] + 15) & ~15;
+                const uint32_t idesc = instr_desc(nn);
+                const UpAcc ua = up_acc(nn, cur);
+                PF_TR(tc = clock64();)
+                for (int b = 0; b < 2 && ok; b++)
+                    if ((ua.mask >> b) & 1) {
+                        if (uses[b] > 0) ok = mbar_wait(&R.cempty[b], (uses[b] - 1) & 1);
+                    }
+                PF_TR(acc[14] += clock64() - tc;)
+                if (!ok) break;
+                tc_fence_after();
+                const uint32_t dacc = tbase + ua.col(mat, par);
+                const bool active = ua.split || par == 0;
+                for (int i = 0; i < nstages && ok; i++, g++) {
+                    if (!active || (ua.split && (i & 1) != par)) continue;
+                    const int sa = g % PF_NA, sb = g % PF_STG;
+                    PF_TR(tc = clock64();)
+                    ok = mbar_wait(&R.afull[sa], (g / PF_NA) & 1);
+                    PF_TR(acc[6] += clock64() - tc; tc = clock64();)
+                    ok = ok && mbar_wait(&R.bfull[sb], (g / PF_STG) & 1);
+                    PF_TR(acc[7] += clock64() - tc; tc = clock64();)
+                    if (!ok) break;
+                    tc_fence_after();
+                    const uint32_t bb = smem_u32(bst + sb * B_STAGE), ta = tbase + UP_A + sa * 64 + mat * 32;
+                    const int first = ua.split ? 2 : 1;  // stages before this accumulator's second
+#pragma unroll
+                    for (int kk = 0; kk < PF_KS / 16; kk++)
+                        mma_bf16_ta(dacc, ta + kk * 8, sw128_desc(bb + kk * 32), idesc, i >= first || kk != 0);
+                    mma_commit(&R.aempty[sa]);
+                    mma_commit(&R.bempty[sb]);
+                    PF_TR(acc[16] += clock64() - tc;)
+                }
+                for (int b = 0; b < 2; b++)
+                    if ((ua.mask >> b) & 1) {
+                        mma_commit(&R.cfull[b]);  // arrives once this issuer's MMAs complete
+                        uses[b]++;
+                    }
+            }
+        }
+    } else if (warp >= PF_DQ0 / 32 && warp < UP_EPI0) {
+        // dequantisers: warp w owns TMEM lanes (= weight rows) 32*(w%4)..,
+        // matrix and nibble half from (w-4)/4
         const int grp = (warp - PF_DQ0 / 32) >> 2, mat = grp >> 1, hh = grp & 1;
         const int r = (warp & 3) * 32 + lane;
         const uint32_t t_st = tbase + ((uint32_t)((warp & 3) * 32) << 16) + UP_A + mat * 32 + hh * 16;
         Q4Scales S;
-        for (int i = 0; i < nstages && ok; i++) {
-            const int sr = i % PF_RAW, sa = i % PF_NA;
+        int g = 0, gr = 0;  // A stages, raw blocks
+        for (int k = 0; k < n_my && ok; k++) {
+            for (int i = 0; i < nblocks && ok; i++, gr++) {
+                const int sr = gr % PF_RAW;
+                PF_TR(tc = clock64();)
+                ok = mbar_wait(&R.rfull[sr], (gr / PF_RAW) & 1);
+                PF_TR(if (threadIdx.x == PF_DQ0) acc[8] += clock64() - tc;)
+                if (!ok) break;
+                const uint8_t *rw = raw + sr * 2 * RAW4 + mat * RAW4;
+                q4_scales(rw, r, hh, S);
+                for (int c = 0; c < QK / PF_KS && ok; c++, g++) {
+                    const int sa = g % PF_NA;
+                    PF_TR(tc = clock64();)
+                    if (g >= PF_NA) ok = mbar_wait(&R.aempty[sa], (g / PF_NA - 1) & 1);
+                    PF_TR(if (threadIdx.x == PF_DQ0) acc[9] += clock64() - tc; tc = clock64();)
+                    if (!ok) break;
+                    tc_fence_after();
+                    uint32_t v[16];
+                    q4_deq(rw, c, r, hh, S, v);
+                    tmem_st16(t_st + sa * 64, v);
+                    tmem_st_wait();
+                    PF_TR(if (threadIdx.x == PF_DQ0) acc[10] += clock64() - tc;)
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&R.afull[sa]);
+                }
+                __syncwarp();
+                if (ok && lane == 0) mbar_arrive(&R.rempty[sr]);
+            }
+        }
+    } else if (warp >= UP_EPI0) {
+        // epilogue: h = bf16(silu(gate) * up) for the unit's 128 rows. Warp
+        // (q, half) reads TMEM lanes 32q.. and alternate 16-token chunks,
+        // turns each 32-row x 16-token block around in shared memory and
+        // stores 16-byte pieces of the tokens' h rows.
+        const int q = warp & 3, half = (warp - UP_EPI0) >> 2, ew = warp - UP_EPI0;
+        const uint32_t lane_off = (uint32_t)(q * 32) << 16;
+        __nv_bfloat16 *blk = epi_tile[ew];  // [16 tokens][40]
+        int cur = 0, uses[2] = {0, 0};
+        for (int k = 0; k < n_my && ok; k++) {
+            const int u = (int)blockIdx.x + k * (int)gridDim.x, tile = u / nblk, m0 = (u - tile * nblk) * PF_M;
+            const int s0 = a.tile_start[tile], n = a.tile_n[tile], nn = (n + 15) & ~15;
+            const UpAcc ua = up_acc(nn, cur);
+            const int mask = ua.mask;
+            bool got = true;
+            for (int b = 0; b < 2; b++)
+                if ((mask >> b) & 1) got = got && mbar_wait(&R.cfull[b], uses[b] & 1);
+            // every epilogue warp reaches this barrier (its waits are
+            // bounded), so they leave together on a timeout
             PF_TR(tc = clock64();)
-            ok = mbar_wait(&R.rfull[sr], (i / PF_RAW) & 1);
-            PF_TR(if (tr && threadIdx.x == PF_DQ0) acc[8] += clock64() - tc; tc = clock64();)
-            if (ok && i >= PF_NA) ok = mbar_wait(&R.aempty[sa], (i / PF_NA - 1) & 1);
-            PF_TR(if (tr && threadIdx.x == PF_DQ0) acc[9] += clock64() - tc; tc = clock64();)
+            ok = bar_and(2, UP_NEPI * 32, got);
+            PF_TR(if (threadIdx.x == UP_EPI0 * 32) acc[17] += clock64() - tc; tc = clock64();)
             if (!ok) break;
             tc_fence_after();
-            const uint8_t *rw = raw + sr * 2 * RAW4 + mat * RAW4;
-            if ((i & 3) == 0) q4_scales(rw, r, hh, S);
-            uint32_t v[16];
-            q4_deq(rw, i & 3, r, hh, S, v);
-            tmem_st16(t_st + sa * 64, v);
-            tmem_st_wait();
-            PF_TR(if (tr && threadIdx.x == PF_DQ0) acc[10] += clock64() - tc; tc = clock64();)
+            const uint32_t tg = tbase + lane_off + ua.col(0, 0), tu = tbase + lane_off + ua.col(1, 0);
+            const uint32_t tg1 = tbase + lane_off + ua.col(0, 1), tu1 = tbase + lane_off + ua.col(1, 1);
+            __nv_bfloat16 *hrow = a.hb + (size_t)s0 * a.H + m0 + q * 32 + 8 * (lane & 3);
+            for (int j0 = half * 16; j0 < n; j0 += 32) {
+#pragma unroll
+                for (int jh = 0; jh < 16; jh += 8) {
+                    float gv[8], uv[8];
+                    tmem_ld8(tg + j0 + jh, gv);
+                    tmem_ld8(tu + j0 + jh, uv);
+                    if (ua.split) {
+                        float g1[8], u1[8];
+                        tmem_ld8(tg1 + j0 + jh, g1);
+                        tmem_ld8(tu1 + j0 + jh, u1);
+#pragma unroll
+                        for (int j = 0; j < 8; j++) {
+                            gv[j] += g1[j];
+                            uv[j] += u1[j];
+                        }
+                    }
+#pragma unroll
+                    for (int j = 0; j < 8; j++) blk[(jh + j) * 40 + lane] = __float2bfloat16_rn(silu_mul(gv[j], uv[j]));
+                }
+                __syncwarp();
+                // lane: token j0 + (lane >> 2) + 8 it, rows 8*(lane & 3)..+7
+#pragma unroll
+                for (int it = 0; it < 2; it++) {
+                    const int jj = (lane >> 2) + 8 * it;
+                    if (j0 + jj < n)
+                        *reinterpret_cast<uint4 *>(hrow + (size_t)(j0 + jj) * a.H) =
+                            *reinterpret_cast<const uint4 *>(blk + jj * 40 + 8 * (lane & 3));
+                }
+                __syncwarp();
+            }
+            PF_TR(if (threadIdx.x == UP_EPI0 * 32) acc[18] += clock64() - tc;)
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) {
-                mbar_arrive(&R.rempty[sr]);
-                mbar_arrive(&R.afull[sa]);
-            }
-            PF_TR(if (tr && threadIdx.x == PF_DQ0) acc[11] += clock64() - tc;)
+            for (int b = 0; b < 2; b++)
+                if ((mask >> b) & 1) {
+                    if (lane == 0) mbar_arrive(&R.cempty[b]);
+                    uses[b]++;
+                }
         }
-        PF_TR(tc = clock64();)
-        if (ok) ok = mbar_wait(&R.done, 0);
-        PF_TR(if (tr && threadIdx.x == PF_DQ0) acc[12] += clock64() - tc;)
     }
     PF_TR(if (tr) {
-        _Pragma("unroll") for (int k = 4; k < 17; k++) if (acc[k]) atomicAdd(&tr[k], acc[k]);
+        _Pragma("unroll") for (int i = 4; i < 20; i++) if (acc[i]) atomicAdd(&tr[i], acc[i]);
     })
     ok = __syncthreads_and(ok);
-    PF_TR(if (tr && threadIdx.x == 0) { tr[2] = clock64() - tc0; tr[13] = nn; })
-    tc_fence_after();
-    if (!ok) {
-        if (threadIdx.x == 0) atomicExch(a.err, 1);
-    } else if (warp >= PF_DQ0 / 32) {
-        // h tile through shared memory (the B ring is free now): the four
-        // warps of lane quarter q write rows m0+32q.. of every fourth
-        // 32-token chunk as stage[token][row], then all 16 warps store whole
-        // 16-byte pieces of each token's 128-row slice of h.
-        PF_TR(const unsigned long long te0 = clock64();)
-        const int q = warp & 3, r = q * 32 + lane;
-        const uint32_t lane_off = (uint32_t)(q * 32) << 16;
-        __nv_bfloat16 *stage = reinterpret_cast<__nv_bfloat16 *>(bst);  // [PF_NMAX][PF_M]
-        for (int j0 = ((warp - PF_DQ0 / 32) >> 2) * 32; j0 < n; j0 += 128) {
-            if (j0 + 32 <= nn) {
-                float g[32], uu[32];
-                tmem_ld32(tbase + lane_off + j0, g);
-                tmem_ld32(tbase + lane_off + UP_ACC_U + j0, uu);
-#pragma unroll
-                for (int j = 0; j < 32; j++) stage[(j0 + j) * PF_M + r] = __float2bfloat16_rn(silu_mul(g[j], uu[j]));
-            } else {
-                for (int j1 = j0; j1 < nn; j1 += 8) {
-                    float g[8], uu[8];
-                    tmem_ld8(tbase + lane_off + j1, g);
-                    tmem_ld8(tbase + lane_off + UP_ACC_U + j1, uu);
-#pragma unroll
-                    for (int j = 0; j < 8; j++) stage[(j1 + j) * PF_M + r] = __float2bfloat16_rn(silu_mul(g[j], uu[j]));
-                }
-            }
-        }
-        asm volatile("bar.sync 1, %0;" ::"n"(PF_NDQW * 32) : "memory");
-        const int t = threadIdx.x - PF_DQ0;
-        for (int k = t; k < n * (PF_M / 8); k += PF_NDQW * 32) {
-            const int j = k / (PF_M / 8), part = k % (PF_M / 8);
-            *reinterpret_cast<uint4 *>(a.hb + (size_t)(s0 + j) * a.H + m0 + part * 8) =
-                *reinterpret_cast<const uint4 *>(stage + j * PF_M + part * 8);
-        }
-        PF_TR(if (tr && threadIdx.x == PF_DQ0) tr[30] = clock64() - te0;)
-    }
+    if (!ok && threadIdx.x == 0) atomicExch(a.err, 1);
+    PF_TR(if (tr && threadIdx.x == 0) { tr[2] = clock64() - tc0; tr[13] = n_my; })
     tmem_free(tbase, 512);
     PF_TR(if (tr && threadIdx.x == 0) tr[3] = clock64() - tc0; pf_end(0);)
 }
@@ -866,8 +960,8 @@ static int encode_bf16_2d(CUtensorMap *map, const void *base, uint64_t cols, uin
     return OFB_OK;
 }
 
-// Q4_K rows as a 3D byte tensor: 16-byte chunk x chunk index in the row x
-// row; boxes of one chunk x 128 rows.
+// Q4_K rows as a 2D byte tensor [rows][row bytes]; boxes of one 144-byte
+// block x 128 rows (x = block * 144, a multiple of 16 bytes).
 static int encode_q4_rows(CUtensorMap *map, const void *base, int D, uint64_t rows) {
     EncodeTiledFn fn = encode_fn();
     if (!fn) {
@@ -879,12 +973,12 @@ static int encode_q4_rows(CUtensorMap *map, const void *base, int D, uint64_t ro
         return OFB_EINVAL;
     }
     const uint64_t row_bytes = (uint64_t)(D / QK) * Q4K_BYTES;
-    const cuuint64_t dims[3] = {16, row_bytes / 16, rows};
-    const cuuint64_t strides[2] = {16, row_bytes};
-    const cuuint32_t box[3] = {16, 1, (cuuint32_t)PF_M};
-    const cuuint32_t estr[3] = {1, 1, 1};
-    CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<void *>(base), dims, strides, box, estr,
-                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+    const cuuint64_t dims[2] = {row_bytes, rows};
+    const cuuint64_t strides[1] = {row_bytes};
+    const cuuint32_t box[2] = {Q4K_BYTES, (cuuint32_t)PF_M};
+    const cuuint32_t estr[2] = {1, 1};
+    CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void *>(base), dims, strides, box, estr,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) {
         set_error("cuTensorMapEncodeTiled (Q4_K rows) failed (%d)", (int)r);
@@ -939,11 +1033,13 @@ int launch_prefill(const LayerArgs &la, const float *x, int *n_slots, __nv_bfloa
     else e = cudaSuccess;
     if (e != cudaSuccess) return cuda_status(e, "prefill out init");
     if (before) cudaEventRecord(before, s);
-    prefill_up_kernel<<<dim3(H / PF_M, max_tiles), PF_NT, smem_up, s>>>(a, xmap, gmap, umap, gmap_sh, umap_sh);
-    if (between) cudaEventRecord(between, s);
     int dev = 0, sms = 148;
     cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    const int up_units = max_tiles * (H / PF_M);
+    prefill_up_kernel<<<up_units < sms ? up_units : sms, UP_THREADS, smem_up, s>>>(a, xmap, gmap, umap, gmap_sh,
+                                                                                     umap_sh);
+    if (between) cudaEventRecord(between, s);
     const int dn_units = max_tiles * (D / PF_M);
     prefill_down_kernel<<<dn_units < sms ? dn_units : sms, DN_THREADS, smem_dn, s>>>(a, hmap);
     OFB_CHECK_LAUNCH("prefill kernels");
