@@ -661,7 +661,7 @@ __global__ void __launch_bounds__(FR_THREADS) route_select_fast(FastRouteArgs a)
 //  * B = (1+2^-9) u (A + S_P + n gamma_n A) + (1+2^-9) gamma_64 A + 2^-60,
 //    A, S_P accumulated in fp32 rounding up; the norms carry a 2^-16
 //    inflation for their own rounding.
-constexpr int RG_T = 64, RG_E = 64, RG_SEG = 64;
+constexpr int RG_SEG = 64;
 
 // Norm of every 64-element segment of `rows` rows: one half-warp per segment.
 __global__ void segment_norms_kernel(const float *__restrict__ m, int rows, int D, float *__restrict__ nrm) {
@@ -683,52 +683,63 @@ __global__ void segment_norms_kernel(const float *__restrict__ m, int rows, int 
 }
 
 constexpr int RG_LD = RG_SEG + 4;  // smem row stride (floats): 16-byte rows, conflict-free float4 reads
-constexpr int RG_SMEM_OPS = 2 * (RG_T + RG_E) * RG_LD * 4;
-constexpr int RG_SMEM = RG_SMEM_OPS + 2 * 32 * 128 * 4;  // + per-thread bound sums (S_P, A) of 32 outputs
+constexpr int RG_THREADS = 128;    // 8 x 16 threads
+
+// Shared memory of a (8 TI) x (16 TJ) output tile: two stages of both
+// operand tiles, then the per-thread bound sums (S_P, A) of its TI x TJ outputs.
+__host__ __device__ constexpr int rg_smem_ops(int TI, int TJ) { return 2 * (8 * TI + 16 * TJ) * RG_LD * 4; }
+__host__ __device__ constexpr int rg_smem(int TI, int TJ) { return rg_smem_ops(TI, TJ) + 2 * TI * TJ * RG_THREADS * 4; }
 
 __device__ __forceinline__ void rg_cp16(float *dst, const float *src, bool valid) {
     const uint32_t d = (uint32_t)__cvta_generic_to_shared(dst);
     asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(d), "l"(src), "r"(valid ? 16 : 0) : "memory");
 }
 
-constexpr int RG_THREADS = 128;
-
 // Two-stage cp.async pipeline over the 64-element segments; thread (ty, tx)
-// owns tokens t0 + ty + 8i (i < 8) and experts e0 + tx + 16j (j < 4), reading
-// float4s along K from [row][k] tiles: 12 shared loads per 128 FMAs.
+// owns tokens t0 + ty + 8i (i < TI) and experts e0 + tx + 16j (j < TJ),
+// reading float4s along K from [row][k] tiles. TI x TJ = 8 x 4 (64 x 64
+// tiles) for large batches; 2 x 2 (16 x 32 tiles) spreads a few hundred
+// tokens over enough CTAs to fill the GPU.
+template <int TI, int TJ>
 __global__ void __launch_bounds__(RG_THREADS) router_bound_gemm(const float *__restrict__ W,
                                                                 const float *__restrict__ x,
                                                                 const float *__restrict__ nx,
                                                                 const float *__restrict__ nw, int T, int D, int E,
                                                                 double bound_scale, double ngam, double gam64,
                                                                 double2 *__restrict__ cand) {
+    constexpr int TT = 8 * TI, TE = 16 * TJ;  // tile tokens, experts
     extern __shared__ __align__(16) float rg_sm[];
-    float *xs = rg_sm;                       // [2][RG_T][RG_LD]
-    float *ws = rg_sm + 2 * RG_T * RG_LD;    // [2][RG_E][RG_LD]
+    float *xs = rg_sm;                       // [2][TT][RG_LD]
+    float *ws = rg_sm + 2 * TT * RG_LD;      // [2][TE][RG_LD]
     const int tid = threadIdx.x, ty = tid >> 4, tx = tid & 15;
-    const int t0 = blockIdx.x * RG_T, e0 = blockIdx.y * RG_E;
+    const int t0 = blockIdx.x * TT, e0 = blockIdx.y * TE;
     const int nseg = D / RG_SEG;
     const float g64 = (float)gam64;
     auto issue = [&](int sg, int buf) {
 #pragma unroll
-        for (int q = 0; q < 8; q++) {
+        for (int q = 0; q < (TT * 16) / RG_THREADS; q++) {
             const int c = tid + RG_THREADS * q, r = c >> 4, kq = c & 15;  // 16 chunks of 16 B per row
-            const int tr = min(t0 + r, T - 1), er = min(e0 + r, E - 1);
-            rg_cp16(xs + (buf * RG_T + r) * RG_LD + 4 * kq, x + (size_t)tr * D + sg * RG_SEG + 4 * kq, t0 + r < T);
-            rg_cp16(ws + (buf * RG_E + r) * RG_LD + 4 * kq, W + (size_t)er * D + sg * RG_SEG + 4 * kq, e0 + r < E);
+            const int tr = min(t0 + r, T - 1);
+            rg_cp16(xs + (buf * TT + r) * RG_LD + 4 * kq, x + (size_t)tr * D + sg * RG_SEG + 4 * kq, t0 + r < T);
+        }
+#pragma unroll
+        for (int q = 0; q < (TE * 16) / RG_THREADS; q++) {
+            const int c = tid + RG_THREADS * q, r = c >> 4, kq = c & 15;
+            const int er = min(e0 + r, E - 1);
+            rg_cp16(ws + (buf * TE + r) * RG_LD + 4 * kq, W + (size_t)er * D + sg * RG_SEG + 4 * kq, e0 + r < E);
         }
         asm volatile("cp.async.commit_group;" ::: "memory");
     };
     // bound sums in shared memory, [output slot][thread] (conflict-free)
-    float *SPs = rg_sm + RG_SMEM_OPS / 4, *Abs = SPs + 32 * RG_THREADS;
-    double P[8][4];
+    float *SPs = rg_sm + rg_smem_ops(TI, TJ) / 4, *Abs = SPs + TI * TJ * RG_THREADS;
+    double P[TI][TJ];
 #pragma unroll
-    for (int i = 0; i < 8; i++)
+    for (int i = 0; i < TI; i++)
 #pragma unroll
-        for (int j = 0; j < 4; j++) {
+        for (int j = 0; j < TJ; j++) {
             P[i][j] = 0.0;
-            SPs[(i * 4 + j) * RG_THREADS + tid] = 0.f;
-            Abs[(i * 4 + j) * RG_THREADS + tid] = 0.f;
+            SPs[(i * TJ + j) * RG_THREADS + tid] = 0.f;
+            Abs[(i * TJ + j) * RG_THREADS + tid] = 0.f;
         }
     issue(0, 0);
     for (int sg = 0; sg < nseg; sg++) {
@@ -740,23 +751,23 @@ __global__ void __launch_bounds__(RG_THREADS) router_bound_gemm(const float *__r
             asm volatile("cp.async.wait_group 0;" ::: "memory");
         }
         __syncthreads();
-        float acc[8][4];
+        float acc[TI][TJ];
 #pragma unroll
-        for (int i = 0; i < 8; i++)
+        for (int i = 0; i < TI; i++)
 #pragma unroll
-            for (int j = 0; j < 4; j++) acc[i][j] = 0.f;
-        const float *xb = xs + (buf * RG_T + ty) * RG_LD, *wb = ws + (buf * RG_E + tx) * RG_LD;
+            for (int j = 0; j < TJ; j++) acc[i][j] = 0.f;
+        const float *xb = xs + (buf * TT + ty) * RG_LD, *wb = ws + (buf * TE + tx) * RG_LD;
 #pragma unroll 2
         for (int k = 0; k < RG_SEG; k += 4) {
-            float4 b[4];
+            float4 b[TJ];
 #pragma unroll
-            for (int j = 0; j < 4; j++) b[j] = *reinterpret_cast<const float4 *>(wb + 16 * j * RG_LD + k);
+            for (int j = 0; j < TJ; j++) b[j] = *reinterpret_cast<const float4 *>(wb + 16 * j * RG_LD + k);
             // the segment's chain runs in k order: one FMA per step and output
 #pragma unroll
-            for (int i = 0; i < 8; i++) {
+            for (int i = 0; i < TI; i++) {
                 const float4 av = *reinterpret_cast<const float4 *>(xb + 8 * i * RG_LD + k);
 #pragma unroll
-                for (int j = 0; j < 4; j++) {
+                for (int j = 0; j < TJ; j++) {
                     acc[i][j] = fmaf(av.x, b[j].x, acc[i][j]);
                     acc[i][j] = fmaf(av.y, b[j].y, acc[i][j]);
                     acc[i][j] = fmaf(av.z, b[j].z, acc[i][j]);
@@ -765,15 +776,15 @@ __global__ void __launch_bounds__(RG_THREADS) router_bound_gemm(const float *__r
             }
         }
         // fold the segment: prefix bound with the sums before it, then the sum
-        float wn[4];
+        float wn[TJ];
 #pragma unroll
-        for (int j = 0; j < 4; j++) wn[j] = nw[(size_t)min(e0 + tx + 16 * j, E - 1) * nseg + sg];
+        for (int j = 0; j < TJ; j++) wn[j] = nw[(size_t)min(e0 + tx + 16 * j, E - 1) * nseg + sg];
 #pragma unroll
-        for (int i = 0; i < 8; i++) {
+        for (int i = 0; i < TI; i++) {
             const float xn = nx[(size_t)min(t0 + ty + 8 * i, T - 1) * nseg + sg];
 #pragma unroll
-            for (int j = 0; j < 4; j++) {
-                float *sp = SPs + (i * 4 + j) * RG_THREADS + tid, *ab = Abs + (i * 4 + j) * RG_THREADS + tid;
+            for (int j = 0; j < TJ; j++) {
+                float *sp = SPs + (i * TJ + j) * RG_THREADS + tid, *ab = Abs + (i * TJ + j) * RG_THREADS + tid;
                 const float as = __fmul_ru(xn, wn[j]), a0 = *ab;
                 const float pb = __fmaf_ru(g64, a0, __double2float_ru(fabs(P[i][j])));
                 *sp = __fmaf_ru(64.f, __fadd_ru(pb, as), *sp);
@@ -784,19 +795,27 @@ __global__ void __launch_bounds__(RG_THREADS) router_bound_gemm(const float *__r
         __syncthreads();  // this buffer is refilled two segments on
     }
 #pragma unroll
-    for (int i = 0; i < 8; i++) {
+    for (int i = 0; i < TI; i++) {
         const int t = t0 + ty + 8 * i;
         if (t >= T) continue;
 #pragma unroll
-        for (int j = 0; j < 4; j++) {
+        for (int j = 0; j < TJ; j++) {
             const int e = e0 + tx + 16 * j;
             if (e >= E) continue;
-            const double A = Abs[(i * 4 + j) * RG_THREADS + tid];
-            const double B = bound_scale * (A + (double)SPs[(i * 4 + j) * RG_THREADS + tid] + ngam * A) +
+            const double A = Abs[(i * TJ + j) * RG_THREADS + tid];
+            const double B = bound_scale * (A + (double)SPs[(i * TJ + j) * RG_THREADS + tid] + ngam * A) +
                              (1.0 + 0x1.0p-9) * gam64 * A + 0x1.0p-60;
             cand[(size_t)t * E + e] = make_double2(P[i][j], B);
         }
     }
+}
+
+template <int TI, int TJ>
+static void launch_rg(const float *W, const float *x, const float *nx, const float *nw, int T, int D, int E,
+                      double bound_scale, double ngam, double gam64, double2 *cand, cudaStream_t s) {
+    cudaFuncSetAttribute(router_bound_gemm<TI, TJ>, cudaFuncAttributeMaxDynamicSharedMemorySize, rg_smem(TI, TJ));
+    router_bound_gemm<TI, TJ><<<dim3((T + 8 * TI - 1) / (8 * TI), (E + 16 * TJ - 1) / (16 * TJ)), RG_THREADS,
+                                rg_smem(TI, TJ), s>>>(W, x, nx, nw, T, D, E, bound_scale, ngam, gam64, cand);
 }
 
 size_t route_fast_smem(int E, int D) {
@@ -858,9 +877,8 @@ int launch_route_fast_large(const float *W, const float *x, int T, int D, int E,
     const int nseg = D / RG_SEG;
     segment_norms_kernel<<<grid_for((uint64_t)T * nseg / 2, 8, 148 * 16), 256, 0, s>>>(x, T, D, nx);
     segment_norms_kernel<<<grid_for((uint64_t)E * nseg / 2, 8, 148 * 16), 256, 0, s>>>(W, E, D, nw);
-    cudaFuncSetAttribute(router_bound_gemm, cudaFuncAttributeMaxDynamicSharedMemorySize, RG_SMEM);
-    router_bound_gemm<<<dim3((T + RG_T - 1) / RG_T, (E + RG_E - 1) / RG_E), RG_THREADS, RG_SMEM, s>>>(
-        W, x, nx, nw, T, D, E, a.bound_scale, a.ngam, gam64, cand);
+    if (T >= 1024) launch_rg<8, 4>(W, x, nx, nw, T, D, E, a.bound_scale, a.ngam, gam64, cand, s);
+    else launch_rg<2, 2>(W, x, nx, nw, T, D, E, a.bound_scale, a.ngam, gam64, cand, s);
     if (E > 32 * FW_PER_LANE) { set_error("route_fast_large: at most %d experts", 32 * FW_PER_LANE); return OFB_EUNSUPPORTED; }
     cudaError_t e = cudaMemsetAsync(n_flagged, 0, sizeof(int), s);
     if (e != cudaSuccess) return cuda_status(e, "route_fast_large memset");
