@@ -107,6 +107,64 @@ __device__ float exact_logit(const float *wrow, const float *xs, int D) {
     return s;
 }
 
+// The same chains for a list of experts, computed by the whole block: the
+// threads stage 256-element chunks of up to 32 router rows in shared memory
+// (cp.async, two buffers, rows padded by 4 floats so the chain threads' float4
+// reads are conflict-free) and thread c < 32 runs expert list[c]'s chain
+// over each chunk. Every thread of the block calls this; out[c] = logit of
+// list[c].
+constexpr int XL_CK = 256, XL_LD = XL_CK + 4, XL_ROWS = 32;
+constexpr int XL_SMEM = 2 * XL_ROWS * XL_LD * 4;  // bytes of the two chunk buffers
+
+__device__ __forceinline__ void xl_cp16(float *dst, const float *src) {
+    const uint32_t d = (uint32_t)__cvta_generic_to_shared(dst);
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(d), "l"(src) : "memory");
+}
+
+__device__ void exact_logits_block(const float *__restrict__ W, int D, const float *xs, const int *list, int n,
+                                   float *out, float *wbuf, int tid, int nthreads) {
+    const int nch = (D + XL_CK - 1) / XL_CK;
+    for (int g0 = 0; g0 < n; g0 += XL_ROWS) {
+        const int ng = min(XL_ROWS, n - g0);
+        auto issue = [&](int ch) {
+            float *dst = wbuf + (ch & 1) * XL_ROWS * XL_LD;
+            const int k0 = ch * XL_CK, q4 = min(XL_CK, D - k0) / 4;
+            for (int i = tid; i < ng * q4; i += nthreads) {
+                const int r = i / q4, q = i - r * q4;
+                xl_cp16(dst + r * XL_LD + 4 * q, W + (size_t)list[g0 + r] * D + k0 + 4 * q);
+            }
+            asm volatile("cp.async.commit_group;" ::: "memory");
+        };
+        float s = 0.0f;
+        issue(0);
+        for (int ch = 0; ch < nch; ch++) {
+            if (ch + 1 < nch) {
+                issue(ch + 1);
+                asm volatile("cp.async.wait_group 1;" ::: "memory");
+            } else {
+                asm volatile("cp.async.wait_group 0;" ::: "memory");
+            }
+            __syncthreads();
+            if (tid < ng) {
+                const float *wr = wbuf + (ch & 1) * XL_ROWS * XL_LD + tid * XL_LD;
+                const float *xc = xs + ch * XL_CK;
+                const int cw = min(XL_CK, D - ch * XL_CK);
+#pragma unroll 8
+                for (int k = 0; k < cw; k += 4) {
+                    const float4 w4 = *reinterpret_cast<const float4 *>(wr + k);
+                    const float4 x4 = *reinterpret_cast<const float4 *>(xc + k);
+                    s = __fadd_rn(s, __fmul_rn(x4.x, w4.x));
+                    s = __fadd_rn(s, __fmul_rn(x4.y, w4.y));
+                    s = __fadd_rn(s, __fmul_rn(x4.z, w4.z));
+                    s = __fadd_rn(s, __fmul_rn(x4.w, w4.w));
+                }
+            }
+            __syncthreads();  // the buffer is refilled next chunk
+        }
+        if (tid < ng) out[g0 + tid] = s;
+    }
+}
+
 __device__ __forceinline__ bool close_ulps(float a, float b, int ulps) {
     int ia = __float_as_int(a), ib = __float_as_int(b);  // non-negative floats
     return abs(ia - ib) <= ulps;
@@ -366,7 +424,7 @@ __device__ void one_token_plan(const FastRouteArgs &a, const WarpSel &ws) {
 }
 
 // Large batches: one warp per token; tokens whose certificate fails go to the
-// flagged list for the block fallback (route_select_fast in list mode).
+// flagged list for the warp fallback (route_fallback_warps).
 __global__ void __launch_bounds__(256) route_certify_warps(FastRouteArgs a, int *flagged, int *n_flagged) {
     __shared__ WarpSel sel[8];
     const int wid = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -375,6 +433,191 @@ __global__ void __launch_bounds__(256) route_certify_warps(FastRouteArgs a, int 
     const bool ok = certify_token_warp(a, t, sel[wid], nullptr, nullptr);
     if (!ok && lane == 0) flagged[atomicAdd(n_flagged, 1)] = t;
 }
+
+// ---- large batches: the tokens the warp certificate left, one warp each ----
+// The block fallback of route_select_fast restated at warp granularity, so
+// that every flagged token of a batch runs at once: top-k of float(L~) (ties
+// to the smaller index), candidates = experts with L~ + B >= min over the
+// top-k of (L~ - B) - margin in ascending expert order, their exact logits
+// (lane c runs candidate c's reference-order chain, exact_logit's
+// arithmetic, its router row streamed through shared memory by cp.async), the
+// reference's selection over the candidates (exchange_pass), weights from L~.
+// Forward routing whose candidate probabilities come within a few ulps
+// recomputes every logit and the reference's softmax exactly.
+constexpr int FB_WARPS = 2;                  // tokens per block (two blocks fit an SM)
+constexpr int FB_CK = 64, FB_LD = FB_CK + 4;  // chain chunk (floats) and padded lane stride
+constexpr int FB_ST = 4;                      // chunks in flight per lane
+
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;
+}
+
+__host__ __device__ inline size_t fb_warp_smem(int E, int D) {
+    return ((size_t)FB_ST * 32 * FB_LD * 4 + (size_t)D * 4 + (size_t)E * 6 * 4 + 15) & ~(size_t)15;
+}
+
+// Reference-order logit of one router row (exact_logit's chain), the row
+// streamed through this lane's FB_ST shared-memory chunk slots.
+__device__ float exact_logit_staged(const float *__restrict__ wrow, const float *xs, int D, float *slots) {
+    const int nch = D / FB_CK;
+    auto issue = [&](int ch) {
+        if (ch < nch) {
+            float *dst = slots + (ch % FB_ST) * 32 * FB_LD;
+#pragma unroll
+            for (int q = 0; q < FB_CK / 4; q++) xl_cp16(dst + 4 * q, wrow + ch * FB_CK + 4 * q);
+        }
+        asm volatile("cp.async.commit_group;" ::: "memory");
+    };
+#pragma unroll
+    for (int c = 0; c < FB_ST - 1; c++) issue(c);
+    float s = 0.0f;
+    for (int ch = 0; ch < nch; ch++) {
+        issue(ch + FB_ST - 1);  // its slot was read by chunk ch - 1
+        asm volatile("cp.async.wait_group %0;" ::"n"(FB_ST - 1) : "memory");
+        const float *wc = slots + (ch % FB_ST) * 32 * FB_LD, *xc = xs + ch * FB_CK;
+#pragma unroll
+        for (int k = 0; k < FB_CK; k += 4) {
+            const float4 w4 = *reinterpret_cast<const float4 *>(wc + k);
+            const float4 x4 = *reinterpret_cast<const float4 *>(xc + k);
+            s = __fadd_rn(s, __fmul_rn(x4.x, w4.x));
+            s = __fadd_rn(s, __fmul_rn(x4.y, w4.y));
+            s = __fadd_rn(s, __fmul_rn(x4.z, w4.z));
+            s = __fadd_rn(s, __fmul_rn(x4.w, w4.w));
+        }
+    }
+    asm volatile("cp.async.wait_group 0;" ::: "memory");
+    return s;
+}
+
+__global__ void __launch_bounds__(FB_WARPS * 32) route_fallback_warps(FastRouteArgs a) {
+    extern __shared__ __align__(16) unsigned char fb_sm[];
+    __shared__ WarpSel sel[FB_WARPS];
+    const int wid = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int E = a.E, D = a.D, K = a.K;
+    unsigned char *mine = fb_sm + wid * fb_warp_smem(E, D);
+    float *slots = reinterpret_cast<float *>(mine) + lane * FB_LD;    // this lane's chunk slots
+    float *xs = reinterpret_cast<float *>(mine) + FB_ST * 32 * FB_LD;  // [D]
+    float *Lf = xs + D;                                                // [E] float(L~)
+    int *clist = reinterpret_cast<int *>(Lf + E);                      // [E] candidates
+    float *cv = reinterpret_cast<float *>(clist + E);                  // [E] their values
+    int *cid = reinterpret_cast<int *>(cv + E);                        // [E]
+    float *cov = reinterpret_cast<float *>(cid + E);                   // [E] exchange scratch
+    int *coid = reinterpret_cast<int *>(cov + E);                      // [E]
+    const int n_tok = *a.n_flagged;
+    for (int it = blockIdx.x * FB_WARPS + wid; it < n_tok; it += gridDim.x * FB_WARPS) {
+        const int t = a.flagged[it];
+        WarpSel &ws = sel[wid];
+        certify_token_warp(a, t, ws, nullptr, nullptr);  // top-k only: the token failed it before
+        const float4 *x4 = reinterpret_cast<const float4 *>(a.x + (size_t)t * D);
+        for (int d = lane; d < D / 4; d += 32) reinterpret_cast<float4 *>(xs)[d] = x4[d];
+        double lo_min = INFINITY;
+        for (int q = 0; q < K; q++) lo_min = fmin(lo_min, ws.L[q] - ws.B[q]);
+        // candidates in ascending expert order
+        const double2 *cd = a.cand + (size_t)t * E;
+        int nc = 0;
+        for (int e0 = 0; e0 < E; e0 += 32) {
+            const int e = e0 + lane;
+            bool cand = false;
+            if (e < E) {
+                const double2 v = cd[e];
+                Lf[e] = (float)v.x;
+                cand = v.x + v.y >= lo_min - FR_MARGIN;
+            }
+            const unsigned bal = __ballot_sync(0xffffffffu, cand);
+            if (cand) clist[nc + __popc(bal & ((1u << lane) - 1u))] = e;
+            nc += __popc(bal);
+        }
+        __syncwarp();
+        for (int c0 = 0; c0 < nc; c0 += 32) {
+            const int c = c0 + lane;
+            if (c < nc) {
+                const int e = clist[c];
+                cv[c] = exact_logit_staged(a.W + (size_t)e * D, xs, D, slots);
+                cid[c] = e;
+            }
+        }
+        __syncwarp();
+        int mode = 1;
+        if (a.routing == OFB_ROUTE_FORWARD) {
+            // probabilities are ordered like expf(l - max) unless two of them
+            // are within a few ulps (then the division could tie them)
+            float m = -INFINITY;
+            for (int c = lane; c < nc; c += 32) m = fmaxf(m, cv[c]);
+            m = warp_max(m);
+            for (int c = lane; c < nc; c += 32) cv[c] = ofb_exact_expf(__fsub_rn(cv[c], m));
+            __syncwarp();
+            bool close = false;
+            for (int c = lane; c < nc; c += 32)
+                for (int c2 = 0; c2 < nc; c2++)
+                    if (c2 != c && close_ulps(cv[c], cv[c2], 4)) close = true;
+            if (__any_sync(0xffffffffu, close)) {
+                // ---- every logit exact, the reference's softmax
+                mode = 2;
+                for (int e0 = 0; e0 < E; e0 += 32) {
+                    const int e = e0 + lane;
+                    if (e < E) {
+                        cv[e] = exact_logit_staged(a.W + (size_t)e * D, xs, D, slots);
+                        cid[e] = e;
+                    }
+                }
+                __syncwarp();
+                float mx = -INFINITY;
+                for (int e = lane; e < E; e += 32) mx = fmaxf(mx, cv[e]);
+                mx = warp_max(mx);
+                for (int e = lane; e < E; e += 32) cv[e] = ofb_exact_expf(__fsub_rn(cv[e], mx));
+                __syncwarp();
+                float sum = 0.0f;
+                if (lane == 0)
+                    for (int e = 0; e < E; e++) sum = __fadd_rn(sum, cv[e]);
+                sum = __shfl_sync(0xffffffffu, sum, 0);
+                for (int e = lane; e < E; e += 32) cv[e] = __fdiv_rn(cv[e], sum);
+                __syncwarp();
+                nc = E;
+            }
+        }
+        for (int i = 0; i < K; i++) exchange_pass(cv, cid, cov, coid, nc, i, lane);
+        uint32_t *io = a.idx + (size_t)t * K;
+        float *wo = a.w + (size_t)t * K;
+        if (mode == 2) {
+            // bit-exact: cv holds the reference's probabilities in its order
+            if (lane == 0) {
+                float ssum = 0.0f;
+                for (int q = 0; q < K; q++) ssum = __fadd_rn(ssum, cv[q]);
+                for (int q = 0; q < K; q++) {
+                    io[q] = (uint32_t)cid[q];
+                    wo[q] = a.renorm ? __fdiv_rn(cv[q], ssum) : cv[q];
+                }
+            }
+        } else {
+            const float m = Lf[cid[0]];
+            float sum = 0.f;
+            if (a.routing == OFB_ROUTE_FORWARD) {
+                for (int e = lane; e < E; e += 32) sum += expf(Lf[e] - m);
+            } else if (lane < K) {
+                sum = expf(Lf[cid[lane]] - m);
+            }
+            sum = warp_sum(sum);
+            float wq = lane < K ? expf(Lf[cid[lane]] - m) / sum : 0.f;
+            float ss = 0.f;
+            for (int q = 0; q < K; q++) ss += __shfl_sync(0xffffffffu, wq, q);
+            if (lane < K) {
+                io[lane] = (uint32_t)cid[lane];
+                wo[lane] = (a.routing == OFB_ROUTE_FORWARD && a.renorm) ? wq / ss : wq;
+            }
+        }
+        if (lane == 0 && a.stats) atomicAdd(&a.stats[mode], 1);
+        __syncwarp();  // the next token reuses this warp's arrays
+    }
+}
+
+// Dynamic shared memory of route_select_fast: Ls, Bs (f64), val, id, oval,
+// oid, xs, taken, then (16-byte aligned) the exact-chain chunk buffers.
+__host__ __device__ inline size_t xl_offset(int E, int D) {
+    return ((size_t)E * (8 + 8 + 4 + 4 + 4 + 4 + 4) + (size_t)D * 4 + 15) & ~(size_t)15;
+}
+constexpr int FR_SMEM_MAX = 160 * 1024;
 
 __global__ void __launch_bounds__(FR_THREADS) route_select_fast(FastRouteArgs a) {
     DTRACE_START(rf, 1)
@@ -391,6 +634,7 @@ __global__ void __launch_bounds__(FR_THREADS) route_select_fast(FastRouteArgs a)
     int *oid = reinterpret_cast<int *>(oval + E);       // [E]
     float *xs = reinterpret_cast<float *>(oid + E);     // [D]
     int *taken = reinterpret_cast<int *>(xs + D);       // [E]
+    float *wbuf = reinterpret_cast<float *>(smem + xl_offset(E, D));  // exact-chain chunk buffers
     __shared__ KeyIdx s_cand[32 * 17];
     __shared__ int s_top[17];
     __shared__ int s_mode;  // 0 certified, 1 candidate recompute, 2 full recompute
@@ -406,13 +650,12 @@ __global__ void __launch_bounds__(FR_THREADS) route_select_fast(FastRouteArgs a)
 
     pdl_wait();
     DTRACE_WAITED(rf, 1)
-    // one token per block, or (list mode, large batches) every flagged token
-    const int n_tok = a.flagged ? *a.n_flagged : 1;
-    for (int it = a.flagged ? blockIdx.x : 0; it < n_tok; it += a.flagged ? gridDim.x : 1) {
-    const int t = a.flagged ? a.flagged[it] : blockIdx.x;
+    // one token per block
+    {
+    const int t = blockIdx.x;
     const float *xt = a.x + (size_t)t * D;
     const double2 *cd = a.cand + (size_t)t * E;
-    if (E <= 32 * FW_PER_LANE && !a.flagged) {
+    if (E <= 32 * FW_PER_LANE) {
         // ---- warp 0: top-k, certificate and (when certified) weights from
         // registers; the block steps below run only for uncertain tokens
         if (wid == 0) {
@@ -480,7 +723,7 @@ __global__ void __launch_bounds__(FR_THREADS) route_select_fast(FastRouteArgs a)
     }
     __syncthreads();
     }
-    const bool warp_done = (E <= 32 * FW_PER_LANE) && !a.flagged && s_mode == 0;  // weights already written
+    const bool warp_done = (E <= 32 * FW_PER_LANE) && s_mode == 0;  // weights already written
 
     if (s_mode != 0) {
         // ---- candidate recompute with the reference's exact chain --------
@@ -515,11 +758,11 @@ __global__ void __launch_bounds__(FR_THREADS) route_select_fast(FastRouteArgs a)
             __syncthreads();
         }
         const int nc = s_nc;
+        exact_logits_block(a.W, D, xs, s_clist, nc, s_cv, wbuf, tid, FR_THREADS);
+        __syncthreads();
         for (int c = tid; c < nc; c += FR_THREADS) {
             const int e = s_clist[c];
-            const float l = exact_logit(a.W + (size_t)e * D, xs, D);
-            val[e] = l;
-            s_cv[c] = l;
+            val[e] = s_cv[c];
             s_cid[c] = e;
         }
         if (tid == 0) s_full = 0;
@@ -615,11 +858,7 @@ __global__ void __launch_bounds__(FR_THREADS) route_select_fast(FastRouteArgs a)
         }
     }
     if (tid == 0 && a.stats && !warp_done) atomicAdd(&a.stats[s_mode], 1);
-    __syncthreads();  // the next token reuses the shared arrays
-    }
-    if (a.flagged) {
-        DTRACE_END(rf, 1)
-        return;
+    __syncthreads();  // the plan below reuses the shared arrays
     }
 
     // ---- the block finishing the last token builds the dispatch plan --------
@@ -819,7 +1058,7 @@ static void launch_rg(const float *W, const float *x, const float *nx, const flo
 }
 
 size_t route_fast_smem(int E, int D) {
-    size_t sel = (size_t)E * (8 + 8 + 4 + 4 + 4 + 4 + 4) + (size_t)D * 4;
+    size_t sel = xl_offset(E, D) + XL_SMEM;
     size_t plan = 2 * 1024 * sizeof(int);
     return sel > plan ? sel : plan;
 }
@@ -843,10 +1082,10 @@ int launch_route_fast(const float *W, const float *x, const float *gate_v, int T
     const size_t smem = route_fast_smem(E, D);
     static bool attr_set = false;
     if (!attr_set) {
-        cudaFuncSetAttribute(route_select_fast, cudaFuncAttributeMaxDynamicSharedMemorySize, 64 * 1024);
+        cudaFuncSetAttribute(route_select_fast, cudaFuncAttributeMaxDynamicSharedMemorySize, FR_SMEM_MAX);
         attr_set = true;
     }
-    if (smem > 64 * 1024) { set_error("route_fast: E/D too large for shared memory"); return OFB_EUNSUPPORTED; }
+    if (smem > FR_SMEM_MAX) { set_error("route_fast: E/D too large for shared memory"); return OFB_EUNSUPPORTED; }
     cudaError_t e = launch_pdl(route_rows_kernel, dim3((E + 1 + RR_WARPS - 1) / RR_WARPS, T),
                                dim3(RR_WARPS * 32), 0, s, a);
     if (e == cudaSuccess) e = launch_pdl(route_select_fast, dim3(T), dim3(FR_THREADS), smem, s, a);
@@ -871,8 +1110,8 @@ int launch_route_fast_large(const float *W, const float *x, int T, int D, int E,
     a.flagged = flagged;
     a.n_flagged = n_flagged;
     const size_t smem = route_fast_smem(E, D);
-    if (smem > 64 * 1024) { set_error("route_fast: E/D too large for shared memory"); return OFB_EUNSUPPORTED; }
-    cudaFuncSetAttribute(route_select_fast, cudaFuncAttributeMaxDynamicSharedMemorySize, 64 * 1024);
+    if (smem > FR_SMEM_MAX) { set_error("route_fast: E/D too large for shared memory"); return OFB_EUNSUPPORTED; }
+    cudaFuncSetAttribute(route_select_fast, cudaFuncAttributeMaxDynamicSharedMemorySize, FR_SMEM_MAX);
     float *nx = norms, *nw = norms + (size_t)T * (D / RG_SEG);
     const int nseg = D / RG_SEG;
     segment_norms_kernel<<<grid_for((uint64_t)T * nseg / 2, 8, 148 * 16), 256, 0, s>>>(x, T, D, nx);
@@ -883,7 +1122,19 @@ int launch_route_fast_large(const float *W, const float *x, int T, int D, int E,
     cudaError_t e = cudaMemsetAsync(n_flagged, 0, sizeof(int), s);
     if (e != cudaSuccess) return cuda_status(e, "route_fast_large memset");
     route_certify_warps<<<(T + 7) / 8, 256, 0, s>>>(a, flagged, n_flagged);
-    route_select_fast<<<T < 148 ? T : 148, FR_THREADS, smem, s>>>(a);  // flagged tokens only
+    // flagged tokens, one warp each, all at once (blocks past the flagged
+    // count exit at once)
+    const size_t fb_smem = FB_WARPS * fb_warp_smem(E, D);
+    if ((reinterpret_cast<uintptr_t>(W) | reinterpret_cast<uintptr_t>(x)) & 15) {
+        set_error("route_fast_large: router and activations must be 16-byte aligned");
+        return OFB_EINVAL;
+    }
+    if (fb_smem > 227 * 1024 || D % FB_CK) {
+        set_error("route_fast_large: d_model %d / %d experts do not fit the fallback", D, E);
+        return OFB_EUNSUPPORTED;
+    }
+    cudaFuncSetAttribute(route_fallback_warps, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)fb_smem);
+    route_fallback_warps<<<(T + FB_WARPS - 1) / FB_WARPS, FB_WARPS * 32, fb_smem, s>>>(a);
     OFB_CHECK_LAUNCH("route_fast_large");
     return OFB_OK;
 }
