@@ -58,7 +58,8 @@ constexpr int PF_NA = 2;         // A stages in TMEM
 constexpr int B_ROWS = 16;       // rows per B box
 constexpr int B_STAGE = PF_NMAX * 128;     // 24 KB: up to 192 rows x 128 B
 constexpr int RAW4 = PF_M * Q4K_BYTES;      // raw Q4_K bytes of one matrix per raw stage (one block)
-constexpr long long WAIT_LIMIT = 1ll << 24;  // try_wait polls before giving up
+constexpr long long WAIT_LIMIT = 1ll << 26;       // try_wait polls before giving up
+constexpr unsigned long long WAIT_NS = 250000000;  // or this much time (0.25 s), whichever comes first
 
 struct PrefillArgs {
     int T, D, H, E, K;
@@ -104,9 +105,11 @@ __device__ __forceinline__ uint32_t smem_u32(const void *p) {
 __device__ __forceinline__ void mbar_init(uint64_t *b, uint32_t count) {
     asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(b)), "r"(count));
 }
-// Bounded wait for the mbarrier phase with the given parity; false on timeout.
+// Bounded wait for the mbarrier phase with the given parity; false on timeout
+// (0.25 s by %globaltimer, read every 256 polls, or 2^26 polls).
 __device__ __forceinline__ bool mbar_wait(uint64_t *b, uint32_t parity) {
     const uint32_t a = smem_u32(b);
+    unsigned long long t0 = 0;
     for (long long i = 0; i < WAIT_LIMIT; i++) {
         uint32_t done;
         asm volatile(
@@ -115,6 +118,12 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *b, uint32_t parity) {
             : "r"(a), "r"(parity)
             : "memory");
         if (done) return true;
+        if ((i & 255) == 255) {
+            unsigned long long t;
+            asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+            if (i == 255) t0 = t;
+            else if (t - t0 > WAIT_NS) return false;
+        }
     }
     return false;
 }
@@ -165,6 +174,11 @@ __device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t v[16]) 
 __device__ __forceinline__ void tmem_st8(uint32_t taddr, const uint32_t v[8]) {
     asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"r"(taddr), "r"(v[0]),
                  "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7])
+                 : "memory");
+}
+__device__ __forceinline__ void tmem_st4(uint32_t taddr, const uint32_t v[4]) {
+    asm volatile("tcgen05.st.sync.aligned.32x32b.x4.b32 [%0], {%1,%2,%3,%4};" ::"r"(taddr), "r"(v[0]), "r"(v[1]),
+                 "r"(v[2]), "r"(v[3])
                  : "memory");
 }
 __device__ __forceinline__ void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
@@ -324,29 +338,42 @@ __device__ __forceinline__ void q4_deq(const uint8_t *raw, int c, int r, int hh,
 }
 
 // ---- A operand, Q6_K (from the raw slab in shared memory) ----------------------------
-// 64-element chunk q of a block: half = q/2, quads 2*(q%2) and 2*(q%2)+1
-// (32 elements each). Four threads per row: thread (r, hh, g) produces
-// elements 16g..16g+15 of quad 2*(q%2)+hh (one scale), TMEM columns
-// 16hh+8g..16hh+8g+7 of the stage. Value = (q-32) exactly
-// (bf16(128+q) - 160) times bf16(d*sc), rounded once to bf16; d*sc is the
-// reference's fp32 product.
-__device__ __forceinline__ void q6_deq(const uint8_t *slab, int row_bytes, int stage, int r, int hh, int g,
-                                       uint32_t out[8]) {
-    const int b = stage >> 2, q64 = stage & 3, half6 = q64 >> 1, quad = 2 * (q64 & 1) + hh;
-    const uint8_t *blk = slab + r * row_bytes + b * Q6K_BYTES;
-    const uint8_t *ql = blk + half6 * 64 + (quad & 1) * 32 + g * 16;
-    const uint8_t *qh = blk + 128 + half6 * 32 + g * 16;
-    const float d = half_bits_ref((uint32_t)blk[208] | ((uint32_t)blk[209] << 8));
-    const __nv_bfloat162 d2 =
-        __float2bfloat162_rn(__fmul_rn(d, (float)(int8_t)blk[192 + half6 * 8 + quad * 2 + g]));
+// 8 bytes at a 2-byte aligned shared-memory address.
+__device__ __forceinline__ void lds_u64_2b(const uint8_t *p, uint32_t &lo, uint32_t &hi) {
+    const uintptr_t a = reinterpret_cast<uintptr_t>(p);
+    const uint32_t *b = reinterpret_cast<const uint32_t *>(a & ~uintptr_t(3));
+    const unsigned sh = (unsigned)(a & 3) * 8;
+    const uint32_t w0 = b[0], w1 = b[1], w2 = b[2];
+    lo = __funnelshift_r(w0, w1, sh);
+    hi = __funnelshift_r(w1, w2, sh);
+}
+// Half hb of a row's Q6_K blocks (block hb/2, elements 128 (hb%2) + 0..127:
+// four quads of 32) for thread g: positions l = 8g..8g+7 of every quad, 32
+// elements, each quant and scale byte read once. out[quad][j]: the bf16
+// pair (l + 2j, l + 2j + 1) of the quad, (q-32) exactly times bf16(d*sc)
+// rounded once (d*sc the reference's fp32 product).
+__device__ __forceinline__ void q6_deq_half(const uint8_t *slab, int row_bytes, int hb, int r, int g,
+                                            uint32_t out[4][4]) {
+    const int half6 = hb & 1;
+    const uint8_t *blk = slab + r * row_bytes + (hb >> 1) * Q6K_BYTES;
+    uint32_t l0[2], l1[2], qh[2];
+    lds_u64_2b(blk + half6 * 64 + 8 * g, l0[0], l0[1]);       // quads 0 (low nibbles) and 2 (high)
+    lds_u64_2b(blk + half6 * 64 + 32 + 8 * g, l1[0], l1[1]);  // quads 1 and 3
+    lds_u64_2b(blk + 128 + half6 * 32 + 8 * g, qh[0], qh[1]);  // two high bits of every quad
+    const float d = half_bits_ref(*reinterpret_cast<const uint16_t *>(blk + 208));
+    const uint8_t *sc = blk + 192 + half6 * 8 + (g >> 1);
     const __nv_bfloat162 c160 = __float2bfloat162_rn(160.f);
-    const int nsh = (quad >= 2) ? 4 : 0, hsh = 2 * quad;
 #pragma unroll
-    for (int k = 0; k < 4; k++) {
-        const uint32_t wl = lds_u32_2b(ql + 4 * k), wh = lds_u32_2b(qh + 4 * k);
-        const uint32_t q = ((wl >> nsh) & 0x0F0F0F0Fu) | (((wh >> hsh) & 0x03030303u) << 4);
-        out[2 * k] = bf2_bits(__hmul2(__hsub2(q_pair128<0>(q), c160), d2));
-        out[2 * k + 1] = bf2_bits(__hmul2(__hsub2(q_pair128<2>(q), c160), d2));
+    for (int quad = 0; quad < 4; quad++) {
+        const __nv_bfloat162 d2 = __float2bfloat162_rn(__fmul_rn(d, (float)(int8_t)sc[quad * 2]));
+        const uint32_t *wl = (quad & 1) ? l1 : l0;
+        const int nsh = quad >= 2 ? 4 : 0, hsh = 2 * quad;
+#pragma unroll
+        for (int k = 0; k < 2; k++) {
+            const uint32_t q = ((wl[k] >> nsh) & 0x0F0F0F0Fu) | (((qh[k] >> hsh) & 0x03030303u) << 4);
+            out[quad][2 * k] = bf2_bits(__hmul2(__hsub2(q_pair128<0>(q), c160), d2));
+            out[quad][2 * k + 1] = bf2_bits(__hmul2(__hsub2(q_pair128<2>(q), c160), d2));
+        }
     }
 }
 
@@ -675,19 +702,27 @@ __global__ void __launch_bounds__(UP_THREADS, 1)
 // at H = 512) come in one bulk copy into one of two slab buffers while the
 // previous unit computes; the tensor core accumulates into one of two TMEM
 // accumulators while 8 epilogue warps add the other one's w * y into out.
-// TMEM: accumulators [0,192) and [192,384), A stages [384,448).
-constexpr int DN_EPI0 = 20;                 // first epilogue warp
+// Dequantising thread (r, g) decodes positions 8g..8g+7 of all four quads of
+// a half block (two A stages at once, every byte read once). Two threads
+// issue the MMAs (a thread waits about a hundred cycles per tcgen05.mma): for
+// units of N <= 96, issuer p takes the stages of parity p into an accumulator
+// of its own (columns +0 and +96 of the unit's buffer) and the epilogue adds
+// the two; wider units use issuer 0 alone.
+// TMEM: accumulators [0,192) and [192,384), four A stages [384,512).
+constexpr int DN_EPI0 = 20;                 // first epilogue warp (warps 1 and 3 issue MMAs)
 constexpr int DN_NEPI = 8;                  // epilogue warps (2 per TMEM lane quarter)
 constexpr int DN_THREADS = (DN_EPI0 + DN_NEPI) * 32;
 constexpr int DN_ACC1 = PF_NMAX;            // TMEM column of the second accumulator
+constexpr int DN_SPLIT = PF_NMAX / 2;       // widest unit with the parity split
 constexpr int DN_A = 2 * PF_NMAX;           // TMEM column of A stage 0 (32 columns each)
+constexpr int DN_NA = 4;                    // A stages (two half blocks in flight)
 
 __host__ __device__ inline int down_slab_bytes(int H) { return PF_M * (H / QK) * Q6K_BYTES; }
 __host__ __device__ inline int down_smem(int H) { return 1024 + PF_STG * B_STAGE + 2 * down_slab_bytes(H); }
 
 struct DownBars {
     uint64_t bfull[PF_STG], bempty[PF_STG];  // B: TMA -> MMA
-    uint64_t afull[PF_NA], aempty[PF_NA];    // A in TMEM: dequant -> MMA
+    uint64_t afull[DN_NA], aempty[DN_NA];    // A in TMEM: dequant -> MMA
     uint64_t sfull[2], sempty[2];            // Q6_K slabs: bulk copy -> dequant
     uint64_t cfull[2], cempty[2];            // accumulators: MMA -> epilogue
 };
@@ -705,7 +740,8 @@ __global__ void __launch_bounds__(DN_THREADS, 1)
     const int n_units = *a.n_tiles * nblk;
     if ((int)blockIdx.x >= n_units) return;
     const int n_my = (n_units - (int)blockIdx.x + (int)gridDim.x - 1) / (int)gridDim.x;
-    PF_TR(unsigned long long *tr = pf_tr(1); const unsigned long long tc0 = clock64();)
+    PF_TR(unsigned long long *tr = pf_tr(1); const unsigned long long tc0 = clock64(); unsigned long long tc;
+          unsigned long long acc[20] = {};)
     const int TK = a.T * a.K;
     const int row_bytes = (a.H / QK) * Q6K_BYTES, slab_bytes = PF_M * row_bytes;
     const size_t exp_bytes = (size_t)row_bytes * a.D;
@@ -717,14 +753,14 @@ __global__ void __launch_bounds__(DN_THREADS, 1)
             mbar_init(&R.bfull[i], 1);
             mbar_init(&R.bempty[i], 1);
         }
-        for (int i = 0; i < PF_NA; i++) {
+        for (int i = 0; i < DN_NA; i++) {
             mbar_init(&R.afull[i], PF_NDQW);
             mbar_init(&R.aempty[i], 1);
         }
         for (int i = 0; i < 2; i++) {
             mbar_init(&R.sfull[i], 1);
             mbar_init(&R.sempty[i], PF_NDQW);
-            mbar_init(&R.cfull[i], 1);
+            mbar_init(&R.cfull[i], 2);
             mbar_init(&R.cempty[i], DN_NEPI);
         }
     }
@@ -756,55 +792,88 @@ __global__ void __launch_bounds__(DN_THREADS, 1)
                 }
             }
         }
-    } else if (warp == 1) {
-        // MMA issuer: unit k accumulates into TMEM accumulator k % 2
+    } else if (warp == 1 || warp == 3) {
+        // MMA issuer p: unit k accumulates into TMEM buffer k % 2; both
+        // issuers wait for the buffer's release and commit to its cfull
+        const int par = warp == 3;
         if (lane == 0) {
             int g = 0;
             for (int k = 0; k < n_my && ok; k++) {
                 const int tile = ((int)blockIdx.x + k * (int)gridDim.x) / nblk;
-                const uint32_t idesc = instr_desc((a.tile_n[tile] + 15) & ~15);
+                const int nn = (a.tile_n[tile] + 15) & ~15;
+                const uint32_t idesc = instr_desc(nn);
+                const bool split = nn <= DN_SPLIT;
                 const int ab = k & 1;
+                PF_TR(tc = clock64();)
                 if (k >= 2) ok = mbar_wait(&R.cempty[ab], ((k >> 1) - 1) & 1);
+                PF_TR(acc[14] += clock64() - tc;)
                 if (!ok) break;
                 tc_fence_after();
-                const uint32_t dacc = tbase + ab * DN_ACC1;
+                const uint32_t dacc = tbase + ab * DN_ACC1 + par * DN_SPLIT;
+                const int first = split ? 2 : 1;  // stages before this accumulator's second
                 for (int i = 0; i < nstages && ok; i++, g++) {
-                    const int sa = g % PF_NA, sb = g % PF_STG;
-                    ok = mbar_wait(&R.afull[sa], (g / PF_NA) & 1) && mbar_wait(&R.bfull[sb], (g / PF_STG) & 1);
+                    if (split ? (i & 1) != par : par != 0) continue;
+                    const int sa = g % DN_NA, sb = g % PF_STG;
+                    PF_TR(tc = clock64();)
+                    ok = mbar_wait(&R.afull[sa], (g / DN_NA) & 1);
+                    PF_TR(acc[6] += clock64() - tc; tc = clock64();)
+                    ok = ok && mbar_wait(&R.bfull[sb], (g / PF_STG) & 1);
+                    PF_TR(acc[7] += clock64() - tc; tc = clock64();)
                     if (!ok) break;
                     tc_fence_after();
                     const uint32_t bb = smem_u32(bst + sb * B_STAGE), ta = tbase + DN_A + sa * 32;
 #pragma unroll
                     for (int kk = 0; kk < PF_KS / 16; kk++)
-                        mma_bf16_ta(dacc, ta + kk * 8, sw128_desc(bb + kk * 32), idesc, (i | kk) != 0);
+                        mma_bf16_ta(dacc, ta + kk * 8, sw128_desc(bb + kk * 32), idesc, i >= first || kk != 0);
                     mma_commit(&R.aempty[sa]);
                     mma_commit(&R.bempty[sb]);
+                    PF_TR(acc[16] += clock64() - tc;)
                 }
-                mma_commit(&R.cfull[ab]);  // arrives once the unit's MMAs complete
+                mma_commit(&R.cfull[ab]);  // arrives once this issuer's MMAs complete
+                // an issuer that sat out a unit waits for it to finish: the
+                // next unit's buffer wait covers the unit before, not this
+                // one, and running on could put its A waits two phases ahead
+                if (!split && par != 0) ok = mbar_wait(&R.cfull[ab], (k >> 1) & 1);
             }
         }
     } else if (warp >= PF_DQ0 / 32 && warp < DN_EPI0) {
-        // dequantisers: warp w owns TMEM lanes (= rows) 32*(w%4).. of A
-        const int grp = (warp - PF_DQ0 / 32) >> 2, hh = grp & 1, gq = grp >> 1;
+        // dequantisers: warp w owns TMEM lanes (= rows) 32*(w%4).. of A and
+        // positions 8g..8g+7 (g = (w-4)/4) of every quad: per half block h
+        // it fills A stages 2h (quads 0, 1) and 2h + 1 (quads 2, 3), columns
+        // 4g.. and 16 + 4g.. of each
+        const int gq = (warp - PF_DQ0 / 32) >> 2;
         const int r = (warp & 3) * 32 + lane;
-        const uint32_t t_st = tbase + ((uint32_t)((warp & 3) * 32) << 16) + DN_A + hh * 16 + gq * 8;
-        int g = 0;
+        const uint32_t t_st = tbase + ((uint32_t)((warp & 3) * 32) << 16) + DN_A + 4 * gq;
+        const int nhalf = nstages / 2;
+        int g = 0;  // A stages
         for (int k = 0; k < n_my && ok; k++) {
             const int sb = k & 1;
+            PF_TR(tc = clock64();)
             ok = mbar_wait(&R.sfull[sb], (k >> 1) & 1);
+            PF_TR(if (threadIdx.x == PF_DQ0) acc[8] += clock64() - tc;)
             const uint8_t *sl = slab + sb * slab_bytes;
-            for (int i = 0; i < nstages && ok; i++, g++) {
-                const int sa = g % PF_NA;
-                if (g >= PF_NA) ok = mbar_wait(&R.aempty[sa], (g / PF_NA - 1) & 1);
+            for (int h = 0; h < nhalf && ok; h++, g += 2) {
+                const int s0 = g % DN_NA;  // stages s0, s0 + 1 (DN_NA is even)
+                PF_TR(tc = clock64();)
+                if (g >= DN_NA)
+                    ok = mbar_wait(&R.aempty[s0], (g / DN_NA - 1) & 1) &&
+                         mbar_wait(&R.aempty[s0 + 1], (g / DN_NA - 1) & 1);
+                PF_TR(if (threadIdx.x == PF_DQ0) acc[9] += clock64() - tc; tc = clock64();)
                 if (!ok) break;
                 tc_fence_after();
-                uint32_t v[8];
-                q6_deq(sl, row_bytes, i, r, hh, gq, v);
-                tmem_st8(t_st + sa * 32, v);
+                uint32_t v[4][4];
+                q6_deq_half(sl, row_bytes, h, r, gq, v);
+#pragma unroll
+                for (int quad = 0; quad < 4; quad++)
+                    tmem_st4(t_st + (s0 + (quad >> 1)) * 32 + (quad & 1) * 16, v[quad]);
                 tmem_st_wait();
+                PF_TR(if (threadIdx.x == PF_DQ0) acc[10] += clock64() - tc;)
                 tc_fence_before();
                 __syncwarp();
-                if (lane == 0) mbar_arrive(&R.afull[sa]);
+                if (lane == 0) {
+                    mbar_arrive(&R.afull[s0]);
+                    mbar_arrive(&R.afull[s0 + 1]);
+                }
             }
             __syncwarp();
             if (ok && lane == 0) mbar_arrive(&R.sempty[sb]);  // done reading this slab
@@ -824,7 +893,9 @@ __global__ void __launch_bounds__(DN_THREADS, 1)
             // every epilogue warp reaches this barrier (its wait is bounded),
             // so they leave together on a timeout; it also marks the
             // previous unit's readers done
+            PF_TR(tc = clock64();)
             ok = bar_and(2, DN_NEPI * 32, mbar_wait(&R.cfull[ab], (k >> 1) & 1));
+            PF_TR(if (threadIdx.x == DN_EPI0 * 32) acc[17] += clock64() - tc; tc = clock64();)
             if (!ok) break;
             tc_fence_after();
             // token and weight of each tile row, shared by the epilogue warps
@@ -836,11 +907,19 @@ __global__ void __launch_bounds__(DN_THREADS, 1)
             }
             asm volatile("bar.sync 2, %0;" ::"n"(DN_NEPI * 32) : "memory");
             const uint32_t tacc = tbase + lane_off + ab * DN_ACC1;
+            const bool split = nn <= DN_SPLIT;
             float *orow = a.out + n0 + q * 32 + 4 * (lane & 7);
             for (int j0 = half * 16; j0 < n; j0 += 32) {
                 float y[16];
                 tmem_ld8(tacc + j0, y);
-                if (j0 + 8 < nn) tmem_ld8(tacc + j0 + 8, y + 8);
+                tmem_ld8(tacc + j0 + 8, y + 8);
+                if (split) {
+                    float y1[16];
+                    tmem_ld8(tacc + DN_SPLIT + j0, y1);
+                    tmem_ld8(tacc + DN_SPLIT + j0 + 8, y1 + 8);
+#pragma unroll
+                    for (int j = 0; j < 16; j++) y[j] += y1[j];
+                }
 #pragma unroll
                 for (int j = 0; j < 16; j++) blk[j * 33 + lane] = y[j];
                 __syncwarp();
@@ -859,11 +938,15 @@ __global__ void __launch_bounds__(DN_THREADS, 1)
                 }
                 __syncwarp();
             }
+            PF_TR(if (threadIdx.x == DN_EPI0 * 32) acc[18] += clock64() - tc;)
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(&R.cempty[ab]);
         }
     }
+    PF_TR(if (tr) {
+        _Pragma("unroll") for (int i = 4; i < 20; i++) if (acc[i]) atomicAdd(&tr[i], acc[i]);
+    })
     ok = __syncthreads_and(ok);
     if (!ok && threadIdx.x == 0) atomicExch(a.err, 1);
     PF_TR(if (tr && threadIdx.x == 0) { tr[2] = clock64() - tc0; tr[13] = n_my; })
