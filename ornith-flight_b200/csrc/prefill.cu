@@ -213,6 +213,29 @@ __device__ __forceinline__ void tmem_ld8(uint32_t taddr, float v[8]) {
 #pragma unroll
     for (int i = 0; i < 8; i++) v[i] = __uint_as_float(r[i]);
 }
+// Loads that leave the wait to the caller (tmem_ld_wait), so several are in
+// flight at once.
+__device__ __forceinline__ void tmem_ld16_nw(uint32_t taddr, uint32_t r[16]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+        : "r"(taddr));
+}
+__device__ __forceinline__ void tmem_ld8_nw(uint32_t taddr, uint32_t r[8]) {
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+                   "=r"(r[7])
+                 : "r"(taddr));
+}
+// Waits for this thread's outstanding TMEM loads; the registers they wrote
+// are passed through so no use of them is moved above the wait.
+template <int N>
+__device__ __forceinline__ void tmem_ld_wait(uint32_t (&r)[N]) {
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+    for (int i = 0; i < N; i++) asm volatile("" : "+r"(r[i]));
+}
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void async_proxy_fence() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
@@ -646,23 +669,31 @@ __global__ void __launch_bounds__(UP_THREADS, 1)
             const uint32_t tg1 = tbase + lane_off + ua.col(0, 1), tu1 = tbase + lane_off + ua.col(1, 1);
             __nv_bfloat16 *hrow = a.hb + (size_t)s0 * a.H + m0 + q * 32 + 8 * (lane & 3);
             for (int j0 = half * 16; j0 < n; j0 += 32) {
+                if (ua.split) {
 #pragma unroll
-                for (int jh = 0; jh < 16; jh += 8) {
-                    float gv[8], uv[8];
-                    tmem_ld8(tg + j0 + jh, gv);
-                    tmem_ld8(tu + j0 + jh, uv);
-                    if (ua.split) {
-                        float g1[8], u1[8];
-                        tmem_ld8(tg1 + j0 + jh, g1);
-                        tmem_ld8(tu1 + j0 + jh, u1);
+                    for (int jh = 0; jh < 16; jh += 8) {
+                        uint32_t r[32];
+                        tmem_ld8_nw(tg + j0 + jh, r);
+                        tmem_ld8_nw(tu + j0 + jh, r + 8);
+                        tmem_ld8_nw(tg1 + j0 + jh, r + 16);
+                        tmem_ld8_nw(tu1 + j0 + jh, r + 24);
+                        tmem_ld_wait(r);
 #pragma unroll
                         for (int j = 0; j < 8; j++) {
-                            gv[j] += g1[j];
-                            uv[j] += u1[j];
+                            const float gv = __uint_as_float(r[j]) + __uint_as_float(r[16 + j]);
+                            const float uv = __uint_as_float(r[8 + j]) + __uint_as_float(r[24 + j]);
+                            blk[(jh + j) * 40 + lane] = __float2bfloat16_rn(silu_mul(gv, uv));
                         }
                     }
+                } else {
+                    uint32_t r[32];
+                    tmem_ld16_nw(tg + j0, r);
+                    tmem_ld16_nw(tu + j0, r + 16);
+                    tmem_ld_wait(r);
 #pragma unroll
-                    for (int j = 0; j < 8; j++) blk[(jh + j) * 40 + lane] = __float2bfloat16_rn(silu_mul(gv[j], uv[j]));
+                    for (int j = 0; j < 16; j++)
+                        blk[j * 40 + lane] =
+                            __float2bfloat16_rn(silu_mul(__uint_as_float(r[j]), __uint_as_float(r[16 + j])));
                 }
                 __syncwarp();
                 // lane: token j0 + (lane >> 2) + 8 it, rows 8*(lane & 3)..+7
@@ -911,14 +942,14 @@ __global__ void __launch_bounds__(DN_THREADS, 1)
             float *orow = a.out + n0 + q * 32 + 4 * (lane & 7);
             for (int j0 = half * 16; j0 < n; j0 += 32) {
                 float y[16];
-                tmem_ld8(tacc + j0, y);
-                tmem_ld8(tacc + j0 + 8, y + 8);
-                if (split) {
-                    float y1[16];
-                    tmem_ld8(tacc + DN_SPLIT + j0, y1);
-                    tmem_ld8(tacc + DN_SPLIT + j0 + 8, y1 + 8);
+                {
+                    uint32_t r[32];
+                    tmem_ld16_nw(tacc + j0, r);
+                    if (split) tmem_ld16_nw(tacc + DN_SPLIT + j0, r + 16);
+                    tmem_ld_wait(r);
 #pragma unroll
-                    for (int j = 0; j < 16; j++) y[j] += y1[j];
+                    for (int j = 0; j < 16; j++)
+                        y[j] = split ? __uint_as_float(r[j]) + __uint_as_float(r[16 + j]) : __uint_as_float(r[j]);
                 }
 #pragma unroll
                 for (int j = 0; j < 16; j++) blk[j * 33 + lane] = y[j];
