@@ -802,19 +802,28 @@ __global__ void __launch_bounds__(DN_THREADS, 1)
     const uint32_t tbase = tmem_alloc(&tslot, 512);  // syncs the CTA
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     bool ok = true;
-    if (warp == 0) {
-        // producer: the unit's slab (one bulk copy), then its h rows per stage
+    if (warp == 2) {
+        // slab producer: the unit's 128 Q6_K rows in one bulk copy, as soon
+        // as a slab buffer is free
         if (lane == 0) {
-            int g = 0;  // stage counter across units
             for (int k = 0; k < n_my && ok; k++) {
                 const int u = (int)blockIdx.x + k * (int)gridDim.x, tile = u / nblk, n0 = (u - tile * nblk) * PF_M;
-                const int e = a.slot_expert[a.tile_slot[tile]], s0 = a.tile_start[tile];
-                const int nn = (a.tile_n[tile] + 15) & ~15;
+                const int e = a.slot_expert[a.tile_slot[tile]];
                 const int sb = k & 1;
                 if (k >= 2) ok = mbar_wait(&R.sempty[sb], ((k >> 1) - 1) & 1);
                 if (!ok) break;
                 bulk_copy(slab + sb * slab_bytes, (e == a.E ? a.down_sh : a.down + e * exp_bytes) + (size_t)n0 * row_bytes,
                           slab_bytes, &R.sfull[sb]);
+            }
+        }
+    } else if (warp == 0) {
+        // h producer: the unit's h rows per stage
+        if (lane == 0) {
+            int g = 0;  // stage counter across units
+            for (int k = 0; k < n_my && ok; k++) {
+                const int tile = ((int)blockIdx.x + k * (int)gridDim.x) / nblk;
+                const int s0 = a.tile_start[tile];
+                const int nn = (a.tile_n[tile] + 15) & ~15;
                 for (int i = 0; i < nstages && ok; i++, g++) {
                     const int rb = g % PF_STG, use = g / PF_STG;
                     if (use > 0) ok = mbar_wait(&R.bempty[rb], (use - 1) & 1);
