@@ -75,7 +75,6 @@ constexpr int UP_R = 2;  // hidden rows per warp
 
 __global__ void __launch_bounds__(256) expert_up_q(LayerArgs a, const unsigned char *__restrict__ xq) {
     DTRACE_START(dc, 0)
-    pdl_trigger();
     const int lane = threadIdx.x & 31;
     const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     const int nwarps = (gridDim.x * blockDim.x) >> 5;
@@ -88,6 +87,9 @@ __global__ void __launch_bounds__(256) expert_up_q(LayerArgs a, const unsigned c
         prefetch_l2(a.up_sh, exp_bytes, gt, nt);
     }
     pdl_wait();
+    // routing is complete: let expert_down_q start (it stages its Q6_K rows
+    // from the plan while this kernel runs)
+    pdl_trigger();
     DTRACE_WAITED(dc, 0)
     {
         // routing is known: pull the routed experts' down rows into L2 so
@@ -191,19 +193,29 @@ __global__ void __launch_bounds__(DQ_WARPS * 32) expert_down_q(LayerArgs a, int 
         const int gt = blockIdx.x * blockDim.x + threadIdx.x, nt = gridDim.x * blockDim.x;
         prefetch_l2(a.down_sh, exp_bytes, gt, nt);
     }
-    pdl_wait();
-    DTRACE_WAITED(dc, 1)
     uint8_t *slab = dsm;                                                        // [64][row_bytes]
     HQuad *hq = reinterpret_cast<HQuad *>(dsm + DQ_ROWS * row_bytes + 16);     // [DQ_TOK][items][4]
-    const int nslots = *a.n_slots;
+    // The routing plan is complete when this grid starts: expert_up_q raises
+    // its trigger only after its own wait on the routing kernel. So the first
+    // unit's Q6_K rows are staged before waiting for h (plan read through L2).
+    const int nslots = __ldcg(a.n_slots);
     const int units = nslots * nblk;
-    for (int unit = blockIdx.x; unit < units; unit += gridDim.x) {
+    auto stage_slab = [&](int unit) {
         const int u = unit / nblk, n0 = (unit - u * nblk) * DQ_ROWS;
-        const int e = a.slot_expert[u];
+        const int e = __ldcg(a.slot_expert + u);
         const uint8_t *src = (e == a.E ? a.down_sh : a.down + e * exp_bytes) + (size_t)n0 * row_bytes;
-        __syncthreads();  // previous unit done with the slab and hq
         for (int i = tid; i < DQ_ROWS * row_bytes / 16; i += DQ_WARPS * 32)
             reinterpret_cast<uint4 *>(slab)[i] = __ldg(reinterpret_cast<const uint4 *>(src) + i);
+    };
+    if ((int)blockIdx.x < units) stage_slab(blockIdx.x);
+    pdl_wait();
+    DTRACE_WAITED(dc, 1)
+    for (int unit = blockIdx.x; unit < units; unit += gridDim.x) {
+        const int u = unit / nblk, n0 = (unit - u * nblk) * DQ_ROWS;
+        if (unit != (int)blockIdx.x) {
+            __syncthreads();  // previous unit done with the slab and hq
+            stage_slab(unit);
+        }
         const int s0 = a.slot_start[u], s1 = a.slot_start[u + 1];
         DTRACE_MARK(dc, 1, 3)
         for (int c0 = s0; c0 < s1; c0 += DQ_TOK) {

@@ -1016,29 +1016,50 @@ __global__ void gather_rows_kernel(const float *__restrict__ x, const int *__res
 }
 
 // One block: split every slot into tiles of at most 256 tokens.
-__global__ void tile_plan_kernel(const int *n_slots, const int *slot_start, int *n_tiles, int *tile_slot,
-                                 int *tile_start, int *tile_n) {
-    __shared__ int base[1025];
-    const int ns = *n_slots;
-    if (threadIdx.x == 0) {
-        int acc = 0;
-        for (int u = 0; u < ns; u++) {
-            base[u] = acc;
-            acc += (slot_start[u + 1] - slot_start[u] + PF_NMAX - 1) / PF_NMAX;
+__global__ void __launch_bounds__(1024) tile_plan_kernel(const int *n_slots, const int *slot_start, int *n_tiles,
+                                                         int *tile_slot, int *tile_start, int *tile_n) {
+    // thread u owns slot u (at most 1025 slots: E <= 1024 routed experts +
+    // the shared one, so 1024 threads and one extra pass for the last)
+    __shared__ int wsum[32], total;
+    const int ns = *n_slots, tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
+    int carry = 0;
+    for (int u0 = 0; u0 < ns; u0 += blockDim.x) {
+        const int u = u0 + tid;
+        const int nt = u < ns ? (slot_start[u + 1] - slot_start[u] + PF_NMAX - 1) / PF_NMAX : 0;
+        int inc = nt;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int v = __shfl_up_sync(0xffffffffu, inc, o);
+            if (lane >= o) inc += v;
         }
-        base[ns] = acc;
-        *n_tiles = acc;
-    }
-    __syncthreads();
-    for (int u = threadIdx.x; u < ns; u += blockDim.x) {
-        const int st = slot_start[u], cnt = slot_start[u + 1] - st;
-        for (int k = 0; k < base[u + 1] - base[u]; k++) {
-            const int t = base[u] + k;
-            tile_slot[t] = u;
-            tile_start[t] = st + k * PF_NMAX;
-            tile_n[t] = min(PF_NMAX, cnt - k * PF_NMAX);
+        if (lane == 31) wsum[wid] = inc;
+        __syncthreads();
+        if (wid == 0) {
+            const int nw = blockDim.x >> 5;
+            const int w = lane < nw ? wsum[lane] : 0;
+            int wi = w;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const int v = __shfl_up_sync(0xffffffffu, wi, o);
+                if (lane >= o) wi += v;
+            }
+            if (lane < nw) wsum[lane] = wi - w;
+            if (lane == 31) total = wi;
         }
+        __syncthreads();
+        const int base = carry + wsum[wid] + inc - nt;
+        if (u < ns) {
+            const int st = slot_start[u];
+            for (int k = 0; k < nt; k++) {
+                tile_slot[base + k] = u;
+                tile_start[base + k] = st + k * PF_NMAX;
+                tile_n[base + k] = min(PF_NMAX, slot_start[u + 1] - st - k * PF_NMAX);
+            }
+        }
+        carry += total;
+        __syncthreads();  // wsum and total are rewritten next pass
     }
+    if (tid == 0) *n_tiles = carry;
 }
 
 int prefill_max_tiles(int T, int K, int E) {
@@ -1134,7 +1155,7 @@ int launch_prefill(const LayerArgs &la, const float *x, int *n_slots, __nv_bfloa
         umap_sh = umap;
     }
     gather_rows_kernel<<<148 * 8, 256, 0, s>>>(x, la.assign, n_slots, la.slot_start, T * la.K, la.K, D, xb);
-    tile_plan_kernel<<<1, 256, 0, s>>>(n_slots, la.slot_start, n_tiles, tile_slot, tile_start, tile_n);
+    tile_plan_kernel<<<1, 1024, 0, s>>>(n_slots, la.slot_start, n_tiles, tile_slot, tile_start, tile_n);
     PrefillArgs a;
     a.T = T; a.D = D; a.H = H; a.E = la.E; a.K = la.K;
     a.shared_gate = la.shared_gate;
