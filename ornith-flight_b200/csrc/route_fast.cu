@@ -216,9 +216,12 @@ __global__ void __launch_bounds__(RR_WARPS * 32) route_rows_kernel(FastRouteArgs
         for (int j = 0; j < PF; j++)
             if (j < seg / 4) xv[j] = __ldg(x4 + j);
     }
-    if (a.xq) {
+    if (a.xq && r > E) {
+        // warps past the router rows and the gate vector quantise x, beside
+        // the rows rather than in front of them
         unsigned char *q = a.xq + (size_t)t * xq_stride(D);
-        for (int sb = r; sb < D / 32; sb += gridDim.x * RR_WARPS)
+        const int nq = gridDim.x * RR_WARPS - (E + 1);
+        for (int sb = r - (E + 1); sb < D / 32; sb += nq)
             quantize_subblock(__ldg(xt + sb * 32 + lane), q, D, sb, lane);
     }
     if (!has_row) {
@@ -1086,7 +1089,10 @@ int launch_route_fast(const float *W, const float *x, const float *gate_v, int T
         attr_set = true;
     }
     if (smem > FR_SMEM_MAX) { set_error("route_fast: E/D too large for shared memory"); return OFB_EUNSUPPORTED; }
-    cudaError_t e = launch_pdl(route_rows_kernel, dim3((E + 1 + RR_WARPS - 1) / RR_WARPS, T),
+    // rows: E router rows, the gate vector, then (when x is quantised) one
+    // warp per 32-element sub-block of x
+    const int rr_rows = E + 1 + (xq ? D / 32 : 0);
+    cudaError_t e = launch_pdl(route_rows_kernel, dim3((rr_rows + RR_WARPS - 1) / RR_WARPS, T),
                                dim3(RR_WARPS * 32), 0, s, a);
     if (e == cudaSuccess) e = launch_pdl(route_select_fast, dim3(T), dim3(FR_THREADS), smem, s, a);
     if (e != cudaSuccess) return cuda_status(e, "route_fast launch");
