@@ -162,7 +162,7 @@ __device__ __forceinline__ void mma_bf16_ta(uint32_t tmem_d, uint32_t tmem_a, ui
         "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p; }" ::"r"(tmem_d),
         "r"(tmem_a), "l"(b), "r"(idesc), "r"(acc));
 }
-// This warp's 32 TMEM lanes, 16 / 8 consecutive 32-bit columns from registers.
+// This warp's 32 TMEM lanes, 16 / 4 consecutive 32-bit columns from registers.
 __device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t v[16]) {
     asm volatile(
         "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(
@@ -170,11 +170,6 @@ __device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t v[16]) 
         "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]),
         "r"(v[9]), "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15])
         : "memory");
-}
-__device__ __forceinline__ void tmem_st8(uint32_t taddr, const uint32_t v[8]) {
-    asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"r"(taddr), "r"(v[0]),
-                 "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7])
-                 : "memory");
 }
 __device__ __forceinline__ void tmem_st4(uint32_t taddr, const uint32_t v[4]) {
     asm volatile("tcgen05.st.sync.aligned.32x32b.x4.b32 [%0], {%1,%2,%3,%4};" ::"r"(taddr), "r"(v[0]), "r"(v[1]),
@@ -186,32 +181,6 @@ __device__ __forceinline__ void mma_commit(uint64_t *bar) {
     asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
         smem_u32(bar))
                  : "memory");
-}
-// 32 consecutive columns of this warp's 32 TMEM lanes (one per thread).
-__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float v[32]) {
-    uint32_t r[32];
-    asm volatile(
-        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
-        "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];\n\t"
-        "tcgen05.wait::ld.sync.aligned;"
-        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
-          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
-          "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
-          "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
-        : "r"(taddr)
-        : "memory");
-#pragma unroll
-    for (int i = 0; i < 32; i++) v[i] = __uint_as_float(r[i]);
-}
-__device__ __forceinline__ void tmem_ld8(uint32_t taddr, float v[8]) {
-    uint32_t r[8];
-    asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
-                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
-                   "=r"(r[7])
-                 : "r"(taddr));
-    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-#pragma unroll
-    for (int i = 0; i < 8; i++) v[i] = __uint_as_float(r[i]);
 }
 // Loads that leave the wait to the caller (tmem_ld_wait), so several are in
 // flight at once.
@@ -238,7 +207,6 @@ __device__ __forceinline__ void tmem_ld_wait(uint32_t (&r)[N]) {
 }
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
-__device__ __forceinline__ void async_proxy_fence() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 
 __device__ __forceinline__ uint32_t tmem_alloc(uint32_t *slot, uint32_t ncols) {
     if ((threadIdx.x >> 5) == 0) {
@@ -268,15 +236,6 @@ __device__ __forceinline__ void bulk_copy(void *dst, const void *src, uint32_t b
                  "l"(src), "r"(bytes), "r"(smem_u32(bar))
                  : "memory");
 }
-// One 3D box at (c0, c1, c2).
-__device__ __forceinline__ void tma_load3d(uint32_t dst, const CUtensorMap *map, int c0, int c1, int c2,
-                                           uint64_t *bar) {
-    asm volatile(
-        "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes"
-        " [%0], [%1, {%2, %3, %4}], [%5];" ::"r"(dst),
-        "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(smem_u32(bar))
-        : "memory");
-}
 // One 2D box of the map at (x, y).
 __device__ __forceinline__ void tma_tile2d(uint32_t dst, const CUtensorMap *map, int x, int y, uint64_t *bar) {
     asm volatile(
@@ -300,12 +259,6 @@ __device__ __forceinline__ __nv_bfloat162 q_pair128(uint32_t w) {
     return *reinterpret_cast<const __nv_bfloat162 *>(&v);
 }
 __device__ __forceinline__ uint32_t bf2_bits(__nv_bfloat162 v) { return *reinterpret_cast<uint32_t *>(&v); }
-// 4 bytes at a 2-byte aligned shared-memory address.
-__device__ __forceinline__ uint32_t lds_u32_2b(const uint8_t *p) {
-    const uintptr_t a = reinterpret_cast<uintptr_t>(p);
-    const uint32_t *b = reinterpret_cast<const uint32_t *>(a & ~uintptr_t(3));
-    return __funnelshift_r(b[0], b[1], (unsigned)(a & 3) * 8);
-}
 
 // ---- A operand, Q4_K ----------------------------------------------------------------
 // Raw bytes of one matrix for one raw stage: Q4_K block b of 128 rows, one

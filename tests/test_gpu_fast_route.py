@@ -1,7 +1,9 @@
-"""The certified decode routing inside ofb_moe_forward (T <= 64, contiguous
-router): top-k indices bit-exact against the reference's sequential CPU
-routing on every path — certified directly, uncertain candidates recomputed
-with the exact chain, and every logit recomputed (probability ties)."""
+"""The certified routing inside ofb_moe_forward (contiguous router): top-k
+indices bit-exact against the reference's sequential CPU routing on every
+path — certified directly, uncertain candidates recomputed with the exact
+chain, and every logit recomputed (probability ties) — at decode sizes
+(T <= 64: route_rows / route_select_fast) and above (bounded GEMM,
+route_certify_warps, route_fallback_warps)."""
 import numpy as np
 import pytest
 import torch
@@ -64,6 +66,38 @@ def test_exact_ties_full_recompute(ofb, oracle, cuda, routing):
     np.testing.assert_allclose(gw, ow, rtol=1e-5)
     if routing == 0:
         assert stats[2] > 0  # probabilities tie -> every logit recomputed
+
+
+@pytest.mark.parametrize("routing", [0, 1])
+def test_large_batch_exact_ties_warp_fallback(ofb, oracle, cuda, routing):
+    # above 64 tokens: bounded GEMM + warp certificate; duplicated router rows
+    # leave every token to route_fallback_warps, whose forward-routing
+    # probabilities tie and so recompute every logit
+    shape = ofb.LayerShape(d_model=256, hidden=256, n_experts=48, top_k=8, routing=routing)
+    rng = np.random.default_rng(15)
+    base = rng.normal(0, 0.05, size=(6, 256)).astype(np.float32)
+    router = base[rng.integers(0, 6, size=48)]
+    x = rng.normal(size=(100, 256)).astype(np.float32)
+    gi, gw, out, oi, ow, want, stats = run_layer(ofb, oracle, cuda, shape, router, x)
+    assert np.array_equal(gi, oi)
+    np.testing.assert_allclose(gw, ow, rtol=1e-5)
+    assert stats[0] + stats[1] + stats[2] == 100
+    if routing == 0:
+        assert stats[2] > 0
+
+
+def test_large_batch_near_ties_warp_fallback(ofb, oracle, cuda):
+    # near-equal expert pairs above 64 tokens: candidates recomputed by the
+    # warp fallback with the reference's exact chain
+    shape = ofb.LayerShape(d_model=512, hidden=256, n_experts=32, top_k=4)
+    rng = np.random.default_rng(14)
+    base = rng.normal(0, 0.05, size=(16, 512)).astype(np.float32)
+    router = np.concatenate([base, base * np.float32(1 + 3e-6)])
+    x = rng.normal(size=(120, 512)).astype(np.float32)
+    gi, gw, out, oi, ow, want, stats = run_layer(ofb, oracle, cuda, shape, router, x)
+    assert np.array_equal(gi, oi)
+    np.testing.assert_allclose(gw, ow, rtol=1e-5)
+    assert stats[1] + stats[2] > 0
 
 
 @pytest.mark.parametrize("T,routing,bias", [(1, 0, False), (17, 1, False), (64, 0, True), (65, 0, False),
