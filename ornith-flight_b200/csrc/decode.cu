@@ -11,9 +11,9 @@
 //    dot product is ~1e-5, well inside the layer's 1e-3 bound.
 //  * expert_up_q: one warp per (slot, 2 hidden rows) streams the Q4_K gate
 //    and up rows (lane = one 64-element chunk: 16 B header + 32 B quants),
-//    writes h = silu(x.G) * (x.U) per token.
-//    Once routing is known it also prefetches the routed experts' down rows
-//    into L2 for the next kernel.
+//    writes h = silu(x.G) * (x.U) per token. It raises its dependent-launch
+//    trigger once routing is known, so expert_down_q stages its rows while
+//    this kernel runs.
 //  * expert_down_q: one CTA per (slot, 64 output rows) stages the 64 Q6_K
 //    rows (26,880 B, 16-byte aligned) in shared memory and quantises each
 //    token's h once per CTA; warp w computes rows 4w..4w+3 and writes y per
@@ -91,17 +91,6 @@ __global__ void __launch_bounds__(256) expert_up_q(LayerArgs a, const unsigned c
     // from the plan while this kernel runs)
     pdl_trigger();
     DTRACE_WAITED(dc, 0)
-    {
-        // routing is known: pull the routed experts' down rows into L2 so
-        // that expert_down_q (next in the stream) reads them from there
-        const size_t dbytes = (size_t)(a.H / QK) * Q6K_BYTES * D, lines = dbytes / 128;
-        const int ns = *a.n_slots;
-        const size_t gt = blockIdx.x * (size_t)blockDim.x + threadIdx.x, nt = (size_t)gridDim.x * blockDim.x;
-        for (size_t i = gt; i < (size_t)ns * lines; i += nt) {
-            const int e = a.slot_expert[i / lines];
-            if (e < a.E) asm volatile("prefetch.global.L2 [%0];" ::"l"(a.down + e * dbytes + (i % lines) * 128));
-        }
-    }
     const size_t xs = xq_stride(D);
     const int groups = a.H / UP_R;
     const int units = *a.n_slots * groups;
@@ -177,7 +166,7 @@ __device__ __forceinline__ uint32_t lds_u32_2(const uint8_t *p) {
 struct HQuad { uint32_t hh, hl; int xs; float sq; };
 
 // One CTA per (slot, 64 output rows): stage the 64 Q6_K rows in shared memory
-// (read from L2: expert_up_q prefetched the routed experts' down rows),
+// (the first unit's before waiting for expert_up_q, which runs meanwhile),
 // quantise each token's h once per CTA (per 16-element Q6_K scale group),
 // then warp w computes rows 4w..4w+3 for every token of the slot.
 __global__ void __launch_bounds__(DQ_WARPS * 32) expert_down_q(LayerArgs a, int *__restrict__ tickets) {
