@@ -198,7 +198,7 @@ size_t ofb_noalloc_capacity(void);
  * n_ranks GPUs, experts_per_rank = n_experts / n_ranks each (rank r owns
  * experts [r*experts_per_rank, (r+1)*experts_per_rank), stored as the
  * CONTIGUOUS layout's expert range); tokens are split too, each rank routing
- * its own. Per layer: ofb_route on own tokens -> ofb_ep_plan + ofb_ep_pack ->
+ * its own. Per layer: ofb_route_certified on own tokens -> ofb_ep_plan + ofb_ep_pack ->
  * all-to-all of rows and metadata (NCCL, by the caller) -> ofb_moe_experts ->
  * all-to-all back -> ofb_moe_shared + ofb_ep_combine. The reference runs its
  * MoE block on one CPU (engine/src/model.c:992-1143) and has no counterpart;
