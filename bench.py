@@ -137,21 +137,38 @@ class ClockSampler:
 
 # ---------------------------------------------------------------- CPU arms ---
 
+CPU_MODES = {
+    # the same layer semantics as the GPU arm: contiguous expert blocks,
+    # renormalised top-8, sigmoid-gated shared expert
+    "C": dict(layout=0, renorm=1, shared_gate=1,
+              desc="Mode C: contiguous expert blocks, whole-block dequant, renormalised top-8, "
+                   "sigmoid-gated shared expert (the GPU arm's semantics)"),
+    # the reference as shipped: expert slices decoded element by element from
+    # the interleaved tensors (engine/src/gguf.c:652-711), no renormalisation,
+    # ungated shared expert (engine/src/model.c:992-1143)
+    "R": dict(layout=1, renorm=0, shared_gate=0,
+              desc="Mode R: the reference as shipped - interleaved expert slices decoded element by "
+                   "element (gguf.c:652-711), top-8 without renormalisation, ungated shared expert"),
+}
+
+
 def _cpu_worker(args):
-    seed, seconds, tokens_per_call, use_ref = args
-    import numpy as np
+    """One process of the CPU arms. Builds its layer with the oracle's host
+    copy of the generator (no product library is loaded in these processes)
+    and runs the oracle layer, with the reference's own compiled gguf.c doing
+    the dequant when oracle/_ref is built."""
+    seed, seconds, tokens_per_call, use_ref, mode = args
     import binding
-    ofb = load_ofb()
     if use_ref:
         binding.use_reference_dequant(True)
-    shape = ofb.LayerShape()
-    lw = ofb.make_layer(shape, seed=seed, device="cpu")
-    w = {k: (None if v is None else v.numpy()) for k, v in vars(lw).items()}
-    cfg = dict(d_model=D, hidden=H, n_experts=E, top_k=K, layout=0, routing=0, renorm=1, shared_gate=1)
+    m = CPU_MODES[mode]
+    w = binding.make_layer_host(D, H, E, layout=m["layout"], seed=seed)
+    cfg = dict(d_model=D, hidden=H, n_experts=E, top_k=K, layout=m["layout"], routing=0,
+               renorm=m["renorm"], shared_gate=m["shared_gate"])
     done, t0 = 0, time.perf_counter()
     i = 0
     while True:
-        x = ofb.make_tokens(shape, tokens_per_call, seed=seed * 1000 + i).numpy()
+        x = binding.make_tokens_host(D, tokens_per_call, seed=seed * 1000 + i)
         binding.moe_forward(cfg, w, x)
         done += tokens_per_call
         i += 1
@@ -160,7 +177,7 @@ def _cpu_worker(args):
     return done, time.perf_counter() - t0
 
 
-def cpu_throughput(procs: int, seconds: float, tokens_per_call: int):
+def cpu_throughput(procs: int, seconds: float, tokens_per_call: int, mode: str = "C"):
     """Tokens/s of the reference CPU layer on `procs` processes (one per core).
     The reference is single-threaded in compute; P independent processes is its
     throughput on P cores."""
@@ -168,11 +185,12 @@ def cpu_throughput(procs: int, seconds: float, tokens_per_call: int):
     use_ref = binding.load_ref() is not None
     ctx = mp.get_context("spawn")
     with ctx.Pool(procs) as pool:
-        res = pool.map(_cpu_worker, [(s + 1, seconds, tokens_per_call, use_ref) for s in range(procs)])
+        res = pool.map(_cpu_worker, [(s + 1, seconds, tokens_per_call, use_ref, mode) for s in range(procs)])
     tokens = sum(r[0] for r in res)
     wall = max(r[1] for r in res)
     kind = "reference" if use_ref else "port"
     sample = (f"{tokens} tokens ({tokens_per_call}/call) over {wall:.1f} s on {procs} process(es); "
+              + CPU_MODES[mode]["desc"] + "; "
               + ("reference engine/src/gguf.c compiled unmodified (oracle/_ref) for the expert "
                  "dequant + C restatement of model.c:992-1143 (router, softmax, top-8, SwiGLU, "
                  "combine)" if use_ref else "C restatement of gguf.c dequant and model.c MoE block"))
@@ -464,6 +482,17 @@ def run_ours(args, rank, world, local_rank):
     print(json.dumps(line), flush=True)
 
 
+def workload_config(workload, world, n_layers=None):
+    """The config dict of a workload's line; both arms print the same one."""
+    wl = WORKLOADS[workload]
+    n_layers = n_layers or wl["layers"]
+    return {"workload": workload, "desc": wl["config"], "tokens_per_step": wl["tokens"],
+            "d_model": D, "hidden": H, "n_experts": E, "top_k": K,
+            "routing": "softmax/top-8/renormalise; indices bit-exact", "shared_gate": True,
+            "l2": f"rotate {n_layers} layer copies ({n_layers * 522} MB) > 126 MB L2",
+            "parallelism": f"replicas x{world}"}
+
+
 def describe(args, world, workload, m, steps, warmup, n_layers):
     wl = WORKLOADS[workload]
     T = m["T"]
@@ -480,11 +509,7 @@ def describe(args, world, workload, m, steps, warmup, n_layers):
         "vs_baseline": None,
         "dtype": wl["dtype"],
         "data": "synthetic (seeded Q4_K/Q6_K blocks, N(0,1) tokens, N(0,0.02) router)",
-        "config": {"workload": workload, "desc": wl["config"], "tokens_per_step": T,
-                   "d_model": D, "hidden": H, "n_experts": E, "top_k": K,
-                   "routing": "softmax/top-8/renormalise; indices bit-exact", "shared_gate": True,
-                   "l2": f"rotate {n_layers} layer copies ({n_layers * 522} MB) > 126 MB L2",
-                   "parallelism": f"replicas x{world}"},
+        "config": workload_config(workload, world, n_layers),
         "phase_ms": {"routing": phase[0], "plan": phase[1], "up": phase[2], "down_combine": phase[3]},
         "e2e": {"value": world * T * steps / (m["e2e_ms"] / 1e3), "unit": "tokens/s",
                 "h2d_bytes_per_step": T * D * 4, "d2h_bytes_per_step": T * D * 4},
@@ -531,26 +556,31 @@ def describe(args, world, workload, m, steps, warmup, n_layers):
 
 
 def run_reference(args, rank, world):
+    """The reference arm: rank 0 times the reference's CPU layer on all host
+    cores; other ranks exit without work. Headline = Mode C (the GPU arm's
+    semantics); Mode R (the reference as shipped) is timed beside it."""
     if rank != 0:
         return
     procs = os.cpu_count() or 1
-    T = WORKLOADS[args.workload]["tokens"]
-    # One token-layer takes ~0.1 s of CPU, so K steps of the GPU arm's size
-    # would run for hours: the arm runs one bounded sample (every core busy
-    # for args.cpu_seconds * 4, at most 90 s) and reports its throughput.
-    # the reference processes one token at a time (inference.c:304-307), so
-    # its tokens/s does not depend on the batch: calls of <= 4 tokens
-    v, kind, sample = cpu_throughput(procs, min(90.0, 4 * args.cpu_seconds), min(T, 4))
+    wl = WORKLOADS[args.workload]
+    T = wl["tokens"]
+    # One token-layer takes ~0.1 s of CPU (Mode R ~0.3 s), so K steps of the
+    # GPU arm's size would run for hours: each mode runs one bounded sample
+    # (every core busy) and reports its throughput. The reference processes
+    # one token at a time (inference.c:304-307), so its tokens/s does not
+    # depend on the batch: calls of <= 4 tokens.
+    v, kind, sample = cpu_throughput(procs, min(60.0, 3 * args.cpu_seconds), min(T, 4), "C")
+    vr, kind_r, sample_r = cpu_throughput(procs, min(40.0, 2 * args.cpu_seconds), 1, "R")
     line = {
         "impl": "reference",
-        "metric": WORKLOADS[args.workload]["metric"], "value": v, "unit": "tokens/s",
+        "metric": wl["metric"], "value": v, "unit": "tokens/s",
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": 1e3 * T / v, "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": args.workload, "desc": WORKLOADS[args.workload]["config"],
-                   "tokens_per_step": T, "d_model": D, "hidden": H, "n_experts": E, "top_k": K},
-        "cpu_baseline": {"value": v, "unit": "tokens/s", "cores": procs, "kind": kind,
-                         "sample": sample},
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded Q4_K/Q6_K blocks, N(0,1) tokens, "
+                                                     "N(0,0.02) router)",
+        "config": workload_config(args.workload, world),
+        "cpu_baseline": {"value": v, "unit": "tokens/s", "cores": procs, "kind": kind, "sample": sample},
+        "mode_r": {"value": vr, "unit": "tokens/s", "cores": procs, "kind": kind_r, "sample": sample_r},
         "e2e": {"value": v, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)

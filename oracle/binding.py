@@ -49,6 +49,8 @@ def load_oracle():
                                   vp, vp, vp]
     L.orc_matmul.restype, L.orc_matmul.argtypes = None, [vp, vp, vp, i32, i32, i32]
     L.orc_expf_batch.restype, L.orc_expf_batch.argtypes = None, [vp, vp, u64]
+    L.orc_synth_blocks.restype, L.orc_synth_blocks.argtypes = None, [vp, i32, u64, u64, u64, u64]
+    L.orc_synth_normal.restype, L.orc_synth_normal.argtypes = None, [vp, u64, u64, u64, f32]
     return L
 
 
@@ -142,3 +144,48 @@ def use_reference_dequant(enable: bool = True) -> bool:
     s = ctypes.cast(ref.ref_dequant_slice, ctypes.c_void_p).value
     L.orc_set_dequant(t, s)
     return True
+
+
+# ---- seeded synthetic layers, built on the host without the product library ----
+# Stream ids and distributions of the library's make_layer / make_tokens.
+STREAM_GATE, STREAM_UP, STREAM_DOWN, STREAM_GATE_SH, STREAM_UP_SH, STREAM_DOWN_SH = 1, 2, 3, 4, 5, 6
+STREAM_ROUTER, STREAM_GATE_V, STREAM_X = 7, 8, 9
+BLOCK_BYTES = {TYPE_Q4_K: 144, TYPE_Q6_K: 210}
+
+
+def synth_blocks(qtype: int, n_blocks: int, seed: int, stream_id: int, first_block: int = 0) -> np.ndarray:
+    out = np.empty(n_blocks * BLOCK_BYTES[qtype], dtype=np.uint8)
+    orc().orc_synth_blocks(_np_ptr(out), qtype, n_blocks, first_block, seed, stream_id)
+    return out
+
+
+def synth_normal(n: int, seed: int, stream_id: int, sigma: float) -> np.ndarray:
+    out = np.empty(n, dtype=np.float32)
+    orc().orc_synth_normal(_np_ptr(out), n, seed, stream_id, sigma)
+    return out
+
+
+def make_layer_host(d_model=2048, hidden=512, n_experts=256, layout=LAYOUT_CONTIGUOUS, seed=0,
+                    shared=True) -> dict:
+    """The bytes of the library's make_layer(shape, seed) as numpy arrays
+    (router laid out per `layout`: [E][D] contiguous, [D][E] interleaved)."""
+    nb = hidden * d_model // 256
+    E, D = n_experts, d_model
+    r = synth_normal(E * D, seed, STREAM_ROUTER, 0.02).reshape(E, D)
+    if layout == LAYOUT_INTERLEAVED:
+        r = np.ascontiguousarray(r.T)
+    w = dict(router=r.reshape(-1),
+             gate_exps=synth_blocks(TYPE_Q4_K, E * nb, seed, STREAM_GATE),
+             up_exps=synth_blocks(TYPE_Q4_K, E * nb, seed, STREAM_UP),
+             down_exps=synth_blocks(TYPE_Q6_K, E * nb, seed, STREAM_DOWN),
+             gate_shexp=None, up_shexp=None, down_shexp=None, shexp_gate=None)
+    if shared:
+        w.update(gate_shexp=synth_blocks(TYPE_Q4_K, nb, seed, STREAM_GATE_SH),
+                 up_shexp=synth_blocks(TYPE_Q4_K, nb, seed, STREAM_UP_SH),
+                 down_shexp=synth_blocks(TYPE_Q6_K, nb, seed, STREAM_DOWN_SH),
+                 shexp_gate=synth_normal(D, seed, STREAM_GATE_V, 0.02))
+    return w
+
+
+def make_tokens_host(d_model: int, n_tokens: int, seed: int) -> np.ndarray:
+    return synth_normal(n_tokens * d_model, seed, STREAM_X, 1.0).reshape(n_tokens, d_model)

@@ -92,6 +92,12 @@ int orc_moe_forward(const orc_moe_cfg *cfg, const orc_moe_weights *wt,
                     const float *x, const float *resid, int n_tokens, float *out,
                     uint32_t *idx, float *w);
 
+/* seeded synthetic inputs: the same bytes / floats as the library's
+ * ofb_synth_blocks_host / ofb_synth_normal_host (synth.c) */
+void orc_synth_blocks(void *dst, int type, uint64_t n_blocks, uint64_t first_block, uint64_t seed,
+                      uint64_t stream_id);
+void orc_synth_normal(float *dst, uint64_t n, uint64_t seed, uint64_t stream_id, float sigma);
+
 /* reference CPU matmul semantics used by the gpu.h contract (gpu.c:104-115) */
 void orc_matmul(float *C, const float *A, const float *B, int M, int N, int K);
 

@@ -17,6 +17,10 @@ constexpr int QK = 256;
 constexpr int Q4K_BYTES = 144;
 constexpr int Q6K_BYTES = 210;
 
+// Current device ordinal (0..63) and its SM count (cached per device).
+int current_device();
+int sm_count();
+
 // Per-host-thread error detail (ofb_last_error).
 void set_error(const char *fmt, ...);
 int cuda_status(cudaError_t e, const char *what);
@@ -99,6 +103,18 @@ __device__ __forceinline__ float warp_sum(float v) {
 
 __device__ __forceinline__ uint16_t ld_u16(const uint8_t *p) {
     return *reinterpret_cast<const uint16_t *>(p);
+}
+
+// Raises a kernel's dynamic shared-memory limit to `bytes` on the current
+// device (function attributes are per device); `cache` remembers, per
+// device, the largest value already set.
+template <typename... KArgs>
+inline cudaError_t ensure_dyn_smem(void (*kernel)(KArgs...), size_t bytes, size_t (&cache)[64]) {
+    const int dev = current_device();
+    if (bytes <= 48 * 1024 || bytes <= cache[dev]) return cudaSuccess;
+    cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
+    if (e == cudaSuccess) cache[dev] = bytes;
+    return e;
 }
 
 inline int grid_for(uint64_t work, int per_block, int cap) {

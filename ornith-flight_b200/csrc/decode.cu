@@ -347,17 +347,6 @@ __global__ void quantize_x_kernel(const float *__restrict__ x, int D, unsigned c
     }
 }
 
-static int sms() {
-    static int n = 0;
-    if (!n) {
-        int dev = 0;
-        cudaGetDevice(&dev);
-        cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
-        if (n <= 0) n = 148;
-    }
-    return n;
-}
-
 int launch_quantize_x(const float *x, int T, int D, unsigned char *xq, cudaStream_t s) {
     dim3 grid((D / 32 + 7) / 8, T);
     quantize_x_kernel<<<grid, 256, 0, s>>>(x, D, xq);
@@ -367,18 +356,16 @@ int launch_quantize_x(const float *x, int T, int D, unsigned char *xq, cudaStrea
 
 int launch_up_q(const LayerArgs &a, const unsigned char *xq, int max_slots, cudaStream_t s) {
     const uint64_t up_units = (uint64_t)max_slots * (a.H / UP_R);
-    cudaError_t e = launch_pdl(expert_up_q, dim3(grid_for(up_units, 8, sms() * 32)), dim3(256), 0, s, a, xq);
+    cudaError_t e = launch_pdl(expert_up_q, dim3(grid_for(up_units, 8, sm_count() * 32)), dim3(256), 0, s, a, xq);
     return e == cudaSuccess ? OFB_OK : cuda_status(e, "expert_up_q launch");
 }
 
 int launch_down_q(const LayerArgs &a, int *tickets, int max_slots, cudaStream_t s) {
-    const int n = sms();
+    const int n = sm_count();
     const size_t smem = (size_t)DQ_ROWS * (a.H / QK) * Q6K_BYTES + 16 + (size_t)DQ_TOK * (a.H / QK) * 16 * 4 * sizeof(HQuad);
-    static size_t attr = 0;
-    if (smem > 48 * 1024 && smem > attr) {
-        cudaFuncSetAttribute(expert_down_q, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        attr = smem;
-    }
+    static size_t attr[64];
+    cudaError_t ea = ensure_dyn_smem(expert_down_q, smem, attr);
+    if (ea != cudaSuccess) return cuda_status(ea, "expert_down_q smem attribute");
     const uint64_t dn_units = (uint64_t)max_slots * (a.D / DQ_ROWS);
     const int grid = (int)(dn_units < (uint64_t)n * 4 ? dn_units : (uint64_t)n * 4);
     cudaError_t e = launch_pdl(expert_down_q, dim3(grid), dim3(DQ_WARPS * 32), smem, s, a, tickets);

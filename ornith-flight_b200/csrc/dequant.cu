@@ -164,17 +164,6 @@ __global__ void slice_kernel(const uint8_t *__restrict__ data, int type, uint64_
     }
 }
 
-static int sm_count() {
-    static int n = 0;
-    if (!n) {
-        int dev = 0;
-        cudaGetDevice(&dev);
-        cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
-        if (n <= 0) n = 148;
-    }
-    return n;
-}
-
 template <typename OutT>
 static int launch_dequant(const void *blocks, int type, uint64_t n_elems, OutT *out,
                           cudaStream_t s) {

@@ -25,6 +25,13 @@
  * as host code and compares all 2^31 inputs); the GPU test compares device
  * results against the host library on a strided sample.
  *
+ * Attribution: the method, the 2^(i/32) table and the polynomial
+ * coefficients are those published in ARM optimized-routines (math/expf.c,
+ * math/exp2f_data.c; Copyright (c) 2017-2018, Arm Limited;
+ * SPDX-License-Identifier: MIT OR Apache-2.0 WITH LLVM-exception), from which
+ * GNU libc 2.28 took its expf. The numeric constants below restate those
+ * published values; the code around them is this library's own.
+ *
  * Inputs below -0x1.9fe368p6 (where the result underflows) return +0, as the
  * library does. Only x <= 0 is supported; routing never produces x > 0.
  */

@@ -205,17 +205,6 @@ int check_config(const ofb_moe_config *c) {
     return OFB_OK;
 }
 
-static int sm_count() {
-    static int n = 0;
-    if (!n) {
-        int dev = 0;
-        cudaGetDevice(&dev);
-        cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
-        if (n <= 0) n = 148;
-    }
-    return n;
-}
-
 int run_moe_layer(const ofb_moe_config *cfg, const ofb_moe_weights *wt, const float *x,
                   const float *resid, float *out, int T, uint32_t *idx_out, float *w_out,
                   uint8_t *base, const WorkspaceLayout &L, cudaStream_t s, cudaEvent_t *ev,

@@ -16,12 +16,17 @@
 // array's name to a kernel (on the host it names a host-side stand-in, not a
 // device address); the device address is looked up once per device with
 // cudaGetSymbolAddress, with that device current, by the first call made on
-// that device. Make that first call before any stream capture.
+// that device. Make that first call before any stream capture. The address
+// is remembered together with the device's current context; if the context
+// changes (cudaDeviceReset, then a new primary context), the next call looks
+// the address up again.
 //
 // All calls share the one array and every call overwrites it, so calls
 // whose GPU work overlaps in time (on different streams, or from different
 // host threads) race and give wrong results; calls in one stream are safe.
 // Each call clears the ticket counters that must start at zero.
+#include <cuda.h>
+
 #include <mutex>
 
 #include "common.cuh"
@@ -35,6 +40,7 @@ static __device__ __align__(256) unsigned char ofb_noalloc_scratch[OFB_NOALLOC_S
 namespace {
 constexpr int kMaxDevices = 64;
 uint8_t *g_scratch_ptr[kMaxDevices];
+CUcontext g_scratch_ctx[kMaxDevices];
 std::mutex g_scratch_mu;
 
 int scratch_for_current_device(uint8_t **out) {
@@ -46,11 +52,25 @@ int scratch_for_current_device(uint8_t **out) {
         return OFB_EUNSUPPORTED;
     }
     std::lock_guard<std::mutex> lock(g_scratch_mu);
-    if (!g_scratch_ptr[dev]) {
+    // the device's current context, through the runtime's driver entry
+    // point (the library does not link the driver library directly)
+    using CtxGetCurrentFn = CUresult (*)(CUcontext *);
+    static CtxGetCurrentFn ctx_get = nullptr;
+    if (!ctx_get) {
+        void *p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            ctx_get = reinterpret_cast<CtxGetCurrentFn>(p);
+    }
+    CUcontext ctx = nullptr;
+    if (!ctx_get || ctx_get(&ctx) != CUDA_SUCCESS) ctx = nullptr;
+    if (!g_scratch_ptr[dev] || g_scratch_ctx[dev] != ctx) {
         void *p = nullptr;
         e = cudaGetSymbolAddress(&p, ofb_noalloc_scratch);
         if (e != cudaSuccess || !p) return ofb::cuda_status(e, "noalloc: cudaGetSymbolAddress");
         g_scratch_ptr[dev] = static_cast<uint8_t *>(p);
+        g_scratch_ctx[dev] = ctx;
     }
     *out = g_scratch_ptr[dev];
     return OFB_OK;

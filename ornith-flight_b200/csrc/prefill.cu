@@ -1119,12 +1119,10 @@ int launch_prefill(const LayerArgs &la, const float *x, int *n_slots, __nv_bfloa
     a.hb = hb; a.w = la.w; a.gsc = la.gsc; a.out = la.out; a.err = err;
     const int smem_up = UP_SMEM;
     const int smem_dn = down_smem(H);
-    static int attr_dn = 0;
-    if (!attr_dn) cudaFuncSetAttribute(prefill_up_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_up);
-    if (smem_dn > attr_dn) {
-        cudaFuncSetAttribute(prefill_down_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_dn);
-        attr_dn = smem_dn;
-    }
+    static size_t attr_up[64], attr_dn[64];
+    cudaError_t ea = ensure_dyn_smem(prefill_up_kernel, (size_t)smem_up, attr_up);
+    if (ea == cudaSuccess) ea = ensure_dyn_smem(prefill_down_kernel, (size_t)smem_dn, attr_dn);
+    if (ea != cudaSuccess) return cuda_status(ea, "prefill smem attribute");
     // out starts as the residual (or zero); the down kernel adds w * y into it
     cudaError_t e;
     if (!la.resid) e = cudaMemsetAsync(la.out, 0, (size_t)T * D * sizeof(float), s);
@@ -1133,9 +1131,7 @@ int launch_prefill(const LayerArgs &la, const float *x, int *n_slots, __nv_bfloa
     else e = cudaSuccess;
     if (e != cudaSuccess) return cuda_status(e, "prefill out init");
     if (before) cudaEventRecord(before, s);
-    int dev = 0, sms = 148;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    const int sms = sm_count();
     const int up_units = max_tiles * (H / PF_M);
     prefill_up_kernel<<<up_units < sms ? up_units : sms, UP_THREADS, smem_up, s>>>(a, xmap, gmap, umap, gmap_sh,
                                                                                      umap_sh);

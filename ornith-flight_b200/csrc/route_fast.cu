@@ -1083,11 +1083,9 @@ int launch_route_fast(const float *W, const float *x, const float *gate_v, int T
     a.flagged = nullptr;
     a.n_flagged = nullptr;
     const size_t smem = route_fast_smem(E, D);
-    static bool attr_set = false;
-    if (!attr_set) {
-        cudaFuncSetAttribute(route_select_fast, cudaFuncAttributeMaxDynamicSharedMemorySize, FR_SMEM_MAX);
-        attr_set = true;
-    }
+    static size_t attr[64];
+    cudaError_t ea = ensure_dyn_smem(route_select_fast, (size_t)FR_SMEM_MAX, attr);
+    if (ea != cudaSuccess) return cuda_status(ea, "route_select_fast smem attribute");
     if (smem > FR_SMEM_MAX) { set_error("route_fast: E/D too large for shared memory"); return OFB_EUNSUPPORTED; }
     // rows: E router rows, the gate vector, then (when x is quantised) one
     // warp per 32-element sub-block of x

@@ -20,6 +20,25 @@ int cuda_status(cudaError_t e, const char *what) {
     return e == cudaErrorMemoryAllocation ? OFB_ENOMEM : OFB_ECUDA;
 }
 
+constexpr int kMaxDev = 64;
+
+int current_device() {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDev) dev = 0;
+    return dev;
+}
+
+int sm_count() {
+    static int n[kMaxDev];
+    const int dev = current_device();
+    if (!n[dev]) {
+        int v = 0;
+        cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev);
+        n[dev] = v > 0 ? v : 148;
+    }
+    return n[dev];
+}
+
 }  // namespace ofb
 
 extern "C" const char *ofb_last_error(void) { return ofb::g_err; }
