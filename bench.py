@@ -41,7 +41,7 @@ sys.path.insert(0, os.path.join(ROOT, "oracle"))
 
 WORKLOADS = {
     "decode1": dict(tokens=1, config="BASELINE config 1: decode batch 1", layers=16, bound="hbm",
-                    dtype="f32 accumulate (int16-quantised activations, dp4a)", launches=4,
+                    dtype="f32 accumulate (int16-quantised activations, dp4a)", launches=1,
                     metric="MoE-layer tokens/s (decode batch 1)"),
     "decode32": dict(tokens=32, config="BASELINE config 2: decode batch 32", layers=16, bound="hbm",
                      dtype="f32 accumulate (int16-quantised activations, dp4a)", launches=4,
@@ -440,6 +440,50 @@ def describe_stack(world, m, steps, warmup):
     }
 
 
+def measure_sweep(ofb, dev, iters=20):
+    """Config 5: whole-block decode of 1, 8 and 256 experts' Q4_K (gate-shaped
+    512x2048) and Q6_K (down-shaped 2048x512) slices to f32 and bf16
+    (ofb_dequantize over the experts' contiguous blocks, the bytes of
+    gguf_dequantize_tensor_from_buf, engine/src/gguf.c:605-638). Two 256-expert
+    tensors per type rotate so every call reads HBM, not L2. GB/s = (blocks
+    read + values written) / device time."""
+    import torch
+    peak, peak_kind = peaks("hbm_gbs")
+    nb = H * D // 256
+    out = torch.empty(256 * nb * 256, dtype=torch.float32, device=dev)
+    res = []
+    for q, name, bb in ((ofb.TYPE_Q4_K, "Q4_K", 144), (ofb.TYPE_Q6_K, "Q6_K", 210)):
+        srcs = [ofb.synth_blocks(q, E * nb, 900 + i, 1, device=dev) for i in range(2)]
+        for n_exp in (1, 8, 256):
+            for odt, osz in ((torch.float32, 4), (torch.bfloat16, 2)):
+                o = out.view(torch.uint8)[: n_exp * nb * 256 * osz].view(odt)
+                n_el = n_exp * nb * 256
+                slices = [(s_, e0) for s_ in srcs for e0 in range(0, E, n_exp)]
+                for k in range(3):
+                    s_, e0 = slices[k % len(slices)]
+                    ofb.dequantize(s_[e0 * nb * bb:(e0 + n_exp) * nb * bb], q, n_el, out=o)
+                n_it = max(iters, min(len(slices), 512))
+                torch.cuda.synchronize()
+                e_a, e_b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e_a.record()
+                for k in range(n_it):
+                    s_, e0 = slices[k % len(slices)]
+                    ofb.dequantize(s_[e0 * nb * bb:(e0 + n_exp) * nb * bb], q, n_el, out=o)
+                e_b.record()
+                torch.cuda.synchronize()
+                ms = e_a.elapsed_time(e_b) / n_it
+                byts = n_exp * nb * bb + n_el * osz
+                gbs = byts / (ms * 1e-3) / 1e9
+                res.append({"type": name, "experts": n_exp, "out": "f32" if osz == 4 else "bf16",
+                            "bytes": byts, "us": ms * 1e3, "GB/s": gbs, "frac": gbs / peak})
+        del srcs
+    torch.cuda.empty_cache()
+    return {"metric": "expert-slice dequant HBM GB/s (config 5)", "unit": "GB/s", "peak": peak,
+            "peak_source": peak_kind + " hbm_gbs", "rotate": "2 tensors x 256 experts per type (>= 300 MB) > L2",
+            "kernel": "q4k_dequant_kernel / q6k_dequant_kernel (bit-exact, tests/test_gpu_dequant.py)",
+            "results": res}
+
+
 def run_ours(args, rank, world, local_rank):
     import torch
     ofb = load_ofb()
@@ -461,6 +505,13 @@ def run_ours(args, rank, world, local_rank):
     if args.workload != "prefill4096" and not args.no_prefill:
         extra = measure(args, ofb, dev, rank, world, local_rank, "prefill4096", args.prefill_steps,
                         3, WORKLOADS["prefill4096"]["layers"], False)
+    d32 = None
+    if args.workload == "decode1" and not args.no_decode32:
+        d32 = measure(args, ofb, dev, rank, world, local_rank, "decode32", args.decode32_steps, 5,
+                      WORKLOADS["decode32"]["layers"], False)
+    sweep = None
+    if not args.no_sweep:
+        sweep = measure_sweep(ofb, dev)
     stack = None
     if not args.no_stack:
         stack = measure_stack(args, ofb, dev, rank, world, local_rank, args.stack_steps, 3)
@@ -473,6 +524,13 @@ def run_ours(args, rank, world, local_rank):
         line["prefill4096"] = {k: sub[k] for k in ("metric", "value", "unit", "ms_per_step", "steps",
                                                    "warmup", "config", "roofline", "layer_roofline",
                                                    "phase_ms", "e2e", "gpu_launches")}
+    if d32 is not None:
+        sub = describe(args, world, "decode32", d32, args.decode32_steps, 5, WORKLOADS["decode32"]["layers"])
+        line["decode32"] = {k: sub[k] for k in ("metric", "value", "unit", "ms_per_step", "steps", "warmup",
+                                                "config", "roofline", "layer_roofline", "phase_ms", "e2e",
+                                                "route_paths", "gpu_launches")}
+    if sweep is not None:
+        line["dequant_sweep"] = sweep
     if stack is not None:
         line["stack40"] = describe_stack(world, stack, args.stack_steps, 3)
     if not args.no_cpu_baseline:
@@ -515,37 +573,51 @@ def describe(args, world, workload, m, steps, warmup, n_layers):
                 "h2d_bytes_per_step": T * D * 4, "d2h_bytes_per_step": T * D * 4},
         "route_paths": {"certified": m["route_stats"][0], "candidates_recomputed": m["route_stats"][1],
                         "all_recomputed": m["route_stats"][2]},
-        "gpu_launches": wl["launches"] * steps,
+        "gpu_launches": (1 if T == 1 else wl["launches"]) * steps,
     }
-    traffic = None
+    traffic, traffic_src = None, None
     tp = os.path.join(ROOT, "profiles", "traffic.json")
     if os.path.exists(tp):
         try:
-            traffic = json.load(open(tp)).get(workload)
+            rec = json.load(open(tp)).get(workload)
+            if rec:
+                traffic, traffic_src = rec["bytes"], "stored ncu capture, not measured in this run: " + rec["source"]
         except Exception:
             traffic = None
     if wl["bound"] == "hbm":
+        # sub-millisecond steps: burst and sustained copy peaks are the same figure
         peak, peak_kind = peaks("hbm_gbs")
         touched = round(m["n_touched"])
-        up_bytes = (touched + 1) * 2 * (H * D // 256) * 144  # gate+up rows read by the up kernel
-        achieved = up_bytes / (phase[2] * 1e-3) / 1e9
         layer_bytes = algorithmic_bytes(T, touched)
-        line["roofline"] = {"bound": "hbm", "kernel": "expert_up_q (gate/up Q4_K dequant-GEMV)",
-                            "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
-                            "traffic": traffic, "peak_source": peak_kind,
-                            "algorithmic_bytes_per_launch": up_bytes, "launch_ms": phase[2]}
+        if T == 1:
+            # decode batch 1 runs as one launch (decode_fused_kernel): the
+            # dominant kernel is the whole layer
+            kname, kbytes, kms = "decode_fused_kernel (whole layer, one launch)", layer_bytes, sum(phase)
+        else:
+            # the chained decode kernels: report the one with the largest share
+            cands = [("route_rows_kernel + route_select_fast (router rows)", E * D * 4 + T * D * 4, phase[0]),
+                     ("expert_up_q (gate/up Q4_K dequant-GEMV)", (touched + 1) * 2 * (H * D // 256) * 144, phase[2]),
+                     ("expert_down_q (down Q6_K dequant-GEMV + combine)", (touched + 1) * (H * D // 256) * 210,
+                      phase[3])]
+            kname, kbytes, kms = max(cands, key=lambda c: c[2])
+        achieved = kbytes / (kms * 1e-3) / 1e9
+        line["roofline"] = {"bound": "hbm", "kernel": kname, "achieved": achieved, "peak": peak, "unit": "GB/s",
+                            "frac": achieved / peak, "traffic": traffic, "traffic_source": traffic_src,
+                            "peak_source": peak_kind + " hbm_gbs", "algorithmic_bytes_per_launch": kbytes,
+                            "launch_ms": kms}
         la = layer_bytes / (step_ms * 1e-3) / 1e9
         line["layer_roofline"] = {"achieved": la, "frac": la / peak, "unit": "GB/s",
                                   "algorithmic_bytes_per_step": layer_bytes, "experts_touched": m["n_touched"]}
     else:
-        peak, peak_kind = peaks("bf16_tflops_sustained")
+        # a sub-millisecond kernel timed alone: the burst GEMM peak
+        peak, peak_kind = peaks("bf16_tflops")
         asg = m["kept"] + T  # routed assignments + shared expert rows
         up_flops = 4.0 * asg * H * D  # gate and up GEMMs
         achieved = up_flops / (phase[2] * 1e-3) / 1e12
         layer_flops = 6.0 * asg * H * D
         line["roofline"] = {"bound": "tensor", "kernel": "prefill_up_kernel (tcgen05 gate+up grouped GEMM)",
                             "achieved": achieved, "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
-                            "traffic": traffic, "peak_source": peak_kind,
+                            "traffic": traffic, "traffic_source": traffic_src, "peak_source": peak_kind + " bf16_tflops (burst)",
                             "algorithmic_flops_per_launch": up_flops, "launch_ms": phase[2]}
         la = layer_flops / (step_ms * 1e-3) / 1e12
         line["layer_roofline"] = {"achieved": la, "frac": la / peak, "unit": "TFLOP/s",
@@ -596,6 +668,9 @@ def main():
     ap.add_argument("--layers", type=int, default=0, help="rotating layer copies (0: workload default)")
     ap.add_argument("--prefill-steps", type=int, default=20)
     ap.add_argument("--no-prefill", action="store_true", help="skip the prefill block of the decode line")
+    ap.add_argument("--decode32-steps", type=int, default=300)
+    ap.add_argument("--no-decode32", action="store_true", help="skip the decode-32 block of the decode line")
+    ap.add_argument("--no-sweep", action="store_true", help="skip the dequant sweep block")
     ap.add_argument("--stack-steps", type=int, default=5)
     ap.add_argument("--no-stack", action="store_true", help="skip the expert-parallel stack block")
     ap.add_argument("--cpu-seconds", type=float, default=12.0)

@@ -175,6 +175,15 @@ int ofb_moe_forward_profiled(const ofb_moe_config *cfg, const ofb_moe_weights *w
  * every logit exactly. Synchronous. Diagnostic; no reference counterpart. */
 int ofb_workspace_route_stats(ofb_workspace *ws, int counts[3]);
 
+/* Device-side failures recorded in the workspace since the last call (bit 0:
+ * a bulk copy did not complete in time, bit 1: a value another CTA publishes
+ * did not arrive in time, bit 2: a tensor-core kernel's pipeline wait
+ * expired). Every wait inside this library's kernels is bounded (about half
+ * a second); on expiry the kernel records the bit and exits instead of
+ * hanging, and its output is not valid. *bits receives the mask, which is
+ * then cleared. Synchronous. No reference counterpart. */
+int ofb_workspace_device_errors(ofb_workspace *ws, unsigned *bits);
+
 /* ofb_moe_forward without any device allocation, for callers that cannot call
  * cudaMalloc: an engine whose device memory is reserved up front by its own
  * pool or budget (a raw allocation could fail or take memory already

@@ -1,0 +1,161 @@
+// async.cuh — bulk copies into shared memory completing on mbarriers, bounded
+// waits, and tagged 64-bit words for producer/consumer exchange between the
+// CTAs of one grid.
+//
+// Tagged words: a producer publishes a 32-bit value together with a 32-bit
+// tag (the launch's epoch) in one aligned 64-bit store; a consumer polls the
+// word with 64-bit loads until the tag matches. Value and tag travel in one
+// single-copy-atomic access, so no fence is needed between them and the
+// consumer needs one L2 round trip once the value is there. Every wait here is
+// bounded in time: on expiry it reports failure and the caller records an
+// error and carries on to its exit.
+#pragma once
+#include <stdint.h>
+
+#include "common.cuh"
+
+namespace ofb {
+namespace ax {
+
+__device__ __forceinline__ uint32_t smem_u32(const void *p) { return (uint32_t)__cvta_generic_to_shared(p); }
+
+__device__ __forceinline__ unsigned long long gtime() {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t)::"memory");
+    return t;
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t *b, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(b)), "r"(count));
+}
+__device__ __forceinline__ void mbar_init_fence() {
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+// One arrival that also announces `bytes` of copies completing on this phase.
+__device__ __forceinline__ void mbar_arrive_expect(uint64_t *b, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(b)), "r"(bytes)
+                 : "memory");
+}
+__device__ __forceinline__ bool mbar_test(uint64_t *b, uint32_t parity) {
+    uint32_t done;
+    asm volatile(
+        "{ .reg .pred p; mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2; selp.b32 %0, 1, 0, p; }"
+        : "=r"(done)
+        : "r"(smem_u32(b)), "r"(parity)
+        : "memory");
+    return done != 0;
+}
+// Waits for the phase of the given parity; false after `limit_ns`.
+__device__ __forceinline__ bool mbar_wait(uint64_t *b, uint32_t parity, unsigned long long limit_ns) {
+    if (mbar_test(b, parity)) return true;
+    const unsigned long long t0 = gtime();
+    for (uint32_t i = 0;; i++) {
+        if (mbar_test(b, parity)) return true;
+        if ((i & 63) == 63 && gtime() - t0 > limit_ns) return false;
+    }
+}
+
+// Bulk copy global -> this CTA's shared memory (addresses 16-byte aligned,
+// size a multiple of 16), completing `bytes` on the mbarrier. Not multicast.
+__device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t bytes, uint64_t *bar) {
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                     smem_u32(dst)),
+                 "l"(src), "r"(bytes), "r"(smem_u32(bar))
+                 : "memory");
+}
+// Orders this thread's earlier generic-proxy shared-memory accesses before
+// later async-proxy (bulk copy) accesses.
+__device__ __forceinline__ void fence_proxy_async_smem() {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+// ---- tagged 64-bit words (value in the low half, tag in the high half) ----
+__device__ __forceinline__ void put_tagged(unsigned long long *p, uint32_t value, uint32_t tag) {
+    const unsigned long long v = ((unsigned long long)tag << 32) | value;
+    asm volatile("st.relaxed.gpu.global.b64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ unsigned long long ld_relaxed64(const unsigned long long *p) {
+    unsigned long long v;
+    asm volatile("ld.relaxed.gpu.global.b64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+// Polls *p until its tag equals `tag`; returns the value, or 0 and sets *failed
+// after `limit_ns`.
+__device__ __forceinline__ uint32_t get_tagged(const unsigned long long *p, uint32_t tag,
+                                               unsigned long long limit_ns, bool &failed) {
+    unsigned long long v = ld_relaxed64(p);
+    if ((uint32_t)(v >> 32) == tag) return (uint32_t)v;
+    const unsigned long long t0 = gtime();
+    for (uint32_t i = 0;; i++) {
+        v = ld_relaxed64(p);
+        if ((uint32_t)(v >> 32) == tag) return (uint32_t)v;
+        if ((i & 15) == 15) {
+            if (gtime() - t0 > limit_ns) {
+                failed = true;
+                return 0u;
+            }
+            __nanosleep(32);
+        }
+    }
+}
+
+// N consecutive tagged words p[0..N): all loads are in flight together, then
+// only the words still missing are polled again. Returns false (and sets the
+// missing values to 0) after `limit_ns`.
+template <int N>
+__device__ __forceinline__ bool get_tagged_n(const unsigned long long *p, uint32_t tag, uint32_t (&out)[N],
+                                             unsigned long long limit_ns) {
+    unsigned long long v[N];
+#pragma unroll
+    for (int i = 0; i < N; i++) v[i] = ld_relaxed64(p + i);
+    bool all = true;
+#pragma unroll
+    for (int i = 0; i < N; i++) all = all && (uint32_t)(v[i] >> 32) == tag;
+    if (!all) {
+        const unsigned long long t0 = gtime();
+        for (uint32_t it = 0; !all; it++) {
+            all = true;
+#pragma unroll
+            for (int i = 0; i < N; i++)
+                if ((uint32_t)(v[i] >> 32) != tag) {
+                    v[i] = ld_relaxed64(p + i);
+                    all = all && (uint32_t)(v[i] >> 32) == tag;
+                }
+            if (!all && (it & 15) == 15) {
+                if (gtime() - t0 > limit_ns) {
+#pragma unroll
+                    for (int i = 0; i < N; i++)
+                        if ((uint32_t)(v[i] >> 32) != tag) v[i] = 0;
+                    break;
+                }
+                __nanosleep(32);
+            }
+        }
+    }
+#pragma unroll
+    for (int i = 0; i < N; i++) out[i] = (uint32_t)v[i];
+    return all;
+}
+
+// Publishes this thread's earlier stores (gpu scope), then adds n to *p.
+__device__ __forceinline__ void count_add(unsigned *p, unsigned n) {
+    __threadfence();
+    atomicAdd(p, n);
+}
+// Waits until the counter has reached `target` (wrap-around aware); the
+// acquire orders the caller's later loads after the counted stores.
+__device__ __forceinline__ bool wait_count(const unsigned *p, unsigned target, unsigned long long limit_ns) {
+    unsigned v;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    if ((int)(v - target) >= 0) return true;
+    const unsigned long long t0 = gtime();
+    for (;;) {
+        __nanosleep(64);
+        asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+        if ((int)(v - target) >= 0) return true;
+        if (gtime() - t0 > limit_ns) return false;
+    }
+}
+
+}  // namespace ax
+}  // namespace ofb

@@ -23,51 +23,11 @@
 //    needs no extra launch.
 #include "common.cuh"
 #include "moe.cuh"
+#include "gemv.cuh"
 
 namespace ofb {
 
 DTRACE_DEFINE(dc)
-
-__device__ __forceinline__ float silu_ref_d(float g) {
-    // engine/src/model.c:340-344
-    if (g < -50.0f) return 0.0f;
-    if (g > 50.0f) return g;
-    return g / (1.0f + expf(-g));
-}
-
-__device__ __forceinline__ int dp4a_s(int a, int b, int c) { return __dp4a(a, b, c); }
-__device__ __forceinline__ int dp4a_u(unsigned a, unsigned b, int c) {
-    return (int)__dp4a(a, b, (unsigned)c);
-}
-
-__device__ __forceinline__ uint32_t comp(const uint4 &v, int i) {
-    return i == 0 ? v.x : i == 1 ? v.y : i == 2 ? v.z : v.w;
-}
-
-// One lane item of a Q4_K row: chunk c of a block (sub-blocks 2c and 2c+1,
-// 32 quant bytes) against the quantised activations of the same 64 elements.
-__device__ __forceinline__ float q4k_item_q(const uint4 &hdr, const uint4 &qa, const uint4 &qb, int c,
-                                            const uint4 xh[4], const uint4 xl[4], float s_lo,
-                                            float s_hi, float xs_lo, float xs_hi) {
-    int ih_lo = 0, il_lo = 0, ih_hi = 0, il_hi = 0;
-#pragma unroll
-    for (int w = 0; w < 8; w++) {
-        const uint32_t q = (w < 4) ? comp(qa, w) : comp(qb, w - 4);
-        const uint32_t lo = q & 0x0F0F0F0Fu, hi = (q >> 4) & 0x0F0F0F0Fu;
-        ih_lo = dp4a_s((int)lo, (int)comp(xh[w >> 2], w & 3), ih_lo);
-        il_lo = dp4a_u(lo, comp(xl[w >> 2], w & 3), il_lo);
-        ih_hi = dp4a_s((int)hi, (int)comp(xh[2 + (w >> 2)], w & 3), ih_hi);
-        il_hi = dp4a_u(hi, comp(xl[2 + (w >> 2)], w & 3), il_hi);
-    }
-    const uint32_t s[3] = {hdr.y, hdr.z, hdr.w};
-    int sc0, m0, sc1, m1;
-    q4k_scale_min(s, 2 * c, sc0, m0);
-    q4k_scale_min(s, 2 * c + 1, sc1, m1);
-    const float d = half_bits_ref(hdr.x & 0xFFFFu), dmin = half_bits_ref(hdr.x >> 16);
-    const float S_lo = (float)(ih_lo * 256 + il_lo), S_hi = (float)(ih_hi * 256 + il_hi);
-    return d * ((float)sc0 * s_lo * S_lo + (float)sc1 * s_hi * S_hi) -
-           dmin * ((float)m0 * xs_lo + (float)m1 * xs_hi);
-}
 
 __device__ __forceinline__ int asg_token_d(int a, int TK, int K) { return a < TK ? a / K : a - TK; }
 
@@ -152,18 +112,6 @@ constexpr int DG = DOWN_TICKET_ROWS;  // output rows per warp (one ticket each)
 constexpr int DQ_WARPS = 16;  // warps per CTA
 constexpr int DQ_ROWS = DG * DQ_WARPS;  // output rows per CTA
 constexpr int DQ_TOK = 8;     // tokens whose quantised h is staged at once
-
-// 4 bytes at a 2-byte aligned shared-memory address.
-__device__ __forceinline__ uint32_t lds_u32_2(const uint8_t *p) {
-    const uintptr_t a = reinterpret_cast<uintptr_t>(p);
-    const uint32_t *b = reinterpret_cast<const uint32_t *>(a & ~uintptr_t(3));
-    return __funnelshift_r(b[0], b[1], (unsigned)(a & 3) * 8);
-}
-
-// Quantised h of one item (16 values: 4 quads x 4) of one token, as the
-// dp4a loop consumes it: int8 high / uint8 low planes, the element sum, and
-// the scale, per quad.
-struct HQuad { uint32_t hh, hl; int xs; float sq; };
 
 // One CTA per (slot, 64 output rows): stage the 64 Q6_K rows in shared memory
 // (the first unit's before waiting for expert_up_q, which runs meanwhile),

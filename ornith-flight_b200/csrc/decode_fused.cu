@@ -1,0 +1,937 @@
+// decode_fused.cu — the whole MoE layer for one token (decode batch 1) in a
+// single persistent launch: router, softmax/top-k/renormalise, expert SwiGLU
+// on the raw Q4_K/Q6_K blocks, sigmoid-gated shared expert and the combine
+// (engine/src/model.c:992-1143 for one token).
+//
+// Why one launch: at batch 1 the layer moves ~20 MB (3.1 us of HBM time)
+// through four dependent steps (router -> top-k -> gate/up -> down). As
+// separate kernels each step pays a launch hand-off and a ramp of its own;
+// here every CTA moves its share of every step's bytes with bulk copies
+// (TMA, cp.async.bulk) into shared memory as soon as it knows the addresses,
+// and CTAs exchange the few values that cross between steps (router logits
+// with bounds, h rows) as tagged 64-bit words in global memory.
+//
+// One CTA per SM (grid = SM count, ~185 KB of shared memory each). CTA c owns
+//  * router rows c, c+G, ... (and the shared-expert gate vector as row E),
+//  * shared-expert hidden rows [c*H/G, (c+1)*H/G),
+//  * routed (slot, hidden row) pairs [c*K*H/G, (c+1)*K*H/G) in top-k slot
+//    order, and
+//  * output rows [n0, n1) (groups of dg rows, 16-byte aligned Q6_K slabs),
+//    for every expert: the CTA computes y of all K+1 experts for its rows and
+//    combines them in the reference's order, so no cross-CTA reduction.
+// Steps:
+//  0. before the dependent-launch wait (the previous kernel may still run):
+//     bulk copies of the static bytes it owns: router rows, shared gate/up
+//     rows, shared down rows.
+//  1. x (bulk copy) -> 16-bit quantised copy for dp4a; router logits of its
+//     rows in fp64 with a rigorous bound B of the distance to the reference's
+//     sequential fp32 sum (the certified routing of route_fast.cu, restated
+//     per CTA); shared-expert h rows. Both published as tagged words.
+//  2. every CTA reads all (L~, B) and runs the same certified selection
+//     (identical inputs, identical result): top-k indices bit-exact, or the
+//     exact recompute of the uncertain candidates with the reference's chain
+//     and the host C library's expf. Then bulk copies of its routed gate/up
+//     rows and of its output rows' Q6_K slabs of the K routed experts; while
+//     they fly, the shared expert's down rows for its outputs.
+//  3. routed h rows (dp4a on the raw nibbles) -> tagged words; then the h of
+//     every routed expert (polled) -> quantised per 16-element scale group ->
+//     y for its rows -> out = resid + g*y_sh + sum_k w_k y_k.
+// Tags are the launch epoch + 1: a device counter the last CTA to finish
+// advances, read after the dependent-launch wait (which orders it after the
+// previous launch), so stale words from earlier launches never match and the
+// kernel can be replayed (e.g. in a CUDA graph) without host bookkeeping.
+// Every wait (mbarrier or tag) is bounded; on expiry the CTA records an error
+// bit in the workspace and runs to its exit on whatever it has.
+//
+// Requirements (checked on the host): T = 1, contiguous layout, router
+// present, E <= 256 (selection by one warp), E + 1 <= 2 * grid, top_k <= 16,
+// the per-CTA shares fit in shared memory.
+#include <algorithm>
+
+#include "async.cuh"
+#include "common.cuh"
+#include "exact_expf.h"
+#include "exact_route.cuh"
+#include "exchange.cuh"
+#include "gemv.cuh"
+#include "moe.cuh"
+
+namespace ofb {
+
+constexpr int FD_THREADS = 512;
+constexpr int FD_WARPS = FD_THREADS / 32;
+constexpr int FD_PER_LANE = 8;                            // selection: experts per lane (E <= 256)
+constexpr unsigned long long FD_WAIT_NS = 500000000ull;  // 0.5 s per wait
+constexpr double FD_MARGIN = 0x1.0p-14;                   // certificate margin (as route_fast.cu)
+
+// Error bits recorded in sync[2] (read by ofb_workspace_check).
+constexpr uint32_t FD_ERR_COPY = 1u, FD_ERR_TAG = 2u;
+
+struct FusedDecodeArgs {
+    const float *W, *x, *gate_v, *resid;
+    float *out;
+    const uint8_t *gate, *up, *down, *gate_sh, *up_sh, *down_sh;
+    int D, H, E, K, routing, renorm, has_shared, use_gate;
+    double bound_scale, ngam;
+    unsigned long long *cand;  // [2E + 1]: (L~, B) per expert, then the shared gate
+    unsigned long long *hll;   // [K + 1][H]: h of each top-k slot, then the shared expert
+    unsigned int *sync;        // [0] epoch, [1] CTAs finished, [2] error bits, [3] router rows
+                               // published, [4 + k] h rows published of slot k (k <= K)
+    uint32_t *idx_out;
+    float *w_out;
+    int *stats;  // [3] tokens per routing path (certified, candidates, full)
+    FusedPlan p;
+};
+
+// Optional per-CTA timeline (build with -DOFB_FD_TRACE): globaltimer at each
+// step boundary of the last launch, read back with ofb_debug_fd_trace.
+#ifdef OFB_FD_TRACE
+__device__ unsigned long long g_fd_tr[256][32];
+#define FD_MARK_IF(cond, i) \
+    if ((cond) && blockIdx.x < 256) g_fd_tr[blockIdx.x][i] = ax::gtime();
+#else
+#define FD_MARK_IF(cond, i)
+#endif
+#define FD_MARK(i) FD_MARK_IF(threadIdx.x == 0, i)
+
+__device__ __forceinline__ float f_of(uint32_t u) { return __uint_as_float(u); }
+__device__ __forceinline__ uint32_t u_of(float f) { return __float_as_uint(f); }
+
+// Dot products of one Q4_K row pair (gate, up) in shared memory with the
+// quantised x; one warp, lane j over 64-element items. Returns h on every lane.
+__device__ __noinline__ float swiglu_pair(const uint8_t *grow, const uint8_t *urow, const unsigned char *xq,
+                                             int D, int lane) {
+    const int items = D / 64;
+    const float *qf = reinterpret_cast<const float *>(xq + 2 * D);
+    float ag = 0.f, au = 0.f;
+    for (int j = lane; j < items; j += 32) {
+        const int b = j >> 2, c = j & 3;
+        const uint8_t *gb = grow + b * Q4K_BYTES, *ub = urow + b * Q4K_BYTES;
+        const uint4 hg = *reinterpret_cast<const uint4 *>(gb);
+        const uint4 ga = *reinterpret_cast<const uint4 *>(gb + 16 + c * 32);
+        const uint4 gq = *reinterpret_cast<const uint4 *>(gb + 32 + c * 32);
+        const uint4 hu = *reinterpret_cast<const uint4 *>(ub);
+        const uint4 ua = *reinterpret_cast<const uint4 *>(ub + 16 + c * 32);
+        const uint4 uq = *reinterpret_cast<const uint4 *>(ub + 32 + c * 32);
+        const int e0 = b * QK + c * 64, sb = e0 / 32;
+        uint4 xh[4], xl[4];
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            xh[i] = reinterpret_cast<const uint4 *>(xq + e0)[i];
+            xl[i] = reinterpret_cast<const uint4 *>(xq + D + e0)[i];
+        }
+        const float s_lo = qf[sb], s_hi = qf[sb + 1];
+        const float xs_lo = qf[D / 32 + sb], xs_hi = qf[D / 32 + sb + 1];
+        ag += q4k_item_q(hg, ga, gq, c, xh, xl, s_lo, s_hi, xs_lo, xs_hi);
+        au += q4k_item_q(hu, ua, uq, c, xh, xl, s_lo, s_hi, xs_lo, xs_hi);
+    }
+    const float g = warp_sum(ag), u = warp_sum(au);
+    return silu_ref_d(g) * u;
+}
+
+// 32-bit shared-memory loads by shared-window address.
+__device__ __forceinline__ uint32_t lds32(uint32_t a) {
+    uint32_t v;
+    asm volatile("ld.shared.b32 %0, [%1];" : "=r"(v) : "r"(a));
+    return v;
+}
+// N consecutive 32-bit words starting at a 2-byte aligned shared address.
+template <int N>
+__device__ __forceinline__ void lds_run2(uint32_t a, uint32_t (&w)[N]) {
+    const uint32_t b = a & ~3u, sh = (a & 3u) * 8u;
+    uint32_t prev = lds32(b);
+#pragma unroll
+    for (int i = 0; i < N; i++) {
+        const uint32_t nx = lds32(b + 4 * (i + 1));
+        w[i] = __funnelshift_r(prev, nx, sh);
+        prev = nx;
+    }
+}
+
+// Quantised h of one expert slot in shared memory: hi / lo byte planes of
+// the 16-bit integer h_int (h ~= s_g * h_int, per 16-element group g), the
+// group scales s_g and the group sums of h_int.
+struct HSlot {
+    int8_t *hh;
+    uint8_t *hl;
+    float *hs;
+    int *hsum;
+};
+__device__ __forceinline__ HSlot hslot(uint8_t *base, int H, int k) {
+    uint8_t *p = base + (size_t)k * (2 * H + H / 2);
+    return HSlot{reinterpret_cast<int8_t *>(p), p + H, reinterpret_cast<float *>(p + 2 * H),
+                 reinterpret_cast<int *>(p + 2 * H + H / 4)};
+}
+// Quantises the 16 h values of group g (positions 16g..16g+15) into the slot.
+__device__ __forceinline__ void quantize_group(const uint32_t (&v)[16], const HSlot &s, int g) {
+    float m = 0.f;
+#pragma unroll
+    for (int i = 0; i < 16; i++) m = fmaxf(m, fabsf(__uint_as_float(v[i])));
+    const float sc = m / 32767.0f, inv = (m > 0.f) ? 32767.0f / m : 0.f;
+    uint32_t hw[4], lw[4];
+    int sum = 0;
+#pragma unroll
+    for (int q = 0; q < 4; q++) {
+        uint32_t h4 = 0, l4 = 0;
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            const int xi = __float2int_rn(__uint_as_float(v[4 * q + i]) * inv);
+            sum += xi;
+            h4 |= ((uint32_t)(xi >> 8) & 0xFFu) << (8 * i);
+            l4 |= ((uint32_t)xi & 0xFFu) << (8 * i);
+        }
+        hw[q] = h4;
+        lw[q] = l4;
+    }
+    *reinterpret_cast<uint4 *>(s.hh + 16 * g) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+    *reinterpret_cast<uint4 *>(s.hl + 16 * g) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
+    s.hs[g] = sc;
+    s.hsum[g] = sum;
+}
+
+// Dot product of one half block (128 weights) of a Q6_K row in shared memory
+// (blk = block start, 2-byte aligned shared address) with the quantised h of
+// the same 128 positions (hb = half-block index within the row).
+__device__ __noinline__ float q6k_half_dot(uint32_t blk, int half, const HSlot &s, int hb) {
+    uint32_t ql[16], qh[8], sc[2], dw[1];
+    lds_run2<16>(blk + half * 64, ql);
+    lds_run2<8>(blk + 128 + half * 32, qh);
+    lds_run2<2>(blk + 192 + half * 8, sc);
+    lds_run2<1>(blk + 208, dw);
+    const int8_t *hh = s.hh + hb * 128;
+    const uint8_t *hl = s.hl + hb * 128;
+    int ahi[8], alo[8];
+#pragma unroll
+    for (int i = 0; i < 8; i++) ahi[i] = alo[i] = 0;
+#pragma unroll
+    for (int q = 0; q < 4; q++) {
+        const uint4 H0 = *reinterpret_cast<const uint4 *>(hh + q * 32);
+        const uint4 H1 = *reinterpret_cast<const uint4 *>(hh + q * 32 + 16);
+        const uint4 L0 = *reinterpret_cast<const uint4 *>(hl + q * 32);
+        const uint4 L1 = *reinterpret_cast<const uint4 *>(hl + q * 32 + 16);
+#pragma unroll
+        for (int st = 0; st < 8; st++) {
+            const uint32_t w = (q & 1) ? ql[8 + st] : ql[st];
+            const uint32_t nib = (q & 2) ? ((w >> 4) & 0x0F0F0F0Fu) : (w & 0x0F0F0F0Fu);
+            const uint32_t top = ((qh[st] >> (2 * q)) & 0x03030303u) << 4;
+            const uint32_t qv = nib | top;
+            const int g = q * 2 + (st >> 2);
+            const uint32_t hw = comp(st < 4 ? H0 : H1, st & 3), lw = comp(st < 4 ? L0 : L1, st & 3);
+            ahi[g] = dp4a_s((int)qv, (int)hw, ahi[g]);
+            alo[g] = dp4a_u(qv, lw, alo[g]);
+        }
+    }
+    const float4 s0 = *reinterpret_cast<const float4 *>(s.hs + hb * 8);
+    const float4 s1 = *reinterpret_cast<const float4 *>(s.hs + hb * 8 + 4);
+    const int4 z0 = *reinterpret_cast<const int4 *>(s.hsum + hb * 8);
+    const int4 z1 = *reinterpret_cast<const int4 *>(s.hsum + hb * 8 + 4);
+    const float hsv[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
+    const int hzv[8] = {z0.x, z0.y, z0.z, z0.w, z1.x, z1.y, z1.z, z1.w};
+    float y = 0.f;
+#pragma unroll
+    for (int g = 0; g < 8; g++) {
+        const int scale = (int)(int8_t)((g < 4 ? sc[0] : sc[1]) >> (8 * (g & 3)));
+        const int S = ahi[g] * 256 + alo[g] - 32 * hzv[g];
+        y += (float)scale * hsv[g] * (float)S;
+    }
+    return half_bits_ref(dw[0] & 0xFFFFu) * y;
+}
+
+__global__ void __launch_bounds__(FD_THREADS, 1) decode_fused_kernel(FusedDecodeArgs a) {
+    extern __shared__ __align__(128) uint8_t sm[];
+    const FusedPlan &P = a.p;
+    const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
+    const int G = gridDim.x, c = blockIdx.x;
+    const int D = a.D, H = a.H, E = a.E, K = a.K;
+    const int rb4 = (D / QK) * Q4K_BYTES, rb6 = (H / QK) * Q6K_BYTES;
+    const size_t exp4 = (size_t)rb4 * H, exp6 = (size_t)rb6 * D;
+    const int NHB = H / 128;  // half blocks per Q6_K row
+
+    float *xs = reinterpret_cast<float *>(sm + P.o_x);
+    unsigned char *xq = sm + P.o_xq;
+    float *rrow = reinterpret_cast<float *>(sm + P.o_rr);
+    uint8_t *shu = sm + P.o_shu;
+    uint8_t *dn = sm + P.o_dn;  // slot K (shared) first, then routed slots 0..K-1
+    uint8_t *upg = sm + P.o_up;
+    uint8_t *upu = upg + (size_t)P.upc * rb4;
+    uint8_t *hqb = sm + P.o_hq;
+    float *Lf = reinterpret_cast<float *>(sm + P.o_sel);
+    float *Bf = Lf + E;
+    float *ysp = reinterpret_cast<float *>(sm + P.o_ys);  // [K+1][ngc*dg][NHB] partial dots
+    uint64_t *bars = reinterpret_cast<uint64_t *>(sm + P.o_bar);
+    uint64_t *mb_pre = bars, *mb_x = bars + 1, *mb_up = bars + 2, *mb_dn = bars + 4;  // mb_dn[K]
+    const int nbars = 4 + K;
+    const size_t sdn = (size_t)P.ngc * P.dg * rb6;  // shared bytes per slot of down rows
+    const int rows_cap = P.ngc * P.dg;
+    auto dnp = [&](int k) { return dn + (size_t)(k == K ? 0 : k + 1) * sdn; };
+
+    __shared__ int s_top[16];
+    __shared__ float s_w[16];
+    __shared__ uint32_t s_tag, s_par;
+    __shared__ int s_mode, s_nc, s_full, s_wcnt[FD_WARPS];
+    __shared__ float s_max, s_sum, s_gsc;
+    __shared__ double s_lo;
+    __shared__ uint32_t s_err;
+    __shared__ int s_next[2];
+
+    // ---- work shares of this CTA ----
+    const int nrows = E + a.use_gate;
+    const int nr_mine = c < nrows ? (nrows - 1 - c) / G + 1 : 0;  // rows c, c+G, ...
+    const int s0 = (int)((long long)c * H / G), s1 = (int)((long long)(c + 1) * H / G);
+    const int u0 = (int)((long long)c * K * H / G), u1 = (int)((long long)(c + 1) * K * H / G);
+    const int NG = D / P.dg;
+    const int n0 = (int)((long long)c * NG / G) * P.dg, n1 = (int)((long long)(c + 1) * NG / G) * P.dg;
+    const int nrow_out = n1 - n0;
+    const int slot_first = u0 / H;  // the CTA's pairs span slots slot_first and (maybe) slot_first + 1
+
+    // Copies of top-k slot q (expert e): my gate/up rows inside slot q and my
+    // output rows' down slab. One arrival on each mbarrier per issue round.
+    auto issue_slot = [&](int q, int e) {
+        const int p0 = max(u0, q * H), p1 = min(u1, (q + 1) * H);
+        if (p1 > p0) {
+            uint64_t *b = mb_up + (q == slot_first ? 0 : 1);
+            ax::mbar_arrive_expect(b, 2u * (p1 - p0) * rb4);
+            const size_t off = (size_t)e * exp4 + (size_t)(p0 - q * H) * rb4;
+            ax::bulk_g2s(upg + (size_t)(p0 - u0) * rb4, a.gate + off, (p1 - p0) * rb4, b);
+            ax::bulk_g2s(upu + (size_t)(p0 - u0) * rb4, a.up + off, (p1 - p0) * rb4, b);
+        }
+        ax::mbar_arrive_expect(mb_dn + q, (uint32_t)nrow_out * rb6);
+        if (nrow_out)
+            ax::bulk_g2s(dnp(q), a.down + (size_t)e * exp6 + (size_t)n0 * rb6, nrow_out * rb6, mb_dn + q);
+    };
+    // up segments that no slot filled still need their arrival
+    auto close_up = [&]() {
+        const bool seg0 = u1 > u0, seg1 = u1 > u0 && (u1 - 1) / H > slot_first;
+        if (!seg0) ax::mbar_arrive_expect(mb_up, 0);
+        if (!seg1) ax::mbar_arrive_expect(mb_up + 1, 0);
+    };
+
+    // ---- step 0: static bytes, before waiting for the producer of x ----
+    FD_MARK(0)
+    if (tid == 0) {
+        s_err = 0;
+        s_par = 0;
+        for (int i = 0; i < nbars; i++) ax::mbar_init(bars + i, 1);
+        ax::mbar_init_fence();
+    }
+    __syncthreads();
+    pdl_trigger();
+    if (tid == 0 && !a.has_shared && s1 > s0) atomicAdd(a.sync + 4 + K, (unsigned)(s1 - s0));
+    if (tid == 0) {
+        uint32_t bytes = (uint32_t)nr_mine * D * 4;
+        if (a.has_shared) bytes += 2u * (s1 - s0) * rb4 + (uint32_t)nrow_out * rb6;
+        ax::mbar_arrive_expect(mb_pre, bytes);
+        for (int i = 0; i < nr_mine; i++) {
+            const int r = c + i * G;
+            const float *src = r < E ? a.W + (size_t)r * D : a.gate_v;
+            ax::bulk_g2s(rrow + (size_t)i * D, src, D * 4, mb_pre);
+        }
+        if (a.has_shared) {
+            if (s1 > s0) {
+                ax::bulk_g2s(shu, a.gate_sh + (size_t)s0 * rb4, (s1 - s0) * rb4, mb_pre);
+                ax::bulk_g2s(shu + (size_t)P.shp * rb4, a.up_sh + (size_t)s0 * rb4, (s1 - s0) * rb4, mb_pre);
+            }
+            if (nrow_out) ax::bulk_g2s(dnp(K), a.down_sh + (size_t)n0 * rb6, nrow_out * rb6, mb_pre);
+        }
+    }
+    pdl_wait();
+    FD_MARK(1)
+    if (tid == 0) {
+        s_tag = *reinterpret_cast<volatile unsigned int *>(a.sync) + 1u;
+        ax::mbar_arrive_expect(mb_x, D * 4);
+        ax::bulk_g2s(xs, a.x, D * 4, mb_x);
+    }
+    bool tag_fail = false, copy_fail = false;
+    if (!ax::mbar_wait(mb_x, 0, FD_WAIT_NS)) copy_fail = true;
+    if (!ax::mbar_wait(mb_pre, 0, FD_WAIT_NS)) copy_fail = true;
+    __syncthreads();
+    const uint32_t tag = s_tag;
+    FD_MARK(2)
+
+    // ---- step 1: router rows (published first) ----
+    {
+        // tpr threads per router row: thread lt owns elements [lt*seg, lt*seg+seg), seg >= 4;
+        // their (sum, sum of |prefix|, sum of |product|) go through shared
+        // memory (the routed gate/up area, unused until the selection) to one
+        // warp per row, which scans them and publishes the row
+        const int tpr = D % 1024 == 0 ? 256 : D / 4, seg = D / tpr;
+        const int ri = tid / tpr, lt = tid - ri * tpr;
+        double *rp = reinterpret_cast<double *>(upg);
+        if (ri < nr_mine) {
+            const float *w = rrow + (size_t)ri * D + lt * seg;
+            const float *xv = xs + lt * seg;
+            // products exact as (p, e) pairs (fma), summed as a float pair
+            // (two-sum): the running sum is exact to ~2^-44 of sum|p|, far
+            // inside the bound's 2^-9 slack; |prefix| and |p| sums in fp32
+            // are upper bounds within a few ulps (same slack)
+            float hi = 0.f, lo = 0.f, SPf = 0.f, Af = 0.f;
+            for (int i = 0; i < seg; i += 4) {
+                const float4 w4 = *reinterpret_cast<const float4 *>(w + i);
+                const float4 x4 = *reinterpret_cast<const float4 *>(xv + i);
+                const float xx[4] = {x4.x, x4.y, x4.z, x4.w}, ww[4] = {w4.x, w4.y, w4.z, w4.w};
+#pragma unroll
+                for (int k = 0; k < 4; k++) {
+                    const float p = __fmul_rn(xx[k], ww[k]), e = __fmaf_rn(xx[k], ww[k], -p);
+                    const float sm = __fadd_rn(hi, p), bb = __fsub_rn(sm, hi);
+                    const float er = __fadd_rn(__fsub_rn(hi, __fsub_rn(sm, bb)), __fsub_rn(p, bb));
+                    hi = sm;
+                    lo = __fadd_rn(lo, __fadd_rn(er, e));
+                    SPf = __fadd_ru(SPf, fabsf(__fadd_rn(hi, lo)));
+                    Af = __fadd_ru(Af, fabsf(p));
+                }
+            }
+            const double Pl = (double)hi + (double)lo;
+            const double SP = (double)SPf * (1.0 + 0x1.0p-20), A = (double)Af * (1.0 + 0x1.0p-20);
+            double *o = rp + ((size_t)ri * tpr + lt) * 3;
+            o[0] = Pl; o[1] = SP; o[2] = A;
+        }
+        FD_MARK(20)
+        __syncthreads();
+        FD_MARK(21)
+        if (wid < nr_mine) {
+            // lane i owns threads [i*per, i*per + per) of row wid
+            const int per = tpr / 32;
+            const double *q = rp + ((size_t)wid * tpr + lane * per) * 3;
+            double tot = 0.0;
+            for (int j = 0; j < per; j++) tot += q[3 * j];
+            double inc = tot;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const double up = __shfl_up_sync(0xffffffffu, inc, o);
+                if (lane >= o) inc += up;
+            }
+            FD_MARK(22)
+            double ex = inc - tot, spb = 0.0, At = 0.0;
+            for (int j = 0; j < per; j++) {
+                spb += (double)seg * fabs(ex) + q[3 * j + 1];
+                At += q[3 * j + 2];
+                ex += q[3 * j];
+            }
+            double L = tot;
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) {
+                L += __shfl_xor_sync(0xffffffffu, L, o);
+                spb += __shfl_xor_sync(0xffffffffu, spb, o);
+                At += __shfl_xor_sync(0xffffffffu, At, o);
+            }
+            const int r = c + wid * G;
+            FD_MARK(23)
+            if (lane == 0) {
+                if (r < E) {
+                    const double Bd = a.bound_scale * (At + spb + a.ngam * At) + 0x1.0p-60;
+                    const float lf = __double2float_rn(L);
+                    const float bf = __double2float_ru(Bd + fabs(L - (double)lf));
+                    ax::put_tagged(a.cand + 2 * r, u_of(lf), tag);
+                    ax::put_tagged(a.cand + 2 * r + 1, u_of(bf), tag);
+                    ax::count_add(a.sync + 3, 1u);
+                } else {
+                    ax::put_tagged(a.cand + 2 * E, u_of(1.0f / (1.0f + expf(-(float)L))), tag);
+                }
+            }
+        }
+    }
+    FD_MARK(3)
+
+    // ---- step 2: two warp groups until the selection is known ----
+    // group A (warps 0-7): all (L~, B) -> warp 0 selects the top-k, issues the
+    //   routed copies and certifies; group B (warps 8-15): quantised x, the
+    //   shared expert's h rows, then its down rows.
+    constexpr int GRP = FD_THREADS / 2;
+    if (tid < GRP) {
+        // one thread waits for the count of published rows, then every
+        // thread reads its entries once (no polling storm on these lines)
+        if (tid == 0 && !ax::wait_count(a.sync + 3, tag * (unsigned)E, FD_WAIT_NS)) tag_fail = true;
+        asm volatile("bar.sync 1, %0;" ::"r"(GRP) : "memory");
+        for (int e = tid; e < E; e += GRP) {
+            uint32_t v[2];
+            if (!ax::get_tagged_n<2>(a.cand + 2 * e, tag, v, FD_WAIT_NS)) tag_fail = true;
+            Lf[e] = f_of(v[0]);
+            Bf[e] = f_of(v[1]);
+        }
+        ax::fence_proxy_async_smem();  // the router partials' area is refilled by bulk copies
+        asm volatile("bar.sync 1, %0;" ::"r"(GRP) : "memory");
+        FD_MARK(6)
+        if (wid == 0) {
+            // keys: the order-preserving bits of L~ truncated to 24 bits, then
+            // 255 - e (a larger key wins; equal values go to the smaller
+            // index). The truncation can only mis-order logits closer than
+            // 2^-15 relative; the certificate below checks the chosen order
+            // on the full values, so such a choice is never certified.
+            uint32_t k8[FD_PER_LANE];
+#pragma unroll
+            for (int j = 0; j < FD_PER_LANE; j++) {
+                const int e = lane + 32 * j;
+                const uint32_t u = e < E ? __float_as_uint(Lf[e]) : 0u;
+                const uint32_t ok = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+                k8[j] = e < E ? ((ok & 0xFFFFFF00u) | (uint32_t)(255 - e)) : 0u;
+            }
+            // sort each lane's 8 keys descending (19-comparator network)
+            auto cx = [&](int p, int q) { const uint32_t hi = max(k8[p], k8[q]), lo = min(k8[p], k8[q]); k8[p] = hi; k8[q] = lo; };
+            cx(0, 2); cx(1, 3); cx(4, 6); cx(5, 7);
+            cx(0, 4); cx(1, 5); cx(2, 6); cx(3, 7);
+            cx(0, 1); cx(2, 3); cx(4, 5); cx(6, 7);
+            cx(2, 4); cx(3, 5);
+            cx(1, 4); cx(3, 6);
+            cx(1, 2); cx(3, 4); cx(5, 6);
+            int my_e = 0;
+            for (int q = 0; q < K; q++) {
+                const uint32_t wk = __reduce_max_sync(0xffffffffu, k8[0]);
+                if (k8[0] == wk) {
+#pragma unroll
+                    for (int j = 0; j < FD_PER_LANE - 1; j++) k8[j] = k8[j + 1];
+                    k8[FD_PER_LANE - 1] = 0u;
+                }
+                if (lane == q) my_e = 255 - (int)(wk & 0xFFu);
+            }
+            // lane q < K issues the copies of slot q
+            if (lane < K) {
+                s_top[lane] = my_e;
+                issue_slot(lane, my_e);
+            }
+            if (lane == 0) close_up();
+            FD_MARK(16)
+            // certificate: every adjacent gap inside the top-k and the gap to
+            // the rest exceed both bounds plus the margin (rounded against success)
+            float hi_rest = -INFINITY;
+#pragma unroll
+            for (int j = 0; j < FD_PER_LANE; j++)
+                if (k8[j]) {
+                    const int e = 255 - (int)(k8[j] & 0xFFu);
+                    hi_rest = fmaxf(hi_rest, __fadd_ru(Lf[e], Bf[e]));
+                }
+            hi_rest = fmaxf(hi_rest, __shfl_xor_sync(0xffffffffu, hi_rest, 16));
+            hi_rest = fmaxf(hi_rest, __shfl_xor_sync(0xffffffffu, hi_rest, 8));
+            hi_rest = fmaxf(hi_rest, __shfl_xor_sync(0xffffffffu, hi_rest, 4));
+            hi_rest = fmaxf(hi_rest, __shfl_xor_sync(0xffffffffu, hi_rest, 2));
+            hi_rest = fmaxf(hi_rest, __shfl_xor_sync(0xffffffffu, hi_rest, 1));
+            const float myL = lane < K ? Lf[my_e] : 0.f, myB = lane < K ? Bf[my_e] : 0.f;
+            const float nL = __shfl_down_sync(0xffffffffu, myL, 1), nB = __shfl_down_sync(0xffffffffu, myB, 1);
+            const float L0 = __shfl_sync(0xffffffffu, myL, 0);
+            bool ok = true;
+            if (lane < K) {
+                const float nxt = lane + 1 < K ? __fadd_ru(nL, nB) : hi_rest;
+                ok = __fsub_rd(myL, myB) > __fadd_ru(nxt, (float)FD_MARGIN);
+                if (lane == K - 1) ok = ok && (myL - L0 > -80.0f);
+            }
+            ok = __all_sync(0xffffffffu, ok);
+            if (lane == 0) s_mode = ok ? 0 : 1;
+            FD_MARK(17)
+            if (ok) {
+                // weights: fp32 softmax of L~ (model.c:1027-1049 / :300-316 forms)
+                float sum = 0.f;
+                if (a.routing == OFB_ROUTE_FORWARD) {
+#pragma unroll
+                    for (int j = 0; j < FD_PER_LANE; j++)
+                        if (lane + 32 * j < E) sum += expf(Lf[lane + 32 * j] - L0);
+                } else if (lane < K) {
+                    sum = expf(myL - L0);
+                }
+                sum = warp_sum(sum);
+                const float wq = lane < K ? expf(myL - L0) / sum : 0.f;
+                const float ss = warp_sum(wq);
+                if (lane < K) s_w[lane] = (a.routing == OFB_ROUTE_FORWARD && a.renorm) ? wq / ss : wq;
+                FD_MARK(18)
+            } else {
+                float lo = lane < K ? __fsub_rd(myL, myB) : INFINITY;
+#pragma unroll
+                for (int o = 16; o > 0; o >>= 1) lo = fminf(lo, __shfl_xor_sync(0xffffffffu, lo, o));
+                if (lane == 0) s_lo = lo;
+            }
+        }
+    } else {
+        const int gt = tid - GRP;  // thread index inside group B
+        // quantised x: one lane per 32-element sub-block, no shuffles
+        for (int sb = gt; sb < D / 32; sb += GRP) {
+            const float4 *v4 = reinterpret_cast<const float4 *>(xs + sb * 32);
+            float v[32];
+#pragma unroll
+            for (int i = 0; i < 8; i++) {
+                const float4 t = v4[i];
+                v[4 * i] = t.x; v[4 * i + 1] = t.y; v[4 * i + 2] = t.z; v[4 * i + 3] = t.w;
+            }
+            float m = 0.f, xsum = 0.f;
+#pragma unroll
+            for (int i = 0; i < 32; i++) { m = fmaxf(m, fabsf(v[i])); xsum += v[i]; }
+            const float s = m / 32767.0f;
+            uint32_t hw[8], lw[8];
+#pragma unroll
+            for (int q = 0; q < 8; q++) {
+                uint32_t h4 = 0, l4 = 0;
+#pragma unroll
+                for (int i = 0; i < 4; i++) {
+                    const int xi = (m > 0.0f) ? __float2int_rn(v[4 * q + i] / s) : 0;
+                    h4 |= ((uint32_t)(xi >> 8) & 0xFFu) << (8 * i);
+                    l4 |= ((uint32_t)xi & 0xFFu) << (8 * i);
+                }
+                hw[q] = h4;
+                lw[q] = l4;
+            }
+            uint4 *qh4 = reinterpret_cast<uint4 *>(xq + sb * 32), *ql4 = reinterpret_cast<uint4 *>(xq + D + sb * 32);
+            qh4[0] = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+            qh4[1] = make_uint4(hw[4], hw[5], hw[6], hw[7]);
+            ql4[0] = make_uint4(lw[0], lw[1], lw[2], lw[3]);
+            ql4[1] = make_uint4(lw[4], lw[5], lw[6], lw[7]);
+            reinterpret_cast<float *>(xq + 2 * D)[sb] = s;
+            reinterpret_cast<float *>(xq + 2 * D)[D / 32 + sb] = xsum;
+        }
+        asm volatile("bar.sync 2, %0;" ::"r"(GRP) : "memory");
+        FD_MARK_IF(gt == 0, 4)
+        if (a.has_shared) {
+            for (int i = (wid - GRP / 32); i < s1 - s0; i += GRP / 32) {
+                const float h = swiglu_pair(shu + (size_t)i * rb4, shu + (size_t)(P.shp + i) * rb4, xq, D, lane);
+                if (lane == 0) {
+                    ax::put_tagged(a.hll + (size_t)K * H + s0 + i, u_of(h), tag);
+                    ax::count_add(a.sync + 4 + K, 1u);
+                }
+            }
+            FD_MARK_IF(gt == 0, 5)
+        }
+    }
+    __syncthreads();
+    FD_MARK(7)
+    if (s_mode != 0) {
+        // ---- uncertain: the reference's exact chain for the candidates ----
+        // The scratch overlays the routed down slabs and gate/up rows: let the
+        // copies already issued land, and issue the final ones afterwards.
+        if (tid == 0)
+            for (int i = 2; i < nbars; i++)
+                if (!ax::mbar_wait(bars + i, 0, FD_WAIT_NS)) copy_fail = true;
+        __syncthreads();
+        float *wbuf = reinterpret_cast<float *>(dn + sdn);
+        float *val = reinterpret_cast<float *>(dn + sdn + XL_SMEM);
+        int *id = reinterpret_cast<int *>(val + E);
+        float *oval = reinterpret_cast<float *>(id + E);
+        int *oid = reinterpret_cast<int *>(oval + E);
+        int *clist = oid + E;
+        float *cv = reinterpret_cast<float *>(clist + E);
+        int *cid = reinterpret_cast<int *>(cv + E);
+        float *cov = reinterpret_cast<float *>(cid + E);
+        int *coid = reinterpret_cast<int *>(cov + E);
+        int *taken = coid + E;
+        const double lo_min = s_lo;
+        if (tid == 0) { s_nc = 0; s_full = 0; }
+        __syncthreads();
+        // candidates in ascending expert order: experts outside the list
+        // never win a strict comparison of the exchange sort, so sorting the
+        // candidates alone gives the full sort's order
+        for (int e0 = 0; e0 < E; e0 += FD_THREADS) {
+            const int e = e0 + tid;
+            const bool cand = e < E && ((double)Lf[e] + (double)Bf[e] >= lo_min - FD_MARGIN);
+            if (e < E) { val[e] = -INFINITY; id[e] = e; taken[e] = cand; }
+            const unsigned bal = __ballot_sync(0xffffffffu, cand);
+            if (lane == 0) s_wcnt[wid] = __popc(bal);
+            __syncthreads();
+            int off = s_nc;
+            for (int q = 0; q < wid; q++) off += s_wcnt[q];
+            if (cand) clist[off + __popc(bal & ((1u << lane) - 1u))] = e;
+            __syncthreads();
+            if (tid == 0)
+                for (int q = 0; q < FD_WARPS; q++) s_nc += s_wcnt[q];
+            __syncthreads();
+        }
+        const int nc = s_nc;
+        exact_logits_block(a.W, D, xs, clist, nc, cv, wbuf, tid, FD_THREADS);
+        __syncthreads();
+        for (int q = tid; q < nc; q += FD_THREADS) {
+            val[clist[q]] = cv[q];
+            cid[q] = clist[q];
+        }
+        __syncthreads();
+        if (a.routing == OFB_ROUTE_FORWARD) {
+            // probabilities order like expf(l - max) unless two of them are
+            // within a few ulps (then the division could tie them)
+            if (wid == 0) {
+                float m = -INFINITY;
+                for (int q = lane; q < nc; q += 32) m = fmaxf(m, cv[q]);
+#pragma unroll
+                for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+                if (lane == 0) s_max = m;
+            }
+            __syncthreads();
+            for (int q = tid; q < nc; q += FD_THREADS) cv[q] = ofb_exact_expf(__fsub_rn(cv[q], s_max));
+            __syncthreads();
+            for (int q = tid; q < nc; q += FD_THREADS)
+                for (int q2 = 0; q2 < nc; q2++)
+                    if (q2 != q && close_ulps(cv[q], cv[q2], 4)) s_full = 1;
+            __syncthreads();
+            if (s_full) {
+                // every logit exact, softmax as the reference computes it
+                for (int e = tid; e < E; e += FD_THREADS)
+                    val[e] = taken[e] ? val[e] : exact_logit(a.W + (size_t)e * D, xs, D);
+                __syncthreads();
+                if (tid == 0) {
+                    float m = val[0];
+                    for (int e = 1; e < E; e++) if (val[e] > m) m = val[e];
+                    s_max = m;
+                }
+                __syncthreads();
+                for (int e = tid; e < E; e += FD_THREADS) val[e] = ofb_exact_expf(__fsub_rn(val[e], s_max));
+                __syncthreads();
+                if (tid == 0) {
+                    float s = 0.0f;
+                    for (int e = 0; e < E; e++) s = __fadd_rn(s, val[e]);
+                    s_sum = s;
+                }
+                __syncthreads();
+                for (int e = tid; e < E; e += FD_THREADS) val[e] = __fdiv_rn(val[e], s_sum);
+                __syncthreads();
+            }
+        }
+        if (wid == 0) {
+            if (s_full) {
+                for (int i = 0; i < K; i++) exchange_pass(val, id, oval, oid, E, i, lane);
+                if (lane == 0) {
+                    float ssum = 0.0f;
+                    for (int q = 0; q < K; q++) ssum = __fadd_rn(ssum, val[q]);
+                    for (int q = 0; q < K; q++) {
+                        s_top[q] = id[q];
+                        s_w[q] = a.renorm ? __fdiv_rn(val[q], ssum) : val[q];
+                    }
+                    s_mode = 2;
+                }
+            } else {
+                for (int i = 0; i < K; i++) exchange_pass(cv, cid, cov, coid, nc, i, lane);
+                __syncwarp();
+                const int tk = lane < K ? cid[lane] : 0;
+                const float m = Lf[cid[0]];
+                float sum = 0.f;
+                if (a.routing == OFB_ROUTE_FORWARD) {
+                    for (int e = lane; e < E; e += 32) sum += expf(Lf[e] - m);
+                } else if (lane < K) {
+                    sum = expf(Lf[tk] - m);
+                }
+                sum = warp_sum(sum);
+                const float wq = lane < K ? expf(Lf[tk] - m) / sum : 0.f;
+                const float ss = warp_sum(wq);
+                if (lane < K) {
+                    s_top[lane] = tk;
+                    s_w[lane] = (a.routing == OFB_ROUTE_FORWARD && a.renorm) ? wq / ss : wq;
+                }
+            }
+        }
+        // this memory is refilled by bulk copies next
+        ax::fence_proxy_async_smem();
+        __syncthreads();
+        if (tid == 0) {
+            s_par = 1;
+            for (int q = 0; q < K; q++) issue_slot(q, s_top[q]);
+            close_up();
+        }
+        __syncthreads();
+    }
+    if (c == 0 && tid < K) {
+        if (a.idx_out) a.idx_out[tid] = (uint32_t)s_top[tid];
+        if (a.w_out) a.w_out[tid] = s_w[tid];
+        if (tid == 0 && a.stats) atomicAdd(&a.stats[s_mode], 1);
+    }
+    const uint32_t par = s_par;
+    FD_MARK(19)
+
+    // ---- step 3: routed h rows as their gate/up rows land; meanwhile the
+    // upper half of the warps runs the shared expert's down rows (resident
+    // since step 0) and then joins. Pairs are taken from a shared counter. ----
+    if (tid == 0) { s_next[0] = 0; s_next[1] = 0; }
+    __syncthreads();
+    if (a.has_shared && wid >= FD_WARPS / 2) {
+        const int gt = tid - FD_THREADS / 2;
+        const HSlot hs = hslot(hqb, H, K);
+        if (gt == 0 && !ax::wait_count(a.sync + 4 + K, tag * (unsigned)H, FD_WAIT_NS)) tag_fail = true;
+        asm volatile("bar.sync 2, %0;" ::"r"(FD_THREADS / 2) : "memory");
+        for (int g = gt; g < H / 16; g += FD_THREADS / 2) {
+            uint32_t v[16];
+            if (!ax::get_tagged_n<16>(a.hll + (size_t)K * H + 16 * g, tag, v, FD_WAIT_NS)) tag_fail = true;
+            quantize_group(v, hs, g);
+        }
+        asm volatile("bar.sync 2, %0;" ::"r"(FD_THREADS / 2) : "memory");
+        const uint32_t base = ax::smem_u32(dnp(K));
+        for (int t = gt; t < nrow_out * NHB; t += FD_THREADS / 2) {
+            const int r = t / NHB, hb = t - r * NHB;
+            ysp[((size_t)K * rows_cap + r) * NHB + hb] =
+                q6k_half_dot(base + r * rb6 + (hb >> 1) * Q6K_BYTES, hb & 1, hs, hb);
+        }
+        FD_MARK_IF(gt == 0, 25)
+    }
+    {
+        int ncnt[2] = {0, 0};
+        for (int sgi = 0; sgi < 2; sgi++) {
+            const int pa = sgi == 0 ? u0 : max(u0, (slot_first + 1) * H), pb = sgi == 0 ? min(u1, (slot_first + 1) * H) : u1;
+            if (pb <= pa) continue;
+            if (!ax::mbar_wait(mb_up + sgi, par, FD_WAIT_NS)) copy_fail = true;
+            for (;;) {
+                int p = 0;
+                if (lane == 0) p = pa + atomicAdd(&s_next[sgi], 1);
+                p = __shfl_sync(0xffffffffu, p, 0);
+                if (p >= pb) break;
+                const int i = p - u0;
+                const float h = swiglu_pair(upg + (size_t)i * rb4, upu + (size_t)i * rb4, xq, D, lane);
+                if (lane == 0) ax::put_tagged(a.hll + p, u_of(h), tag);
+                ncnt[sgi]++;
+            }
+        }
+        // one fence per warp, then the counts of the h rows it wrote, per slot
+        if (lane == 0 && ncnt[0] + ncnt[1]) {
+            __threadfence();
+            if (ncnt[0]) atomicAdd(a.sync + 4 + slot_first, (unsigned)ncnt[0]);
+            if (ncnt[1]) atomicAdd(a.sync + 4 + slot_first + 1, (unsigned)ncnt[1]);
+        }
+    }
+    FD_MARK(9)
+    // ---- step 4: every routed slot's h, quantised; y of my rows ----
+    // thread k waits for slot k's count (the waits overlap)
+    if (tid < K && !ax::wait_count(a.sync + 4 + tid, tag * (unsigned)H, FD_WAIT_NS)) tag_fail = true;
+    __syncthreads();
+    for (int t = tid; t < K * (H / 16); t += FD_THREADS) {
+        const int k = t / (H / 16), g = t - k * (H / 16);
+        uint32_t v[16];
+        if (!ax::get_tagged_n<16>(a.hll + (size_t)k * H + 16 * g, tag, v, FD_WAIT_NS)) tag_fail = true;
+        quantize_group(v, hslot(hqb, H, k), g);
+    }
+    if (tid == 0) s_gsc = a.use_gate ? f_of(ax::get_tagged(a.cand + 2 * E, tag, FD_WAIT_NS, tag_fail)) : 1.0f;
+    __syncthreads();
+    FD_MARK(11)
+    for (int t = tid; t < K * nrow_out * NHB; t += FD_THREADS) {
+        const int k = t / (nrow_out * NHB), rem = t - k * nrow_out * NHB, r = rem / NHB, hb = rem - r * NHB;
+        if (!ax::mbar_wait(mb_dn + k, par, FD_WAIT_NS)) copy_fail = true;
+        const uint32_t base = ax::smem_u32(dnp(k));
+        ysp[((size_t)k * rows_cap + r) * NHB + hb] =
+            q6k_half_dot(base + r * rb6 + (hb >> 1) * Q6K_BYTES, hb & 1, hslot(hqb, H, k), hb);
+    }
+    __syncthreads();
+    FD_MARK(13)
+    // y per (slot, row): the half-block partials summed in a fixed order,
+    // into the first partial's place
+    for (int t = tid; t < (K + 1) * nrow_out; t += FD_THREADS) {
+        const int k = t / nrow_out, r = t - k * nrow_out;
+        float *pp = ysp + ((size_t)k * rows_cap + r) * NHB;
+        float v = 0.f;
+        for (int hb = 0; hb < NHB; hb++) v += pp[hb];
+        pp[0] = v;
+    }
+    __syncthreads();
+    for (int r = tid; r < nrow_out; r += FD_THREADS) {
+        const int n = n0 + r;
+        float acc = a.resid ? a.resid[n] : 0.f;
+        float yv[16], wv[16];
+#pragma unroll
+        for (int k = 0; k < 16; k++) {
+            yv[k] = k < K ? ysp[((size_t)k * rows_cap + r) * NHB] : 0.f;
+            wv[k] = k < K ? s_w[k] : 0.f;
+        }
+        if (a.has_shared) {
+            const float y = ysp[((size_t)K * rows_cap + r) * NHB];
+            acc += a.use_gate ? s_gsc * y : y;
+        }
+        float rr = 0.f;
+#pragma unroll
+        for (int k = 0; k < 16; k++)
+            if (k < K && !(wv[k] < 1e-6f)) rr += wv[k] * yv[k];  // model.c:1066 skip rule
+        a.out[n] = acc + rr;
+    }
+    FD_MARK(14)
+
+    // ---- exit: errors, copies in flight, epoch ----
+    if (copy_fail || tag_fail) atomicOr(&s_err, (copy_fail ? FD_ERR_COPY : 0u) | (tag_fail ? FD_ERR_TAG : 0u));
+    __syncthreads();
+    if (tid == 0) {
+        if (s_err) {
+            atomicOr(&a.sync[2], s_err);
+            // let every copy this CTA issued land before its shared memory goes
+            for (int i = 0; i < nbars; i++) ax::mbar_wait(bars + i, i < 2 ? 0 : par, FD_WAIT_NS);
+        }
+        __threadfence();
+        if (atomicAdd(&a.sync[1], 1u) == (unsigned)G - 1) {
+            a.sync[1] = 0;
+            // every CTA is done: set the exchange counters to their exact
+            // values for this epoch (repairs them after an expired wait)
+            a.sync[3] = tag * (unsigned)E;
+            for (int k = 0; k <= K; k++) a.sync[4 + k] = tag * (unsigned)H;
+            __threadfence();
+            atomicAdd(&a.sync[0], 1u);
+        }
+    }
+    FD_MARK(15)
+}
+
+// ---- host ----------------------------------------------------------------------
+#ifdef OFB_FD_TRACE
+extern "C" int ofb_debug_fd_trace(unsigned long long *host) {
+    return cudaMemcpyFromSymbol(host, g_fd_tr, sizeof(g_fd_tr)) == cudaSuccess ? 0 : 1;
+}
+#endif
+
+static int gcd_i(int a, int b) { return b ? gcd_i(b, a % b) : a; }
+
+bool fused_plan(const ofb_moe_config *cfg, bool use_gate, int G, FusedPlan &p) {
+    const int D = cfg->d_model, H = cfg->hidden, E = cfg->n_experts, K = cfg->top_k;
+    if (E > 32 * FD_PER_LANE || K > 16 || K > E || G < 1) return false;
+    const int nrows = E + (use_gate ? 1 : 0);
+    p.G = G;
+    p.rmax = (nrows + G - 1) / G;
+    const int tpr = D % 1024 == 0 ? 256 : D / 4;
+    if (tpr > FD_THREADS || p.rmax > FD_THREADS / tpr) return false;
+    const int nbk = H / QK, rb4 = (D / QK) * Q4K_BYTES, rb6 = nbk * Q6K_BYTES;
+    // output rows per group: 16-byte aligned Q6_K slabs (dg * rb6 % 16 == 0)
+    int dg = 8 / gcd_i(nbk, 8);
+    if (dg < 4) dg = 4;
+    if (D % dg) return false;
+    p.dg = dg;
+    p.shp = (H + G - 1) / G;
+    p.upc = (K * H + G - 1) / G;
+    if (p.upc > H) return false;  // a CTA's gate/up pairs span at most two slots
+    p.ngc = (D / dg + G - 1) / G;
+    const int rows_cap = p.ngc * dg, nhb = H / 128;
+    size_t off = 0;
+    auto take = [&](size_t bytes) { size_t o = off; off = (off + bytes + 127) & ~(size_t)127; return (uint32_t)o; };
+    p.o_x = take((size_t)D * 4);
+    p.o_xq = take(xq_stride(D));
+    p.o_rr = take((size_t)p.rmax * D * 4);
+    p.o_shu = take((size_t)2 * p.shp * rb4);
+    // down slabs (shared expert first, then the routed slots) directly
+    // followed by the routed gate/up rows: the selection's exact-recompute
+    // scratch overlays the routed part of both
+    const size_t sdn = (size_t)rows_cap * rb6;
+    p.o_dn = take((size_t)(K + 1) * sdn);
+    // (the router rows' partial sums use the gate/up area before it is filled)
+    const size_t up = std::max((size_t)2 * p.upc * rb4, (size_t)p.rmax * tpr * 24);
+    p.o_up = take(up);
+    const size_t fb = (size_t)XL_SMEM + (size_t)11 * E * 4;
+    if ((size_t)p.o_up + up - ((size_t)p.o_dn + sdn) < fb) {
+        off = (size_t)p.o_dn + sdn + fb;
+        off = (off + 127) & ~(size_t)127;
+    }
+    p.o_hq = take((size_t)(K + 1) * (2 * H + H / 2));
+    p.o_sel = take((size_t)2 * E * 4);
+    p.o_ys = take((size_t)(K + 1) * rows_cap * nhb * 4);
+    p.o_bar = take((size_t)(4 + K) * 8);
+    p.total = (uint32_t)off;
+    return p.total <= 227 * 1024;
+}
+
+int launch_decode_fused(const ofb_moe_config *cfg, const ofb_moe_weights *wt, const float *x, const float *resid,
+                        float *out, uint32_t *idx_out, float *w_out, const FusedPlan &plan,
+                        unsigned long long *cand, unsigned long long *hll, unsigned int *sync, int *stats,
+                        cudaStream_t s) {
+    FusedDecodeArgs a;
+    a.W = wt->router; a.x = x; a.gate_v = wt->shexp_gate; a.resid = resid; a.out = out;
+    a.gate = (const uint8_t *)wt->gate_exps; a.up = (const uint8_t *)wt->up_exps;
+    a.down = (const uint8_t *)wt->down_exps;
+    a.gate_sh = (const uint8_t *)wt->gate_shexp; a.up_sh = (const uint8_t *)wt->up_shexp;
+    a.down_sh = (const uint8_t *)wt->down_shexp;
+    a.D = cfg->d_model; a.H = cfg->hidden; a.E = cfg->n_experts; a.K = cfg->top_k;
+    a.routing = cfg->routing; a.renorm = cfg->renorm;
+    a.has_shared = wt->gate_shexp && wt->up_shexp && wt->down_shexp;
+    a.use_gate = a.has_shared && cfg->shared_gate && wt->shexp_gate;
+    const double u = 0x1.0p-24, n = (double)cfg->d_model;
+    a.bound_scale = (1.0 + 0x1.0p-9) * u;
+    a.ngam = n * (n * u / (1.0 - n * u));
+    a.cand = cand; a.hll = hll; a.sync = sync;
+    a.idx_out = idx_out; a.w_out = w_out; a.stats = stats;
+    a.p = plan;
+    static size_t attr[64];
+    cudaError_t e = ensure_dyn_smem(decode_fused_kernel, plan.total, attr);
+    if (e != cudaSuccess) return cuda_status(e, "decode_fused smem attribute");
+    e = launch_pdl(decode_fused_kernel, dim3(plan.G), dim3(FD_THREADS), plan.total, s, a);
+    return e == cudaSuccess ? OFB_OK : cuda_status(e, "decode_fused launch");
+}
+
+}  // namespace ofb

@@ -150,6 +150,11 @@ WorkspaceLayout workspace_layout(const ofb_moe_config *c, int max_tokens) {
     const size_t A = T * K + T;  // routed + shared assignments
     size_t off = 0;
     auto take = [&](size_t bytes) { size_t o = off; off = align_up(off + bytes, 256); return o; };
+    // single-launch decode words first (their size depends on the shape only)
+    L.fsync = take((5 + 16) * 4);
+    L.fcand = take((2 * E + 1) * 8);
+    L.fh = take((K + 1) * (size_t)c->hidden * 8);
+    L.fused_bytes = off;
     L.logits = take(T * E * 4);
     L.idx = take(T * K * 4);
     L.w = take(T * K * 4);
@@ -226,6 +231,22 @@ int run_moe_layer(const ofb_moe_config *cfg, const ofb_moe_weights *wt, const fl
     p.slot_start = (int *)(base + L.slot_start);
     p.assign = (int *)(base + L.assign);
     int st;
+    if (T == 1 && !given_idx && wt->router && cfg->layout == OFB_LAYOUT_CONTIGUOUS) {
+        // decode batch 1: the whole layer in one launch when the shape fits
+        const bool has_sh = wt->gate_shexp && wt->up_shexp && wt->down_shexp;
+        const bool use_gate = has_sh && cfg->shared_gate && wt->shexp_gate;
+        FusedPlan fp;
+        if ((!use_gate || !(reinterpret_cast<uintptr_t>(wt->shexp_gate) & 15)) &&
+            fused_plan(cfg, use_gate, sm_count(), fp)) {
+            int *ctr = (int *)(base + L.counters);
+            st = launch_decode_fused(cfg, wt, x, resid, out, idx_out, w_out, fp,
+                                     (unsigned long long *)(base + L.fcand), (unsigned long long *)(base + L.fh),
+                                     (unsigned int *)(base + L.fsync), ctr + FAST_ROUTE_MAX_T + 1, s);
+            if (st) return st;
+            for (int i = 1; i <= 4; i++) mark(i);
+            return OFB_OK;
+        }
+    }
     const bool fast = !given_idx && wt->router && cfg->layout == OFB_LAYOUT_CONTIGUOUS && T <= FAST_ROUTE_MAX_T;
     if (fast) {
         // one launch: certified routing, shared-expert gates, dispatch plan
@@ -353,8 +374,10 @@ extern "C" int ofb_workspace_create(const ofb_moe_config *cfg, int max_tokens, o
     w->layout = workspace_layout(cfg, max_tokens);
     cudaError_t e = cudaMalloc((void **)&w->base, w->layout.total);
     if (e != cudaSuccess) { free(w); return cuda_status(e, "workspace cudaMalloc"); }
-    // routing tickets must start at zero (each call leaves them at zero)
+    // routing tickets must start at zero (each call leaves them at zero); the
+    // single-launch decode's epoch and tagged words start at zero once
     e = cudaMemset(w->base + w->layout.counters, 0, w->layout.counters_bytes);
+    if (e == cudaSuccess) e = cudaMemset(w->base, 0, w->layout.fused_bytes);
     if (e == cudaSuccess) e = cudaDeviceSynchronize();
     if (e != cudaSuccess) { cudaFree(w->base); free(w); return cuda_status(e, "workspace init"); }
     *ws = w;
@@ -567,4 +590,21 @@ extern "C" int ofb_workspace_route_stats(ofb_workspace *ws, int counts[3]) {
     cudaError_t e = cudaMemcpy(counts, ws->base + ws->layout.counters + (FAST_ROUTE_MAX_T + 1) * 4,
                                3 * sizeof(int), cudaMemcpyDeviceToHost);
     return e == cudaSuccess ? OFB_OK : cuda_status(e, "route_stats copy");
+}
+
+extern "C" int ofb_workspace_device_errors(ofb_workspace *ws, unsigned *bits) {
+    if (!ws || !bits) { set_error("device_errors: NULL argument"); return OFB_EINVAL; }
+    const WorkspaceLayout &L = ws->layout;
+    const int D = ws->cfg.d_model;
+    unsigned fused = 0;
+    int prefill = 0;
+    unsigned *fw = (unsigned *)(ws->base + L.fsync) + 2;
+    int *pf = (int *)(ws->base + L.counters) + FAST_ROUTE_MAX_T + 4 + D / DOWN_TICKET_ROWS;
+    cudaError_t e = cudaMemcpy(&fused, fw, sizeof(fused), cudaMemcpyDeviceToHost);
+    if (e == cudaSuccess) e = cudaMemcpy(&prefill, pf, sizeof(prefill), cudaMemcpyDeviceToHost);
+    if (e == cudaSuccess) e = cudaMemset(fw, 0, sizeof(unsigned));
+    if (e == cudaSuccess) e = cudaMemset(pf, 0, sizeof(int));
+    if (e != cudaSuccess) return cuda_status(e, "device_errors copy");
+    *bits = (fused & 3u) | (prefill ? 4u : 0u);
+    return OFB_OK;
 }

@@ -34,6 +34,11 @@ struct LayerArgs {
 
 // Byte offsets of the scratch regions inside one workspace allocation.
 struct WorkspaceLayout {
+    // single-launch decode (T = 1): epoch / finished / error words, tagged
+    // (L~, B) per expert + shared gate, tagged h per top-k slot + shared
+    // expert. First in the workspace at a size that depends only on the layer
+    // shape, so a fixed scratch keeps it in place across calls of any size.
+    size_t fsync, fcand, fh, fused_bytes;
     size_t logits, idx, w, gsc, n_slots, slot_expert, slot_start, assign, h, y;
     size_t cand;      // fast routing: (approximate logit, bound) per (token, row)
     size_t norms;     // large-batch routing: segment norms of x rows and router rows
@@ -90,6 +95,18 @@ int launch_route_fast(const float *W, const float *x, const float *gate_v, int T
 // Quantised activations of one token: int8 xh[D], uint8 xl[D], then per
 // 32-element sub-block the f32 scale s and the f32 sum of x.
 __host__ __device__ inline size_t xq_stride(int D) { return (size_t)2 * D + (size_t)8 * (D / 32); }
+
+// Shared-memory plan of the single-launch decode kernel (decode_fused.cu):
+// per-CTA share sizes and region offsets, identical on host and device.
+struct FusedPlan {
+    int G, rmax, shp, upc, ngc, dg;
+    uint32_t o_x, o_xq, o_rr, o_shu, o_dn, o_up, o_hq, o_sel, o_ys, o_bar, total;
+};
+bool fused_plan(const ofb_moe_config *cfg, bool use_gate, int grid, FusedPlan &p);
+int launch_decode_fused(const ofb_moe_config *cfg, const ofb_moe_weights *wt, const float *x, const float *resid,
+                        float *out, uint32_t *idx_out, float *w_out, const FusedPlan &plan,
+                        unsigned long long *cand, unsigned long long *hll, unsigned int *sync, int *stats,
+                        cudaStream_t s);
 
 WorkspaceLayout workspace_layout(const ofb_moe_config *c, int max_tokens);
 int check_config(const ofb_moe_config *c);

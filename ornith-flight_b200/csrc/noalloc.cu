@@ -69,6 +69,11 @@ int scratch_for_current_device(uint8_t **out) {
         void *p = nullptr;
         e = cudaGetSymbolAddress(&p, ofb_noalloc_scratch);
         if (e != cudaSuccess || !p) return ofb::cuda_status(e, "noalloc: cudaGetSymbolAddress");
+        // the single-launch decode keeps an epoch and tagged words at the
+        // start of the scratch across calls: they start from zero once
+        e = cudaMemset(p, 0, OFB_NOALLOC_SCRATCH_BYTES);
+        if (e == cudaSuccess) e = cudaDeviceSynchronize();
+        if (e != cudaSuccess) return ofb::cuda_status(e, "noalloc: scratch set-up");
         g_scratch_ptr[dev] = static_cast<uint8_t *>(p);
         g_scratch_ctx[dev] = ctx;
     }

@@ -68,6 +68,7 @@ def _load() -> ctypes.CDLL:
         "ofb_moe_forward": (i32, [cfgp, wp, vp, vp, vp, i32, vp, vp, vp, vp]),
         "ofb_moe_forward_profiled": (i32, [cfgp, wp, vp, vp, vp, i32, vp, vp, vp]),
         "ofb_workspace_route_stats": (i32, [vp, ctypes.POINTER(ctypes.c_int * 3)]),
+        "ofb_workspace_device_errors": (i32, [vp, ctypes.POINTER(ctypes.c_uint)]),
         "ofb_moe_forward_noalloc": (i32, [cfgp, wp, vp, vp, vp, i32, vp, vp, vp]),
         "ofb_noalloc_capacity": (sz, []),
         "ofb_synth_blocks": (i32, [vp, i32, u64, u64, u64, u64, vp]),
@@ -93,7 +94,8 @@ lib = _load()
 EXPORTED = [
     "ofb_status_string", "ofb_last_error", "ofb_build_info", "ofb_dequantize",
     "ofb_dequantize_expert_slice", "ofb_route", "ofb_workspace_size", "ofb_workspace_create",
-    "ofb_workspace_destroy", "ofb_moe_forward", "ofb_moe_forward_profiled", "ofb_workspace_route_stats", "ofb_synth_blocks", "ofb_synth_blocks_host",
+    "ofb_workspace_destroy", "ofb_moe_forward", "ofb_moe_forward_profiled", "ofb_workspace_route_stats",
+    "ofb_workspace_device_errors", "ofb_synth_blocks", "ofb_synth_blocks_host",
     "ofb_synth_normal_host",
 ]
 
@@ -305,6 +307,12 @@ class Workspace:
         c = (ctypes.c_int * 3)()
         _check(lib.ofb_workspace_route_stats(self.handle, ctypes.byref(c)))
         return tuple(c)
+
+    def device_errors(self) -> int:
+        """Bits of device-side wait expiries since the last call (0: none)."""
+        b = ctypes.c_uint()
+        _check(lib.ofb_workspace_device_errors(self.handle, ctypes.byref(b)))
+        return b.value
 
     def close(self):
         if self.handle:
