@@ -592,7 +592,9 @@ def describe(args, world, workload, m, steps, warmup, n_layers):
         if T == 1:
             # decode batch 1 runs as one launch (decode_fused_kernel): the
             # dominant kernel is the whole layer
-            kname, kbytes, kms = "decode_fused_kernel (whole layer, one launch)", layer_bytes, sum(phase)
+            # dominant kernel is the whole layer; its average launch duration is
+            # the timed region's device time / K (one launch per step)
+            kname, kbytes, kms = "decode_fused_kernel (whole layer, one launch)", layer_bytes, step_ms
         else:
             # the chained decode kernels: report the one with the largest share
             cands = [("route_rows_kernel + route_select_fast (router rows)", E * D * 4 + T * D * 4, phase[0]),
