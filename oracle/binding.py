@@ -166,12 +166,14 @@ def synth_normal(n: int, seed: int, stream_id: int, sigma: float) -> np.ndarray:
 
 
 def make_layer_host(d_model=2048, hidden=512, n_experts=256, layout=LAYOUT_CONTIGUOUS, seed=0,
-                    shared=True) -> dict:
+                    shared=True, router_bias=None) -> dict:
     """The bytes of the library's make_layer(shape, seed) as numpy arrays
     (router laid out per `layout`: [E][D] contiguous, [D][E] interleaved)."""
     nb = hidden * d_model // 256
     E, D = n_experts, d_model
     r = synth_normal(E * D, seed, STREAM_ROUTER, 0.02).reshape(E, D)
+    if router_bias is not None:
+        r[:, 0] = np.asarray(router_bias, dtype=np.float32)
     if layout == LAYOUT_INTERLEAVED:
         r = np.ascontiguousarray(r.T)
     w = dict(router=r.reshape(-1),
@@ -189,3 +191,25 @@ def make_layer_host(d_model=2048, hidden=512, n_experts=256, layout=LAYOUT_CONTI
 
 def make_tokens_host(d_model: int, n_tokens: int, seed: int) -> np.ndarray:
     return synth_normal(n_tokens * d_model, seed, STREAM_X, 1.0).reshape(n_tokens, d_model)
+
+
+def _chunk_worker(args):
+    cfg, seed, bias, x = args
+    w = make_layer_host(cfg["d_model"], cfg["hidden"], cfg["n_experts"], cfg["layout"], seed,
+                        router_bias=bias)
+    return moe_forward(cfg, w, x)
+
+
+def moe_forward_seeded_parallel(cfg: dict, seed: int, x: np.ndarray, router_bias=None, procs=None,
+                                chunk=128):
+    """moe_forward over the seeded synthetic layer make_layer_host(seed) for
+    many tokens, split into token chunks run by a pool of processes (each
+    builds the layer itself). The layer is per token, so the result equals
+    one call over all tokens."""
+    import multiprocessing as mp
+    procs = procs or min(32, os.cpu_count() or 1)
+    jobs = [(cfg, seed, router_bias, x[i:i + chunk]) for i in range(0, x.shape[0], chunk)]
+    with mp.get_context("spawn").Pool(min(procs, len(jobs))) as pool:
+        res = pool.map(_chunk_worker, jobs)
+    return (np.concatenate([r[0] for r in res]), np.concatenate([r[1] for r in res]),
+            np.concatenate([r[2] for r in res]))

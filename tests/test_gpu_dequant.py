@@ -80,3 +80,50 @@ def test_empty_input_is_a_noop(ofb, cuda):
     ofb.dequantize(blocks, 12, 0, out=out)
     torch.cuda.synchronize()
     assert torch.all(out == 7.0)
+
+
+def test_f16_every_bit_pattern(ofb, oracle, cuda):
+    # gguf_dequantize_tensor_from_buf's F16 branch (engine/src/gguf.c:605-638)
+    # uses the reference's non-IEEE fp16 rule (gguf.c:16-26): only 0x0000 maps
+    # to zero; -0, subnormals and exponent-31 patterns decode as if normal.
+    # All 65,536 patterns, as f32 bits and as bf16 (RNE of the f32 value).
+    pats = np.arange(65536, dtype=np.uint16)
+    dev = torch.from_numpy(pats.view(np.uint8).copy()).to(cuda)
+    got = ofb.dequantize(dev, ofb.TYPE_F16, 65536).cpu().numpy()
+    want = oracle.dequant(pats.view(np.uint8), ofb.TYPE_F16, 65536)
+    assert np.array_equal(got.view(np.uint32), want.view(np.uint32))
+    for p in (0x8000, 0x0001, 0x03FF, 0x7C00, 0xFC00, 0x7FFF):  # the rebias edge cases
+        assert np.isfinite(want[p]) and want[p] != 0.0, hex(p)
+    got16 = ofb.dequantize(dev, ofb.TYPE_F16, 65536, out_dtype=torch.bfloat16).cpu().view(torch.int16).numpy()
+    assert np.array_equal(got16.view(np.uint16), bf16_rne_bits(want))
+
+
+def test_f32_copies_bits(ofb, oracle, cuda):
+    # F32 branch: a bit copy (NaN payloads, infinities and -0 included); to
+    # bf16 it rounds to nearest even like torch (checked on finite values)
+    rng = np.random.default_rng(3)
+    bits = rng.integers(0, 2**32, size=4096, dtype=np.uint64).astype(np.uint32)
+    bits[:6] = [0x80000000, 0x7F800000, 0xFF800000, 0x7FC00001, 0x00000001, 0x3F800000]
+    dev = torch.from_numpy(bits.view(np.uint8).copy()).to(cuda)
+    got = ofb.dequantize(dev, ofb.TYPE_F32, 4096).cpu().numpy()
+    want = oracle.dequant(bits.view(np.uint8), ofb.TYPE_F32, 4096)
+    assert np.array_equal(got.view(np.uint32), want.view(np.uint32))
+    finite = np.isfinite(want)
+    got16 = ofb.dequantize(dev, ofb.TYPE_F32, 4096, out_dtype=torch.bfloat16).cpu().view(torch.int16).numpy()
+    assert np.array_equal(got16.view(np.uint16)[finite], bf16_rne_bits(want)[finite])
+
+
+@pytest.mark.parametrize("qtype", [0, 1])
+def test_plain_type_slices(ofb, oracle, cuda, qtype):
+    # expert slices of F32 / F16 tensors (gguf.c:652-711 handles every type)
+    ne, per = 5, 300
+    rng = np.random.default_rng(qtype)
+    if qtype == 0:
+        raw = rng.normal(size=ne * per).astype(np.float32).view(np.uint8)
+    else:
+        raw = rng.integers(0, 65536, size=ne * per, dtype=np.uint32).astype(np.uint16).view(np.uint8)
+    dev = torch.from_numpy(raw.copy()).to(cuda)
+    for e in range(ne):
+        got = ofb.dequantize_slice(dev, qtype, ne * per, ne, e).cpu().numpy()
+        want = oracle.dequant_slice(raw, qtype, ne * per, ne, e)
+        assert np.array_equal(got.view(np.uint32), want.view(np.uint32)), e

@@ -151,3 +151,24 @@ def test_full_size_prefill_4096(ofb, oracle, cuda):
     assert np.array_equal(idx.cpu().numpy()[sample].view(np.uint32), oi)
     err = rel_err(out[sample], want)
     assert err <= TOL_BF16, f"relative error {err}"
+
+
+def test_full_size_prefill_4096_every_token(ofb, oracle, cuda):
+    # BASELINE config 3 with all 4096 tokens compared: the oracle runs in
+    # token chunks on a process pool (each worker builds the same seeded
+    # layer on the host); indices bit-exact, outputs within the bf16
+    # tensor-core tolerance per token
+    shape = ofb.LayerShape()
+    T = 4096
+    bias = ofb.zipf_bias(256, 7)
+    lw = ofb.make_layer(shape, seed=7, device=cuda, router_bias=bias)
+    x = ofb.make_tokens(shape, T, seed=8, bias_coordinate=True)
+    layer = ofb.MoeLayer(shape, lw, max_tokens=T)
+    idx = torch.empty(T, 8, dtype=torch.int32, device=cuda)
+    out = layer.forward(x.to(cuda), idx=idx).cpu().numpy()
+    del layer, lw
+    cfg = dict(d_model=2048, hidden=512, n_experts=256, top_k=8, layout=0, routing=0, renorm=1, shared_gate=1)
+    want, oi, _ = oracle.moe_forward_seeded_parallel(cfg, 7, x.numpy(), router_bias=bias.numpy())
+    assert np.array_equal(idx.cpu().numpy().view(np.uint32), oi)
+    err = rel_err(out, want)
+    assert err <= TOL_BF16, f"relative error {err}"

@@ -47,3 +47,23 @@ def test_noalloc_rejects_oversized_calls(ofb, cuda):
     with pytest.raises(ofb.OfbError) as ei:
         layer.forward_noalloc(x)
     assert ei.value.status == ofb.ETOOLARGE
+
+
+def test_noalloc_tensor_core_batch_against_oracle(ofb, oracle, cuda):
+    # 40 tokens take the tensor-core (bf16) branch and still fit the fixed
+    # scratch: checked against the CPU oracle at that path's tolerance (2e-2)
+    # on two calls in a row, routing indices bit-exact
+    shape = ofb.LayerShape()
+    T = 40
+    lw = ofb.make_layer(shape, seed=43, device=cuda)
+    layer = ofb.MoeLayer(shape, lw, max_tokens=1)
+    cfg = dict(d_model=2048, hidden=512, n_experts=256, top_k=8, layout=0, routing=0, renorm=1, shared_gate=1)
+    wd = {k: (None if v is None else v.cpu().numpy()) for k, v in vars(lw).items()}
+    for call in range(2):
+        x = ofb.make_tokens(shape, T, seed=300 + call)
+        idx = torch.empty(T, shape.top_k, dtype=torch.int32, device=cuda)
+        got = layer.forward_noalloc(x.to(cuda), idx=idx).cpu().numpy()
+        want, oi, _ = oracle.moe_forward(cfg, wd, x.numpy())
+        assert np.array_equal(idx.cpu().numpy().view(np.uint32), oi), f"call {call}: routing differs"
+        err = (np.abs(got - want).max(axis=1) / np.abs(want).max(axis=1)).max()
+        assert err <= 2e-2, f"call {call}: relative error {err}"
