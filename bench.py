@@ -50,9 +50,9 @@ WORKLOADS = {
                         config="BASELINE config 3: 4096-token prefill, Zipf(1.1)-skewed routing",
                         launches=7, metric="MoE-layer tokens/s (4096-token prefill)"),
     "stack40": dict(tokens=256, layers=40, bound="hbm", ep=True,
-                    dtype="bf16 tensor-core / f32 dp4a experts (fp32 accumulate), f32 rows exchanged",
+                    dtype="bf16 tensor-core / f32 dp4a experts (fp32 accumulate); rows sent bf16, results f32",
                     config="BASELINE config 4: 40-layer MoE stack, batch 256, experts sharded over the GPUs, "
-                           "NCCL all-to-all dispatch/combine",
+                           "device-side dispatch/combine over NVLink",
                     metric="MoE-stack tokens/s (40 layers, batch 256, expert parallel)"),
 }
 D, H, E, K = 2048, 512, 256, 8
@@ -308,16 +308,19 @@ def load_ep():
     return mod
 
 
-def layer_launches(rows: int, tokens: int) -> int:
-    """Kernels of this library one expert-parallel layer launches (the
-    dispatch logic of moe.cu: <= 32 rows take the dp4a decode kernels, more
-    the tensor-core prefill kernels)."""
-    def grouped(n):  # plan + expert kernels of one run_moe_layer with given routing
-        return 1 + (3 if n <= 32 else 4)  # plan; quantize, up, down | gather, tiles, up, down
-    route = 2  # router logits, select
-    experts = (1 + grouped(rows)) if rows else 0  # unpack + grouped
-    shared = 1 + grouped(tokens)  # gate (or fill) + grouped
-    return route + 2 + experts + shared + 1 + 1  # + plan, pack, combine, rmsnorm
+def layer_launches(rows: int, tokens: int, world: int) -> int:
+    """Kernels of this library one layer of the stack launches (rmsnorm
+    included; the dispatch logic of moe.cu: <= 32 rows take the dp4a decode
+    kernels, more the tensor-core prefill kernels)."""
+    if world == 1:
+        # whole layer: routing (2 certified kernels at <= 64 tokens, else 4),
+        # plan + 4 tensor-core kernels, or the 2 decode kernels
+        route = 2 if tokens <= 64 else 4
+        return 1 + route + (2 if tokens <= 32 else 1 + 4)
+    route = 2 if tokens <= 64 else 4
+    shared = 1 + (3 if tokens <= 32 else 4) + 1  # gate, plan + expert kernels
+    experts = 1 + 1 + 4  # unpack, plan, gather/tiles/up/down (padded rows > 32)
+    return 1 + route + 1 + 1 + shared + 1 + experts + 1 + 1  # rmsnorm .. plan, dispatch, receive, return, combine
 
 
 def measure_stack(args, ofb, dev, rank, world, local_rank, steps, warmup):
@@ -344,6 +347,9 @@ def measure_stack(args, ofb, dev, rank, world, local_rank, steps, warmup):
 
 
 def _measure_stack(ofb, ep, dev, rank, world, steps, warmup):
+    """One rank: the whole layers (no exchange). Several ranks: EPGroup /
+    EPLayerP2P, the device-side exchange over NVLink (no host sync)."""
+    import ctypes
     import torch
     import torch.distributed as dist
     wl = WORKLOADS["stack40"]
@@ -352,15 +358,18 @@ def _measure_stack(ofb, ep, dev, rank, world, steps, warmup):
     if E % world or T % world:
         raise SystemExit(f"stack40 needs the world size to divide {E} experts and {T} tokens")
     epr, tpr = E // world, T // world
-    ops = ep.EPOps(shape, world, tpr)
-    layers = [ep.EPLayer(shape, ofb.make_layer_slice(shape, 5000 + l, rank * epr, (rank + 1) * epr, device=dev),
-                         ops, tpr, dev) for l in range(L)]
-    stack = ep.EPStack(layers, ops, tpr, dev)
+    if world == 1:
+        layers = [ep.LocalLayer(shape, ofb.make_layer(shape, 5000 + l, device=dev), tpr) for l in range(L)]
+        group = None
+    else:
+        group = ep.EPGroup(shape, tpr, dev)
+        layers = [ep.EPLayerP2P(shape, ofb.make_layer_slice(shape, 5000 + l, rank * epr, (rank + 1) * epr,
+                                                             device=dev), group) for l in range(L)]
+    stack = ep.EPStack(layers, None, tpr, dev)
     x = ofb.make_tokens(shape, T, seed=99)[rank * tpr:(rank + 1) * tpr].contiguous().to(dev)
     stream = torch.cuda.current_stream()
     for _ in range(warmup):
         stack.forward(x)
-    rows = [sum(l.last_counts[1]) for l in layers]  # rows each layer's experts received here
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
@@ -390,23 +399,38 @@ def _measure_stack(ofb, ep, dev, rank, world, steps, warmup):
     te = torch.tensor([e0.elapsed_time(e1)], device=dev)
     if world > 1:
         dist.all_reduce(te, op=dist.ReduceOp.MAX)
-    # experts this rank's slice had rows for, per layer (for the HBM bytes)
-    touched = []
-    for l in layers:
-        idx = l.idx[:tpr]
-        touched.append(idx)
-    all_idx = torch.cat([i.reshape(-1) for i in touched]).to(torch.int64)
+    errors = group.device_errors() if group else 0
+    # the experts each layer routed to, for the HBM bytes: one untimed pass
+    # that also routes every layer's normalised input (full router)
+    ws = ofb.Workspace(shape, tpr)
+    cfg = shape.config()
+    idx = torch.empty(tpr, K, dtype=torch.int32, device=dev)
+    wts = torch.empty(tpr, K, dtype=torch.float32, device=dev)
+    xn = torch.empty_like(x)
+    cur, per_layer = x, []
+    for lay in layers:
+        ofb._check(ofb.lib.ofb_rmsnorm(ofb._ptr(cur), tpr, D, ctypes.c_float(1e-6), ofb._ptr(xn), ofb._stream()))
+        w = lay.weights if hasattr(lay, "weights") else lay.layer.weights
+        ofb._check(ofb.lib.ofb_route_certified(ctypes.byref(cfg), ofb._ptr(w.router), ofb._ptr(xn), tpr,
+                                               ofb._ptr(idx), ofb._ptr(wts), ws.handle, ofb._stream()))
+        per_layer.append(idx.clone().reshape(-1).to(torch.int64))
+        nxt = torch.empty_like(cur)
+        lay.forward(xn, cur, nxt)
+        cur = nxt
+    all_idx = torch.stack(per_layer)  # [L][tpr*K]
     if world > 1:
         g = [torch.empty_like(all_idx) for _ in range(world)]
         dist.all_gather(g, all_idx)
-        all_idx = torch.cat(g)
-    per_layer = all_idx.view(world, L, tpr * K).permute(1, 0, 2).reshape(L, -1)
-    local = [((pl // epr) == rank) for pl in per_layer]
-    n_local = [len(set(pl[m].tolist())) for pl, m in zip(per_layer, local)]
-    launches = sum(layer_launches(r, tpr) for r in rows)
+        all_idx = torch.cat(g, dim=1)
+    n_local = [len(set(row[(row // epr) == rank].tolist())) for row in all_idx]
+    rows = [int(((row // epr) == rank).sum().item()) for row in all_idx]
+    launches = sum(layer_launches(r, tpr, world) for r in rows)
     del layers, stack
+    if group:
+        group.close()
     torch.cuda.empty_cache()
-    return dict(T=T, ms=ms, e2e_ms=float(te.item()), n_local=n_local, rows=rows, launches=launches)
+    return dict(T=T, ms=ms, e2e_ms=float(te.item()), n_local=n_local, rows=rows, launches=launches,
+                device_errors=errors)
 
 
 def describe_stack(world, m, steps, warmup):
@@ -418,7 +442,8 @@ def describe_stack(world, m, steps, warmup):
     # router, shared expert and gate vector, of every layer
     gpu_bytes = sum(n * EXPERT_BYTES + EXPERT_BYTES + E * D * 4 + D * 4 for n in m["n_local"])
     achieved = gpu_bytes / (step_ms * 1e-3) / 1e9
-    nvlink = L * 2 * (T // world) * K * D * 4 * (world - 1) / world  # rows out and back, per GPU
+    # rows out (bf16 on the tensor-core receive path) and results back (f32), per GPU
+    nvlink = L * (T // world) * K * D * (2 + 4) * (world - 1) / world
     return {
         "metric": wl["metric"], "value": T * steps / (m["ms"] / 1e3), "unit": "tokens/s",
         "n_gpus": world, "steps": steps, "warmup": warmup, "ms_per_step": step_ms,
@@ -427,6 +452,9 @@ def describe_stack(world, m, steps, warmup):
         "config": {"workload": "stack40", "desc": wl["config"], "tokens_per_step": T, "layers": L,
                    "d_model": D, "hidden": H, "n_experts": E, "top_k": K, "experts_per_gpu": E // world,
                    "tokens_per_gpu": T // world, "between_layers": "unit-weight RMSNorm, residual add",
+                   "exchange": "none (one rank holds every expert)" if world == 1 else
+                               "device-side peer stores over NVLink with epoch-tagged flags (ofb_ep_layer_forward), "
+                               "no host sync",
                    "l2": f"{L} distinct layers per step ({L * 522 // world} MB of experts per GPU) > 126 MB L2",
                    "parallelism": f"ep{world}"},
         "roofline": {"bound": "hbm", "kernel": "whole stack step (per GPU)", "achieved": achieved, "peak": peak,
@@ -437,6 +465,7 @@ def describe_stack(world, m, steps, warmup):
         "e2e": {"value": T * steps / (m["e2e_ms"] / 1e3), "unit": "tokens/s",
                 "h2d_bytes_per_step": (T // world) * D * 4, "d2h_bytes_per_step": (T // world) * D * 4},
         "gpu_launches": m["launches"] * steps,
+        "device_errors": m.get("device_errors", 0),
     }
 
 

@@ -249,6 +249,44 @@ int ofb_ep_combine(const float *y_back, const int32_t *slot_of_assignment, int n
  * with every per-channel weight 1). out may alias x. */
 int ofb_rmsnorm(const float *x, int n_tokens, int d_model, float eps, float *out, void *stream);
 
+/* ---- expert parallelism with device-side exchange over NVLink -------------
+ * One call per layer, no host synchronisation: rows travel rank to rank as
+ * peer stores into a window (device memory every rank of the group maps),
+ * with epoch-tagged flags; every wait is bounded (about a second) and
+ * records an error instead of hanging (ofb_ep_group_device_errors). Per
+ * layer and rank: certified routing of own tokens -> dispatch plan -> rows
+ * (bf16 when the receiver's batch takes the tensor-core path, else f32) and
+ * {local expert, weight, slot} written into each destination's receive
+ * region -> the shared expert on own tokens while rows arrive -> routed
+ * experts on the received rows -> each result row stored back into its
+ * source's y_back -> the combine in top-k order (model.c:1090, :1142).
+ * The reference runs its MoE block on one CPU (engine/src/model.c:992-1143)
+ * and has no counterpart; the arithmetic per (token, expert) is that block's.
+ *
+ * Set-up: ofb_ep_group_create (allocates the window and scratch, returns an
+ * IPC handle of OFB_EP_HANDLE_BYTES), the caller gathers every rank's handle
+ * (any transport), then ofb_ep_group_connect opens the peers' windows;
+ * ofb_ep_group_create_nccl does both with an ncclComm_t (libnccl loaded at
+ * run time). Every rank must call ofb_ep_layer_forward for the same layers
+ * in the same order (the epochs advance together). */
+#define OFB_EP_HANDLE_BYTES 64
+typedef struct ofb_ep_group ofb_ep_group;
+int ofb_ep_group_create(const ofb_moe_config *cfg, int rank, int n_ranks, int max_tokens_per_rank,
+                        ofb_ep_group **group, void *ipc_handle_out);
+int ofb_ep_group_connect(ofb_ep_group *group, const void *all_handles /* n_ranks * OFB_EP_HANDLE_BYTES */);
+int ofb_ep_group_create_nccl(const ofb_moe_config *cfg, void *nccl_comm, int max_tokens_per_rank,
+                             ofb_ep_group **group, void *stream);
+int ofb_ep_group_destroy(ofb_ep_group *group);
+/* w: the full router, the shared expert and gate vector, and this rank's
+ * routed experts [rank*E/n, (rank+1)*E/n) (contiguous layout, 16-byte
+ * aligned). out = resid + g*shared(x) + sum_k w_k expert_k(x) for this rank's
+ * n_tokens tokens x; out may alias resid but not x. */
+int ofb_ep_layer_forward(ofb_ep_group *group, const ofb_moe_weights *w, const float *x, const float *resid,
+                         float *out, int n_tokens, void *stream);
+/* Bits of expired device waits since the last call (bit 0: rows or flags of
+ * a peer did not arrive in time); cleared by the call. Synchronous. */
+int ofb_ep_group_device_errors(ofb_ep_group *group, unsigned *bits);
+
 /* ---- seeded synthetic inputs ---------------------------------------------- */
 
 /* Fills n_blocks Q4_K or Q6_K super-blocks on the device from a counter-based

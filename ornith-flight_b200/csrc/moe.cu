@@ -213,7 +213,7 @@ int check_config(const ofb_moe_config *c) {
 int run_moe_layer(const ofb_moe_config *cfg, const ofb_moe_weights *wt, const float *x,
                   const float *resid, float *out, int T, uint32_t *idx_out, float *w_out,
                   uint8_t *base, const WorkspaceLayout &L, cudaStream_t s, cudaEvent_t *ev,
-                  const uint32_t *given_idx, const float *given_w) {
+                  const uint32_t *given_idx, const float *given_w, const __nv_bfloat16 *x_bf16) {
     const int D = cfg->d_model, H = cfg->hidden, E = cfg->n_experts, K = cfg->top_k;
     auto mark = [&](int i) { if (ev) cudaEventRecord(ev[i], s); };
     mark(0);
@@ -315,6 +315,12 @@ int run_moe_layer(const ofb_moe_config *cfg, const ofb_moe_weights *wt, const fl
         mark(4);
         return OFB_OK;
     }
+    a.xb_in = x_bf16;
+    if (x_bf16 && (use_gemv(T, K, E, H) || H > PREFILL_MAX_H)) {
+        set_error("bf16 token rows need the tensor-core path (more than %d rows, hidden <= %d)", MAX_DECODE_T,
+                  PREFILL_MAX_H);
+        return OFB_EUNSUPPORTED;
+    }
     if (use_gemv(T, K, E, H)) {
         if ((size_t)T > L.gemv_tokens || (size_t)T * K + (has_shared ? T : 0) > L.gemv_rows) {
             set_error("workspace holds %zu decode-path tokens; call needs %d", L.gemv_tokens, T);
@@ -351,12 +357,6 @@ int run_moe_layer(const ofb_moe_config *cfg, const ofb_moe_weights *wt, const fl
 
 using namespace ofb;
 
-struct ofb_workspace {
-    ofb_moe_config cfg;
-    int max_tokens;
-    uint8_t *base;
-    WorkspaceLayout layout;
-};
 
 extern "C" size_t ofb_workspace_size(const ofb_moe_config *cfg, int max_tokens) {
     if (check_config(cfg) || max_tokens < 1) return 0;
@@ -391,7 +391,7 @@ extern "C" int ofb_workspace_destroy(ofb_workspace *ws) {
     return e == cudaSuccess ? OFB_OK : cuda_status(e, "workspace cudaFree");
 }
 
-static int check_ws(const ofb_moe_config *cfg, const ofb_workspace *ws, int T) {
+int ofb::check_ws(const ofb_moe_config *cfg, const ofb_workspace *ws, int T) {
     if (!ws) { set_error("NULL workspace"); return OFB_EINVAL; }
     if (T > ws->max_tokens) { set_error("n_tokens %d > workspace max_tokens %d", T, ws->max_tokens); return OFB_ETOOLARGE; }
     const ofb_moe_config &c = ws->cfg;
@@ -500,6 +500,28 @@ __global__ void fill_kernel(float *__restrict__ p, int n, float v) {
 
 static bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
 
+int ofb::run_experts_given(const ofb_moe_config *cfg, const ofb_moe_weights *w, const float *x_rows,
+                      const __nv_bfloat16 *x_rows_bf16, int n_rows, const int32_t *row_meta, float *out_rows,
+                      ofb_workspace *ws, cudaStream_t s) {
+    ofb_moe_weights routed = *w;  // routed experts only
+    routed.router = nullptr;
+    routed.gate_shexp = routed.up_shexp = routed.down_shexp = nullptr;
+    routed.shexp_gate = nullptr;
+    uint32_t *idx = (uint32_t *)(ws->base + ws->layout.idx);
+    float *wt = (float *)(ws->base + ws->layout.w);
+    unpack_meta_kernel<<<grid_for((size_t)n_rows, 256, 148 * 4), 256, 0, s>>>(row_meta, n_rows, idx, wt);
+    OFB_CHECK_LAUNCH("unpack row metadata");
+    // rows whose weight is below the skip threshold get no expert term; on
+    // the decode-sized path the combine writes rows only when some row has
+    // one, so start from zeros (the tensor-core path initialises out itself)
+    if (use_gemv(n_rows, 1, cfg->n_experts, cfg->hidden)) {
+        cudaError_t e = cudaMemsetAsync(out_rows, 0, (size_t)n_rows * cfg->d_model * sizeof(float), s);
+        if (e != cudaSuccess) return cuda_status(e, "ofb_moe_experts memset");
+    }
+    return run_moe_layer(cfg, &routed, x_rows, nullptr, out_rows, n_rows, nullptr, nullptr, ws->base, ws->layout,
+                         s, nullptr, idx, wt, x_rows_bf16);
+}
+
 extern "C" int ofb_moe_experts(const ofb_moe_config *cfg, const ofb_moe_weights *w, const float *x_rows,
                                int n_rows, const int32_t *row_meta, float *out_rows, ofb_workspace *ws,
                                void *stream) {
@@ -520,24 +542,8 @@ extern "C" int ofb_moe_experts(const ofb_moe_config *cfg, const ofb_moe_weights 
         set_error("ofb_moe_experts: tensors must be 16-byte aligned");
         return OFB_EINVAL;
     }
-    ofb_moe_weights routed = *w;  // routed experts only
-    routed.router = nullptr;
-    routed.gate_shexp = routed.up_shexp = routed.down_shexp = nullptr;
-    routed.shexp_gate = nullptr;
-    cudaStream_t s = static_cast<cudaStream_t>(stream);
-    uint32_t *idx = (uint32_t *)(ws->base + ws->layout.idx);
-    float *wt = (float *)(ws->base + ws->layout.w);
-    unpack_meta_kernel<<<grid_for((size_t)n_rows, 256, 148 * 4), 256, 0, s>>>(row_meta, n_rows, idx, wt);
-    OFB_CHECK_LAUNCH("unpack row metadata");
-    // rows whose weight is below the skip threshold get no expert term; on
-    // the decode-sized path the combine writes rows only when some row has
-    // one, so start from zeros (the tensor-core path initialises out itself)
-    if (use_gemv(n_rows, 1, cfg->n_experts, cfg->hidden)) {
-        cudaError_t e = cudaMemsetAsync(out_rows, 0, (size_t)n_rows * cfg->d_model * sizeof(float), s);
-        if (e != cudaSuccess) return cuda_status(e, "ofb_moe_experts memset");
-    }
-    return run_moe_layer(cfg, &routed, x_rows, nullptr, out_rows, n_rows, nullptr, nullptr, ws->base, ws->layout,
-                         s, nullptr, idx, wt);
+    return run_experts_given(cfg, w, x_rows, nullptr, n_rows, row_meta, out_rows, ws,
+                             static_cast<cudaStream_t>(stream));
 }
 
 extern "C" int ofb_moe_shared(const ofb_moe_config *cfg, const ofb_moe_weights *w, const float *x,

@@ -1,6 +1,7 @@
 // moe.cuh — internal structures of the MoE layer kernels.
 #pragma once
 #include <cuda_runtime.h>
+#include <cuda_bf16.h>
 #include <stddef.h>
 #include <stdint.h>
 
@@ -30,6 +31,7 @@ struct LayerArgs {
     const float *w, *gsc;
     const int *n_slots, *slot_expert, *slot_start, *assign;
     float *h, *y;
+    const __nv_bfloat16 *xb_in;  // token rows already bf16 (tensor-core path only), else NULL
 };
 
 // Byte offsets of the scratch regions inside one workspace allocation.
@@ -116,6 +118,24 @@ int run_moe_layer(const ofb_moe_config *cfg, const ofb_moe_weights *wt, const fl
                   const float *resid, float *out, int T, uint32_t *idx_out, float *w_out,
                   uint8_t *base, const WorkspaceLayout &L, cudaStream_t s,
                   cudaEvent_t *phase_events /* 5 events or NULL */,
-                  const uint32_t *given_idx = nullptr, const float *given_w = nullptr);
+                  const uint32_t *given_idx = nullptr, const float *given_w = nullptr,
+                  const __nv_bfloat16 *x_bf16 = nullptr);
 
+}  // namespace ofb
+
+// A workspace: the scratch of one layer shape for up to max_tokens tokens.
+struct ofb_workspace {
+    ofb_moe_config cfg;
+    int max_tokens;
+    uint8_t *base;
+    ofb::WorkspaceLayout layout;
+};
+
+namespace ofb {
+int check_ws(const ofb_moe_config *cfg, const ofb_workspace *ws, int T);
+// Routed experts over rows with given (local expert, weight) metadata; the
+// rows are f32 (x_rows) or, on the tensor-core path, bf16 (x_rows_bf16).
+int run_experts_given(const ofb_moe_config *cfg, const ofb_moe_weights *w, const float *x_rows,
+                      const __nv_bfloat16 *x_rows_bf16, int n_rows, const int32_t *row_meta, float *out_rows,
+                      ofb_workspace *ws, cudaStream_t s);
 }  // namespace ofb

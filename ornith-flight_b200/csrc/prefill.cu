@@ -968,6 +968,19 @@ __global__ void gather_rows_kernel(const float *__restrict__ x, const int *__res
     }
 }
 
+// The same for token rows that are already bf16 (rows received from peers).
+__global__ void gather_rows_bf16_kernel(const __nv_bfloat16 *__restrict__ x, const int *__restrict__ assign,
+                                        const int *n_slots, const int *slot_start, int TK, int K, int D,
+                                        __nv_bfloat16 *__restrict__ xg) {
+    const int rows = slot_start[*n_slots];
+    const int lane = threadIdx.x & 31;
+    for (int p = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; p < rows; p += (gridDim.x * blockDim.x) >> 5) {
+        const uint4 *src = reinterpret_cast<const uint4 *>(x + (size_t)asg_token_p(assign[p], TK, K) * D);
+        uint4 *dst = reinterpret_cast<uint4 *>(xg + (size_t)p * D);
+        for (int c = lane; c < D / 8; c += 32) dst[c] = __ldcg(src + c);
+    }
+}
+
 // One block: split every slot into tiles of at most 256 tokens.
 __global__ void __launch_bounds__(1024) tile_plan_kernel(const int *n_slots, const int *slot_start, int *n_tiles,
                                                          int *tile_slot, int *tile_start, int *tile_n) {
@@ -1107,7 +1120,11 @@ int launch_prefill(const LayerArgs &la, const float *x, int *n_slots, __nv_bfloa
         gmap_sh = gmap;  // never read: no slot names the shared expert
         umap_sh = umap;
     }
-    gather_rows_kernel<<<148 * 8, 256, 0, s>>>(x, la.assign, n_slots, la.slot_start, T * la.K, la.K, D, xb);
+    if (la.xb_in)
+        gather_rows_bf16_kernel<<<148 * 8, 256, 0, s>>>(la.xb_in, la.assign, n_slots, la.slot_start, T * la.K, la.K,
+                                                         D, xb);
+    else
+        gather_rows_kernel<<<148 * 8, 256, 0, s>>>(x, la.assign, n_slots, la.slot_start, T * la.K, la.K, D, xb);
     tile_plan_kernel<<<1, 1024, 0, s>>>(n_slots, la.slot_start, n_tiles, tile_slot, tile_start, tile_n);
     PrefillArgs a;
     a.T = T; a.D = D; a.H = H; a.E = la.E; a.K = la.K;

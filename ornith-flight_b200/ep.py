@@ -163,14 +163,78 @@ class EPLayer:
         return out
 
 
+class EPGroup:
+    """Device-side exchange over NVLink for the ranks of `group`
+    (ofb_ep_group_*: every rank maps every other rank's window; rows, results
+    and epoch-tagged flags travel as peer stores, no host synchronisation).
+    Set-up gathers the ranks' IPC handles with torch.distributed."""
+
+    def __init__(self, shape: ofb.LayerShape, max_tokens: int, device, group=None):
+        self.shape = shape
+        self.max_tokens = max_tokens
+        self._cfg = shape.config()
+        rank, world = dist.get_rank(group), dist.get_world_size(group)
+        hb = ofb.lib  # noqa: F841 (binding loaded)
+        h = (ctypes.c_uint8 * 64)()
+        self.handle = ctypes.c_void_p()
+        ofb._check(ofb.lib.ofb_ep_group_create(ctypes.byref(self._cfg), rank, world, max_tokens,
+                                               ctypes.byref(self.handle), h))
+        mine = torch.tensor(list(h), dtype=torch.uint8, device=device)
+        every = torch.empty(world * 64, dtype=torch.uint8, device=device)
+        dist.all_gather_into_tensor(every, mine, group=group)
+        allh = (ctypes.c_uint8 * (world * 64))(*every.cpu().tolist())
+        ofb._check(ofb.lib.ofb_ep_group_connect(self.handle, allh))
+
+    def forward(self, weights: ofb.LayerWeights, wstruct, x, resid, out):
+        ofb._check(ofb.lib.ofb_ep_layer_forward(self.handle, ctypes.byref(wstruct), ofb._ptr(x), ofb._ptr(resid),
+                                                ofb._ptr(out), x.shape[0], ofb._stream()))
+        return out
+
+    def device_errors(self) -> int:
+        b = ctypes.c_uint()
+        ofb._check(ofb.lib.ofb_ep_group_device_errors(self.handle, ctypes.byref(b)))
+        return b.value
+
+    def close(self):
+        if self.handle:
+            ofb._check(ofb.lib.ofb_ep_group_destroy(self.handle))
+            self.handle = None
+
+
+class EPLayerP2P:
+    """One expert-parallel MoE layer through an EPGroup (one C call per layer):
+    weights = the full router, shared expert and gate vector plus this rank's
+    routed experts (ofb.make_layer_slice)."""
+
+    def __init__(self, shape: ofb.LayerShape, weights: ofb.LayerWeights, group: EPGroup):
+        self.shape = shape
+        self.weights = weights
+        self.group = group
+        self._w = weights.struct()
+
+    def forward(self, x: torch.Tensor, resid: torch.Tensor | None, out: torch.Tensor) -> torch.Tensor:
+        return self.group.forward(self.weights, self._w, x, resid, out)
+
+
+class LocalLayer:
+    """One rank holding every expert: the whole layer, no exchange."""
+
+    def __init__(self, shape: ofb.LayerShape, weights: ofb.LayerWeights, max_tokens: int):
+        self.shape = shape
+        self.layer = ofb.MoeLayer(shape, weights, max_tokens)
+
+    def forward(self, x: torch.Tensor, resid: torch.Tensor | None, out: torch.Tensor) -> torch.Tensor:
+        return self.layer.forward(x, resid, out=out)
+
+
 class EPStack:
     """A stack of expert-parallel MoE layers: x <- x + MoE_l(rmsnorm(x)) for
     each layer l (the FFN half of the model's blocks, engine/src/model.c:992,
     with unit norm weights and no attention)."""
 
-    def __init__(self, layers: list[EPLayer], ops, max_tokens: int, device):
+    def __init__(self, layers: list, ops, max_tokens: int, device):
         self.layers = layers
-        self.ops = ops
+        self.ops = ops  # EPOps, or None: the library's RMSNorm directly
         D = layers[0].shape.d_model
         self.xn = torch.empty(max_tokens, D, dtype=torch.float32, device=device)
         self.bufs = torch.empty(2, max_tokens, D, dtype=torch.float32, device=device)
@@ -182,7 +246,10 @@ class EPStack:
         xn, cur = self.xn[:T], x
         for i, layer in enumerate(self.layers):
             nxt = self.bufs[i % 2, :T]
-            self.ops.rmsnorm(cur, xn)
+            if self.ops is not None:
+                self.ops.rmsnorm(cur, xn)
+            else:
+                ofb._check(ofb.lib.ofb_rmsnorm(ofb._ptr(cur), T, cur.shape[1], 1e-6, ofb._ptr(xn), ofb._stream()))
             layer.forward(xn, cur, nxt)
             cur = nxt
         return cur

@@ -80,6 +80,12 @@ def _load() -> ctypes.CDLL:
         "ofb_moe_shared": (i32, [cfgp, wp, vp, vp, vp, i32, vp, vp]),
         "ofb_ep_combine": (i32, [vp, vp, i32, i32, i32, vp, vp]),
         "ofb_rmsnorm": (i32, [vp, i32, i32, ctypes.c_float, vp, vp]),
+        "ofb_ep_group_create": (i32, [cfgp, i32, i32, i32, ctypes.POINTER(vp), vp]),
+        "ofb_ep_group_connect": (i32, [vp, vp]),
+        "ofb_ep_group_create_nccl": (i32, [cfgp, vp, i32, ctypes.POINTER(vp), vp]),
+        "ofb_ep_group_destroy": (i32, [vp]),
+        "ofb_ep_layer_forward": (i32, [vp, wp, vp, vp, vp, i32, vp]),
+        "ofb_ep_group_device_errors": (i32, [vp, ctypes.POINTER(ctypes.c_uint)]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(lib, name)

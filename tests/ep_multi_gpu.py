@@ -58,6 +58,23 @@ def main():
         print(f"rank {rank} T={T_global}: layer {e1:.2e} stack {e2:.2e} oracle {e3:.2e} (tol {tol})", flush=True)
         if not (e1 <= tol and e2 <= tol and e3 <= tol):
             fails.append(T_global)
+        # the device-side exchange (EPGroup / EPLayerP2P): same layers, same checks
+        grp = ep.EPGroup(shape, tpr, dev)
+        p2p = [ep.EPLayerP2P(shape, l.weights, grp) for l in layers]
+        out2 = torch.empty_like(x)
+        p2p[0].forward(x, x, out2)
+        e4 = rel_err((out2 - x).cpu().numpy(), (ref - x).cpu().numpy())
+        got2 = ep.EPStack(p2p, None, tpr, dev).forward(x)
+        e5 = rel_err(got2.cpu().numpy(), cur[rank * tpr:(rank + 1) * tpr].cpu().numpy())
+        # repeated layers in one stream: the epochs advance, results repeat
+        again = ep.EPStack(p2p, None, tpr, dev).forward(x)
+        e6 = rel_err(again.cpu().numpy(), got2.cpu().numpy())
+        errs = grp.device_errors()
+        grp.close()
+        print(f"rank {rank} T={T_global} p2p: layer {e4:.2e} stack {e5:.2e} repeat {e6:.2e} device errors {errs}",
+              flush=True)
+        if not (e4 <= tol and e5 <= tol and e6 <= 1e-6 and errs == 0):
+            fails.append(-T_global)
     ok = torch.tensor([0 if fails else 1], device=dev)
     dist.all_reduce(ok, op=dist.ReduceOp.MIN)
     dist.destroy_process_group()
