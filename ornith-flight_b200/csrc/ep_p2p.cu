@@ -253,9 +253,9 @@ extern "C" int ofb_ep_group_create(const ofb_moe_config *cfg, int rank, int n_ra
     g->loc_cfg.n_experts = g->epr;
     g->loc_cfg.top_k = 1;
     const int rows = n * g->cap;
-    // the receiver's batch takes the tensor-core path above MAX_DECODE_T rows:
-    // bf16 rows then (that path computes in bf16 anyway), f32 otherwise
-    const bool bf16 = rows > MAX_DECODE_T && cfg->hidden <= PREFILL_MAX_H;
+    // the receiver's batch takes the tensor-core path above the decode-kernel
+    // limit: bf16 rows then (that path computes in bf16 anyway), f32 otherwise
+    const bool bf16 = rows > gemv_limit(cfg->hidden) && cfg->hidden <= PREFILL_MAX_H;
     EPArgs &a = g->args;
     a.n = n; a.me = rank; a.cap = g->cap; a.D = D; a.K = K; a.epr = g->epr; a.bf16 = bf16;
     a.row_bytes = (size_t)D * (bf16 ? 2 : 4);

@@ -173,8 +173,8 @@ WorkspaceLayout workspace_layout(const ofb_moe_config *c, int max_tokens) {
     L.y = take(Ad * (size_t)c->d_model * 4);
     // tensor-core buffers whenever a call may exceed the fixed decode size:
     // the layer itself above gemv_max_tokens, and one-expert runs over the
-    // same tokens (ofb_moe_shared) above MAX_DECODE_T
-    const bool prefill = !inter && max_tokens > MAX_DECODE_T && c->hidden <= PREFILL_MAX_H;
+    // same tokens (ofb_moe_shared) above the decode-kernel limit
+    const bool prefill = !inter && max_tokens > gemv_limit(c->hidden) && c->hidden <= PREFILL_MAX_H;
     L.xb = take(prefill ? A * (size_t)c->d_model * 2 : 0);
     L.hb = take(prefill ? A * (size_t)c->hidden * 2 : 0);
     L.tiles = take(prefill ? (1 + 3 * (size_t)prefill_max_tiles(max_tokens, K, E)) * 4 : 0);
@@ -317,8 +317,8 @@ int run_moe_layer(const ofb_moe_config *cfg, const ofb_moe_weights *wt, const fl
     }
     a.xb_in = x_bf16;
     if (x_bf16 && (use_gemv(T, K, E, H) || H > PREFILL_MAX_H)) {
-        set_error("bf16 token rows need the tensor-core path (more than %d rows, hidden <= %d)", MAX_DECODE_T,
-                  PREFILL_MAX_H);
+        set_error("bf16 token rows need the tensor-core path (more than %d rows, hidden <= %d)",
+                  gemv_limit(H), PREFILL_MAX_H);
         return OFB_EUNSUPPORTED;
     }
     if (use_gemv(T, K, E, H)) {

@@ -66,12 +66,16 @@ constexpr int MAX_DECODE_H = 1024;
 constexpr int DOWN_TICKET_ROWS = 4;
 // Tensor-core prefill kernels: the down kernel holds 128 Q6_K rows in shared memory.
 constexpr int PREFILL_MAX_H = 512;
-// Batches the dp4a decode kernels take. Above 32 tokens the tensor-core
-// kernels win even at a few rows per expert (measured: a 2048-row,
-// 8-rows-per-expert batch ran 2.5x slower on the decode kernels).
-__host__ __device__ inline int gemv_max_tokens(int, int) { return MAX_DECODE_T; }
+// Batches the dp4a decode kernels take: up to 4 tokens when the tensor-core
+// kernels can take over (hidden <= PREFILL_MAX_H), up to MAX_DECODE_T
+// otherwise. Measured on the 2048 x 512, 256-expert layer (us per layer,
+// decode kernels / tensor-core kernels): 8 tokens 135 / 114, 16 tokens 240 /
+// 158, 32 tokens 381 / 233; at 4 tokens they tie.
+constexpr int GEMV_T_WITH_TC = 4;
+__host__ __device__ inline int gemv_limit(int H) { return H <= PREFILL_MAX_H ? GEMV_T_WITH_TC : MAX_DECODE_T; }
+__host__ __device__ inline int gemv_max_tokens(int, int) { return MAX_DECODE_T; }  // decode buffer sizing
 __host__ __device__ inline bool use_gemv(int T, int K, int E, int H) {
-    return H <= MAX_DECODE_H && T <= gemv_max_tokens(K, E);
+    return H <= MAX_DECODE_H && T <= gemv_limit(H);
 }
 
 int launch_quantize_x(const float *x, int T, int D, unsigned char *xq, cudaStream_t s);

@@ -120,6 +120,13 @@ def _stream(stream=None) -> int:
     return s.cuda_stream
 
 
+def decode_path(n_rows: int, hidden: int) -> bool:
+    """True when a batch of n_rows token rows runs on the fp32-accumulating
+    dp4a decode kernels (tolerance 1e-3), False on the bf16 tensor-core
+    kernels (2e-2); the library's dispatch rule (moe.cuh use_gemv)."""
+    return n_rows <= (4 if hidden <= 512 else 32)
+
+
 # ---- dequant ----------------------------------------------------------------
 
 def dequantize(blocks: torch.Tensor, qtype: int, n_elems: int, out_dtype=torch.float32,

@@ -37,7 +37,7 @@ def main():
         x = x_all[rank * tpr:(rank + 1) * tpr].contiguous()
         # single-GPU reference on this rank: the whole layers, all tokens
         full = [ofb.MoeLayer(shape, ofb.make_layer(shape, s, device=dev), T_global) for s in seeds]
-        tol = TOL if tpr * shape.top_k <= 32 and T_global <= 32 else TOL_BF16
+        tol = TOL if ofb.decode_path(tpr * shape.top_k * world, shape.hidden) and ofb.decode_path(T_global, shape.hidden) else TOL_BF16
         out = torch.empty_like(x)
         layers[0].forward(x, x, out)
         ref = full[0].forward(x_all, x_all)[rank * tpr:(rank + 1) * tpr]

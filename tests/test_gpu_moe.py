@@ -12,7 +12,7 @@ import torch
 
 pytestmark = pytest.mark.gpu
 TOL = 1e-3       # decode and interleaved paths: fp32 accumulation
-TOL_BF16 = 2e-2  # contiguous batches above 32 tokens: bf16 tensor-core GEMMs
+TOL_BF16 = 2e-2  # contiguous batches past the decode-kernel limit: bf16 tensor-core GEMMs
 WEIGHT_RTOL = 1e-5
 
 
@@ -51,7 +51,7 @@ def check(ofb, oracle, cuda, shape, T, seed, resid=False, shared=True, router=Tr
     else:
         assert np.array_equal(w.cpu().numpy().view(np.uint32), ow.view(np.uint32))
     err = rel_err(got, want)
-    tol = TOL if (shape.layout == 1 or T <= 32) else TOL_BF16
+    tol = TOL if (shape.layout == 1 or ofb.decode_path(T, shape.hidden)) else TOL_BF16
     assert err <= tol, f"relative error {err}"
     return got, want
 
@@ -91,27 +91,40 @@ def test_full_size_interleaved_decode(ofb, oracle, cuda):
     check(ofb, oracle, cuda, ofb.LayerShape(layout=1), 1, seed=2)
 
 
-def test_output_may_alias_residual(ofb, cuda):
+@pytest.mark.parametrize("T", [4, 8])
+def test_output_may_alias_residual(ofb, cuda, T):
+    # T = 4: decode kernels (deterministic combine); T = 8: tensor-core
+    # kernels, whose down GEMM adds w*y into out with fp32 reductions in
+    # arrival order, so the two runs agree to rounding, not bit for bit
     shape = ofb.LayerShape(**SMALL)
     lw = ofb.make_layer(shape, seed=21, device=cuda)
-    layer = ofb.MoeLayer(shape, lw, max_tokens=8)
-    x = ofb.make_tokens(shape, 8, seed=1).to(cuda)
-    r = ofb.make_tokens(shape, 8, seed=2).to(cuda)
+    layer = ofb.MoeLayer(shape, lw, max_tokens=T)
+    x = ofb.make_tokens(shape, T, seed=1).to(cuda)
+    r = ofb.make_tokens(shape, T, seed=2).to(cuda)
     want = layer.forward(x, r.clone())
     inplace = r.clone()
     layer.forward(x, inplace, out=inplace)
     torch.cuda.synchronize()
-    assert torch.equal(want, inplace)
+    if ofb.decode_path(T, shape.hidden):
+        assert torch.equal(want, inplace)
+    else:
+        assert rel_err(inplace.cpu().numpy(), want.cpu().numpy()) <= 1e-6
 
 
-def test_repeatable(ofb, cuda):
+@pytest.mark.parametrize("T", [1, 4, 32])
+def test_repeatable(ofb, cuda, T):
+    # the decode paths (T = 1 single launch, T = 4 decode kernels) give the
+    # same bits every call; the tensor-core path (T = 32) agrees to rounding
     shape = ofb.LayerShape()
     lw = ofb.make_layer(shape, seed=1, device=cuda)
-    layer = ofb.MoeLayer(shape, lw, max_tokens=32)
-    x = ofb.make_tokens(shape, 32, seed=1).to(cuda)
+    layer = ofb.MoeLayer(shape, lw, max_tokens=T)
+    x = ofb.make_tokens(shape, T, seed=1).to(cuda)
     a = layer.forward(x).clone()
     b = layer.forward(x)
-    assert torch.equal(a, b)
+    if ofb.decode_path(T, shape.hidden):
+        assert torch.equal(a, b)
+    else:
+        assert rel_err(b.cpu().numpy(), a.cpu().numpy()) <= 1e-6
 
 
 def test_workspace_limits(ofb, cuda):
