@@ -202,6 +202,36 @@ int ofb_moe_forward_noalloc(const ofb_moe_config *cfg, const ofb_moe_weights *w,
                             float *w_out, void *stream);
 size_t ofb_noalloc_capacity(void);
 
+/* ---- GGUF -> HBM ------------------------------------------------------------
+ * Replaces gguf_open / gguf_read_tensor_bytes (engine/src/gguf.c:408-445,
+ * 588-601) on the path that feeds the MoE layer: the file is parsed once and a
+ * layer's tensors are uploaded as stored (raw Q4_K/Q6_K blocks, F32 router and
+ * gate vector), so the experts stay resident in HBM instead of being read
+ * per token. Parameters are looked up with the architecture prefix
+ * (gguf.c:726-744). layout: OFB_LAYOUT_INTERLEAVED reads the tensors the way
+ * the reference's model_forward does (router [d_model][n_experts], expert
+ * index fastest, matrices [in][out]); OFB_LAYOUT_CONTIGUOUS reads them in
+ * ggml's native order (router rows per expert, each expert's blocks
+ * contiguous, matrices [out][in]). Host-side parsing needs no GPU. */
+typedef struct ofb_gguf ofb_gguf;
+int ofb_gguf_open(const char *path, ofb_gguf **gguf);
+int ofb_gguf_close(ofb_gguf *gguf);
+/* Type code, dims (fastest first), absolute file offset and byte size (0 when
+ * the type's size is unknown) of a tensor. Any output may be NULL. */
+int ofb_gguf_tensor(const ofb_gguf *gguf, const char *name, int *type, int *n_dims, uint64_t dims[4],
+                    uint64_t *file_offset, uint64_t *n_bytes);
+int ofb_gguf_param_u32(const ofb_gguf *gguf, const char *param, uint32_t *value);
+/* Copies a tensor's bytes into device memory dst (capacity bytes); synchronous. */
+int ofb_gguf_upload(const ofb_gguf *gguf, const char *name, void *dst, uint64_t capacity, void *stream);
+typedef struct {
+    ofb_moe_config cfg;      /* from the metadata (renorm 1, shared_gate if a gate vector exists) */
+    ofb_moe_weights weights; /* device allocations owned by the struct */
+} ofb_gguf_moe_layer;
+/* blk.<layer>.ffn_{gate,up,down}_exps (required), ffn_gate_inp (router),
+ * ffn_{gate,up,down}_shexp and ffn_gate_inp_shexp (optional). */
+int ofb_gguf_upload_moe_layer(const ofb_gguf *gguf, int layer, int layout, ofb_gguf_moe_layer *out, void *stream);
+int ofb_gguf_free_moe_layer(ofb_gguf_moe_layer *layer);
+
 /* ---- expert parallelism (experts sharded over GPUs) ------------------------
  * Building blocks for one MoE layer whose routed experts are split over
  * n_ranks GPUs, experts_per_rank = n_experts / n_ranks each (rank r owns

@@ -48,6 +48,11 @@ class MoeWeights(ctypes.Structure):
         "shexp_gate")]
 
 
+class GgufMoeLayer(ctypes.Structure):
+    """ofb_gguf_moe_layer: config read from the file + device weight pointers."""
+    _fields_ = [("cfg", MoeConfig), ("weights", MoeWeights)]
+
+
 def _load() -> ctypes.CDLL:
     if not os.path.exists(LIB_PATH):
         raise ImportError(f"{LIB_PATH} is not built; run `make -C {_HERE}` (or __graft_entry__.build())")
@@ -80,6 +85,14 @@ def _load() -> ctypes.CDLL:
         "ofb_moe_shared": (i32, [cfgp, wp, vp, vp, vp, i32, vp, vp]),
         "ofb_ep_combine": (i32, [vp, vp, i32, i32, i32, vp, vp]),
         "ofb_rmsnorm": (i32, [vp, i32, i32, ctypes.c_float, vp, vp]),
+        "ofb_gguf_open": (i32, [ctypes.c_char_p, ctypes.POINTER(vp)]),
+        "ofb_gguf_close": (i32, [vp]),
+        "ofb_gguf_tensor": (i32, [vp, ctypes.c_char_p, ctypes.POINTER(i32), ctypes.POINTER(i32),
+                                  ctypes.POINTER(ctypes.c_uint64 * 4), ctypes.POINTER(u64), ctypes.POINTER(u64)]),
+        "ofb_gguf_param_u32": (i32, [vp, ctypes.c_char_p, ctypes.POINTER(ctypes.c_uint32)]),
+        "ofb_gguf_upload": (i32, [vp, ctypes.c_char_p, vp, u64, vp]),
+        "ofb_gguf_upload_moe_layer": (i32, [vp, i32, i32, vp, vp]),
+        "ofb_gguf_free_moe_layer": (i32, [vp]),
         "ofb_ep_group_create": (i32, [cfgp, i32, i32, i32, ctypes.POINTER(vp), vp]),
         "ofb_ep_group_connect": (i32, [vp, vp]),
         "ofb_ep_group_create_nccl": (i32, [cfgp, vp, i32, ctypes.POINTER(vp), vp]),

@@ -18,6 +18,26 @@ from conftest import load_ep, load_ofb  # noqa: E402
 from test_gpu_moe import TOL, TOL_BF16, oracle_layer, rel_err  # noqa: E402
 
 
+def nccl_comm(rank, world, dev):
+    """A raw ncclComm_t from the NCCL library torch loaded (the unique id is
+    broadcast with torch.distributed), for ofb_ep_group_create_nccl."""
+    import ctypes
+
+    class UID(ctypes.Structure):
+        _fields_ = [("internal", ctypes.c_char * 128)]
+
+    nccl = ctypes.CDLL("libnccl.so.2")
+    uid = UID()
+    if rank == 0:
+        assert nccl.ncclGetUniqueId(ctypes.byref(uid)) == 0
+    t = torch.tensor(list(bytes(uid.internal)) if rank == 0 else [0] * 128, dtype=torch.uint8, device=dev)
+    dist.broadcast(t, 0)
+    uid = UID(bytes(t.cpu().tolist()))
+    comm = ctypes.c_void_p()
+    assert nccl.ncclCommInitRank(ctypes.byref(comm), world, uid, rank) == 0
+    return nccl, comm
+
+
 def main():
     rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
     torch.cuda.set_device(int(os.environ["LOCAL_RANK"]))
@@ -71,6 +91,22 @@ def main():
         e6 = rel_err(again.cpu().numpy(), got2.cpu().numpy())
         errs = grp.device_errors()
         grp.close()
+        # the same layer through a group made from a raw NCCL communicator
+        import ctypes
+        nccl, comm = nccl_comm(rank, world, dev)
+        h = ctypes.c_void_p()
+        ofb._check(ofb.lib.ofb_ep_group_create_nccl(ctypes.byref(shape.config()), comm, tpr, ctypes.byref(h),
+                                                    ofb._stream()))
+        out3 = torch.empty_like(x)
+        ofb._check(ofb.lib.ofb_ep_layer_forward(h, ctypes.byref(layers[0].weights.struct()), ofb._ptr(x),
+                                                ofb._ptr(x), ofb._ptr(out3), tpr, ofb._stream()))
+        torch.cuda.synchronize()
+        e7 = rel_err(out3.cpu().numpy(), out2.cpu().numpy())
+        ofb._check(ofb.lib.ofb_ep_group_destroy(h))
+        nccl.ncclCommDestroy(comm)
+        print(f"rank {rank} T={T_global} nccl-made group: vs p2p {e7:.2e}", flush=True)
+        if not e7 <= 1e-6:
+            fails.append(-2 * T_global)
         print(f"rank {rank} T={T_global} p2p: layer {e4:.2e} stack {e5:.2e} repeat {e6:.2e} device errors {errs}",
               flush=True)
         if not (e4 <= tol and e5 <= tol and e6 <= 1e-6 and errs == 0):
