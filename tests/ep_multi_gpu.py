@@ -24,17 +24,18 @@ def nccl_comm(rank, world, dev):
     import ctypes
 
     class UID(ctypes.Structure):
-        _fields_ = [("internal", ctypes.c_char * 128)]
+        _fields_ = [("internal", ctypes.c_ubyte * 128)]
 
     nccl = ctypes.CDLL("libnccl.so.2")
     uid = UID()
     if rank == 0:
         assert nccl.ncclGetUniqueId(ctypes.byref(uid)) == 0
-    t = torch.tensor(list(bytes(uid.internal)) if rank == 0 else [0] * 128, dtype=torch.uint8, device=dev)
+    t = torch.tensor(list(uid.internal) if rank == 0 else [0] * 128, dtype=torch.uint8, device=dev)
     dist.broadcast(t, 0)
-    uid = UID(bytes(t.cpu().tolist()))
+    uid = UID((ctypes.c_ubyte * 128)(*t.cpu().tolist()))
     comm = ctypes.c_void_p()
-    assert nccl.ncclCommInitRank(ctypes.byref(comm), world, uid, rank) == 0
+    rc = nccl.ncclCommInitRank(ctypes.byref(comm), world, uid, rank)
+    assert rc == 0, f"ncclCommInitRank: {rc}"
     return nccl, comm
 
 
@@ -44,10 +45,15 @@ def main():
     dev = torch.device("cuda", int(os.environ["LOCAL_RANK"]))
     dist.init_process_group("nccl", device_id=dev)
     ofb, ep = load_ofb(), load_ep()
-    shape = ofb.LayerShape(d_model=512, hidden=256, n_experts=16, top_k=4)
-    epr = shape.n_experts // world
+    # hidden 768: every part runs the fp32 decode kernels (tensor-core kernels
+    # need hidden <= 512), so the 3-layer stacks compare at 1e-3 with no
+    # routing flips; hidden 256 at 40 tokens per rank: the bf16 tensor-core
+    # kernels
+    shapes = {4 * world: ofb.LayerShape(d_model=512, hidden=768, n_experts=16, top_k=4),
+              40 * world: ofb.LayerShape(d_model=512, hidden=256, n_experts=16, top_k=4)}
     fails = []
-    for T_global in (4 * world, 40 * world):
+    for T_global, shape in shapes.items():
+        epr = shape.n_experts // world
         tpr = T_global // world
         ops = ep.EPOps(shape, world, max_tokens=tpr)
         seeds = [31 + l for l in range(3)]
