@@ -513,6 +513,43 @@ def measure_sweep(ofb, dev, iters=20):
             "results": res}
 
 
+def measure_lm_head(ofb, dev, iters=20):
+    """The LM head (model.c:1219-1231): logits = x . W for an F32
+    [2048][248,320] weight (2.03 GB, > L2), one token, ofb_matvec, then
+    ofb_sample. GB/s = weight + x + logits bytes / device time."""
+    import torch
+    peak, peak_kind = peaks("hbm_gbs")
+    V = 248320
+    w = torch.randn(D * V, device=dev) * 0.02
+    x = torch.randn(1, D, device=dev)
+    out = torch.empty(1, V, device=dev)
+    scratch = torch.empty(V, device=dev)
+    tok = torch.empty(1, dtype=torch.int32, device=dev)
+    for _ in range(3):
+        ofb._check(ofb.lib.ofb_matvec(ofb._ptr(x), 1, D, V, ofb._ptr(w), 0, ofb._ptr(out), ofb._stream()))
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(iters):
+        ofb._check(ofb.lib.ofb_matvec(ofb._ptr(x), 1, D, V, ofb._ptr(w), 0, ofb._ptr(out), ofb._stream()))
+    b.record()
+    torch.cuda.synchronize()
+    ms = a.elapsed_time(b) / iters
+    a.record()
+    for _ in range(iters):
+        ofb._check(ofb.lib.ofb_sample(ofb._ptr(out), V, 0.8, 0.5, ofb._ptr(scratch), ofb._ptr(tok), ofb._stream()))
+    b.record()
+    torch.cuda.synchronize()
+    ms_s = a.elapsed_time(b) / iters
+    byts = D * V * 4 + D * 4 + V * 4
+    gbs = byts / (ms * 1e-3) / 1e9
+    del w
+    torch.cuda.empty_cache()
+    return {"metric": "LM head GEMV (F32 2048 x 248,320, one token) + sampling", "lm_head_us": ms * 1e3,
+            "GB/s": gbs, "frac": gbs / peak, "peak": peak, "peak_source": peak_kind + " hbm_gbs",
+            "sample_us": ms_s * 1e3, "kernel": "matvec_kernel<F32> (bit-exact sequential sums), sample_kernel"}
+
+
 def run_ours(args, rank, world, local_rank):
     import torch
     ofb = load_ofb()
@@ -538,9 +575,10 @@ def run_ours(args, rank, world, local_rank):
     if args.workload == "decode1" and not args.no_decode32:
         d32 = measure(args, ofb, dev, rank, world, local_rank, "decode32", args.decode32_steps, 5,
                       WORKLOADS["decode32"]["layers"], False)
-    sweep = None
+    sweep = lm = None
     if not args.no_sweep:
         sweep = measure_sweep(ofb, dev)
+        lm = measure_lm_head(ofb, dev)
     stack = None
     if not args.no_stack:
         stack = measure_stack(args, ofb, dev, rank, world, local_rank, args.stack_steps, 3)
@@ -560,6 +598,8 @@ def run_ours(args, rank, world, local_rank):
                                                 "route_paths", "gpu_launches")}
     if sweep is not None:
         line["dequant_sweep"] = sweep
+    if lm is not None:
+        line["lm_head"] = lm
     if stack is not None:
         line["stack40"] = describe_stack(world, stack, args.stack_steps, 3)
     if not args.no_cpu_baseline:

@@ -202,6 +202,24 @@ int ofb_moe_forward_noalloc(const ofb_moe_config *cfg, const ofb_moe_weights *w,
                             float *w_out, void *stream);
 size_t ofb_noalloc_capacity(void);
 
+/* ---- dense projections, LM head and sampling --------------------------------
+ * out[t][j] = sum_i x[t][i] * W[i*out_dim + j] for W stored as a GGUF tensor
+ * (OFB_TYPE_F32 / F16 / Q4_K / Q6_K, element i*out_dim + j): cpu_matmul_vec
+ * over the dequantised weight (engine/src/model.c:351-357, :785-843), and with
+ * an F32 [d_model][vocab] weight the LM head (model.c:1219-1231). Every output
+ * is a sequential sum with separate multiply and add over the reference's
+ * per-element dequant, so results are bit-identical to the reference's. */
+int ofb_matvec(const float *x, int n_tokens, int in_dim, int out_dim, const void *w, int w_type, float *out,
+               void *stream);
+/* model_sample (model.c:1238-1260) for one row of logits on the device:
+ * temperature (when > 0 and != 1), softmax with the host library's expf, and
+ * the first index whose cumulative probability reaches r in [0, 1) (the
+ * caller's uniform draw). scratch: vocab floats. The sums run in a fixed
+ * order (deterministic); the index can differ from the reference's only when
+ * r is within ~vocab * 2^-24 of a cumulative boundary. */
+int ofb_sample(const float *logits, int vocab, float temperature, float r, float *scratch, uint32_t *token,
+               void *stream);
+
 /* ---- GGUF -> HBM ------------------------------------------------------------
  * Replaces gguf_open / gguf_read_tensor_bytes (engine/src/gguf.c:408-445,
  * 588-601) on the path that feeds the MoE layer: the file is parsed once and a

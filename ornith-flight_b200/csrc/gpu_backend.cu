@@ -230,11 +230,24 @@ void gpu_copy_buffer(gpu_context *ctx, gpu_buffer *dst, const gpu_buffer *src, s
 void gpu_matmul(gpu_context *ctx, gpu_buffer *C, const gpu_buffer *A, const gpu_buffer *B, int M,
                 int N, int K, quant_mode a_quant, quant_mode b_quant) {
     (void)a_quant;
-    (void)b_quant;
     if (!ctx || !C || !A || !B || M <= 0 || N <= 0 || K <= 0) return;
-    if ((size_t)M * N * 4 > C->size || (size_t)M * K * 4 > A->size || (size_t)K * N * 4 > B->size) {
+    // EXT: B as stored GGUF blocks (Q4_K, Q6_K, F16), element k*N + j: the
+    // sequential-sum matvec of dense.cu, bit-identical to dequantise + gpu.c's
+    // matmul (gpu.c:104-129)
+    int wt = -1;
+    size_t bbytes = (size_t)K * N * 4;
+    if (b_quant == QUANT_Q4_K) { wt = OFB_TYPE_Q4_K; bbytes = (size_t)K * N / 256 * 144; }
+    else if (b_quant == QUANT_Q6_K) { wt = OFB_TYPE_Q6_K; bbytes = (size_t)K * N / 256 * 210; }
+    else if (b_quant == QUANT_FP16) { wt = OFB_TYPE_F16; bbytes = (size_t)K * N * 2; }
+    if ((size_t)M * N * 4 > C->size || (size_t)M * K * 4 > A->size || bbytes > B->size) {
         ofb::set_error("gpu_matmul: buffer too small for %dx%dx%d", M, N, K);
         fail(ctx, OFB_EINVAL);
+        return;
+    }
+    if (wt >= 0) {
+        const int st = ofb_matvec((const float *)A->ptr, M, K, N, B->ptr, wt, (float *)C->ptr, ctx->stream);
+        if (st) { fail(ctx, st); return; }
+        finish(ctx, "gpu_matmul");
         return;
     }
     dim3 grid((N + 15) / 16, (M + 15) / 16);

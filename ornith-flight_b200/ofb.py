@@ -85,6 +85,8 @@ def _load() -> ctypes.CDLL:
         "ofb_moe_shared": (i32, [cfgp, wp, vp, vp, vp, i32, vp, vp]),
         "ofb_ep_combine": (i32, [vp, vp, i32, i32, i32, vp, vp]),
         "ofb_rmsnorm": (i32, [vp, i32, i32, ctypes.c_float, vp, vp]),
+        "ofb_matvec": (i32, [vp, i32, i32, i32, vp, i32, vp, vp]),
+        "ofb_sample": (i32, [vp, i32, ctypes.c_float, ctypes.c_float, vp, vp, vp]),
         "ofb_gguf_open": (i32, [ctypes.c_char_p, ctypes.POINTER(vp)]),
         "ofb_gguf_close": (i32, [vp]),
         "ofb_gguf_tensor": (i32, [vp, ctypes.c_char_p, ctypes.POINTER(i32), ctypes.POINTER(i32),
@@ -160,6 +162,23 @@ def dequantize_slice(blocks: torch.Tensor, qtype: int, n_elems: int, n_experts: 
     _check(lib.ofb_dequantize_expert_slice(_ptr(blocks), qtype, n_elems, n_experts, expert,
                                            _ptr(out), ot, _stream(stream)))
     return out
+
+
+# ---- dense projections and sampling ---------------------------------------------
+
+def matvec(x: torch.Tensor, w: torch.Tensor, w_type: int, out_dim: int, stream=None) -> torch.Tensor:
+    """out[t][j] = sum_i x[t][i] * W[i*out_dim + j] for a GGUF-typed W (bit-exact)."""
+    T, in_dim = x.shape
+    out = torch.empty(T, out_dim, dtype=torch.float32, device=x.device)
+    _check(lib.ofb_matvec(_ptr(x), T, in_dim, out_dim, _ptr(w), w_type, _ptr(out), _stream(stream)))
+    return out
+
+
+def sample(logits: torch.Tensor, temperature: float, r: float, stream=None) -> int:
+    scratch = torch.empty_like(logits)
+    tok = torch.empty(1, dtype=torch.int32, device=logits.device)
+    _check(lib.ofb_sample(_ptr(logits), logits.numel(), temperature, r, _ptr(scratch), _ptr(tok), _stream(stream)))
+    return int(tok.item())
 
 
 # ---- synthetic inputs ---------------------------------------------------------
