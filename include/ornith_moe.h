@@ -202,6 +202,14 @@ int ofb_moe_forward_noalloc(const ofb_moe_config *cfg, const ofb_moe_weights *w,
                             float *w_out, void *stream);
 size_t ofb_noalloc_capacity(void);
 
+/* Copies bytes with a kernel (launched with programmatic dependent launch,
+ * like the layer kernels), for a decode step's activations between pinned
+ * host memory and the device: either pointer may be pinned host memory
+ * (device-accessible under unified addressing) or device memory. A few KB
+ * this way cost less than a copy-engine transfer and let the next kernel
+ * begin its weight loads early. Stream-ordered. No reference counterpart. */
+int ofb_copy(void *dst, const void *src, size_t bytes, void *stream);
+
 /* ---- dense projections, LM head and sampling --------------------------------
  * out[t][j] = sum_i x[t][i] * W[i*out_dim + j] for W stored as a GGUF tensor
  * (OFB_TYPE_F32 / F16 / Q4_K / Q6_K, element i*out_dim + j): cpu_matmul_vec

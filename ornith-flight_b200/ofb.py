@@ -85,6 +85,7 @@ def _load() -> ctypes.CDLL:
         "ofb_moe_shared": (i32, [cfgp, wp, vp, vp, vp, i32, vp, vp]),
         "ofb_ep_combine": (i32, [vp, vp, i32, i32, i32, vp, vp]),
         "ofb_rmsnorm": (i32, [vp, i32, i32, ctypes.c_float, vp, vp]),
+        "ofb_copy": (i32, [vp, vp, sz, vp]),
         "ofb_matvec": (i32, [vp, i32, i32, i32, vp, i32, vp, vp]),
         "ofb_sample": (i32, [vp, i32, ctypes.c_float, ctypes.c_float, vp, vp, vp]),
         "ofb_gguf_open": (i32, [ctypes.c_char_p, ctypes.POINTER(vp)]),
@@ -165,6 +166,13 @@ def dequantize_slice(blocks: torch.Tensor, qtype: int, n_elems: int, n_experts: 
 
 
 # ---- dense projections and sampling ---------------------------------------------
+
+def copy(dst: torch.Tensor, src: torch.Tensor, stream=None) -> torch.Tensor:
+    """dst <- src by a kernel; either may be pinned host memory (ofb_copy)."""
+    assert dst.numel() * dst.element_size() == src.numel() * src.element_size()
+    _check(lib.ofb_copy(_ptr(dst), _ptr(src), src.numel() * src.element_size(), _stream(stream)))
+    return dst
+
 
 def matvec(x: torch.Tensor, w: torch.Tensor, w_type: int, out_dim: int, stream=None) -> torch.Tensor:
     """out[t][j] = sum_i x[t][i] * W[i*out_dim + j] for a GGUF-typed W (bit-exact)."""

@@ -97,3 +97,17 @@ def test_gpu_matmul_quantised_b(ofb, oracle, cuda):
         want = ref_matmul(oracle, A, oracle.dequant(blocks, wt, K * N).reshape(K, N))
         assert np.array_equal(got.view(np.uint32), want.view(np.uint32))
     L.gpu_destroy(ctx)
+
+
+@pytest.mark.parametrize("nbytes,off", [(8192, 0), (8190, 0), (4096, 3), (1 << 20, 0)])
+def test_copy_kernel_host_and_device(ofb, cuda, nbytes, off):
+    # ofb_copy between pinned host memory and the device, both directions,
+    # aligned (16-byte path) and unaligned (byte path)
+    src = torch.randint(0, 256, (nbytes + off,), dtype=torch.uint8).pin_memory()
+    dev = torch.empty(nbytes + off, dtype=torch.uint8, device=cuda)
+    back = torch.zeros(nbytes + off, dtype=torch.uint8).pin_memory()
+    ofb._check(ofb.lib.ofb_copy(dev.data_ptr() + off, src.data_ptr() + off, nbytes, ofb._stream()))
+    ofb._check(ofb.lib.ofb_copy(back.data_ptr() + off, dev.data_ptr() + off, nbytes, ofb._stream()))
+    torch.cuda.synchronize()
+    assert torch.equal(dev.cpu()[off:], src[off:])
+    assert torch.equal(back[off:], src[off:])
