@@ -66,3 +66,42 @@ def moe_layer_gguf(path, binding, d_model, hidden, n_experts, top_k, seed, layer
               "rope.freq_base": (T_F32, 10000.0)}
     write_gguf(path, "ornith", params, tensors)
     return w
+
+
+def engine_model_gguf(path, binding, d_model=256, hidden=256, n_experts=8, top_k=2, seed=1):
+    """A one-layer model the reference engine's model_load / model_forward
+    accept: attention weights zero (the attention adds nothing), norm weights
+    one, output.weight the identity (vocab = d_model), so the logits are
+    x + MoE(rmsnorm(x)) for x = the token's embedding row. MoE tensors in the
+    reference's reading (router [D][E], expert index fastest) with the bytes
+    of binding.make_layer_host(layout=1)."""
+    D, H, E, V = d_model, hidden, n_experts, d_model
+    nh, nkv = 2, 1
+    w = binding.make_layer_host(D, H, E, layout=1, seed=seed)
+    f32 = lambda a: np.ascontiguousarray(a, dtype=np.float32).tobytes()
+    emb = np.random.default_rng(seed).normal(size=(D, V)).astype(np.float32)
+    b = "blk.0."
+    tensors = [("token_embd.weight", [V, D], 0, f32(emb)),
+               (b + "attn_norm.weight", [D], 0, f32(np.ones(D))),
+               (b + "attn_q.weight", [nh * D, D], 0, f32(np.zeros(D * nh * D))),
+               (b + "attn_k.weight", [nkv * 2, D], 0, f32(np.zeros(D * nkv * 2))),
+               (b + "attn_v.weight", [nkv * 2, D], 0, f32(np.zeros(D * nkv * 2))),
+               (b + "attn_output.weight", [D, nh * 2], 0, f32(np.zeros(nh * 2 * D))),
+               (b + "post_attention_norm.weight", [D], 0, f32(np.ones(D))),
+               (b + "ffn_gate_shexp.weight", [H, D], 12, w["gate_shexp"].tobytes()),
+               (b + "ffn_up_shexp.weight", [H, D], 12, w["up_shexp"].tobytes()),
+               (b + "ffn_down_shexp.weight", [D, H], 14, w["down_shexp"].tobytes()),
+               (b + "ffn_gate_inp.weight", [E, D], 0, w["router"].tobytes()),
+               (b + "ffn_gate_exps.weight", [D, H, E], 12, w["gate_exps"].tobytes()),
+               (b + "ffn_up_exps.weight", [D, H, E], 12, w["up_exps"].tobytes()),
+               (b + "ffn_down_exps.weight", [H, D, E], 14, w["down_exps"].tobytes()),
+               ("output.weight", [V, D], 0, f32(np.eye(D)))]
+    params = {"block_count": (T_U32, 1), "embedding_length": (T_U32, D), "attention.head_count": (T_U32, nh),
+              "attention.head_count_kv": (T_U32, nkv), "expert_count": (T_U32, E),
+              "expert_used_count": (T_U32, top_k), "feed_forward_length": (T_U32, H),
+              "expert_feed_forward_length": (T_U32, H), "context_length": (T_U32, 64),
+              "vocab_size": (T_U32, V), "attention.key_length": (T_U32, 2),
+              "attention.value_length": (T_U32, 2), "rope.dimension_count": (T_U32, 2),
+              "rope.freq_base": (T_F32, 10000.0), "full_attention_interval": (T_U32, 1)}
+    write_gguf(path, "qwen2moe", params, tensors)
+    return w, emb
