@@ -536,7 +536,7 @@ def measure_lm_head(ofb, dev, iters=20):
     w = torch.randn(D * V, device=dev) * 0.02
     x = torch.randn(1, D, device=dev)
     out = torch.empty(1, V, device=dev)
-    scratch = torch.empty(V, device=dev)
+    scratch = torch.empty(ofb.sample_scratch(V), device=dev)
     tok = torch.empty(1, dtype=torch.int32, device=dev)
     for _ in range(3):
         ofb._check(ofb.lib.ofb_matvec(ofb._ptr(x), 1, D, V, ofb._ptr(w), 0, ofb._ptr(out), ofb._stream()))

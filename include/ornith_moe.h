@@ -222,9 +222,10 @@ int ofb_matvec(const float *x, int n_tokens, int in_dim, int out_dim, const void
 /* model_sample (model.c:1238-1260) for one row of logits on the device:
  * temperature (when > 0 and != 1), softmax with the host library's expf, and
  * the first index whose cumulative probability reaches r in [0, 1) (the
- * caller's uniform draw). scratch: vocab floats. The sums run in a fixed
+ * caller's uniform draw). scratch: OFB_SAMPLE_SCRATCH(vocab) floats. The sums run in a fixed
  * order (deterministic); the index can differ from the reference's only when
  * r is within ~vocab * 2^-24 of a cumulative boundary. */
+#define OFB_SAMPLE_SCRATCH(vocab) ((vocab) + 2 * (((vocab) + 1023) / 1024))
 int ofb_sample(const float *logits, int vocab, float temperature, float r, float *scratch, uint32_t *token,
                void *stream);
 

@@ -69,6 +69,12 @@ __device__ __forceinline__ void fence_proxy_async_smem() {
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
 
+// Orders this thread's view of global memory (e.g. data acquired from other
+// CTAs) before its later async-proxy (bulk copy) reads of it.
+__device__ __forceinline__ void fence_proxy_async_global() {
+    asm volatile("fence.proxy.async.global;" ::: "memory");
+}
+
 // ---- tagged 64-bit words (value in the low half, tag in the high half) ----
 __device__ __forceinline__ void put_tagged(unsigned long long *p, uint32_t value, uint32_t tag) {
     const unsigned long long v = ((unsigned long long)tag << 32) | value;
@@ -79,6 +85,39 @@ __device__ __forceinline__ unsigned long long ld_relaxed64(const unsigned long l
     asm volatile("ld.relaxed.gpu.global.b64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
     return v;
 }
+// Two consecutive tagged words (16-byte aligned) in one access; each 64-bit
+// element is single-copy atomic on its own.
+__device__ __forceinline__ void ld_relaxed64x2(const unsigned long long *p, unsigned long long &a,
+                                               unsigned long long &b) {
+    asm volatile("ld.relaxed.gpu.global.v2.b64 {%0, %1}, [%2];" : "=l"(a), "=l"(b) : "l"(p) : "memory");
+}
+// Polls the pair p[0], p[1] (16-byte aligned) until both tags equal `tag`;
+// false (missing values 0) after `limit_ns`. A warp issuing this on
+// consecutive pairs reads whole lines per instruction.
+__device__ __forceinline__ bool get_tagged2(const unsigned long long *p, uint32_t tag, uint32_t &v0, uint32_t &v1,
+                                            unsigned long long limit_ns) {
+    unsigned long long a, b;
+    ld_relaxed64x2(p, a, b);
+    if ((uint32_t)(a >> 32) != tag || (uint32_t)(b >> 32) != tag) {
+        const unsigned long long t0 = gtime();
+        for (uint32_t i = 0;; i++) {
+            ld_relaxed64x2(p, a, b);
+            if ((uint32_t)(a >> 32) == tag && (uint32_t)(b >> 32) == tag) break;
+            if ((i & 15) == 15) {
+                if (gtime() - t0 > limit_ns) {
+                    v0 = (uint32_t)(a >> 32) == tag ? (uint32_t)a : 0u;
+                    v1 = (uint32_t)(b >> 32) == tag ? (uint32_t)b : 0u;
+                    return false;
+                }
+                __nanosleep(32);
+            }
+        }
+    }
+    v0 = (uint32_t)a;
+    v1 = (uint32_t)b;
+    return true;
+}
+
 // Polls *p until its tag equals `tag`; returns the value, or 0 and sets *failed
 // after `limit_ns`.
 __device__ __forceinline__ uint32_t get_tagged(const unsigned long long *p, uint32_t tag,
@@ -141,6 +180,11 @@ __device__ __forceinline__ bool get_tagged_n(const unsigned long long *p, uint32
 __device__ __forceinline__ void count_add(unsigned *p, unsigned n) {
     __threadfence();
     atomicAdd(p, n);
+}
+// Adds n to *p with release semantics (gpu scope): this thread's earlier
+// stores are visible to a thread that acquires the new value.
+__device__ __forceinline__ void count_add_release(unsigned *p, unsigned n) {
+    asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(p), "r"(n) : "memory");
 }
 // Waits until the counter has reached `target` (wrap-around aware); the
 // acquire orders the caller's later loads after the counted stores.

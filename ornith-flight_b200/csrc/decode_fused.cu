@@ -62,6 +62,7 @@ constexpr int FD_THREADS = 512;
 constexpr int FD_WARPS = FD_THREADS / 32;
 constexpr int FD_PER_LANE = 8;                            // selection: experts per lane (E <= 256)
 constexpr unsigned long long FD_WAIT_NS = 500000000ull;  // 0.5 s per wait
+constexpr int FD_H_PAIRS = 4;    // tagged h pairs in flight per thread per pass
 constexpr double FD_MARGIN = 0x1.0p-14;                   // certificate margin (as route_fast.cu)
 
 // Error bits recorded in sync[2] (read by ofb_workspace_check).
@@ -86,7 +87,7 @@ struct FusedDecodeArgs {
 // Optional per-CTA timeline (build with -DOFB_FD_TRACE): globaltimer at each
 // step boundary of the last launch, read back with ofb_debug_fd_trace.
 #ifdef OFB_FD_TRACE
-__device__ unsigned long long g_fd_tr[256][32];
+__device__ unsigned long long g_fd_tr[256][64];
 #define FD_MARK_IF(cond, i) \
     if ((cond) && blockIdx.x < 256) g_fd_tr[blockIdx.x][i] = ax::gtime();
 #else
@@ -127,6 +128,47 @@ __device__ __noinline__ float swiglu_pair(const uint8_t *grow, const uint8_t *ur
     }
     const float g = warp_sum(ag), u = warp_sum(au);
     return silu_ref_d(g) * u;
+}
+
+// Two row pairs at once (rows i and j of the CTA's gate/up copies): the same
+// arithmetic as swiglu_pair per pair, interleaved so one warp has four
+// independent dot products and four independent reductions in flight.
+__device__ __noinline__ float2 swiglu_pair2(const uint8_t *g0, const uint8_t *u0, const uint8_t *g1,
+                                            const uint8_t *u1, const unsigned char *xq, int D, int lane) {
+    const int items = D / 64;
+    const float *qf = reinterpret_cast<const float *>(xq + 2 * D);
+    float ag0 = 0.f, au0 = 0.f, ag1 = 0.f, au1 = 0.f;
+    for (int j = lane; j < items; j += 32) {
+        const int b = j >> 2, c = j & 3;
+        const int e0 = b * QK + c * 64, sb = e0 / 32;
+        uint4 xh[4], xl[4];
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            xh[i] = reinterpret_cast<const uint4 *>(xq + e0)[i];
+            xl[i] = reinterpret_cast<const uint4 *>(xq + D + e0)[i];
+        }
+        const float s_lo = qf[sb], s_hi = qf[sb + 1];
+        const float xs_lo = qf[D / 32 + sb], xs_hi = qf[D / 32 + sb + 1];
+        const uint8_t *rows[4] = {g0, u0, g1, u1};
+        float r[4];
+#pragma unroll
+        for (int m = 0; m < 4; m++) {
+            const uint8_t *bb = rows[m] + b * Q4K_BYTES;
+            const uint4 hd = *reinterpret_cast<const uint4 *>(bb);
+            const uint4 qa = *reinterpret_cast<const uint4 *>(bb + 16 + c * 32);
+            const uint4 qb = *reinterpret_cast<const uint4 *>(bb + 32 + c * 32);
+            r[m] = q4k_item_q(hd, qa, qb, c, xh, xl, s_lo, s_hi, xs_lo, xs_hi);
+        }
+        ag0 += r[0]; au0 += r[1]; ag1 += r[2]; au1 += r[3];
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        ag0 += __shfl_xor_sync(0xffffffffu, ag0, o);
+        au0 += __shfl_xor_sync(0xffffffffu, au0, o);
+        ag1 += __shfl_xor_sync(0xffffffffu, ag1, o);
+        au1 += __shfl_xor_sync(0xffffffffu, au1, o);
+    }
+    return make_float2(silu_ref_d(ag0) * au0, silu_ref_d(ag1) * au1);
 }
 
 // 32-bit shared-memory loads by shared-window address.
@@ -187,6 +229,94 @@ __device__ __forceinline__ void quantize_group(const uint32_t (&v)[16], const HS
     *reinterpret_cast<uint4 *>(s.hl + 16 * g) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
     s.hs[g] = sc;
     s.hsum[g] = sum;
+}
+
+// Quantises one pair of h values held by lane L of a warp (words 2L, 2L+1 of
+// the warp's 64 consecutive words) exactly as quantize_group does: a 16-word
+// scale group is 8 adjacent lanes, combined by shuffles. Word w belongs to
+// slot slot0 + w / H at position w % H. Every lane of the warp must call this;
+// lanes with valid == false only take part in the shuffles.
+__device__ __forceinline__ void quant_pair(uint32_t v0, uint32_t v1, bool valid, int w, uint8_t *hqb, int H,
+                                           int slot0) {
+    const float f0 = __uint_as_float(v0), f1 = __uint_as_float(v1);
+    float m = fmaxf(fabsf(f0), fabsf(f1));
+    m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 1));
+    m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 2));
+    m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 4));
+    const float inv = (m > 0.f) ? 32767.0f / m : 0.f;
+    const int i0 = __float2int_rn(f0 * inv), i1 = __float2int_rn(f1 * inv);
+    int sum = i0 + i1;
+    sum += __shfl_xor_sync(0xffffffffu, sum, 1);
+    sum += __shfl_xor_sync(0xffffffffu, sum, 2);
+    sum += __shfl_xor_sync(0xffffffffu, sum, 4);
+    if (valid) {
+        const int k = slot0 + w / H, pos = w - (w / H) * H, g = pos >> 4;
+        const HSlot s = hslot(hqb, H, k);
+        *reinterpret_cast<uint16_t *>(s.hh + pos) = (uint16_t)(((i0 >> 8) & 0xFF) | (((i1 >> 8) & 0xFF) << 8));
+        *reinterpret_cast<uint16_t *>(s.hl + pos) = (uint16_t)((i0 & 0xFF) | ((i1 & 0xFF) << 8));
+        if ((pos & 15) == 0) {
+            s.hs[g] = m / 32767.0f;
+            s.hsum[g] = sum;
+        }
+    }
+}
+
+// Reads the tagged h words [0, nw) of src with nthr threads (this one is t)
+// as consecutive 16-byte pairs, so each warp load covers whole lines; in each
+// pass a thread's NP loads are all in flight before any is waited on. Then
+// quantises them (quant_pair). Returns false if a wait expired.
+template <int NP>
+__device__ __noinline__ bool read_quant_h(const unsigned long long *src, int nw, uint32_t tag, uint8_t *hqb,
+                                             int H, int slot0, int t, int nthr) {
+    bool ok = true;
+    for (int base = 0; base < nw; base += NP * 2 * nthr) {
+        unsigned long long a[NP], b[NP];
+#pragma unroll
+        for (int j = 0; j < NP; j++) {
+            const int w = base + 2 * t + j * 2 * nthr;
+            a[j] = b[j] = 0;
+            if (w < nw) ax::ld_relaxed64x2(src + w, a[j], b[j]);
+        }
+#pragma unroll
+        for (int j = 0; j < NP; j++) {
+            const int w = base + 2 * t + j * 2 * nthr;
+            if (w >= nw) continue;
+            uint32_t v0 = (uint32_t)a[j], v1 = (uint32_t)b[j];
+            if ((uint32_t)(a[j] >> 32) != tag || (uint32_t)(b[j] >> 32) != tag)
+                ok = ax::get_tagged2(src + w, tag, v0, v1, FD_WAIT_NS) && ok;
+            a[j] = v0;
+            b[j] = v1;
+        }
+#pragma unroll
+        for (int j = 0; j < NP; j++) {
+            const int w = base + 2 * t + j * 2 * nthr;
+            if (base + j * 2 * nthr < nw)  // warp-uniform
+                quant_pair((uint32_t)a[j], (uint32_t)b[j], w < nw, w, hqb, H, slot0);
+        }
+    }
+    return ok;
+}
+
+// read_quant_h on a shared-memory copy (sm) of the tagged words at src: a
+// word whose tag is not the launch's is polled again from src.
+__device__ __noinline__ bool read_quant_copy(const unsigned long long *sm, const unsigned long long *src, int nw,
+                                             uint32_t tag, uint8_t *hqb, int H, int slot0, int t, int nthr) {
+    bool ok = true;
+    for (int w = 2 * t; w - 2 * t < nw; w += 2 * nthr) {
+        const bool valid = w < nw;
+        uint32_t v0 = 0, v1 = 0;
+        if (valid) {
+            const ulonglong2 q = *reinterpret_cast<const ulonglong2 *>(sm + w);
+            v0 = (uint32_t)q.x;
+            v1 = (uint32_t)q.y;
+            if ((uint32_t)(q.x >> 32) != tag || (uint32_t)(q.y >> 32) != tag)
+                ok = ax::get_tagged2(src + w, tag, v0, v1, FD_WAIT_NS) && ok;
+        }
+        FD_MARK_IF(t == 0 && w < 8 * nthr, 41 + w / (2 * nthr))
+        quant_pair(v0, v1, valid, w, hqb, H, slot0);
+        FD_MARK_IF(t == 0 && w < 8 * nthr, 45 + w / (2 * nthr))
+    }
+    return ok;
 }
 
 // Dot product of one half block (128 weights) of a Q6_K row in shared memory
@@ -260,7 +390,8 @@ __global__ void __launch_bounds__(FD_THREADS, 1) decode_fused_kernel(FusedDecode
     float *ysp = reinterpret_cast<float *>(sm + P.o_ys);  // [K+1][ngc*dg][NHB] partial dots
     uint64_t *bars = reinterpret_cast<uint64_t *>(sm + P.o_bar);
     uint64_t *mb_pre = bars, *mb_x = bars + 1, *mb_up = bars + 2, *mb_dn = bars + 4;  // mb_dn[K]
-    const int nbars = 4 + K;
+    uint64_t *mb_h = bars + 4 + K;  // the copy of every routed h (step 4)
+    const int nbars = 5 + K;
     const size_t sdn = (size_t)P.ngc * P.dg * rb6;  // shared bytes per slot of down rows
     const int rows_cap = P.ngc * P.dg;
     auto dnp = [&](int k) { return dn + (size_t)(k == K ? 0 : k + 1) * sdn; };
@@ -272,7 +403,6 @@ __global__ void __launch_bounds__(FD_THREADS, 1) decode_fused_kernel(FusedDecode
     __shared__ float s_max, s_sum, s_gsc;
     __shared__ double s_lo;
     __shared__ uint32_t s_err;
-    __shared__ int s_next[2];
 
     // ---- work shares of this CTA ----
     const int nrows = E + a.use_gate;
@@ -443,10 +573,10 @@ __global__ void __launch_bounds__(FD_THREADS, 1) decode_fused_kernel(FusedDecode
         if (tid == 0 && !ax::wait_count(a.sync + 3, tag * (unsigned)E, FD_WAIT_NS)) tag_fail = true;
         asm volatile("bar.sync 1, %0;" ::"r"(GRP) : "memory");
         for (int e = tid; e < E; e += GRP) {
-            uint32_t v[2];
-            if (!ax::get_tagged_n<2>(a.cand + 2 * e, tag, v, FD_WAIT_NS)) tag_fail = true;
-            Lf[e] = f_of(v[0]);
-            Bf[e] = f_of(v[1]);
+            uint32_t v0, v1;
+            if (!ax::get_tagged2(a.cand + 2 * e, tag, v0, v1, FD_WAIT_NS)) tag_fail = true;
+            Lf[e] = f_of(v0);
+            Bf[e] = f_of(v1);
         }
         ax::fence_proxy_async_smem();  // the router partials' area is refilled by bulk copies
         asm volatile("bar.sync 1, %0;" ::"r"(GRP) : "memory");
@@ -585,7 +715,15 @@ __global__ void __launch_bounds__(FD_THREADS, 1) decode_fused_kernel(FusedDecode
                 }
             }
             FD_MARK_IF(gt == 0, 5)
+            // every CTA's shared h, quantised into slot K (used with the
+            // routed slots' down rows in step 4)
+            if (gt == 0 && !ax::wait_count(a.sync + 4 + K, tag * (unsigned)H, FD_WAIT_NS)) tag_fail = true;
+            asm volatile("bar.sync 2, %0;" ::"r"(GRP) : "memory");
+            FD_MARK_IF(gt == 0, 29)
+            if (!read_quant_h<FD_H_PAIRS>(a.hll + (size_t)K * H, H, tag, hqb, H, K, gt, GRP)) tag_fail = true;
+            FD_MARK_IF(gt == 0, 30)
         }
+        if (gt == 0) s_gsc = a.use_gate ? f_of(ax::get_tagged(a.cand + 2 * E, tag, FD_WAIT_NS, tag_fail)) : 1.0f;
     }
     __syncthreads();
     FD_MARK(7)
@@ -727,71 +865,86 @@ __global__ void __launch_bounds__(FD_THREADS, 1) decode_fused_kernel(FusedDecode
     const uint32_t par = s_par;
     FD_MARK(19)
 
-    // ---- step 3: routed h rows as their gate/up rows land; meanwhile the
-    // upper half of the warps runs the shared expert's down rows (resident
-    // since step 0) and then joins. Pairs are taken from a shared counter. ----
-    if (tid == 0) { s_next[0] = 0; s_next[1] = 0; }
-    __syncthreads();
-    if (a.has_shared && wid >= FD_WARPS / 2) {
-        const int gt = tid - FD_THREADS / 2;
-        const HSlot hs = hslot(hqb, H, K);
-        if (gt == 0 && !ax::wait_count(a.sync + 4 + K, tag * (unsigned)H, FD_WAIT_NS)) tag_fail = true;
-        asm volatile("bar.sync 2, %0;" ::"r"(FD_THREADS / 2) : "memory");
-        for (int g = gt; g < H / 16; g += FD_THREADS / 2) {
-            uint32_t v[16];
-            if (!ax::get_tagged_n<16>(a.hll + (size_t)K * H + 16 * g, tag, v, FD_WAIT_NS)) tag_fail = true;
-            quantize_group(v, hs, g);
-        }
-        asm volatile("bar.sync 2, %0;" ::"r"(FD_THREADS / 2) : "memory");
-        const uint32_t base = ax::smem_u32(dnp(K));
-        for (int t = gt; t < nrow_out * NHB; t += FD_THREADS / 2) {
-            const int r = t / NHB, hb = t - r * NHB;
-            ysp[((size_t)K * rows_cap + r) * NHB + hb] =
-                q6k_half_dot(base + r * rb6 + (hb >> 1) * Q6K_BYTES, hb & 1, hs, hb);
-        }
-        FD_MARK_IF(gt == 0, 25)
-    }
+    // ---- step 3: routed h rows as their gate/up rows land, on every warp:
+    // warp w takes pairs w and w + FD_WARPS together, then w + 2 FD_WARPS ...
+    // (two independent rows per warp hide the dot / reduction latency) ----
     {
+        const int np = u1 - u0;
+        const int seg_b = (slot_first + 1) * H - u0;  // pairs at or past this index are in slot_first + 1
         int ncnt[2] = {0, 0};
-        for (int sgi = 0; sgi < 2; sgi++) {
-            const int pa = sgi == 0 ? u0 : max(u0, (slot_first + 1) * H), pb = sgi == 0 ? min(u1, (slot_first + 1) * H) : u1;
-            if (pb <= pa) continue;
-            if (!ax::mbar_wait(mb_up + sgi, par, FD_WAIT_NS)) copy_fail = true;
-            for (;;) {
-                int p = 0;
-                if (lane == 0) p = pa + atomicAdd(&s_next[sgi], 1);
-                p = __shfl_sync(0xffffffffu, p, 0);
-                if (p >= pb) break;
-                const int i = p - u0;
+        for (int i = wid; i < np; i += 2 * FD_WARPS) {
+            const int j = i + FD_WARPS;
+            const bool two = j < np;
+            const int si = i < seg_b ? 0 : 1, sj = j < seg_b ? 0 : 1;
+            if (!ax::mbar_wait(mb_up + si, par, FD_WAIT_NS)) copy_fail = true;
+            if (two && !ax::mbar_wait(mb_up + sj, par, FD_WAIT_NS)) copy_fail = true;
+            FD_MARK_IF(tid == 0 && i == 0, 28)
+            if (two) {
+                const float2 h = swiglu_pair2(upg + (size_t)i * rb4, upu + (size_t)i * rb4, upg + (size_t)j * rb4,
+                                              upu + (size_t)j * rb4, xq, D, lane);
+                if (lane == 0) {
+                    ax::put_tagged(a.hll + u0 + i, u_of(h.x), tag);
+                    ax::put_tagged(a.hll + u0 + j, u_of(h.y), tag);
+                }
+                ncnt[si]++;
+                ncnt[sj]++;
+            } else {
                 const float h = swiglu_pair(upg + (size_t)i * rb4, upu + (size_t)i * rb4, xq, D, lane);
-                if (lane == 0) ax::put_tagged(a.hll + p, u_of(h), tag);
-                ncnt[sgi]++;
+                if (lane == 0) ax::put_tagged(a.hll + u0 + i, u_of(h), tag);
+                ncnt[si]++;
             }
+            FD_MARK_IF(tid == 0 && i == 0, 8)
         }
+        FD_MARK(10)
         // one fence per warp, then the counts of the h rows it wrote, per slot
         if (lane == 0 && ncnt[0] + ncnt[1]) {
+#ifdef OFB_FD_RELEASE
+            if (ncnt[0]) ax::count_add_release(a.sync + 4 + slot_first, (unsigned)ncnt[0]);
+            if (ncnt[1]) ax::count_add_release(a.sync + 4 + slot_first + 1, (unsigned)ncnt[1]);
+        }
+        if (false) {
+#endif
             __threadfence();
+            FD_MARK(34)
             if (ncnt[0]) atomicAdd(a.sync + 4 + slot_first, (unsigned)ncnt[0]);
             if (ncnt[1]) atomicAdd(a.sync + 4 + slot_first + 1, (unsigned)ncnt[1]);
         }
     }
     FD_MARK(9)
-    // ---- step 4: every routed slot's h, quantised; y of my rows ----
-    // thread k waits for slot k's count (the waits overlap)
-    if (tid < K && !ax::wait_count(a.sync + 4 + tid, tag * (unsigned)H, FD_WAIT_NS)) tag_fail = true;
+#ifdef OFB_FD_TRACE
     __syncthreads();
-    for (int t = tid; t < K * (H / 16); t += FD_THREADS) {
-        const int k = t / (H / 16), g = t - k * (H / 16);
-        uint32_t v[16];
-        if (!ax::get_tagged_n<16>(a.hll + (size_t)k * H + 16 * g, tag, v, FD_WAIT_NS)) tag_fail = true;
-        quantize_group(v, hslot(hqb, H, k), g);
+    FD_MARK(27)
+#endif
+    // ---- step 4: every routed slot's h, quantised; y of my rows ----
+    // thread k waits for slot k's count (the waits overlap); then one bulk
+    // copy brings every routed h word into the (consumed) gate/up area
+    if (tid < K && !ax::wait_count(a.sync + 4 + tid, tag * (unsigned)H, FD_WAIT_NS)) tag_fail = true;
+    ax::fence_proxy_async_smem();  // the gate/up rows read above are overwritten by the copy
+    __syncthreads();
+    FD_MARK(26)
+    const unsigned long long *hsm = reinterpret_cast<const unsigned long long *>(upg);
+    if (P.hcopy) {
+        if (tid == 0) {
+            ax::fence_proxy_async_global();  // the acquired h words, seen by the copy
+            ax::mbar_arrive_expect(mb_h, (uint32_t)K * H * 8);
+            ax::bulk_g2s(upg, a.hll, (uint32_t)K * H * 8, mb_h);
+        }
+        if (!ax::mbar_wait(mb_h, 0, FD_WAIT_NS)) copy_fail = true;
+        FD_MARK(38)
+        if (!read_quant_copy(hsm, a.hll, K * H, tag, hqb, H, 0, tid, FD_THREADS)) tag_fail = true;
+    } else {
+        if (tid == 0) ax::mbar_arrive_expect(mb_h, 0);
+        if (!read_quant_h<FD_H_PAIRS>(a.hll, K * H, tag, hqb, H, 0, tid, FD_THREADS)) tag_fail = true;
     }
-    if (tid == 0) s_gsc = a.use_gate ? f_of(ax::get_tagged(a.cand + 2 * E, tag, FD_WAIT_NS, tag_fail)) : 1.0f;
+    FD_MARK(31)
     __syncthreads();
     FD_MARK(11)
-    for (int t = tid; t < K * nrow_out * NHB; t += FD_THREADS) {
+    // the routed slots and (slot K) the shared expert: one task per thread at
+    // the BASELINE shape
+    const int nslot = K + (a.has_shared ? 1 : 0);
+    for (int t = tid; t < nslot * nrow_out * NHB; t += FD_THREADS) {
         const int k = t / (nrow_out * NHB), rem = t - k * nrow_out * NHB, r = rem / NHB, hb = rem - r * NHB;
-        if (!ax::mbar_wait(mb_dn + k, par, FD_WAIT_NS)) copy_fail = true;
+        if (k < K && !ax::mbar_wait(mb_dn + k, par, FD_WAIT_NS)) copy_fail = true;
         const uint32_t base = ax::smem_u32(dnp(k));
         ysp[((size_t)k * rows_cap + r) * NHB + hb] =
             q6k_half_dot(base + r * rb6 + (hb >> 1) * Q6K_BYTES, hb & 1, hslot(hqb, H, k), hb);
@@ -836,7 +989,7 @@ __global__ void __launch_bounds__(FD_THREADS, 1) decode_fused_kernel(FusedDecode
         if (s_err) {
             atomicOr(&a.sync[2], s_err);
             // let every copy this CTA issued land before its shared memory goes
-            for (int i = 0; i < nbars; i++) ax::mbar_wait(bars + i, i < 2 ? 0 : par, FD_WAIT_NS);
+            for (int i = 0; i < nbars; i++) ax::mbar_wait(bars + i, (i < 2 || i == nbars - 1) ? 0 : par, FD_WAIT_NS);
         }
         __threadfence();
         if (atomicAdd(&a.sync[1], 1u) == (unsigned)G - 1) {
@@ -902,7 +1055,9 @@ bool fused_plan(const ofb_moe_config *cfg, bool use_gate, int G, FusedPlan &p) {
     p.o_hq = take((size_t)(K + 1) * (2 * H + H / 2));
     p.o_sel = take((size_t)2 * E * 4);
     p.o_ys = take((size_t)(K + 1) * rows_cap * nhb * 4);
-    p.o_bar = take((size_t)(4 + K) * 8);
+    p.o_bar = take((size_t)(5 + K) * 8);
+    // step 4 copies every routed h word (tagged, 8 bytes) into the gate/up area
+    p.hcopy = (size_t)K * H * 8 <= up;
     p.total = (uint32_t)off;
     return p.total <= 227 * 1024;
 }

@@ -17,7 +17,8 @@
 // logits: divide by the temperature (when > 0 and != 1), softmax with the
 // host library's expf, and the first index whose cumulative probability
 // reaches r. The reference sums the 248k probabilities sequentially; here the
-// sums are a fixed-order tree (deterministic, not bit-identical), so the
+// sums are fixed-order trees and scans over 1024-logit chunks spread over the
+// whole GPU (deterministic, not bit-identical), so the
 // chosen index can differ from the reference's only when r lies within the
 // rounding difference of two cumulative sums (about vocab * 2^-24).
 #include "common.cuh"
@@ -63,73 +64,165 @@ __global__ void __launch_bounds__(MV_THREADS) matvec_kernel(const float *__restr
 }
 
 // ---- sampling ----------------------------------------------------------------
-constexpr int SM_THREADS = 1024;
+// Three launches over chunks of SC_CHUNK logits (one chunk per CTA, so the
+// whole GPU streams the row): (1) divided logits and chunk maxima, (2) e_i =
+// expf(l_i - max) and chunk sums, (3) one CTA: the total, the first chunk
+// whose cumulative probability reaches r, then the first index inside it.
+constexpr int SC_THREADS = 256;
+constexpr int SC_CHUNK = 1024;
+constexpr int SC_PER = SC_CHUNK / SC_THREADS;
+constexpr int SP_THREADS = 1024;
 
-__global__ void __launch_bounds__(SM_THREADS) sample_kernel(const float *__restrict__ logits, int V, float temp,
-                                                            float r, float *__restrict__ scratch,
-                                                            uint32_t *__restrict__ token) {
-    __shared__ float red[SM_THREADS / 32];
-    __shared__ float s_max, s_sum;
-    __shared__ float part[SM_THREADS];
-    __shared__ int s_tok;
-    const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
-    const bool div = temp > 0.0f && temp != 1.0f;
-    // max of the (divided) logits
-    float m = -INFINITY;
-    for (int i = tid; i < V; i += SM_THREADS) {
-        const float l = div ? __fdiv_rn(logits[i], temp) : logits[i];
-        scratch[i] = l;
-        m = fmaxf(m, l);
-    }
+__device__ __forceinline__ float block_max_256(float m, float *red) {
+    const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
     if (lane == 0) red[wid] = m;
     __syncthreads();
-    if (tid == 0) {
-        float mm = red[0];
-        for (int w = 1; w < SM_THREADS / 32; w++) mm = fmaxf(mm, red[w]);
-        s_max = mm;
-    }
-    __syncthreads();
-    // e_i = expf(l_i - max) (the host library's function); thread tid owns the
-    // contiguous chunk [tid*per, tid*per + per), summed in order
-    const int per = (V + SM_THREADS - 1) / SM_THREADS;
-    const int a = min(V, tid * per), b = min(V, a + per);
-    float s = 0.0f;
-    for (int i = a; i < b; i++) {
-        const float e = ofb_exact_expf(__fsub_rn(scratch[i], s_max));
-        scratch[i] = e;
-        s = __fadd_rn(s, e);
-    }
-    part[tid] = s;
-    __syncthreads();
-    if (tid == 0) {
-        float tot = 0.0f;
-        for (int w = 0; w < SM_THREADS; w++) tot = __fadd_rn(tot, part[w]);
-        s_sum = tot;
-        s_tok = V - 1;
-    }
-    __syncthreads();
-    // cumulative probability: chunk prefix (one thread), then inside the
-    // chunk; the first index whose cumulative sum reaches r
-    if (tid == 0) {
-        float c = 0.0f;
-        for (int w = 0; w < SM_THREADS; w++) {
-            const float nc = __fadd_rn(c, __fdiv_rn(part[w], s_sum));
-            part[w] = c;  // exclusive prefix of chunk w
-            c = nc;
+    float r = red[0];
+#pragma unroll
+    for (int w = 1; w < SC_THREADS / 32; w++) r = fmaxf(r, red[w]);
+    return r;
+}
+
+__global__ void __launch_bounds__(SC_THREADS) sample_max_kernel(const float *__restrict__ logits, int V, float temp,
+                                                                float *__restrict__ scratch,
+                                                                float *__restrict__ cmax) {
+    __shared__ float red[SC_THREADS / 32];
+    const bool div = temp > 0.0f && temp != 1.0f;
+    const int base = blockIdx.x * SC_CHUNK;
+    float m = -INFINITY;
+#pragma unroll
+    for (int j = 0; j < SC_PER; j++) {
+        const int i = base + j * SC_THREADS + threadIdx.x;
+        if (i < V) {
+            const float l = div ? __fdiv_rn(logits[i], temp) : logits[i];
+            scratch[i] = l;
+            m = fmaxf(m, l);
         }
     }
-    __syncthreads();
-    float cum = part[tid];
-    int found = 0x7fffffff;
-    for (int i = a; i < b; i++) {
-        cum = __fadd_rn(cum, __fdiv_rn(scratch[i], s_sum));
-        if (cum >= r) { found = i; break; }
+    m = block_max_256(m, red);
+    if (threadIdx.x == 0) cmax[blockIdx.x] = m;
+}
+
+__global__ void __launch_bounds__(SC_THREADS) sample_exp_kernel(int V, int NB, float *__restrict__ scratch,
+                                                                const float *__restrict__ cmax,
+                                                                float *__restrict__ csum) {
+    __shared__ float red[SC_THREADS / 32];
+    float m = -INFINITY;
+    for (int b = threadIdx.x; b < NB; b += SC_THREADS) m = fmaxf(m, cmax[b]);
+    m = block_max_256(m, red);
+    __syncthreads();  // red is reused below
+    const int base = blockIdx.x * SC_CHUNK;
+    float s = 0.0f;
+#pragma unroll
+    for (int j = 0; j < SC_PER; j++) {
+        const int i = base + j * SC_THREADS + threadIdx.x;
+        if (i < V) {
+            const float e = ofb_exact_expf(__fsub_rn(scratch[i], m));
+            scratch[i] = e;
+            s = __fadd_rn(s, e);
+        }
     }
-    atomicMin(&s_tok, found);
+    // fixed-order tree: lanes by xor, then warps in order
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) s = __fadd_rn(s, __shfl_xor_sync(0xffffffffu, s, o));
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = s;
     __syncthreads();
-    if (tid == 0) *token = (uint32_t)s_tok;
+    if (threadIdx.x == 0) {
+        float t = 0.0f;
+        for (int w = 0; w < SC_THREADS / 32; w++) t = __fadd_rn(t, red[w]);
+        csum[blockIdx.x] = t;
+    }
+}
+
+// Inclusive scan of v over the 1024 threads (warp shuffles, then warp totals);
+// returns this thread's inclusive value and the block total in *total.
+__device__ __forceinline__ float block_scan_1024(float v, float *wsum, float *total) {
+    const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const float u = __shfl_up_sync(0xffffffffu, v, o);
+        if (lane >= o) v = __fadd_rn(v, u);
+    }
+    if (lane == 31) wsum[wid] = v;
+    __syncthreads();
+    if (wid == 0) {
+        float w = wsum[lane];
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const float u = __shfl_up_sync(0xffffffffu, w, o);
+            if (lane >= o) w = __fadd_rn(w, u);
+        }
+        wsum[lane] = w;
+    }
+    __syncthreads();
+    const float r = wid ? __fadd_rn(v, wsum[wid - 1]) : v;
+    *total = wsum[31];
+    __syncthreads();  // wsum is reused by the next call
+    return r;
+}
+
+__global__ void __launch_bounds__(SP_THREADS) sample_pick_kernel(int V, int NB, float r,
+                                                                 const float *__restrict__ scratch,
+                                                                 const float *__restrict__ csum,
+                                                                 uint32_t *__restrict__ token) {
+    __shared__ float red[SP_THREADS / 32];
+    __shared__ float s_sum;
+    __shared__ int s_hit;
+    const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
+    float s = 0.0f;
+    for (int b = tid; b < NB; b += SP_THREADS) s = __fadd_rn(s, csum[b]);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) s = __fadd_rn(s, __shfl_xor_sync(0xffffffffu, s, o));
+    if (lane == 0) red[wid] = s;
+    __syncthreads();
+    if (tid == 0) {
+        float t = 0.0f;
+        for (int w = 0; w < SP_THREADS / 32; w++) t = __fadd_rn(t, red[w]);
+        s_sum = t;
+        s_hit = 0x7fffffff;
+    }
+    __syncthreads();
+    const float sum = s_sum;
+    // the first chunk whose cumulative probability reaches r
+    float carry = 0.0f, prefix = 0.0f;
+    int chunk = -1;
+    for (int b0 = 0; b0 < NB; b0 += SP_THREADS) {
+        const int b = b0 + tid;
+        const float v = b < NB ? __fdiv_rn(csum[b], sum) : 0.0f;
+        float tot;
+        const float inc = __fadd_rn(carry, block_scan_1024(v, red, &tot));
+        if (b < NB && inc >= r) atomicMin(&s_hit, b);
+        __syncthreads();
+        if (s_hit != 0x7fffffff) {
+            chunk = s_hit;
+            if (b == chunk) red[0] = __fsub_rn(inc, v);  // exclusive prefix of the chunk
+            __syncthreads();
+            prefix = red[0];
+            __syncthreads();
+            break;
+        }
+        carry = __fadd_rn(carry, tot);
+    }
+    if (chunk < 0) {  // r above every cumulative sum: the reference's last index
+        if (tid == 0) *token = (uint32_t)(V - 1);
+        return;
+    }
+    if (tid == 0) s_hit = 0x7fffffff;
+    __syncthreads();
+    const int i = chunk * SC_CHUNK + tid;
+    const float v = i < V ? __fdiv_rn(scratch[i], sum) : 0.0f;
+    float tot;
+    const float inc = __fadd_rn(prefix, block_scan_1024(v, red, &tot));
+    if (i < V && inc >= r) atomicMin(&s_hit, i);
+    __syncthreads();
+    if (tid == 0) {
+        // rounding between the chunk-level and element-level sums can leave r
+        // just above the chunk's last element: take that element
+        const int last = min(V, (chunk + 1) * SC_CHUNK) - 1;
+        *token = (uint32_t)(s_hit != 0x7fffffff ? s_hit : last);
+    }
 }
 
 }  // namespace ofb
@@ -187,8 +280,14 @@ extern "C" int ofb_matvec(const float *x, int n_tokens, int in_dim, int out_dim,
 extern "C" int ofb_sample(const float *logits, int vocab, float temperature, float r, float *scratch,
                           uint32_t *token, void *stream) {
     if (!logits || !scratch || !token || vocab < 1) { set_error("ofb_sample: bad arguments"); return OFB_EINVAL; }
-    sample_kernel<<<1, SM_THREADS, 0, static_cast<cudaStream_t>(stream)>>>(logits, vocab, temperature, r, scratch,
-                                                                           token);
-    OFB_CHECK_LAUNCH("ofb_sample");
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    const int NB = (vocab + SC_CHUNK - 1) / SC_CHUNK;
+    float *cmax = scratch + vocab, *csum = cmax + NB;
+    sample_max_kernel<<<NB, SC_THREADS, 0, s>>>(logits, vocab, temperature, scratch, cmax);
+    OFB_CHECK_LAUNCH("ofb_sample max");
+    sample_exp_kernel<<<NB, SC_THREADS, 0, s>>>(vocab, NB, scratch, cmax, csum);
+    OFB_CHECK_LAUNCH("ofb_sample exp");
+    sample_pick_kernel<<<1, SP_THREADS, 0, s>>>(vocab, NB, r, scratch, csum, token);
+    OFB_CHECK_LAUNCH("ofb_sample pick");
     return OFB_OK;
 }

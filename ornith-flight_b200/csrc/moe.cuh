@@ -107,6 +107,7 @@ __host__ __device__ inline size_t xq_stride(int D) { return (size_t)2 * D + (siz
 struct FusedPlan {
     int G, rmax, shp, upc, ngc, dg;
     uint32_t o_x, o_xq, o_rr, o_shu, o_dn, o_up, o_hq, o_sel, o_ys, o_bar, total;
+    bool hcopy;  // step 4 bulk-copies the routed h words into the gate/up area
 };
 bool fused_plan(const ofb_moe_config *cfg, bool use_gate, int grid, FusedPlan &p);
 int launch_decode_fused(const ofb_moe_config *cfg, const ofb_moe_weights *wt, const float *x, const float *resid,

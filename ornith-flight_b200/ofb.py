@@ -182,8 +182,14 @@ def matvec(x: torch.Tensor, w: torch.Tensor, w_type: int, out_dim: int, stream=N
     return out
 
 
+def sample_scratch(vocab: int) -> int:
+    """Floats of scratch ofb_sample needs (OFB_SAMPLE_SCRATCH)."""
+    return vocab + 2 * ((vocab + 1023) // 1024)
+
+
 def sample(logits: torch.Tensor, temperature: float, r: float, stream=None) -> int:
-    scratch = torch.empty_like(logits)
+    V = logits.numel()
+    scratch = torch.empty(sample_scratch(V), dtype=torch.float32, device=logits.device)
     tok = torch.empty(1, dtype=torch.int32, device=logits.device)
     _check(lib.ofb_sample(_ptr(logits), logits.numel(), temperature, r, _ptr(scratch), _ptr(tok), _stream(stream)))
     return int(tok.item())

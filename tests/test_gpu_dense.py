@@ -68,6 +68,24 @@ def test_sample_matches_reference_cumulative_rule(ofb, cuda, temp):
             assert abs(cum[min(tok, want)] - r) < V * 2.0 ** -24, (tok, want, r)
 
 
+@pytest.mark.parametrize("V", [1, 7, 1024, 1025, 3000, 70001])
+def test_sample_ragged_vocab_and_edges(ofb, cuda, V):
+    # chunk edges (1024 logits per CTA), r = 0 (index 0) and r above every
+    # cumulative sum (the reference's vocab - 1)
+    rng = np.random.default_rng(V)
+    logits = (rng.normal(size=V) * 2).astype(np.float32)
+    dl = torch.from_numpy(logits).to(cuda)
+    p = np.exp(logits.astype(np.float64) - logits.max())
+    cum = np.cumsum(p / p.sum())
+    assert ofb.sample(dl, 1.0, 0.0) == 0
+    assert ofb.sample(dl, 1.0, 1.5) == V - 1
+    for r in rng.uniform(0, 1, size=20):
+        tok = ofb.sample(dl, 1.0, float(r))
+        want = min(int(np.searchsorted(cum, r)), V - 1)
+        if tok != want:
+            assert abs(cum[min(tok, want)] - r) < max(V, 1024) * 2.0 ** -24, (tok, want, r)
+
+
 def test_gpu_matmul_quantised_b(ofb, oracle, cuda):
     L = ctypes.CDLL(ofb.LIB_PATH)
     vp, i32, sz = ctypes.c_void_p, ctypes.c_int, ctypes.c_size_t
