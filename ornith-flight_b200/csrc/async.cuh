@@ -138,44 +138,6 @@ __device__ __forceinline__ uint32_t get_tagged(const unsigned long long *p, uint
     }
 }
 
-// N consecutive tagged words p[0..N): all loads are in flight together, then
-// only the words still missing are polled again. Returns false (and sets the
-// missing values to 0) after `limit_ns`.
-template <int N>
-__device__ __forceinline__ bool get_tagged_n(const unsigned long long *p, uint32_t tag, uint32_t (&out)[N],
-                                             unsigned long long limit_ns) {
-    unsigned long long v[N];
-#pragma unroll
-    for (int i = 0; i < N; i++) v[i] = ld_relaxed64(p + i);
-    bool all = true;
-#pragma unroll
-    for (int i = 0; i < N; i++) all = all && (uint32_t)(v[i] >> 32) == tag;
-    if (!all) {
-        const unsigned long long t0 = gtime();
-        for (uint32_t it = 0; !all; it++) {
-            all = true;
-#pragma unroll
-            for (int i = 0; i < N; i++)
-                if ((uint32_t)(v[i] >> 32) != tag) {
-                    v[i] = ld_relaxed64(p + i);
-                    all = all && (uint32_t)(v[i] >> 32) == tag;
-                }
-            if (!all && (it & 15) == 15) {
-                if (gtime() - t0 > limit_ns) {
-#pragma unroll
-                    for (int i = 0; i < N; i++)
-                        if ((uint32_t)(v[i] >> 32) != tag) v[i] = 0;
-                    break;
-                }
-                __nanosleep(32);
-            }
-        }
-    }
-#pragma unroll
-    for (int i = 0; i < N; i++) out[i] = (uint32_t)v[i];
-    return all;
-}
-
 // Publishes this thread's earlier stores (gpu scope), then adds n to *p.
 __device__ __forceinline__ void count_add(unsigned *p, unsigned n) {
     __threadfence();

@@ -8,14 +8,15 @@
 // separate kernels each step pays a launch hand-off and a ramp of its own;
 // here every CTA moves its share of every step's bytes with bulk copies
 // (TMA, cp.async.bulk) into shared memory as soon as it knows the addresses,
-// and CTAs exchange the few values that cross between steps (router logits
-// with bounds, h rows) as tagged 64-bit words in global memory.
+// and CTAs exchange the few values that cross between steps: router logits
+// with bounds (tagged 64-bit words) and the quantised h of each expert (one
+// global image, brought into every CTA by one bulk copy).
 //
-// One CTA per SM (grid = SM count, ~185 KB of shared memory each). CTA c owns
+// One CTA per SM (grid = SM count, ~190 KB of shared memory each). In units
+// of 16-row h groups (fd_share), CTA c owns
 //  * router rows c, c+G, ... (and the shared-expert gate vector as row E),
-//  * shared-expert hidden rows [c*H/G, (c+1)*H/G),
-//  * routed (slot, hidden row) pairs [c*K*H/G, (c+1)*K*H/G) in top-k slot
-//    order, and
+//  * routed (slot, hidden row) pairs [u0, u1) in top-k slot order, and, on
+//    the CTAs with the fewest of those, shared-expert hidden rows [s0, s1),
 //  * output rows [n0, n1) (groups of dg rows, 16-byte aligned Q6_K slabs),
 //    for every expert: the CTA computes y of all K+1 experts for its rows and
 //    combines them in the reference's order, so no cross-CTA reduction.
@@ -24,24 +25,28 @@
 //     bulk copies of the static bytes it owns: router rows, shared gate/up
 //     rows, shared down rows.
 //  1. x (bulk copy) -> 16-bit quantised copy for dp4a; router logits of its
-//     rows in fp64 with a rigorous bound B of the distance to the reference's
-//     sequential fp32 sum (the certified routing of route_fast.cu, restated
-//     per CTA); shared-expert h rows. Both published as tagged words.
+//     rows as float pairs with a rigorous bound B of the distance to the
+//     reference's sequential fp32 sum (the certified routing of
+//     route_fast.cu, restated per CTA), published as tagged words.
 //  2. every CTA reads all (L~, B) and runs the same certified selection
 //     (identical inputs, identical result): top-k indices bit-exact, or the
 //     exact recompute of the uncertain candidates with the reference's chain
-//     and the host C library's expf. Then bulk copies of its routed gate/up
-//     rows and of its output rows' Q6_K slabs of the K routed experts; while
-//     they fly, the shared expert's down rows for its outputs.
-//  3. routed h rows (dp4a on the raw nibbles) -> tagged words; then the h of
-//     every routed expert (polled) -> quantised per 16-element scale group ->
-//     y for its rows -> out = resid + g*y_sh + sum_k w_k y_k.
-// Tags are the launch epoch + 1: a device counter the last CTA to finish
-// advances, read after the dependent-launch wait (which orders it after the
-// previous launch), so stale words from earlier launches never match and the
-// kernel can be replayed (e.g. in a CUDA graph) without host bookkeeping.
-// Every wait (mbarrier or tag) is bounded; on expiry the CTA records an error
-// bit in the workspace and runs to its exit on whatever it has.
+//     and the host C library's expf; then bulk copies of its routed gate/up
+//     rows and of its output rows' Q6_K slabs of the K routed experts.
+//     Meanwhile the other half of the warps quantise x and compute, quantise
+//     and publish the CTA's shared-expert h groups.
+//  3. routed h rows (dp4a on the raw nibbles); each 16-row group quantised
+//     (per-group scale, int8 high / uint8 low planes) by the CTA that
+//     computed it, stored into the global slot image and counted.
+//  4. once every group is counted: one bulk copy of all slots; y for its
+//     rows -> out = resid + g*y_sh + sum_k w_k y_k.
+// Tags and counter targets come from the launch epoch + 1: a device counter
+// the last CTA to finish advances, read after the dependent-launch wait
+// (which orders it after the previous launch), so stale words from earlier
+// launches never match and the kernel can be replayed (e.g. in a CUDA graph)
+// without host bookkeeping. Every wait (mbarrier, tag, counter) is bounded; on
+// expiry the CTA records an error bit in the workspace and runs to its exit on
+// whatever it has.
 //
 // Requirements (checked on the host): T = 1, contiguous layout, router
 // present, E <= 256 (selection by one warp), E + 1 <= 2 * grid, top_k <= 16,
@@ -62,7 +67,7 @@ constexpr int FD_THREADS = 512;
 constexpr int FD_WARPS = FD_THREADS / 32;
 constexpr int FD_PER_LANE = 8;                            // selection: experts per lane (E <= 256)
 constexpr unsigned long long FD_WAIT_NS = 500000000ull;  // 0.5 s per wait
-constexpr int FD_H_PAIRS = 4;    // tagged h pairs in flight per thread per pass
+constexpr int FD_GROUP_BYTES = 48;  // staging of one quantised h group (40 bytes used)
 constexpr double FD_MARGIN = 0x1.0p-14;                   // certificate margin (as route_fast.cu)
 
 // Error bits recorded in sync[2] (read by ofb_workspace_check).
@@ -75,7 +80,7 @@ struct FusedDecodeArgs {
     int D, H, E, K, routing, renorm, has_shared, use_gate;
     double bound_scale, ngam;
     unsigned long long *cand;  // [2E + 1]: (L~, B) per expert, then the shared gate
-    unsigned long long *hll;   // [K + 1][H]: h of each top-k slot, then the shared expert
+    unsigned long long *hll;   // global image of the K + 1 quantised h slots (hslot layout)
     unsigned int *sync;        // [0] epoch, [1] CTAs finished, [2] error bits, [3] router rows
                                // published, [4 + k] h rows published of slot k (k <= K)
     uint32_t *idx_out;
@@ -199,124 +204,49 @@ struct HSlot {
     float *hs;
     int *hsum;
 };
+// Each plane keeps the 128 values of a Q6_K half block in FD_HBS bytes, so
+// the half blocks of a plane start in different shared-memory banks.
+constexpr int FD_HBS = 144;
+__host__ __device__ __forceinline__ int hslot_bytes(int H) { return 2 * (H / 128) * FD_HBS + H / 2; }
 __device__ __forceinline__ HSlot hslot(uint8_t *base, int H, int k) {
-    uint8_t *p = base + (size_t)k * (2 * H + H / 2);
-    return HSlot{reinterpret_cast<int8_t *>(p), p + H, reinterpret_cast<float *>(p + 2 * H),
-                 reinterpret_cast<int *>(p + 2 * H + H / 4)};
+    uint8_t *p = base + (size_t)k * hslot_bytes(H);
+    const int pl = (H / 128) * FD_HBS;
+    return HSlot{reinterpret_cast<int8_t *>(p), p + pl, reinterpret_cast<float *>(p + 2 * pl),
+                 reinterpret_cast<int *>(p + 2 * pl + H / 4)};
 }
-// Quantises the 16 h values of group g (positions 16g..16g+15) into the slot.
-__device__ __forceinline__ void quantize_group(const uint32_t (&v)[16], const HSlot &s, int g) {
-    float m = 0.f;
+// Quantises one 16-row h group (lanes 0..15 hold one value each; lanes
+// 16..31 only take part in the shuffles): h_int = rn(h * 32767 / max|h|),
+// scale max|h| / 32767, and the sum of h_int, as HSlot holds them. Stages
+// it in shared memory and lets lane 0 store it to group g of the global slot
+// image (hslot layout) and count it: its stores, one fence, one add, so the
+// count releases exactly the bytes it covers.
+__device__ __noinline__ void publish_group(float v, uint8_t *stage, uint8_t *slot, int H, int g, unsigned *count,
+                                           int lane) {
+    if (lane >= 16) v = 0.f;
+    float m = fabsf(v);
 #pragma unroll
-    for (int i = 0; i < 16; i++) m = fmaxf(m, fabsf(__uint_as_float(v[i])));
-    const float sc = m / 32767.0f, inv = (m > 0.f) ? 32767.0f / m : 0.f;
-    uint32_t hw[4], lw[4];
-    int sum = 0;
-#pragma unroll
-    for (int q = 0; q < 4; q++) {
-        uint32_t h4 = 0, l4 = 0;
-#pragma unroll
-        for (int i = 0; i < 4; i++) {
-            const int xi = __float2int_rn(__uint_as_float(v[4 * q + i]) * inv);
-            sum += xi;
-            h4 |= ((uint32_t)(xi >> 8) & 0xFFu) << (8 * i);
-            l4 |= ((uint32_t)xi & 0xFFu) << (8 * i);
-        }
-        hw[q] = h4;
-        lw[q] = l4;
-    }
-    *reinterpret_cast<uint4 *>(s.hh + 16 * g) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
-    *reinterpret_cast<uint4 *>(s.hl + 16 * g) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
-    s.hs[g] = sc;
-    s.hsum[g] = sum;
-}
-
-// Quantises one pair of h values held by lane L of a warp (words 2L, 2L+1 of
-// the warp's 64 consecutive words) exactly as quantize_group does: a 16-word
-// scale group is 8 adjacent lanes, combined by shuffles. Word w belongs to
-// slot slot0 + w / H at position w % H. Every lane of the warp must call this;
-// lanes with valid == false only take part in the shuffles.
-__device__ __forceinline__ void quant_pair(uint32_t v0, uint32_t v1, bool valid, int w, uint8_t *hqb, int H,
-                                           int slot0) {
-    const float f0 = __uint_as_float(v0), f1 = __uint_as_float(v1);
-    float m = fmaxf(fabsf(f0), fabsf(f1));
-    m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 1));
-    m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 2));
-    m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 4));
+    for (int o = 1; o < 16; o <<= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
     const float inv = (m > 0.f) ? 32767.0f / m : 0.f;
-    const int i0 = __float2int_rn(f0 * inv), i1 = __float2int_rn(f1 * inv);
-    int sum = i0 + i1;
-    sum += __shfl_xor_sync(0xffffffffu, sum, 1);
-    sum += __shfl_xor_sync(0xffffffffu, sum, 2);
-    sum += __shfl_xor_sync(0xffffffffu, sum, 4);
-    if (valid) {
-        const int k = slot0 + w / H, pos = w - (w / H) * H, g = pos >> 4;
-        const HSlot s = hslot(hqb, H, k);
-        *reinterpret_cast<uint16_t *>(s.hh + pos) = (uint16_t)(((i0 >> 8) & 0xFF) | (((i1 >> 8) & 0xFF) << 8));
-        *reinterpret_cast<uint16_t *>(s.hl + pos) = (uint16_t)((i0 & 0xFF) | ((i1 & 0xFF) << 8));
-        if ((pos & 15) == 0) {
-            s.hs[g] = m / 32767.0f;
-            s.hsum[g] = sum;
-        }
-    }
-}
-
-// Reads the tagged h words [0, nw) of src with nthr threads (this one is t)
-// as consecutive 16-byte pairs, so each warp load covers whole lines; in each
-// pass a thread's NP loads are all in flight before any is waited on. Then
-// quantises them (quant_pair). Returns false if a wait expired.
-template <int NP>
-__device__ __noinline__ bool read_quant_h(const unsigned long long *src, int nw, uint32_t tag, uint8_t *hqb,
-                                             int H, int slot0, int t, int nthr) {
-    bool ok = true;
-    for (int base = 0; base < nw; base += NP * 2 * nthr) {
-        unsigned long long a[NP], b[NP];
+    const int xi = __float2int_rn(v * inv);
+    int sum = xi;
 #pragma unroll
-        for (int j = 0; j < NP; j++) {
-            const int w = base + 2 * t + j * 2 * nthr;
-            a[j] = b[j] = 0;
-            if (w < nw) ax::ld_relaxed64x2(src + w, a[j], b[j]);
-        }
-#pragma unroll
-        for (int j = 0; j < NP; j++) {
-            const int w = base + 2 * t + j * 2 * nthr;
-            if (w >= nw) continue;
-            uint32_t v0 = (uint32_t)a[j], v1 = (uint32_t)b[j];
-            if ((uint32_t)(a[j] >> 32) != tag || (uint32_t)(b[j] >> 32) != tag)
-                ok = ax::get_tagged2(src + w, tag, v0, v1, FD_WAIT_NS) && ok;
-            a[j] = v0;
-            b[j] = v1;
-        }
-#pragma unroll
-        for (int j = 0; j < NP; j++) {
-            const int w = base + 2 * t + j * 2 * nthr;
-            if (base + j * 2 * nthr < nw)  // warp-uniform
-                quant_pair((uint32_t)a[j], (uint32_t)b[j], w < nw, w, hqb, H, slot0);
-        }
+    for (int o = 1; o < 16; o <<= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+    if (lane < 16) {
+        stage[lane] = (uint8_t)((xi >> 8) & 0xFF);
+        stage[16 + lane] = (uint8_t)(xi & 0xFF);
     }
-    return ok;
-}
-
-// read_quant_h on a shared-memory copy (sm) of the tagged words at src: a
-// word whose tag is not the launch's is polled again from src.
-__device__ __noinline__ bool read_quant_copy(const unsigned long long *sm, const unsigned long long *src, int nw,
-                                             uint32_t tag, uint8_t *hqb, int H, int slot0, int t, int nthr) {
-    bool ok = true;
-    for (int w = 2 * t; w - 2 * t < nw; w += 2 * nthr) {
-        const bool valid = w < nw;
-        uint32_t v0 = 0, v1 = 0;
-        if (valid) {
-            const ulonglong2 q = *reinterpret_cast<const ulonglong2 *>(sm + w);
-            v0 = (uint32_t)q.x;
-            v1 = (uint32_t)q.y;
-            if ((uint32_t)(q.x >> 32) != tag || (uint32_t)(q.y >> 32) != tag)
-                ok = ax::get_tagged2(src + w, tag, v0, v1, FD_WAIT_NS) && ok;
-        }
-        FD_MARK_IF(t == 0 && w < 8 * nthr, 41 + w / (2 * nthr))
-        quant_pair(v0, v1, valid, w, hqb, H, slot0);
-        FD_MARK_IF(t == 0 && w < 8 * nthr, 45 + w / (2 * nthr))
+    __syncwarp();
+    if (lane == 0) {
+        const uint4 hh = *reinterpret_cast<const uint4 *>(stage), hl = *reinterpret_cast<const uint4 *>(stage + 16);
+        const int pl = (H / 128) * FD_HBS, at = (g >> 3) * FD_HBS + (g & 7) * 16;
+        *reinterpret_cast<uint4 *>(slot + at) = hh;
+        *reinterpret_cast<uint4 *>(slot + pl + at) = hl;
+        reinterpret_cast<float *>(slot + 2 * pl)[g] = m / 32767.0f;
+        reinterpret_cast<int *>(slot + 2 * pl + H / 4)[g] = sum;
+        __threadfence();
+        atomicAdd(count, 1u);
     }
-    return ok;
+    __syncwarp();
 }
 
 // Dot product of one half block (128 weights) of a Q6_K row in shared memory
@@ -328,8 +258,8 @@ __device__ __noinline__ float q6k_half_dot(uint32_t blk, int half, const HSlot &
     lds_run2<8>(blk + 128 + half * 32, qh);
     lds_run2<2>(blk + 192 + half * 8, sc);
     lds_run2<1>(blk + 208, dw);
-    const int8_t *hh = s.hh + hb * 128;
-    const uint8_t *hl = s.hl + hb * 128;
+    const int8_t *hh = s.hh + hb * FD_HBS;
+    const uint8_t *hl = s.hl + hb * FD_HBS;
     int ahi[8], alo[8];
 #pragma unroll
     for (int i = 0; i < 8; i++) ahi[i] = alo[i] = 0;
@@ -380,7 +310,10 @@ __global__ void __launch_bounds__(FD_THREADS, 1) decode_fused_kernel(FusedDecode
     float *xs = reinterpret_cast<float *>(sm + P.o_x);
     unsigned char *xq = sm + P.o_xq;
     float *rrow = reinterpret_cast<float *>(sm + P.o_rr);
-    uint8_t *shu = sm + P.o_shu;
+    float *hbuf = reinterpret_cast<float *>(sm + P.o_hb);  // h of my row slots (routed, then shared)
+    uint8_t *hst = sm + P.o_hst;                            // [FD_WARPS][FD_GROUP_BYTES] staging
+    uint8_t *hqg = reinterpret_cast<uint8_t *>(a.hll);      // global image of the quantised h slots
+    const int SLOT = hslot_bytes(H);                         // bytes per slot (hslot layout)
     uint8_t *dn = sm + P.o_dn;  // slot K (shared) first, then routed slots 0..K-1
     uint8_t *upg = sm + P.o_up;
     uint8_t *upu = upg + (size_t)P.upc * rb4;
@@ -407,8 +340,11 @@ __global__ void __launch_bounds__(FD_THREADS, 1) decode_fused_kernel(FusedDecode
     // ---- work shares of this CTA ----
     const int nrows = E + a.use_gate;
     const int nr_mine = c < nrows ? (nrows - 1 - c) / G + 1 : 0;  // rows c, c+G, ...
-    const int s0 = (int)((long long)c * H / G), s1 = (int)((long long)(c + 1) * H / G);
-    const int u0 = (int)((long long)c * K * H / G), u1 = (int)((long long)(c + 1) * K * H / G);
+    const int NRG = K * H / 16, NSG = a.has_shared ? H / 16 : 0;  // routed / shared h groups
+    const FdShare share = fd_share(c, G, NRG, NSG);
+    const int u0 = 16 * share.rg0, u1 = 16 * share.rg1;  // routed pairs, top-k slot order
+    const int s0 = 16 * share.sg0, s1 = 16 * share.sg1;  // shared-expert rows
+    const int nrp = u1 - u0;                              // row slots [0, nrp) routed, then shared
     const int NG = D / P.dg;
     const int n0 = (int)((long long)c * NG / G) * P.dg, n1 = (int)((long long)(c + 1) * NG / G) * P.dg;
     const int nrow_out = n1 - n0;
@@ -446,7 +382,6 @@ __global__ void __launch_bounds__(FD_THREADS, 1) decode_fused_kernel(FusedDecode
     }
     __syncthreads();
     pdl_trigger();
-    if (tid == 0 && !a.has_shared && s1 > s0) atomicAdd(a.sync + 4 + K, (unsigned)(s1 - s0));
     if (tid == 0) {
         uint32_t bytes = (uint32_t)nr_mine * D * 4;
         if (a.has_shared) bytes += 2u * (s1 - s0) * rb4 + (uint32_t)nrow_out * rb6;
@@ -458,8 +393,8 @@ __global__ void __launch_bounds__(FD_THREADS, 1) decode_fused_kernel(FusedDecode
         }
         if (a.has_shared) {
             if (s1 > s0) {
-                ax::bulk_g2s(shu, a.gate_sh + (size_t)s0 * rb4, (s1 - s0) * rb4, mb_pre);
-                ax::bulk_g2s(shu + (size_t)P.shp * rb4, a.up_sh + (size_t)s0 * rb4, (s1 - s0) * rb4, mb_pre);
+                ax::bulk_g2s(upg + (size_t)nrp * rb4, a.gate_sh + (size_t)s0 * rb4, (s1 - s0) * rb4, mb_pre);
+                ax::bulk_g2s(upu + (size_t)nrp * rb4, a.up_sh + (size_t)s0 * rb4, (s1 - s0) * rb4, mb_pre);
             }
             if (nrow_out) ax::bulk_g2s(dnp(K), a.down_sh + (size_t)n0 * rb6, nrow_out * rb6, mb_pre);
         }
@@ -480,14 +415,20 @@ __global__ void __launch_bounds__(FD_THREADS, 1) decode_fused_kernel(FusedDecode
 
     // ---- step 1: router rows (published first) ----
     {
-        // tpr threads per router row: thread lt owns elements [lt*seg, lt*seg+seg), seg >= 4;
-        // their (sum, sum of |prefix|, sum of |product|) go through shared
-        // memory (the routed gate/up area, unused until the selection) to one
-        // warp per row, which scans them and publishes the row
-        const int tpr = D % 1024 == 0 ? 256 : D / 4, seg = D / tpr;
-        const int ri = tid / tpr, lt = tid - ri * tpr;
-        double *rp = reinterpret_cast<double *>(upg);
-        if (ri < nr_mine) {
+        // tpr threads per router row (wpr warps): thread lt owns elements
+        // [lt*seg, lt*seg+seg), seg >= 4, and forms (P = its sum, SP = sum of
+        // |prefix| inside the segment, A = sum of |product|). The row's
+        // prefix before each segment comes from a warp scan plus the totals
+        // of the row's earlier warps; S_P <= sum over segments of
+        // seg*|prefix before| + SP.
+        const int tpr = D % 1024 == 0 ? 256 : D / 4, seg = D / tpr, wpr = tpr / 32;
+        const int ri = tid / tpr, lt = tid - ri * tpr, wr = lt >> 5;
+        const bool mine = ri < nr_mine;
+        // scratch: the routed down slabs, filled only after the selection
+        double *wtot = reinterpret_cast<double *>(dn + sdn);  // [rmax][wpr] warp sums of P
+        double *wsa = wtot + P.rmax * wpr;                    // [rmax][wpr][2] warp sums of (S_P bound, A)
+        double Pd = 0.0, SPd = 0.0, Ad = 0.0;
+        if (mine) {
             const float *w = rrow + (size_t)ri * D + lt * seg;
             const float *xv = xs + lt * seg;
             // products exact as (p, e) pairs (fma), summed as a float pair
@@ -510,54 +451,60 @@ __global__ void __launch_bounds__(FD_THREADS, 1) decode_fused_kernel(FusedDecode
                     Af = __fadd_ru(Af, fabsf(p));
                 }
             }
-            const double Pl = (double)hi + (double)lo;
-            const double SP = (double)SPf * (1.0 + 0x1.0p-20), A = (double)Af * (1.0 + 0x1.0p-20);
-            double *o = rp + ((size_t)ri * tpr + lt) * 3;
-            o[0] = Pl; o[1] = SP; o[2] = A;
+            Pd = (double)hi + (double)lo;
+            SPd = (double)SPf * (1.0 + 0x1.0p-20);
+            Ad = (double)Af * (1.0 + 0x1.0p-20);
         }
         FD_MARK(20)
+        double inc = Pd;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const double up = __shfl_up_sync(0xffffffffu, inc, o);
+            if (lane >= o) inc += up;
+        }
+        if (mine && lane == 31) wtot[ri * wpr + wr] = inc;
         __syncthreads();
         FD_MARK(21)
-        if (wid < nr_mine) {
-            // lane i owns threads [i*per, i*per + per) of row wid
-            const int per = tpr / 32;
-            const double *q = rp + ((size_t)wid * tpr + lane * per) * 3;
-            double tot = 0.0;
-            for (int j = 0; j < per; j++) tot += q[3 * j];
-            double inc = tot;
+        double base = 0.0, L = 0.0;
+        if (mine)
+            for (int q = 0; q < wpr; q++) {
+                const double v = wtot[ri * wpr + q];
+                if (q < wr) base += v;
+                L += v;
+            }
+        double spb = (double)seg * fabs(base + inc - Pd) + SPd, At = Ad;
 #pragma unroll
-            for (int o = 1; o < 32; o <<= 1) {
-                const double up = __shfl_up_sync(0xffffffffu, inc, o);
-                if (lane >= o) inc += up;
+        for (int o = 16; o > 0; o >>= 1) {
+            spb += __shfl_xor_sync(0xffffffffu, spb, o);
+            At += __shfl_xor_sync(0xffffffffu, At, o);
+        }
+        if (mine && lane == 0) {
+            wsa[2 * (ri * wpr + wr)] = spb;
+            wsa[2 * (ri * wpr + wr) + 1] = At;
+        }
+        ax::fence_proxy_async_smem();  // this area is refilled by bulk copies after the selection
+        __syncthreads();
+        FD_MARK(22)
+        if (mine && lt == 0) {
+            spb = 0.0;
+            At = 0.0;
+            for (int q = 0; q < wpr; q++) {
+                spb += wsa[2 * (ri * wpr + q)];
+                At += wsa[2 * (ri * wpr + q) + 1];
             }
-            FD_MARK(22)
-            double ex = inc - tot, spb = 0.0, At = 0.0;
-            for (int j = 0; j < per; j++) {
-                spb += (double)seg * fabs(ex) + q[3 * j + 1];
-                At += q[3 * j + 2];
-                ex += q[3 * j];
-            }
-            double L = tot;
-#pragma unroll
-            for (int o = 16; o > 0; o >>= 1) {
-                L += __shfl_xor_sync(0xffffffffu, L, o);
-                spb += __shfl_xor_sync(0xffffffffu, spb, o);
-                At += __shfl_xor_sync(0xffffffffu, At, o);
-            }
-            const int r = c + wid * G;
+            ax::fence_proxy_async_smem();  // (those reads) before the bulk copies that refill it
+            const int r = c + ri * G;
             FD_MARK(23)
-            if (lane == 0) {
-                if (r < E) {
-                    const double Bd = a.bound_scale * (At + spb + a.ngam * At) + 0x1.0p-60;
-                    const float lf = __double2float_rn(L);
-                    const float bf = __double2float_ru(Bd + fabs(L - (double)lf));
-                    ax::put_tagged(a.cand + 2 * r, u_of(lf), tag);
-                    ax::put_tagged(a.cand + 2 * r + 1, u_of(bf), tag);
-                    ax::count_add(a.sync + 3, 1u);
-                } else {
-                    ax::put_tagged(a.cand + 2 * E, u_of(1.0f / (1.0f + expf(-(float)L))), tag);
-                }
+            if (r < E) {
+                const double Bd = a.bound_scale * (At + spb + a.ngam * At) + 0x1.0p-60;
+                const float lf = __double2float_rn(L);
+                const float bf = __double2float_ru(Bd + fabs(L - (double)lf));
+                ax::put_tagged(a.cand + 2 * r, u_of(lf), tag);
+                ax::put_tagged(a.cand + 2 * r + 1, u_of(bf), tag);
+            } else {
+                ax::put_tagged(a.cand + 2 * E, u_of(1.0f / (1.0f + expf(-(float)L))), tag);
             }
+            ax::count_add(a.sync + 3, 1u);
         }
     }
     FD_MARK(3)
@@ -570,7 +517,8 @@ __global__ void __launch_bounds__(FD_THREADS, 1) decode_fused_kernel(FusedDecode
     if (tid < GRP) {
         // one thread waits for the count of published rows, then every
         // thread reads its entries once (no polling storm on these lines)
-        if (tid == 0 && !ax::wait_count(a.sync + 3, tag * (unsigned)E, FD_WAIT_NS)) tag_fail = true;
+        // (the shared gate's logit is counted with the router rows)
+        if (tid == 0 && !ax::wait_count(a.sync + 3, tag * (unsigned)nrows, FD_WAIT_NS)) tag_fail = true;
         asm volatile("bar.sync 1, %0;" ::"r"(GRP) : "memory");
         for (int e = tid; e < E; e += GRP) {
             uint32_t v0, v1;
@@ -578,7 +526,8 @@ __global__ void __launch_bounds__(FD_THREADS, 1) decode_fused_kernel(FusedDecode
             Lf[e] = f_of(v0);
             Bf[e] = f_of(v1);
         }
-        ax::fence_proxy_async_smem();  // the router partials' area is refilled by bulk copies
+        if (tid == GRP - 1)
+            s_gsc = a.use_gate ? f_of(ax::get_tagged(a.cand + 2 * E, tag, FD_WAIT_NS, tag_fail)) : 1.0f;
         asm volatile("bar.sync 1, %0;" ::"r"(GRP) : "memory");
         FD_MARK(6)
         if (wid == 0) {
@@ -706,24 +655,29 @@ __global__ void __launch_bounds__(FD_THREADS, 1) decode_fused_kernel(FusedDecode
         }
         asm volatile("bar.sync 2, %0;" ::"r"(GRP) : "memory");
         FD_MARK_IF(gt == 0, 4)
-        if (a.has_shared) {
-            for (int i = (wid - GRP / 32); i < s1 - s0; i += GRP / 32) {
-                const float h = swiglu_pair(shu + (size_t)i * rb4, shu + (size_t)(P.shp + i) * rb4, xq, D, lane);
-                if (lane == 0) {
-                    ax::put_tagged(a.hll + (size_t)K * H + s0 + i, u_of(h), tag);
-                    ax::count_add(a.sync + 4 + K, 1u);
+        if (a.has_shared && s1 > s0) {
+            // my shared-expert rows (row slots nrp..), two per warp at a time,
+            // then each 16-row group quantised and published to slot K
+            const int gw = wid - GRP / 32, NW = GRP / 32, ns = s1 - s0;
+            for (int i = gw; i < ns; i += 2 * NW) {
+                const int j = i + NW;
+                const uint8_t *gi = upg + (size_t)(nrp + i) * rb4, *ui = upu + (size_t)(nrp + i) * rb4;
+                if (j < ns) {
+                    const float2 h = swiglu_pair2(gi, ui, upg + (size_t)(nrp + j) * rb4, upu + (size_t)(nrp + j) * rb4,
+                                                  xq, D, lane);
+                    if (lane == 0) { hbuf[nrp + i] = h.x; hbuf[nrp + j] = h.y; }
+                } else {
+                    const float h = swiglu_pair(gi, ui, xq, D, lane);
+                    if (lane == 0) hbuf[nrp + i] = h;
                 }
             }
-            FD_MARK_IF(gt == 0, 5)
-            // every CTA's shared h, quantised into slot K (used with the
-            // routed slots' down rows in step 4)
-            if (gt == 0 && !ax::wait_count(a.sync + 4 + K, tag * (unsigned)H, FD_WAIT_NS)) tag_fail = true;
             asm volatile("bar.sync 2, %0;" ::"r"(GRP) : "memory");
+            FD_MARK_IF(gt == 0, 5)
+            for (int g = gw; g < ns / 16; g += NW)
+                publish_group(hbuf[nrp + 16 * g + (lane & 15)], hst + wid * FD_GROUP_BYTES, hqg + (size_t)K * SLOT, H,
+                              share.sg0 + g, a.sync + 4, lane);
             FD_MARK_IF(gt == 0, 29)
-            if (!read_quant_h<FD_H_PAIRS>(a.hll + (size_t)K * H, H, tag, hqb, H, K, gt, GRP)) tag_fail = true;
-            FD_MARK_IF(gt == 0, 30)
         }
-        if (gt == 0) s_gsc = a.use_gate ? f_of(ax::get_tagged(a.cand + 2 * E, tag, FD_WAIT_NS, tag_fail)) : 1.0f;
     }
     __syncthreads();
     FD_MARK(7)
@@ -869,9 +823,8 @@ __global__ void __launch_bounds__(FD_THREADS, 1) decode_fused_kernel(FusedDecode
     // warp w takes pairs w and w + FD_WARPS together, then w + 2 FD_WARPS ...
     // (two independent rows per warp hide the dot / reduction latency) ----
     {
-        const int np = u1 - u0;
+        const int np = nrp;
         const int seg_b = (slot_first + 1) * H - u0;  // pairs at or past this index are in slot_first + 1
-        int ncnt[2] = {0, 0};
         for (int i = wid; i < np; i += 2 * FD_WARPS) {
             const int j = i + FD_WARPS;
             const bool two = j < np;
@@ -882,73 +835,56 @@ __global__ void __launch_bounds__(FD_THREADS, 1) decode_fused_kernel(FusedDecode
             if (two) {
                 const float2 h = swiglu_pair2(upg + (size_t)i * rb4, upu + (size_t)i * rb4, upg + (size_t)j * rb4,
                                               upu + (size_t)j * rb4, xq, D, lane);
-                if (lane == 0) {
-                    ax::put_tagged(a.hll + u0 + i, u_of(h.x), tag);
-                    ax::put_tagged(a.hll + u0 + j, u_of(h.y), tag);
-                }
-                ncnt[si]++;
-                ncnt[sj]++;
+                if (lane == 0) { hbuf[i] = h.x; hbuf[j] = h.y; }
             } else {
                 const float h = swiglu_pair(upg + (size_t)i * rb4, upu + (size_t)i * rb4, xq, D, lane);
-                if (lane == 0) ax::put_tagged(a.hll + u0 + i, u_of(h), tag);
-                ncnt[si]++;
+                if (lane == 0) hbuf[i] = h;
             }
             FD_MARK_IF(tid == 0 && i == 0, 8)
         }
+        __syncthreads();
         FD_MARK(10)
-        // one fence per warp, then the counts of the h rows it wrote, per slot
-        if (lane == 0 && ncnt[0] + ncnt[1]) {
-#ifdef OFB_FD_RELEASE
-            if (ncnt[0]) ax::count_add_release(a.sync + 4 + slot_first, (unsigned)ncnt[0]);
-            if (ncnt[1]) ax::count_add_release(a.sync + 4 + slot_first + 1, (unsigned)ncnt[1]);
-        }
-        if (false) {
-#endif
-            __threadfence();
-            FD_MARK(34)
-            if (ncnt[0]) atomicAdd(a.sync + 4 + slot_first, (unsigned)ncnt[0]);
-            if (ncnt[1]) atomicAdd(a.sync + 4 + slot_first + 1, (unsigned)ncnt[1]);
+        // each 16-row group quantised once, here, and published to its slot
+        for (int g = wid; g < np / 16; g += FD_WARPS) {
+            const int rg = u0 / 16 + g, k = rg / (H / 16), gs = rg - k * (H / 16);
+            publish_group(hbuf[16 * g + (lane & 15)], hst + wid * FD_GROUP_BYTES, hqg + (size_t)k * SLOT, H, gs,
+                          a.sync + 4, lane);
         }
     }
     FD_MARK(9)
-#ifdef OFB_FD_TRACE
-    __syncthreads();
-    FD_MARK(27)
-#endif
-    // ---- step 4: every routed slot's h, quantised; y of my rows ----
-    // thread k waits for slot k's count (the waits overlap); then one bulk
-    // copy brings every routed h word into the (consumed) gate/up area
-    if (tid < K && !ax::wait_count(a.sync + 4 + tid, tag * (unsigned)H, FD_WAIT_NS)) tag_fail = true;
-    ax::fence_proxy_async_smem();  // the gate/up rows read above are overwritten by the copy
-    __syncthreads();
-    FD_MARK(26)
-    const unsigned long long *hsm = reinterpret_cast<const unsigned long long *>(upg);
-    if (P.hcopy) {
-        if (tid == 0) {
-            ax::fence_proxy_async_global();  // the acquired h words, seen by the copy
-            ax::mbar_arrive_expect(mb_h, (uint32_t)K * H * 8);
-            ax::bulk_g2s(upg, a.hll, (uint32_t)K * H * 8, mb_h);
-        }
-        if (!ax::mbar_wait(mb_h, 0, FD_WAIT_NS)) copy_fail = true;
-        FD_MARK(38)
-        if (!read_quant_copy(hsm, a.hll, K * H, tag, hqb, H, 0, tid, FD_THREADS)) tag_fail = true;
-    } else {
-        if (tid == 0) ax::mbar_arrive_expect(mb_h, 0);
-        if (!read_quant_h<FD_H_PAIRS>(a.hll, K * H, tag, hqb, H, 0, tid, FD_THREADS)) tag_fail = true;
+    // ---- step 4: the quantised h of every slot (one bulk copy of the
+    // global slot image once every group is counted); y of my rows ----
+    const int nslot = K + (a.has_shared ? 1 : 0);
+    if (tid == 0) {
+        if (!ax::wait_count(a.sync + 4, tag * (unsigned)(NRG + NSG), FD_WAIT_NS)) tag_fail = true;
+        FD_MARK(26)
+        ax::fence_proxy_async_global();  // the acquired groups, seen by the copy
+        ax::mbar_arrive_expect(mb_h, (uint32_t)nslot * SLOT);
+        ax::bulk_g2s(hqb, hqg, (uint32_t)nslot * SLOT, mb_h);
     }
-    FD_MARK(31)
-    __syncthreads();
+    if (!ax::mbar_wait(mb_h, 0, FD_WAIT_NS)) copy_fail = true;
     FD_MARK(11)
     // the routed slots and (slot K) the shared expert: one task per thread at
     // the BASELINE shape
-    const int nslot = K + (a.has_shared ? 1 : 0);
     for (int t = tid; t < nslot * nrow_out * NHB; t += FD_THREADS) {
-        const int k = t / (nrow_out * NHB), rem = t - k * nrow_out * NHB, r = rem / NHB, hb = rem - r * NHB;
+        const int kh = t / nrow_out, r = t - kh * nrow_out, k = kh / NHB, hb = kh - k * NHB;
         if (k < K && !ax::mbar_wait(mb_dn + k, par, FD_WAIT_NS)) copy_fail = true;
         const uint32_t base = ax::smem_u32(dnp(k));
         ysp[((size_t)k * rows_cap + r) * NHB + hb] =
             q6k_half_dot(base + r * rb6 + (hb >> 1) * Q6K_BYTES, hb & 1, hslot(hqb, H, k), hb);
     }
+    FD_MARK(12)
+#ifdef OFB_FD_TRACE
+    __syncthreads();
+    FD_MARK(49)
+    for (int t = tid; t < nslot * nrow_out * NHB; t += FD_THREADS) {
+        const int kh = t / nrow_out, r = t - kh * nrow_out, k = kh / NHB, hb = kh - k * NHB;
+        const uint32_t base = ax::smem_u32(dnp(k));
+        ysp[((size_t)k * rows_cap + r) * NHB + hb] =
+            q6k_half_dot(base + r * rb6 + (hb >> 1) * Q6K_BYTES, hb & 1, hslot(hqb, H, k), hb);
+    }
+    FD_MARK(50)
+#endif
     __syncthreads();
     FD_MARK(13)
     // y per (slot, row): the half-block partials summed in a fixed order,
@@ -996,8 +932,8 @@ __global__ void __launch_bounds__(FD_THREADS, 1) decode_fused_kernel(FusedDecode
             a.sync[1] = 0;
             // every CTA is done: set the exchange counters to their exact
             // values for this epoch (repairs them after an expired wait)
-            a.sync[3] = tag * (unsigned)E;
-            for (int k = 0; k <= K; k++) a.sync[4 + k] = tag * (unsigned)H;
+            a.sync[3] = tag * (unsigned)nrows;
+            a.sync[4] = tag * (unsigned)(NRG + NSG);
             __threadfence();
             atomicAdd(&a.sync[0], 1u);
         }
@@ -1014,9 +950,9 @@ extern "C" int ofb_debug_fd_trace(unsigned long long *host) {
 
 static int gcd_i(int a, int b) { return b ? gcd_i(b, a % b) : a; }
 
-bool fused_plan(const ofb_moe_config *cfg, bool use_gate, int G, FusedPlan &p) {
+bool fused_plan(const ofb_moe_config *cfg, bool use_gate, bool has_shared, int G, FusedPlan &p) {
     const int D = cfg->d_model, H = cfg->hidden, E = cfg->n_experts, K = cfg->top_k;
-    if (E > 32 * FD_PER_LANE || K > 16 || K > E || G < 1) return false;
+    if (E > 32 * FD_PER_LANE || K > 16 || K > E || G < 1 || H % 16) return false;
     const int nrows = E + (use_gate ? 1 : 0);
     p.G = G;
     p.rmax = (nrows + G - 1) / G;
@@ -1028,9 +964,16 @@ bool fused_plan(const ofb_moe_config *cfg, bool use_gate, int G, FusedPlan &p) {
     if (dg < 4) dg = 4;
     if (D % dg) return false;
     p.dg = dg;
-    p.shp = (H + G - 1) / G;
-    p.upc = (K * H + G - 1) / G;
-    if (p.upc > H) return false;  // a CTA's gate/up pairs span at most two slots
+    // gate/up row slots: the CTA's routed pairs, then its shared-expert rows
+    const int NR = K * H / 16, NS = has_shared ? H / 16 : 0;
+    int most = 0, most_r = 0;
+    for (int c = 0; c < G; c++) {
+        const FdShare sh = fd_share(c, G, NR, NS);
+        most = std::max(most, sh.rg1 - sh.rg0 + sh.sg1 - sh.sg0);
+        most_r = std::max(most_r, sh.rg1 - sh.rg0);
+    }
+    p.upc = 16 * most;
+    if (16 * most_r > H) return false;  // a CTA's routed pairs span at most two slots
     p.ngc = (D / dg + G - 1) / G;
     const int rows_cap = p.ngc * dg, nhb = H / 128;
     size_t off = 0;
@@ -1038,26 +981,26 @@ bool fused_plan(const ofb_moe_config *cfg, bool use_gate, int G, FusedPlan &p) {
     p.o_x = take((size_t)D * 4);
     p.o_xq = take(xq_stride(D));
     p.o_rr = take((size_t)p.rmax * D * 4);
-    p.o_shu = take((size_t)2 * p.shp * rb4);
     // down slabs (shared expert first, then the routed slots) directly
-    // followed by the routed gate/up rows: the selection's exact-recompute
-    // scratch overlays the routed part of both
+    // followed by the gate/up rows: the router rows' partial sums use the
+    // routed down slabs before they are filled, and the selection's
+    // exact-recompute scratch overlays the routed part of both
     const size_t sdn = (size_t)rows_cap * rb6;
+    if ((size_t)p.rmax * (tpr / 32) * 24 > (size_t)K * sdn) return false;  // router partials
     p.o_dn = take((size_t)(K + 1) * sdn);
-    // (the router rows' partial sums use the gate/up area before it is filled)
-    const size_t up = std::max((size_t)2 * p.upc * rb4, (size_t)p.rmax * tpr * 24);
+    const size_t up = (size_t)2 * p.upc * rb4;
     p.o_up = take(up);
     const size_t fb = (size_t)XL_SMEM + (size_t)11 * E * 4;
     if ((size_t)p.o_up + up - ((size_t)p.o_dn + sdn) < fb) {
         off = (size_t)p.o_dn + sdn + fb;
         off = (off + 127) & ~(size_t)127;
     }
-    p.o_hq = take((size_t)(K + 1) * (2 * H + H / 2));
+    p.o_hb = take((size_t)p.upc * 4);
+    p.o_hst = take((size_t)FD_WARPS * FD_GROUP_BYTES);
+    p.o_hq = take((size_t)(K + 1) * hslot_bytes(H));
     p.o_sel = take((size_t)2 * E * 4);
     p.o_ys = take((size_t)(K + 1) * rows_cap * nhb * 4);
     p.o_bar = take((size_t)(5 + K) * 8);
-    // step 4 copies every routed h word (tagged, 8 bytes) into the gate/up area
-    p.hcopy = (size_t)K * H * 8 <= up;
     p.total = (uint32_t)off;
     return p.total <= 227 * 1024;
 }

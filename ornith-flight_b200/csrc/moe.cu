@@ -237,7 +237,7 @@ int run_moe_layer(const ofb_moe_config *cfg, const ofb_moe_weights *wt, const fl
         const bool use_gate = has_sh && cfg->shared_gate && wt->shexp_gate;
         FusedPlan fp;
         if ((!use_gate || !(reinterpret_cast<uintptr_t>(wt->shexp_gate) & 15)) &&
-            fused_plan(cfg, use_gate, sm_count(), fp)) {
+            fused_plan(cfg, use_gate, has_sh, sm_count(), fp)) {
             int *ctr = (int *)(base + L.counters);
             st = launch_decode_fused(cfg, wt, x, resid, out, idx_out, w_out, fp,
                                      (unsigned long long *)(base + L.fcand), (unsigned long long *)(base + L.fh),

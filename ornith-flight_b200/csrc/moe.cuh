@@ -105,11 +105,30 @@ __host__ __device__ inline size_t xq_stride(int D) { return (size_t)2 * D + (siz
 // Shared-memory plan of the single-launch decode kernel (decode_fused.cu):
 // per-CTA share sizes and region offsets, identical on host and device.
 struct FusedPlan {
-    int G, rmax, shp, upc, ngc, dg;
-    uint32_t o_x, o_xq, o_rr, o_shu, o_dn, o_up, o_hq, o_sel, o_ys, o_bar, total;
-    bool hcopy;  // step 4 bulk-copies the routed h words into the gate/up area
+    int G, rmax, upc, ngc, dg;
+    uint32_t o_x, o_xq, o_rr, o_dn, o_up, o_hb, o_hst, o_hq, o_sel, o_ys, o_bar, total;
 };
-bool fused_plan(const ofb_moe_config *cfg, bool use_gate, int grid, FusedPlan &p);
+bool fused_plan(const ofb_moe_config *cfg, bool use_gate, bool has_shared, int grid, FusedPlan &p);
+
+// Work shares of the single-launch decode kernel in 16-row h groups (one Q6_K
+// scale group of h each): CTA c computes routed groups [rg0, rg1) of the
+// K * H / 16 (pairs 16 * rg0 .. 16 * rg1 in top-k slot order) and, if it has
+// the fewest routed groups, shared-expert groups [sg0, sg1) of H / 16, so
+// every group is quantised by the CTA that computed it.
+struct FdShare { int rg0, rg1, sg0, sg1; };
+__host__ __device__ inline FdShare fd_share(int c, int G, int NR, int NS) {
+    FdShare s;
+    s.rg0 = (int)((long long)c * NR / G);
+    s.rg1 = (int)((long long)(c + 1) * NR / G);
+    s.sg0 = s.sg1 = 0;
+    const int q = NR / G, L = G - NR % G;  // L CTAs have q routed groups
+    if (s.rg1 - s.rg0 == q) {
+        const int j = c * (1 + q) - s.rg0;  // rank among them
+        s.sg0 = (int)((long long)j * NS / L);
+        s.sg1 = (int)((long long)(j + 1) * NS / L);
+    }
+    return s;
+}
 int launch_decode_fused(const ofb_moe_config *cfg, const ofb_moe_weights *wt, const float *x, const float *resid,
                         float *out, uint32_t *idx_out, float *w_out, const FusedPlan &plan,
                         unsigned long long *cand, unsigned long long *hll, unsigned int *sync, int *stats,
