@@ -103,77 +103,138 @@ __device__ unsigned long long g_fd_tr[256][64];
 __device__ __forceinline__ float f_of(uint32_t u) { return __uint_as_float(u); }
 __device__ __forceinline__ uint32_t u_of(float f) { return __float_as_uint(f); }
 
-// Dot products of one Q4_K row pair (gate, up) in shared memory with the
-// quantised x; one warp, lane j over 64-element items. Returns h on every lane.
-__device__ __noinline__ float swiglu_pair(const uint8_t *grow, const uint8_t *urow, const unsigned char *xq,
-                                             int D, int lane) {
-    const int items = D / 64;
-    const float *qf = reinterpret_cast<const float *>(xq + 2 * D);
-    float ag = 0.f, au = 0.f;
-    for (int j = lane; j < items; j += 32) {
-        const int b = j >> 2, c = j & 3;
-        const uint8_t *gb = grow + b * Q4K_BYTES, *ub = urow + b * Q4K_BYTES;
-        const uint4 hg = *reinterpret_cast<const uint4 *>(gb);
-        const uint4 ga = *reinterpret_cast<const uint4 *>(gb + 16 + c * 32);
-        const uint4 gq = *reinterpret_cast<const uint4 *>(gb + 32 + c * 32);
-        const uint4 hu = *reinterpret_cast<const uint4 *>(ub);
-        const uint4 ua = *reinterpret_cast<const uint4 *>(ub + 16 + c * 32);
-        const uint4 uq = *reinterpret_cast<const uint4 *>(ub + 32 + c * 32);
-        const int e0 = b * QK + c * 64, sb = e0 / 32;
-        uint4 xh[4], xl[4];
-#pragma unroll
-        for (int i = 0; i < 4; i++) {
-            xh[i] = reinterpret_cast<const uint4 *>(xq + e0)[i];
-            xl[i] = reinterpret_cast<const uint4 *>(xq + D + e0)[i];
-        }
-        const float s_lo = qf[sb], s_hi = qf[sb + 1];
-        const float xs_lo = qf[D / 32 + sb], xs_hi = qf[D / 32 + sb + 1];
-        ag += q4k_item_q(hg, ga, gq, c, xh, xl, s_lo, s_hi, xs_lo, xs_hi);
-        au += q4k_item_q(hu, ua, uq, c, xh, xl, s_lo, s_hi, xs_lo, xs_hi);
-    }
-    const float g = warp_sum(ag), u = warp_sum(au);
-    return silu_ref_d(g) * u;
+// ---- gate/up rows on the tensor cores (mma.sync m16n8k32, u8 x s8 -> s32) ----
+// A tile is 8 row pairs: rows 0-7 gate rows, rows 8-15 the same pairs' up
+// rows; row g of a tile lies in shared-memory area g of its segment (see
+// FdSegs), areas RS bytes apart with RS % 128 == 32, so the 4 rows a
+// half-warp reads fall in different banks. One MMA covers one 32-weight
+// Q4_K sub-block: A = its 4-bit quants (0..15), B = the activations as 16-bit
+// integers x_int = 128 * hi + lo (hi int8, lo 0..127) of the same positions.
+// Sub-block j puts hi / lo in B columns 2(j%4) / 2(j%4)+1 (other columns
+// zero), so four consecutive sub-blocks accumulate into one C, and lane
+// (g, tig) then holds the sums of sub-block 4m+tig for gate row g (c0, c1)
+// and up row g (c2, c3). The k order inside a sub-block is permuted so that
+// a lane's A and B registers are 8 consecutive bytes each: MMA k = 4 tig + i
+// is byte 8 tig + i, k = 16 + 4 tig + i is byte 8 tig + 4 + i.
+// Per sub-block j of a row: sum_i w_i x_i ~= s_j (d sc_j S - dmin m_j xsum_j)
+// with S = sum_i q_i x_int,i = 128 c_hi + c_lo (exact in int32), s_j the
+// activations' scale and xsum_j the sum of their (unquantised) values.
+__device__ __forceinline__ void mma_u8s8(int (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                         uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};"
+        : "+r"(c[0]), "+r"(c[1]), "+r"(c[2]), "+r"(c[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
-// Two row pairs at once (rows i and j of the CTA's gate/up copies): the same
-// arithmetic as swiglu_pair per pair, interleaved so one warp has four
-// independent dot products and four independent reductions in flight.
-__device__ __noinline__ float2 swiglu_pair2(const uint8_t *g0, const uint8_t *u0, const uint8_t *g1,
-                                            const uint8_t *u1, const unsigned char *xq, int D, int lane) {
-    const int items = D / 64;
-    const float *qf = reinterpret_cast<const float *>(xq + 2 * D);
-    float ag0 = 0.f, au0 = 0.f, ag1 = 0.f, au1 = 0.f;
-    for (int j = lane; j < items; j += 32) {
-        const int b = j >> 2, c = j & 3;
-        const int e0 = b * QK + c * 64, sb = e0 / 32;
-        uint4 xh[4], xl[4];
+// Partial (gate, up) dot products of tile t over Q4_K blocks [b0, b1) for
+// pair 8t + g (returned on the lanes with tig == 0). G / U: the tile's first
+// gate / up row; xq7: hi plane, lo plane (D bytes each), then per 32
+// elements the scale s_j and xsum_j (floats).
+__device__ __forceinline__ float2 tile_dots(const uint8_t *G, const uint8_t *U, int RS, int b0, int b1,
+                                            const unsigned char *xq7, int D, int lane) {
+    const int g = lane >> 2, tig = lane & 3;
+    const uint8_t *gr = G + (size_t)g * RS, *ur = U + (size_t)g * RS;
+    const float *xs = reinterpret_cast<const float *>(xq7 + 2 * D), *xsum = xs + D / 32;
+    // B source of this lane: column n = g is plane (g & 1) of sub-block pair slot (g >> 1)
+    const unsigned char *xpl = xq7 + (g & 1) * D + 8 * tig;
+    float ag = 0.f, au = 0.f;
+    for (int b = b0; b < b1; b++) {
+        const uint4 hg = *reinterpret_cast<const uint4 *>(gr + b * Q4K_BYTES);
+        const uint4 hu = *reinterpret_cast<const uint4 *>(ur + b * Q4K_BYTES);
+        const float dg = half_bits_ref(hg.x & 0xFFFFu), dmg = half_bits_ref(hg.x >> 16);
+        const float du = half_bits_ref(hu.x & 0xFFFFu), dmu = half_bits_ref(hu.x >> 16);
 #pragma unroll
-        for (int i = 0; i < 4; i++) {
-            xh[i] = reinterpret_cast<const uint4 *>(xq + e0)[i];
-            xl[i] = reinterpret_cast<const uint4 *>(xq + D + e0)[i];
+        for (int m = 0; m < 2; m++) {  // sub-blocks 4m .. 4m+3 of the block
+            int cc[4] = {0, 0, 0, 0};
+#pragma unroll
+            for (int ch = 0; ch < 2; ch++) {  // 32-byte chunk 2m + ch: sub-blocks 2(2m+ch), 2(2m+ch)+1
+                const int chunk = 2 * m + ch;
+                const uint2 wg = *reinterpret_cast<const uint2 *>(gr + b * Q4K_BYTES + 16 + 32 * chunk + 8 * tig);
+                const uint2 wu = *reinterpret_cast<const uint2 *>(ur + b * Q4K_BYTES + 16 + 32 * chunk + 8 * tig);
+#pragma unroll
+                for (int hi = 0; hi < 2; hi++) {
+                    const int jj = 2 * ch + hi;  // sub-block within the group of four
+                    const int j = b * 8 + 4 * m + jj;
+                    uint2 bx = make_uint2(0u, 0u);
+                    if ((g >> 1) == jj) bx = *reinterpret_cast<const uint2 *>(xpl + 32 * j);
+                    const uint32_t sh = 4 * hi;
+                    mma_u8s8(cc, (wg.x >> sh) & 0x0F0F0F0Fu, (wu.x >> sh) & 0x0F0F0F0Fu, (wg.y >> sh) & 0x0F0F0F0Fu,
+                             (wu.y >> sh) & 0x0F0F0F0Fu, bx.x, bx.y);
+                }
+            }
+            // epilogue: this lane's sub-block 4m + tig of the block
+            const int jb = 4 * m + tig, j = b * 8 + jb;
+            const float sx = xs[j], xm = xsum[j];
+            {
+                const uint32_t sc3[3] = {hg.y, hg.z, hg.w};
+                int sc, mn;
+                q4k_scale_min(sc3, jb, sc, mn);
+                ag += dg * (float)sc * sx * (float)(128 * cc[0] + cc[1]) - dmg * (float)mn * xm;
+            }
+            {
+                const uint32_t sc3[3] = {hu.y, hu.z, hu.w};
+                int sc, mn;
+                q4k_scale_min(sc3, jb, sc, mn);
+                au += du * (float)sc * sx * (float)(128 * cc[2] + cc[3]) - dmu * (float)mn * xm;
+            }
         }
-        const float s_lo = qf[sb], s_hi = qf[sb + 1];
-        const float xs_lo = qf[D / 32 + sb], xs_hi = qf[D / 32 + sb + 1];
-        const uint8_t *rows[4] = {g0, u0, g1, u1};
-        float r[4];
-#pragma unroll
-        for (int m = 0; m < 4; m++) {
-            const uint8_t *bb = rows[m] + b * Q4K_BYTES;
-            const uint4 hd = *reinterpret_cast<const uint4 *>(bb);
-            const uint4 qa = *reinterpret_cast<const uint4 *>(bb + 16 + c * 32);
-            const uint4 qb = *reinterpret_cast<const uint4 *>(bb + 32 + c * 32);
-            r[m] = q4k_item_q(hd, qa, qb, c, xh, xl, s_lo, s_hi, xs_lo, xs_hi);
-        }
-        ag0 += r[0]; au0 += r[1]; ag1 += r[2]; au1 += r[3];
     }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-        ag0 += __shfl_xor_sync(0xffffffffu, ag0, o);
-        au0 += __shfl_xor_sync(0xffffffffu, au0, o);
-        ag1 += __shfl_xor_sync(0xffffffffu, ag1, o);
-        au1 += __shfl_xor_sync(0xffffffffu, au1, o);
+    ag += __shfl_xor_sync(0xffffffffu, ag, 1);
+    au += __shfl_xor_sync(0xffffffffu, au, 1);
+    ag += __shfl_xor_sync(0xffffffffu, ag, 2);
+    au += __shfl_xor_sync(0xffffffffu, au, 2);
+    return make_float2(ag, au);
+}
+
+// Gate / up rows of a CTA in shared memory, per segment (pairs of one
+// expert: top-k slot first, the next slot, the shared expert): its n pairs
+// (a multiple of 16) arrive in 8 copies of c = n / 8 consecutive pairs, copy
+// m into area m (areas as[s] bytes apart, as[s] % 128 == 32), so pair
+// start + m * c + t is row t of area m, and tile t of the segment takes row t
+// of every area (8 rows in 8 bank offsets).
+struct FdSegs {
+    int ns;                                          // segments in use
+    int start[3], c[3], off[3], as[3], tile0[3], nt;  // off: byte offset in the gate (and up) region
+};
+__host__ __device__ __forceinline__ int fd_area_stride(int c, int rb4) {
+    const int b = c * rb4;
+    return b + ((32 - b % 128) + 128) % 128;
+}
+__device__ __forceinline__ int fd_seg_of(const FdSegs &S, int i) {
+    int s = 0;
+    while (s + 1 < S.ns && i >= S.start[s + 1]) s++;
+    return s;
+}
+
+// Partial dots of the segments' pairs by warps w = 0..NW-1: every tile x
+// (NW / tiles) k-parts; part[kp][8 * tile + g] = (gate, up) of row g.
+__device__ __noinline__ void pairs_dots(const uint8_t *upg, const uint8_t *upu, const FdSegs *Sp, int rb4,
+                                        const unsigned char *xq7, int D, float2 *part, int w, int NW, int lane) {
+    const FdSegs &S = *Sp;
+    const int nt = S.nt, KP = nt >= NW ? 1 : NW / nt, nb = D / QK;
+    for (int it = w; it < nt * KP; it += NW) {
+        const int T = it % nt, kp = it / nt;
+        int s = 0;
+        while (s + 1 < S.ns && T >= S.tile0[s + 1]) s++;
+        const size_t o = (size_t)S.off[s] + (size_t)(T - S.tile0[s]) * rb4;
+        const float2 r = tile_dots(upg + o, upu + o, S.as[s], kp * nb / KP, (kp + 1) * nb / KP, xq7, D, lane);
+        if ((lane & 3) == 0) part[kp * 8 * nt + 8 * T + (lane >> 2)] = r;
     }
-    return make_float2(silu_ref_d(ag0) * au0, silu_ref_d(ag1) * au1);
+}
+// h of pair i (index in the segments' numbering) from the k-part partials
+// (after a barrier over the NW warps).
+__device__ __forceinline__ float pair_h(const float2 *part, const FdSegs &S, int NW, int i) {
+    const int nt = S.nt, KP = nt >= NW ? 1 : NW / nt;
+    const int s = fd_seg_of(S, i), li = i - S.start[s], g = li / S.c[s], T = S.tile0[s] + li - g * S.c[s];
+    float gs = 0.f, us = 0.f;
+    for (int kp = 0; kp < KP; kp++) {
+        const float2 v = part[kp * 8 * nt + 8 * T + g];
+        gs += v.x;
+        us += v.y;
+    }
+    return silu_ref_d(gs) * us;
 }
 
 // 32-bit shared-memory loads by shared-window address.
@@ -311,12 +372,13 @@ __global__ void __launch_bounds__(FD_THREADS, 1) decode_fused_kernel(FusedDecode
     unsigned char *xq = sm + P.o_xq;
     float *rrow = reinterpret_cast<float *>(sm + P.o_rr);
     float *hbuf = reinterpret_cast<float *>(sm + P.o_hb);  // h of my row slots (routed, then shared)
+    float2 *part = reinterpret_cast<float2 *>(sm + P.o_part);  // k-part partial dots (pairs_dots)
     uint8_t *hst = sm + P.o_hst;                            // [FD_WARPS][FD_GROUP_BYTES] staging
     uint8_t *hqg = reinterpret_cast<uint8_t *>(a.hll);      // global image of the quantised h slots
     const int SLOT = hslot_bytes(H);                         // bytes per slot (hslot layout)
     uint8_t *dn = sm + P.o_dn;  // slot K (shared) first, then routed slots 0..K-1
     uint8_t *upg = sm + P.o_up;
-    uint8_t *upu = upg + (size_t)P.upc * rb4;
+    uint8_t *upu = upg + P.upb;  // up rows: the same layout as the gate rows
     uint8_t *hqb = sm + P.o_hq;
     float *Lf = reinterpret_cast<float *>(sm + P.o_sel);
     float *Bf = Lf + E;
@@ -349,27 +411,56 @@ __global__ void __launch_bounds__(FD_THREADS, 1) decode_fused_kernel(FusedDecode
     const int n0 = (int)((long long)c * NG / G) * P.dg, n1 = (int)((long long)(c + 1) * NG / G) * P.dg;
     const int nrow_out = n1 - n0;
     const int slot_first = u0 / H;  // the CTA's pairs span slots slot_first and (maybe) slot_first + 1
+    // row segments: routed pairs of slot_first, of slot_first + 1, then the
+    // shared-expert rows (s_seg[0] routed, s_seg[1] shared)
+    __shared__ FdSegs s_seg[2];
+    if (tid == 0) {
+        const int n0s = min(u1, (slot_first + 1) * H) - u0, ns = s1 - s0;
+        const int n[3] = {n0s, nrp - n0s, ns};
+        int off = 0;
+        for (int q = 0; q < 3; q++) {
+            FdSegs &S = s_seg[q < 2 ? 0 : 1];
+            const int j = q < 2 ? q : 0;
+            if (j == 0) { S.ns = 0; S.nt = 0; }
+            if (n[q] == 0) continue;
+            const int cq = n[q] / 8, asq = fd_area_stride(cq, rb4);
+            S.start[S.ns] = q == 2 ? 0 : (q == 0 ? 0 : n0s);
+            S.c[S.ns] = cq;
+            S.off[S.ns] = off;
+            S.as[S.ns] = asq;
+            S.tile0[S.ns] = S.nt;
+            S.nt += cq;
+            S.ns++;
+            off += 8 * asq;
+        }
+    }
+    // (s_seg is published by the __syncthreads after the mbarrier set-up)
 
     // Copies of top-k slot q (expert e): my gate/up rows inside slot q and my
     // output rows' down slab. One arrival on each mbarrier per issue round.
-    auto issue_slot = [&](int q, int e) {
-        const int p0 = max(u0, q * H), p1 = min(u1, (q + 1) * H);
-        if (p1 > p0) {
+    // Routed copies: per segment 8 copies per matrix (FdSegs); expect_up
+    // announces each segment's bytes once (slot_first, slot_first + 1).
+    auto expect_up = [&]() {
+        const int sb = min(u1, (slot_first + 1) * H);
+        ax::mbar_arrive_expect(mb_up, 2u * (uint32_t)(sb - u0) * rb4);
+        ax::mbar_arrive_expect(mb_up + 1, 2u * (uint32_t)(u1 - sb) * rb4);
+    };
+    // copy v (0..31) of the routed rows: segment v / 16, matrix (v / 8) & 1, area v & 7
+    auto issue_rows = [&](int v0, int step) {
+        const FdSegs &S = s_seg[0];
+        for (int v = v0; v < 16 * S.ns; v += step) {
+            const int sg = v >> 4, mat = (v >> 3) & 1, m = v & 7;
+            const int p = u0 + S.start[sg] + m * S.c[sg], q = p / H;
             uint64_t *b = mb_up + (q == slot_first ? 0 : 1);
-            ax::mbar_arrive_expect(b, 2u * (p1 - p0) * rb4);
-            const size_t off = (size_t)e * exp4 + (size_t)(p0 - q * H) * rb4;
-            ax::bulk_g2s(upg + (size_t)(p0 - u0) * rb4, a.gate + off, (p1 - p0) * rb4, b);
-            ax::bulk_g2s(upu + (size_t)(p0 - u0) * rb4, a.up + off, (p1 - p0) * rb4, b);
+            const size_t src = (size_t)s_top[q] * exp4 + (size_t)(p - q * H) * rb4;
+            ax::bulk_g2s((mat ? upu : upg) + S.off[sg] + (size_t)m * S.as[sg], (mat ? a.up : a.gate) + src,
+                         (uint32_t)S.c[sg] * rb4, b);
         }
+    };
+    auto issue_dn = [&](int q, int e) {
         ax::mbar_arrive_expect(mb_dn + q, (uint32_t)nrow_out * rb6);
         if (nrow_out)
             ax::bulk_g2s(dnp(q), a.down + (size_t)e * exp6 + (size_t)n0 * rb6, nrow_out * rb6, mb_dn + q);
-    };
-    // up segments that no slot filled still need their arrival
-    auto close_up = [&]() {
-        const bool seg0 = u1 > u0, seg1 = u1 > u0 && (u1 - 1) / H > slot_first;
-        if (!seg0) ax::mbar_arrive_expect(mb_up, 0);
-        if (!seg1) ax::mbar_arrive_expect(mb_up + 1, 0);
     };
 
     // ---- step 0: static bytes, before waiting for the producer of x ----
@@ -393,8 +484,12 @@ __global__ void __launch_bounds__(FD_THREADS, 1) decode_fused_kernel(FusedDecode
         }
         if (a.has_shared) {
             if (s1 > s0) {
-                ax::bulk_g2s(upg + (size_t)nrp * rb4, a.gate_sh + (size_t)s0 * rb4, (s1 - s0) * rb4, mb_pre);
-                ax::bulk_g2s(upu + (size_t)nrp * rb4, a.up_sh + (size_t)s0 * rb4, (s1 - s0) * rb4, mb_pre);
+                const FdSegs &S = s_seg[1];
+                for (int m = 0; m < 8; m++) {
+                    const size_t src = (size_t)(s0 + m * S.c[0]) * rb4, dst = S.off[0] + (size_t)m * S.as[0];
+                    ax::bulk_g2s(upg + dst, a.gate_sh + src, (uint32_t)S.c[0] * rb4, mb_pre);
+                    ax::bulk_g2s(upu + dst, a.up_sh + src, (uint32_t)S.c[0] * rb4, mb_pre);
+                }
             }
             if (nrow_out) ax::bulk_g2s(dnp(K), a.down_sh + (size_t)n0 * rb6, nrow_out * rb6, mb_pre);
         }
@@ -562,12 +657,12 @@ __global__ void __launch_bounds__(FD_THREADS, 1) decode_fused_kernel(FusedDecode
                 }
                 if (lane == q) my_e = 255 - (int)(wk & 0xFFu);
             }
-            // lane q < K issues the copies of slot q
-            if (lane < K) {
-                s_top[lane] = my_e;
-                issue_slot(lane, my_e);
-            }
-            if (lane == 0) close_up();
+            // every lane issues gate / up rows, lane q < K slot q's down slab
+            if (lane < K) s_top[lane] = my_e;
+            __syncwarp();
+            if (lane == 0) expect_up();
+            issue_rows(lane, 32);
+            if (lane < K) issue_dn(lane, my_e);
             FD_MARK(16)
             // certificate: every adjacent gap inside the top-k and the gap to
             // the rest exceed both bounds plus the margin (rounded against success)
@@ -619,7 +714,8 @@ __global__ void __launch_bounds__(FD_THREADS, 1) decode_fused_kernel(FusedDecode
         }
     } else {
         const int gt = tid - GRP;  // thread index inside group B
-        // quantised x: one lane per 32-element sub-block, no shuffles
+        // quantised x for the tensor-core dots: one lane per 32-element
+        // sub-block, no shuffles
         for (int sb = gt; sb < D / 32; sb += GRP) {
             const float4 *v4 = reinterpret_cast<const float4 *>(xs + sb * 32);
             float v[32];
@@ -631,16 +727,17 @@ __global__ void __launch_bounds__(FD_THREADS, 1) decode_fused_kernel(FusedDecode
             float m = 0.f, xsum = 0.f;
 #pragma unroll
             for (int i = 0; i < 32; i++) { m = fmaxf(m, fabsf(v[i])); xsum += v[i]; }
-            const float s = m / 32767.0f;
+            // x_int = rn(x * 16383 / max|x|) = 128 * hi + lo, hi int8, lo 0..127
+            const float s = m / 16383.0f, inv = (m > 0.0f) ? 16383.0f / m : 0.0f;
             uint32_t hw[8], lw[8];
 #pragma unroll
             for (int q = 0; q < 8; q++) {
                 uint32_t h4 = 0, l4 = 0;
 #pragma unroll
                 for (int i = 0; i < 4; i++) {
-                    const int xi = (m > 0.0f) ? __float2int_rn(v[4 * q + i] / s) : 0;
-                    h4 |= ((uint32_t)(xi >> 8) & 0xFFu) << (8 * i);
-                    l4 |= ((uint32_t)xi & 0xFFu) << (8 * i);
+                    const int xi = __float2int_rn(v[4 * q + i] * inv);
+                    h4 |= ((uint32_t)(xi >> 7) & 0xFFu) << (8 * i);
+                    l4 |= ((uint32_t)xi & 0x7Fu) << (8 * i);
                 }
                 hw[q] = h4;
                 lw[q] = l4;
@@ -656,21 +753,12 @@ __global__ void __launch_bounds__(FD_THREADS, 1) decode_fused_kernel(FusedDecode
         asm volatile("bar.sync 2, %0;" ::"r"(GRP) : "memory");
         FD_MARK_IF(gt == 0, 4)
         if (a.has_shared && s1 > s0) {
-            // my shared-expert rows (row slots nrp..), two per warp at a time,
+            // my shared-expert rows (row slots nrp..) on the tensor cores,
             // then each 16-row group quantised and published to slot K
             const int gw = wid - GRP / 32, NW = GRP / 32, ns = s1 - s0;
-            for (int i = gw; i < ns; i += 2 * NW) {
-                const int j = i + NW;
-                const uint8_t *gi = upg + (size_t)(nrp + i) * rb4, *ui = upu + (size_t)(nrp + i) * rb4;
-                if (j < ns) {
-                    const float2 h = swiglu_pair2(gi, ui, upg + (size_t)(nrp + j) * rb4, upu + (size_t)(nrp + j) * rb4,
-                                                  xq, D, lane);
-                    if (lane == 0) { hbuf[nrp + i] = h.x; hbuf[nrp + j] = h.y; }
-                } else {
-                    const float h = swiglu_pair(gi, ui, xq, D, lane);
-                    if (lane == 0) hbuf[nrp + i] = h;
-                }
-            }
+            pairs_dots(upg, upu, &s_seg[1], rb4, xq, D, part, gw, NW, lane);
+            asm volatile("bar.sync 2, %0;" ::"r"(GRP) : "memory");
+            for (int i = gt; i < ns; i += GRP) hbuf[nrp + i] = pair_h(part, s_seg[1], NW, i);
             asm volatile("bar.sync 2, %0;" ::"r"(GRP) : "memory");
             FD_MARK_IF(gt == 0, 5)
             for (int g = gw; g < ns / 16; g += NW)
@@ -686,7 +774,7 @@ __global__ void __launch_bounds__(FD_THREADS, 1) decode_fused_kernel(FusedDecode
         // The scratch overlays the routed down slabs and gate/up rows: let the
         // copies already issued land, and issue the final ones afterwards.
         if (tid == 0)
-            for (int i = 2; i < nbars; i++)
+            for (int i = 2; i < 4 + K; i++)  // mb_up, mb_dn (not mb_h: step 4)
                 if (!ax::mbar_wait(bars + i, 0, FD_WAIT_NS)) copy_fail = true;
         __syncthreads();
         float *wbuf = reinterpret_cast<float *>(dn + sdn);
@@ -806,8 +894,9 @@ __global__ void __launch_bounds__(FD_THREADS, 1) decode_fused_kernel(FusedDecode
         __syncthreads();
         if (tid == 0) {
             s_par = 1;
-            for (int q = 0; q < K; q++) issue_slot(q, s_top[q]);
-            close_up();
+            expect_up();
+            issue_rows(0, 1);
+            for (int q = 0; q < K; q++) issue_dn(q, s_top[q]);
         }
         __syncthreads();
     }
@@ -819,29 +908,18 @@ __global__ void __launch_bounds__(FD_THREADS, 1) decode_fused_kernel(FusedDecode
     const uint32_t par = s_par;
     FD_MARK(19)
 
-    // ---- step 3: routed h rows as their gate/up rows land, on every warp:
-    // warp w takes pairs w and w + FD_WARPS together, then w + 2 FD_WARPS ...
-    // (two independent rows per warp hide the dot / reduction latency) ----
+    // ---- step 3: routed h rows on the tensor cores, every warp (tiles of 8
+    // pairs x k-parts), once both segments' rows have landed ----
     {
         const int np = nrp;
-        const int seg_b = (slot_first + 1) * H - u0;  // pairs at or past this index are in slot_first + 1
-        for (int i = wid; i < np; i += 2 * FD_WARPS) {
-            const int j = i + FD_WARPS;
-            const bool two = j < np;
-            const int si = i < seg_b ? 0 : 1, sj = j < seg_b ? 0 : 1;
-            if (!ax::mbar_wait(mb_up + si, par, FD_WAIT_NS)) copy_fail = true;
-            if (two && !ax::mbar_wait(mb_up + sj, par, FD_WAIT_NS)) copy_fail = true;
-            FD_MARK_IF(tid == 0 && i == 0, 28)
-            if (two) {
-                const float2 h = swiglu_pair2(upg + (size_t)i * rb4, upu + (size_t)i * rb4, upg + (size_t)j * rb4,
-                                              upu + (size_t)j * rb4, xq, D, lane);
-                if (lane == 0) { hbuf[i] = h.x; hbuf[j] = h.y; }
-            } else {
-                const float h = swiglu_pair(upg + (size_t)i * rb4, upu + (size_t)i * rb4, xq, D, lane);
-                if (lane == 0) hbuf[i] = h;
-            }
-            FD_MARK_IF(tid == 0 && i == 0, 8)
-        }
+        if (!ax::mbar_wait(mb_up, par, FD_WAIT_NS)) copy_fail = true;
+        if (!ax::mbar_wait(mb_up + 1, par, FD_WAIT_NS)) copy_fail = true;
+        FD_MARK(28)
+        pairs_dots(upg, upu, &s_seg[0], rb4, xq, D, part, wid, FD_WARPS, lane);
+        FD_MARK(51)
+        __syncthreads();
+        FD_MARK(8)
+        for (int i = tid; i < np; i += FD_THREADS) hbuf[i] = pair_h(part, s_seg[0], FD_WARPS, i);
         __syncthreads();
         FD_MARK(10)
         // each 16-row group quantised once, here, and published to its slot
@@ -874,17 +952,6 @@ __global__ void __launch_bounds__(FD_THREADS, 1) decode_fused_kernel(FusedDecode
             q6k_half_dot(base + r * rb6 + (hb >> 1) * Q6K_BYTES, hb & 1, hslot(hqb, H, k), hb);
     }
     FD_MARK(12)
-#ifdef OFB_FD_TRACE
-    __syncthreads();
-    FD_MARK(49)
-    for (int t = tid; t < nslot * nrow_out * NHB; t += FD_THREADS) {
-        const int kh = t / nrow_out, r = t - kh * nrow_out, k = kh / NHB, hb = kh - k * NHB;
-        const uint32_t base = ax::smem_u32(dnp(k));
-        ysp[((size_t)k * rows_cap + r) * NHB + hb] =
-            q6k_half_dot(base + r * rb6 + (hb >> 1) * Q6K_BYTES, hb & 1, hslot(hqb, H, k), hb);
-    }
-    FD_MARK(50)
-#endif
     __syncthreads();
     FD_MARK(13)
     // y per (slot, row): the half-block partials summed in a fixed order,
@@ -973,6 +1040,9 @@ bool fused_plan(const ofb_moe_config *cfg, bool use_gate, bool has_shared, int G
         most_r = std::max(most_r, sh.rg1 - sh.rg0);
     }
     p.upc = 16 * most;
+    // gate (and up) region: up to three segments of 8 areas, each padded to
+    // a bank offset of 32 bytes
+    p.upb = (uint32_t)(((size_t)p.upc * rb4 + 24 * 128 + 127) & ~(size_t)127);
     if (16 * most_r > H) return false;  // a CTA's routed pairs span at most two slots
     p.ngc = (D / dg + G - 1) / G;
     const int rows_cap = p.ngc * dg, nhb = H / 128;
@@ -988,7 +1058,7 @@ bool fused_plan(const ofb_moe_config *cfg, bool use_gate, bool has_shared, int G
     const size_t sdn = (size_t)rows_cap * rb6;
     if ((size_t)p.rmax * (tpr / 32) * 24 > (size_t)K * sdn) return false;  // router partials
     p.o_dn = take((size_t)(K + 1) * sdn);
-    const size_t up = (size_t)2 * p.upc * rb4;
+    const size_t up = (size_t)2 * p.upb;
     p.o_up = take(up);
     const size_t fb = (size_t)XL_SMEM + (size_t)11 * E * 4;
     if ((size_t)p.o_up + up - ((size_t)p.o_dn + sdn) < fb) {
@@ -996,6 +1066,7 @@ bool fused_plan(const ofb_moe_config *cfg, bool use_gate, bool has_shared, int G
         off = (off + 127) & ~(size_t)127;
     }
     p.o_hb = take((size_t)p.upc * 4);
+    p.o_part = take((size_t)std::max(8 * FD_WARPS, p.upc + 8) * 8);
     p.o_hst = take((size_t)FD_WARPS * FD_GROUP_BYTES);
     p.o_hq = take((size_t)(K + 1) * hslot_bytes(H));
     p.o_sel = take((size_t)2 * E * 4);

@@ -23,7 +23,7 @@ def cfg_of(shape):
                 layout=shape.layout, routing=shape.routing, renorm=shape.renorm, shared_gate=shape.shared_gate)
 
 
-def run_tokens(ofb, oracle, cuda, shape, lw, xs, resid=None):
+def run_tokens(ofb, oracle, cuda, shape, lw, xs, resid=None, errors=False):
     """One T = 1 call per token on one layer; returns the worst relative error
     and the routing stats; asserts indices / weights per token."""
     layer = ofb.MoeLayer(shape, lw, max_tokens=1)
@@ -43,6 +43,9 @@ def run_tokens(ofb, oracle, cuda, shape, lw, xs, resid=None):
         err = np.abs(got - want).max() / np.abs(want).max()
         worst = max(worst, err)
         assert err <= TOL, f"token {t}: relative error {err}"
+    if errors:
+        torch.cuda.synchronize()
+        return worst, layer.ws.route_stats(), layer.ws.device_errors()
     return worst, layer.ws.route_stats()
 
 
@@ -90,8 +93,9 @@ def test_near_ties_recompute_candidates(ofb, oracle, cuda):
     lw = ofb.make_layer(shape, seed=3, device=cuda)
     lw.router = torch.from_numpy(router.reshape(-1)).to(cuda)
     xs = rng.normal(size=(12, 512)).astype(np.float32)
-    _, stats = run_tokens(ofb, oracle, cuda, shape, lw, xs)
+    _, stats, errs = run_tokens(ofb, oracle, cuda, shape, lw, xs, errors=True)
     assert stats[1] + stats[2] > 0
+    assert errs == 0  # no bounded wait expired on the recompute path
 
 
 @pytest.mark.parametrize("routing", [0, 1])
@@ -105,9 +109,10 @@ def test_exact_ties_full_recompute(ofb, oracle, cuda, routing):
     lw = ofb.make_layer(shape, seed=3, device=cuda)
     lw.router = torch.from_numpy(np.ascontiguousarray(router).reshape(-1)).to(cuda)
     xs = rng.normal(size=(8, 256)).astype(np.float32)
-    _, stats = run_tokens(ofb, oracle, cuda, shape, lw, xs)
+    _, stats, errs = run_tokens(ofb, oracle, cuda, shape, lw, xs, errors=True)
     if routing == 0:
         assert stats[2] > 0
+    assert errs == 0
 
 
 def test_back_to_back_calls_in_one_stream(ofb, oracle, cuda):
