@@ -121,7 +121,7 @@ __device__ __forceinline__ uint32_t u_of(float f) { return __float_as_uint(f); }
 // activations' scale and xsum_j the sum of their (unquantised) values.
 __device__ __forceinline__ void mma_u8s8(int (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
                                          uint32_t b0, uint32_t b1) {
-    asm volatile(
+    asm(  // a pure function of its operands: free to schedule
         "mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
         "{%0,%1,%2,%3};"
         : "+r"(c[0]), "+r"(c[1]), "+r"(c[2]), "+r"(c[3])
@@ -237,11 +237,11 @@ __device__ __forceinline__ float pair_h(const float2 *part, const FdSegs &S, int
     return silu_ref_d(gs) * us;
 }
 
-// 32-bit shared-memory loads by shared-window address.
+// 32-bit shared-memory loads by shared-window address (ordinary loads, so
+// the compiler may schedule them early; barriers and mbarrier waits carry
+// memory clobbers).
 __device__ __forceinline__ uint32_t lds32(uint32_t a) {
-    uint32_t v;
-    asm volatile("ld.shared.b32 %0, [%1];" : "=r"(v) : "r"(a));
-    return v;
+    return *reinterpret_cast<const uint32_t *>(__cvta_shared_to_generic(a));
 }
 // N consecutive 32-bit words starting at a 2-byte aligned shared address.
 template <int N>
@@ -257,8 +257,8 @@ __device__ __forceinline__ void lds_run2(uint32_t a, uint32_t (&w)[N]) {
 }
 
 // Quantised h of one expert slot in shared memory: hi / lo byte planes of
-// the 16-bit integer h_int (h ~= s_g * h_int, per 16-element group g), the
-// group scales s_g and the group sums of h_int.
+// the integer h_int = 256 * hi + lo (h ~= s_g * h_int, per 16-element group
+// g), the group scales s_g and the group sums of h_int.
 struct HSlot {
     int8_t *hh;
     uint8_t *hl;
@@ -276,8 +276,9 @@ __device__ __forceinline__ HSlot hslot(uint8_t *base, int H, int k) {
                  reinterpret_cast<int *>(p + 2 * pl + H / 4)};
 }
 // Quantises one 16-row h group (lanes 0..15 hold one value each; lanes
-// 16..31 only take part in the shuffles): h_int = rn(h * 32767 / max|h|),
-// scale max|h| / 32767, and the sum of h_int, as HSlot holds them. Stages
+// 16..31 only take part in the shuffles): h_int = rn(h * 32767 / max|h|) =
+// 256 * hi + lo (hi int8, lo 0..255), scale max|h| / 32767, and the sum of
+// h_int, as HSlot holds them. Stages
 // it in shared memory and lets lane 0 store it to group g of the global slot
 // image (hslot layout) and count it: its stores, one fence, one add, so the
 // count releases exactly the bytes it covers.
@@ -366,7 +367,6 @@ __global__ void __launch_bounds__(FD_THREADS, 1) decode_fused_kernel(FusedDecode
     const int D = a.D, H = a.H, E = a.E, K = a.K;
     const int rb4 = (D / QK) * Q4K_BYTES, rb6 = (H / QK) * Q6K_BYTES;
     const size_t exp4 = (size_t)rb4 * H, exp6 = (size_t)rb6 * D;
-    const int NHB = H / 128;  // half blocks per Q6_K row
 
     float *xs = reinterpret_cast<float *>(sm + P.o_x);
     unsigned char *xq = sm + P.o_xq;
@@ -382,13 +382,14 @@ __global__ void __launch_bounds__(FD_THREADS, 1) decode_fused_kernel(FusedDecode
     uint8_t *hqb = sm + P.o_hq;
     float *Lf = reinterpret_cast<float *>(sm + P.o_sel);
     float *Bf = Lf + E;
-    float *ysp = reinterpret_cast<float *>(sm + P.o_ys);  // [K+1][ngc*dg][NHB] partial dots
+    float *ysp = reinterpret_cast<float *>(sm + P.o_ys);  // [K+1][rows_cap][NHB] partial dots
     uint64_t *bars = reinterpret_cast<uint64_t *>(sm + P.o_bar);
     uint64_t *mb_pre = bars, *mb_x = bars + 1, *mb_up = bars + 2, *mb_dn = bars + 4;  // mb_dn[K]
     uint64_t *mb_h = bars + 4 + K;  // the copy of every routed h (step 4)
     const int nbars = 5 + K;
-    const size_t sdn = (size_t)P.ngc * P.dg * rb6;  // shared bytes per slot of down rows
-    const int rows_cap = P.ngc * P.dg;
+    const size_t sdn = P.sdn;      // shared bytes per slot of down rows
+    const int rows_cap = P.ngc;    // output rows per CTA at most
+    const int NHB = H / 128;       // half blocks per Q6_K row
     auto dnp = [&](int k) { return dn + (size_t)(k == K ? 0 : k + 1) * sdn; };
 
     __shared__ int s_top[16];
@@ -407,9 +408,12 @@ __global__ void __launch_bounds__(FD_THREADS, 1) decode_fused_kernel(FusedDecode
     const int u0 = 16 * share.rg0, u1 = 16 * share.rg1;  // routed pairs, top-k slot order
     const int s0 = 16 * share.sg0, s1 = 16 * share.sg1;  // shared-expert rows
     const int nrp = u1 - u0;                              // row slots [0, nrp) routed, then shared
-    const int NG = D / P.dg;
-    const int n0 = (int)((long long)c * NG / G) * P.dg, n1 = (int)((long long)(c + 1) * NG / G) * P.dg;
-    const int nrow_out = n1 - n0;
+    // output rows [n0, n1), as even as rows go; the down slabs are copied
+    // from a0 = n0 rounded down to dg rows (16-byte aligned), their size
+    // rounded up to 16 bytes (the rows past n1 are never read)
+    const int n0 = (int)((long long)c * D / G), n1 = (int)((long long)(c + 1) * D / G);
+    const int nrow_out = n1 - n0, a0 = n0 - n0 % P.dg;
+    const uint32_t slab = (uint32_t)(((n1 - a0) * rb6 + 15) & ~15);
     const int slot_first = u0 / H;  // the CTA's pairs span slots slot_first and (maybe) slot_first + 1
     // row segments: routed pairs of slot_first, of slot_first + 1, then the
     // shared-expert rows (s_seg[0] routed, s_seg[1] shared)
@@ -458,9 +462,8 @@ __global__ void __launch_bounds__(FD_THREADS, 1) decode_fused_kernel(FusedDecode
         }
     };
     auto issue_dn = [&](int q, int e) {
-        ax::mbar_arrive_expect(mb_dn + q, (uint32_t)nrow_out * rb6);
-        if (nrow_out)
-            ax::bulk_g2s(dnp(q), a.down + (size_t)e * exp6 + (size_t)n0 * rb6, nrow_out * rb6, mb_dn + q);
+        ax::mbar_arrive_expect(mb_dn + q, nrow_out ? slab : 0u);
+        if (nrow_out) ax::bulk_g2s(dnp(q), a.down + (size_t)e * exp6 + (size_t)a0 * rb6, slab, mb_dn + q);
     };
 
     // ---- step 0: static bytes, before waiting for the producer of x ----
@@ -475,7 +478,7 @@ __global__ void __launch_bounds__(FD_THREADS, 1) decode_fused_kernel(FusedDecode
     pdl_trigger();
     if (tid == 0) {
         uint32_t bytes = (uint32_t)nr_mine * D * 4;
-        if (a.has_shared) bytes += 2u * (s1 - s0) * rb4 + (uint32_t)nrow_out * rb6;
+        if (a.has_shared) bytes += 2u * (s1 - s0) * rb4 + (nrow_out ? slab : 0u);
         ax::mbar_arrive_expect(mb_pre, bytes);
         for (int i = 0; i < nr_mine; i++) {
             const int r = c + i * G;
@@ -491,7 +494,7 @@ __global__ void __launch_bounds__(FD_THREADS, 1) decode_fused_kernel(FusedDecode
                     ax::bulk_g2s(upu + dst, a.up_sh + src, (uint32_t)S.c[0] * rb4, mb_pre);
                 }
             }
-            if (nrow_out) ax::bulk_g2s(dnp(K), a.down_sh + (size_t)n0 * rb6, nrow_out * rb6, mb_pre);
+            if (nrow_out) ax::bulk_g2s(dnp(K), a.down_sh + (size_t)a0 * rb6, slab, mb_pre);
         }
     }
     pdl_wait();
@@ -947,7 +950,7 @@ __global__ void __launch_bounds__(FD_THREADS, 1) decode_fused_kernel(FusedDecode
     for (int t = tid; t < nslot * nrow_out * NHB; t += FD_THREADS) {
         const int kh = t / nrow_out, r = t - kh * nrow_out, k = kh / NHB, hb = kh - k * NHB;
         if (k < K && !ax::mbar_wait(mb_dn + k, par, FD_WAIT_NS)) copy_fail = true;
-        const uint32_t base = ax::smem_u32(dnp(k));
+        const uint32_t base = ax::smem_u32(dnp(k)) + (n0 - a0) * rb6;
         ysp[((size_t)k * rows_cap + r) * NHB + hb] =
             q6k_half_dot(base + r * rb6 + (hb >> 1) * Q6K_BYTES, hb & 1, hslot(hqb, H, k), hb);
     }
@@ -1044,8 +1047,8 @@ bool fused_plan(const ofb_moe_config *cfg, bool use_gate, bool has_shared, int G
     // a bank offset of 32 bytes
     p.upb = (uint32_t)(((size_t)p.upc * rb4 + 24 * 128 + 127) & ~(size_t)127);
     if (16 * most_r > H) return false;  // a CTA's routed pairs span at most two slots
-    p.ngc = (D / dg + G - 1) / G;
-    const int rows_cap = p.ngc * dg, nhb = H / 128;
+    p.ngc = (D + G - 1) / G;  // output rows per CTA at most
+    const int rows_cap = p.ngc;
     size_t off = 0;
     auto take = [&](size_t bytes) { size_t o = off; off = (off + bytes + 127) & ~(size_t)127; return (uint32_t)o; };
     p.o_x = take((size_t)D * 4);
@@ -1055,7 +1058,8 @@ bool fused_plan(const ofb_moe_config *cfg, bool use_gate, bool has_shared, int G
     // followed by the gate/up rows: the router rows' partial sums use the
     // routed down slabs before they are filled, and the selection's
     // exact-recompute scratch overlays the routed part of both
-    const size_t sdn = (size_t)rows_cap * rb6;
+    const size_t sdn = ((size_t)(rows_cap + dg - 1) * rb6 + 15) & ~(size_t)15;  // slab from the aligned-down start
+    p.sdn = (uint32_t)sdn;
     if ((size_t)p.rmax * (tpr / 32) * 24 > (size_t)K * sdn) return false;  // router partials
     p.o_dn = take((size_t)(K + 1) * sdn);
     const size_t up = (size_t)2 * p.upb;
@@ -1070,7 +1074,7 @@ bool fused_plan(const ofb_moe_config *cfg, bool use_gate, bool has_shared, int G
     p.o_hst = take((size_t)FD_WARPS * FD_GROUP_BYTES);
     p.o_hq = take((size_t)(K + 1) * hslot_bytes(H));
     p.o_sel = take((size_t)2 * E * 4);
-    p.o_ys = take((size_t)(K + 1) * rows_cap * nhb * 4);
+    p.o_ys = take((size_t)(K + 1) * rows_cap * (H / 128) * 4);
     p.o_bar = take((size_t)(5 + K) * 8);
     p.total = (uint32_t)off;
     return p.total <= 227 * 1024;
