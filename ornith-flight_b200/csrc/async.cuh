@@ -148,6 +148,12 @@ __device__ __forceinline__ void count_add(unsigned *p, unsigned n) {
 __device__ __forceinline__ void count_add_release(unsigned *p, unsigned n) {
     asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(p), "r"(n) : "memory");
 }
+// Adds n to *p with acquire-release semantics (gpu scope); returns the old value.
+__device__ __forceinline__ unsigned count_add_acq_rel(unsigned *p, unsigned n) {
+    unsigned old;
+    asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(n) : "memory");
+    return old;
+}
 // Waits until the counter has reached `target` (wrap-around aware); the
 // acquire orders the caller's later loads after the counted stores.
 __device__ __forceinline__ bool wait_count(const unsigned *p, unsigned target, unsigned long long limit_ns) {

@@ -284,6 +284,7 @@ __device__ __forceinline__ HSlot hslot(uint8_t *base, int H, int k) {
 // count releases exactly the bytes it covers.
 __device__ __noinline__ void publish_group(float v, uint8_t *stage, uint8_t *slot, int H, int g, unsigned *count,
                                            int lane) {
+    FD_MARK_IF(threadIdx.x == 0, 56)
     if (lane >= 16) v = 0.f;
     float m = fabsf(v);
 #pragma unroll
@@ -305,8 +306,9 @@ __device__ __noinline__ void publish_group(float v, uint8_t *stage, uint8_t *slo
         *reinterpret_cast<uint4 *>(slot + pl + at) = hl;
         reinterpret_cast<float *>(slot + 2 * pl)[g] = m / 32767.0f;
         reinterpret_cast<int *>(slot + 2 * pl + H / 4)[g] = sum;
-        __threadfence();
-        atomicAdd(count, 1u);
+        FD_MARK_IF(threadIdx.x == 0, 54)
+        ax::count_add_release(count, 1u);
+        FD_MARK_IF(threadIdx.x == 0, 55)
     }
     __syncwarp();
 }
@@ -602,7 +604,7 @@ __global__ void __launch_bounds__(FD_THREADS, 1) decode_fused_kernel(FusedDecode
             } else {
                 ax::put_tagged(a.cand + 2 * E, u_of(1.0f / (1.0f + expf(-(float)L))), tag);
             }
-            ax::count_add(a.sync + 3, 1u);
+            ax::count_add_release(a.sync + 3, 1u);
         }
     }
     FD_MARK(3)
@@ -997,8 +999,7 @@ __global__ void __launch_bounds__(FD_THREADS, 1) decode_fused_kernel(FusedDecode
             // let every copy this CTA issued land before its shared memory goes
             for (int i = 0; i < nbars; i++) ax::mbar_wait(bars + i, (i < 2 || i == nbars - 1) ? 0 : par, FD_WAIT_NS);
         }
-        __threadfence();
-        if (atomicAdd(&a.sync[1], 1u) == (unsigned)G - 1) {
+        if (ax::count_add_acq_rel(&a.sync[1], 1u) == (unsigned)G - 1) {
             a.sync[1] = 0;
             // every CTA is done: set the exchange counters to their exact
             // values for this epoch (repairs them after an expired wait)
