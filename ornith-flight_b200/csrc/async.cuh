@@ -148,6 +148,12 @@ __device__ __forceinline__ void count_add(unsigned *p, unsigned n) {
 __device__ __forceinline__ void count_add_release(unsigned *p, unsigned n) {
     asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(p), "r"(n) : "memory");
 }
+// Adds n to *p with no ordering: for counts that only say when to look, over
+// data that validates itself (tagged words), so the adder need not wait for its
+// earlier stores to become visible first.
+__device__ __forceinline__ void count_add_relaxed(unsigned *p, unsigned n) {
+    asm volatile("red.relaxed.gpu.global.add.u32 [%0], %1;" ::"l"(p), "r"(n) : "memory");
+}
 // Adds n to *p with acquire-release semantics (gpu scope); returns the old value.
 __device__ __forceinline__ unsigned count_add_acq_rel(unsigned *p, unsigned n) {
     unsigned old;

@@ -41,7 +41,8 @@
 //  4. once every group is counted: one bulk copy of all slots; y for its
 //     rows -> out = resid + g*y_sh + sum_k w_k y_k.
 // Tags and counter targets come from the launch epoch + 1: a device counter
-// the last CTA to finish advances, read after the dependent-launch wait
+// advanced by the last CTA to finish publishing (every CTA has read the epoch
+// by then), read after the dependent-launch wait
 // (which orders it after the previous launch), so stale words from earlier
 // launches never match and the kernel can be replayed (e.g. in a CUDA graph)
 // without host bookkeeping. Every wait (mbarrier, tag, counter) is bounded; on
@@ -501,6 +502,9 @@ __global__ void __launch_bounds__(FD_THREADS, 1) decode_fused_kernel(FusedDecode
     }
     pdl_wait();
     FD_MARK(1)
+    // the residual of my output rows, read now (used by the combine)
+    float *res_s = reinterpret_cast<float *>(sm + P.o_res);
+    if (tid < nrow_out) res_s[tid] = a.resid ? a.resid[n0 + tid] : 0.f;
     if (tid == 0) {
         s_tag = *reinterpret_cast<volatile unsigned int *>(a.sync) + 1u;
         ax::mbar_arrive_expect(mb_x, D * 4);
@@ -604,7 +608,9 @@ __global__ void __launch_bounds__(FD_THREADS, 1) decode_fused_kernel(FusedDecode
             } else {
                 ax::put_tagged(a.cand + 2 * E, u_of(1.0f / (1.0f + expf(-(float)L))), tag);
             }
-            ax::count_add_release(a.sync + 3, 1u);
+            // relaxed: the count only says when to read; a reader that sees
+            // it before a word's store polls that word until its tag matches
+            ax::count_add_relaxed(a.sync + 3, 1u);
         }
     }
     FD_MARK(3)
@@ -630,6 +636,14 @@ __global__ void __launch_bounds__(FD_THREADS, 1) decode_fused_kernel(FusedDecode
             s_gsc = a.use_gate ? f_of(ax::get_tagged(a.cand + 2 * E, tag, FD_WAIT_NS, tag_fail)) : 1.0f;
         asm volatile("bar.sync 1, %0;" ::"r"(GRP) : "memory");
         FD_MARK(6)
+        if (wid != 0) {
+            // copy v: routed gate/up row copies [0, 16 * ns), then the down
+            // slab of slot v - 16 * ns; warp w (1..7), lane l takes v = 7 l + w - 1
+            asm volatile("bar.sync 3, %0;" ::"r"(GRP) : "memory");
+            const int nv = 16 * s_seg[0].ns, v = 7 * lane + wid - 1;
+            if (v < nv) issue_rows(v, nv);
+            else if (v < nv + K) issue_dn(v - nv, s_top[v - nv]);
+        }
         if (wid == 0) {
             // keys: the order-preserving bits of L~ truncated to 24 bits, then
             // 255 - e (a larger key wins; equal values go to the smaller
@@ -652,6 +666,7 @@ __global__ void __launch_bounds__(FD_THREADS, 1) decode_fused_kernel(FusedDecode
             cx(2, 4); cx(3, 5);
             cx(1, 4); cx(3, 6);
             cx(1, 2); cx(3, 4); cx(5, 6);
+            FD_MARK(30)
             int my_e = 0;
             for (int q = 0; q < K; q++) {
                 const uint32_t wk = __reduce_max_sync(0xffffffffu, k8[0]);
@@ -663,11 +678,13 @@ __global__ void __launch_bounds__(FD_THREADS, 1) decode_fused_kernel(FusedDecode
                 if (lane == q) my_e = 255 - (int)(wk & 0xFFu);
             }
             // every lane issues gate / up rows, lane q < K slot q's down slab
+            FD_MARK(31)
             if (lane < K) s_top[lane] = my_e;
             __syncwarp();
             if (lane == 0) expect_up();
-            issue_rows(lane, 32);
-            if (lane < K) issue_dn(lane, my_e);
+            // warps 1-7 issue the copies (a warp issues its lanes' bulk
+            // copies one after another, so spreading them shortens the issue)
+            asm volatile("bar.arrive 3, %0;" ::"r"(GRP) : "memory");
             FD_MARK(16)
             // certificate: every adjacent gap inside the top-k and the gap to
             // the rest exceed both bounds plus the margin (rounded against success)
@@ -934,6 +951,22 @@ __global__ void __launch_bounds__(FD_THREADS, 1) decode_fused_kernel(FusedDecode
                           a.sync + 4, lane);
         }
     }
+    // every CTA has published everything it publishes in this launch: count
+    // it finished (off the critical path: the h groups of the other CTAs are
+    // still arriving). The last one sets the exchange counters to their exact
+    // values for this epoch (repairing them after an expired wait) and
+    // advances the epoch; every CTA read the epoch before publishing its
+    // router rows, and nothing reads it again in this launch.
+    __syncthreads();
+    if (tid == 32) {
+        if (ax::count_add_acq_rel(&a.sync[1], 1u) == (unsigned)G - 1) {
+            a.sync[1] = 0;
+            a.sync[3] = tag * (unsigned)nrows;
+            a.sync[4] = tag * (unsigned)(NRG + NSG);
+            __threadfence();
+            atomicAdd(&a.sync[0], 1u);
+        }
+    }
     FD_MARK(9)
     // ---- step 4: the quantised h of every slot (one bulk copy of the
     // global slot image once every group is counted); y of my rows ----
@@ -971,7 +1004,7 @@ __global__ void __launch_bounds__(FD_THREADS, 1) decode_fused_kernel(FusedDecode
     __syncthreads();
     for (int r = tid; r < nrow_out; r += FD_THREADS) {
         const int n = n0 + r;
-        float acc = a.resid ? a.resid[n] : 0.f;
+        float acc = res_s[r];  // thread r wrote it after the dependent-launch wait
         float yv[16], wv[16];
 #pragma unroll
         for (int k = 0; k < 16; k++) {
@@ -998,15 +1031,6 @@ __global__ void __launch_bounds__(FD_THREADS, 1) decode_fused_kernel(FusedDecode
             atomicOr(&a.sync[2], s_err);
             // let every copy this CTA issued land before its shared memory goes
             for (int i = 0; i < nbars; i++) ax::mbar_wait(bars + i, (i < 2 || i == nbars - 1) ? 0 : par, FD_WAIT_NS);
-        }
-        if (ax::count_add_acq_rel(&a.sync[1], 1u) == (unsigned)G - 1) {
-            a.sync[1] = 0;
-            // every CTA is done: set the exchange counters to their exact
-            // values for this epoch (repairs them after an expired wait)
-            a.sync[3] = tag * (unsigned)nrows;
-            a.sync[4] = tag * (unsigned)(NRG + NSG);
-            __threadfence();
-            atomicAdd(&a.sync[0], 1u);
         }
     }
     FD_MARK(15)
@@ -1076,6 +1100,8 @@ bool fused_plan(const ofb_moe_config *cfg, bool use_gate, bool has_shared, int G
     p.o_hq = take((size_t)(K + 1) * hslot_bytes(H));
     p.o_sel = take((size_t)2 * E * 4);
     p.o_ys = take((size_t)(K + 1) * rows_cap * (H / 128) * 4);
+    p.o_res = take((size_t)rows_cap * 4);
+    if (rows_cap > FD_THREADS) return false;  // residual rows: one thread each
     p.o_bar = take((size_t)(5 + K) * 8);
     p.total = (uint32_t)off;
     return p.total <= 227 * 1024;

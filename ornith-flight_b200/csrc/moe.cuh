@@ -108,7 +108,7 @@ struct FusedPlan {
     int G, rmax, upc, ngc, dg;
     uint32_t upb;  // bytes of the gate-row region (the up rows follow)
     uint32_t sdn;  // bytes of one slot's down slab (ngc output rows + alignment)
-    uint32_t o_x, o_xq, o_rr, o_dn, o_up, o_hb, o_part, o_hst, o_hq, o_sel, o_ys, o_bar, total;
+    uint32_t o_x, o_xq, o_rr, o_dn, o_up, o_hb, o_part, o_hst, o_hq, o_sel, o_ys, o_res, o_bar, total;
 };
 bool fused_plan(const ofb_moe_config *cfg, bool use_gate, bool has_shared, int grid, FusedPlan &p);
 
