@@ -33,9 +33,128 @@ __device__ __forceinline__ float silu_ref(float g) {
 
 __device__ __forceinline__ int asg_token(int a, int TK, int K) { return a < TK ? a / K : a - TK; }
 
-__global__ void __launch_bounds__(1024) plan_kernel(PlanArgs p) {
-    __shared__ int cnt[1024], cursor[1024], wsum[66];
-    build_plan(p, cnt, cursor, wsum);
+// ---- dispatch plan over many CTAs ------------------------------------------------
+// The CSR plan of build_plan (kept routed assignments grouped by expert in
+// ascending expert order, then the shared slot) for large batches, in three
+// launches: CTA b counts the kept assignments [b*PLAN_CH, (b+1)*PLAN_CH) per
+// expert (hist[b][e]); one block turns the counts into each CTA's first
+// position per expert, the slot list and (for the tensor-core path) the tile
+// list; CTA b then places its assignments. Within one expert the
+// assignments of a CTA land in any order (the expert kernels treat every row
+// on its own).
+__global__ void __launch_bounds__(256) plan_hist_kernel(PlanArgs p, int *__restrict__ hist) {
+    __shared__ int cnt[1024];
+    const int tid = threadIdx.x, TK = p.T * p.K, i0 = blockIdx.x * PLAN_CH, i1 = min(TK, i0 + PLAN_CH);
+    for (int e = tid; e < p.E; e += blockDim.x) cnt[e] = 0;
+    __syncthreads();
+    for (int i = i0 + tid; i < i1; i += blockDim.x)
+        if (!(__ldcg(p.w + i) < 1e-6f)) atomicAdd(&cnt[__ldcg(p.idx + i)], 1);  // model.c:1066 skip rule
+    __syncthreads();
+    for (int e = tid; e < p.E; e += blockDim.x) hist[(size_t)blockIdx.x * p.E + e] = cnt[e];
+}
+
+// One block of 1024 threads, thread e owning expert e (E <= 1024). hist[b][e]
+// becomes CTA b's offset inside expert e's run, hist[nb][e] the run's start,
+// hist[nb][E] the number of kept routed assignments.
+__global__ void __launch_bounds__(1024) plan_scan_kernel(PlanArgs p, int *__restrict__ hist, int nb,
+                                                         int *__restrict__ tiles, int max_tiles) {
+    __shared__ int ws[32][3], tot[3];
+    const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5, E = p.E;
+    int c = 0;
+    if (tid < E)
+        for (int b = 0; b < nb; b++) {
+            const int v = hist[(size_t)b * E + tid];
+            hist[(size_t)b * E + tid] = c;
+            c += v;
+        }
+    // exclusive scans over experts of (has slot, count, tiles)
+    const int nt = (c + PF_NMAX - 1) / PF_NMAX;
+    int v[3] = {c > 0, c, nt}, inc[3] = {v[0], v[1], v[2]};
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1)
+#pragma unroll
+        for (int q = 0; q < 3; q++) {
+            const int u = __shfl_up_sync(0xffffffffu, inc[q], o);
+            if (lane >= o) inc[q] += u;
+        }
+    if (lane == 31)
+        for (int q = 0; q < 3; q++) ws[wid][q] = inc[q];
+    __syncthreads();
+    if (wid == 0) {
+        int a[3], ai[3];
+        for (int q = 0; q < 3; q++) ai[q] = a[q] = ws[lane][q];
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1)
+#pragma unroll
+            for (int q = 0; q < 3; q++) {
+                const int u = __shfl_up_sync(0xffffffffu, ai[q], o);
+                if (lane >= o) ai[q] += u;
+            }
+        for (int q = 0; q < 3; q++) {
+            ws[lane][q] = ai[q] - a[q];
+            if (lane == 31) tot[q] = ai[q];
+        }
+    }
+    __syncthreads();
+    const int F = inc[0] - v[0] + ws[wid][0], C = inc[1] - v[1] + ws[wid][1], Tb = inc[2] - v[2] + ws[wid][2];
+    int *n_tiles = tiles, *tile_slot = tiles + 1, *tile_start = tile_slot + max_tiles, *tile_n = tile_start + max_tiles;
+    if (tid < E) {
+        hist[(size_t)nb * E + tid] = C;
+        if (c > 0) {
+            p.slot_expert[F] = tid;
+            p.slot_start[F] = C;
+            if (tiles)
+                for (int k = 0; k < nt; k++) {
+                    tile_slot[Tb + k] = F;
+                    tile_start[Tb + k] = C + k * PF_NMAX;
+                    tile_n[Tb + k] = min(PF_NMAX, c - k * PF_NMAX);
+                }
+        }
+    }
+    if (tid == 0) {
+        const int ns = tot[0], total = tot[1];
+        int u = ns, ntl = tot[2];
+        hist[(size_t)nb * E + E] = total;
+        if (p.has_shared) {
+            p.slot_expert[u] = E;
+            p.slot_start[u] = total;
+            if (tiles)
+                for (int k = 0; k * PF_NMAX < p.T; k++, ntl++) {
+                    tile_slot[ntl] = u;
+                    tile_start[ntl] = total + k * PF_NMAX;
+                    tile_n[ntl] = min(PF_NMAX, p.T - k * PF_NMAX);
+                }
+            u++;
+            p.slot_start[u] = total + p.T;
+        } else {
+            p.slot_start[u] = total;
+        }
+        *p.n_slots = u;
+        if (tiles) *n_tiles = ntl;
+    }
+}
+
+__global__ void __launch_bounds__(256) plan_scatter_kernel(PlanArgs p, const int *__restrict__ hist, int nb) {
+    __shared__ int cur[1024];
+    const int tid = threadIdx.x, E = p.E, TK = p.T * p.K, i0 = blockIdx.x * PLAN_CH, i1 = min(TK, i0 + PLAN_CH);
+    for (int e = tid; e < E; e += blockDim.x) cur[e] = hist[(size_t)blockIdx.x * E + e] + hist[(size_t)nb * E + e];
+    __syncthreads();
+    for (int i = i0 + tid; i < i1; i += blockDim.x)
+        if (!(__ldcg(p.w + i) < 1e-6f)) p.assign[atomicAdd(&cur[__ldcg(p.idx + i)], 1)] = i;
+    if (p.has_shared) {
+        const int total = hist[(size_t)nb * E + E];
+        for (int t = blockIdx.x * blockDim.x + tid; t < p.T; t += gridDim.x * blockDim.x) p.assign[total + t] = TK + t;
+    }
+}
+
+int launch_plan(const PlanArgs &p, int *hist, int *tiles, int max_tiles, cudaStream_t s) {
+    if (p.E > 1024) { set_error("plan: at most 1024 experts"); return OFB_EUNSUPPORTED; }
+    const int nb = (p.T * p.K + PLAN_CH - 1) / PLAN_CH;
+    if (nb > 0) plan_hist_kernel<<<nb, 256, 0, s>>>(p, hist);
+    plan_scan_kernel<<<1, 1024, 0, s>>>(p, hist, nb, tiles, max_tiles);
+    plan_scatter_kernel<<<nb > 0 ? nb : 1, 256, 0, s>>>(p, hist, nb);
+    OFB_CHECK_LAUNCH("plan");
+    return OFB_OK;
 }
 
 // Shared-expert gates sigmoid(x . v), one warp per token (tolerance-level:
@@ -163,6 +282,7 @@ WorkspaceLayout workspace_layout(const ofb_moe_config *c, int max_tokens) {
     L.slot_expert = take((E + 1) * 4);
     L.slot_start = take((E + 2) * 4);
     L.assign = take(A * 4);
+    L.phist = take(plan_hist_ints(max_tokens, (int)K, (int)E) * 4);
     // h / y (f32) serve the decode kernels (T <= gemv_max_tokens) and the
     // interleaved path; the tensor-core prefill path uses bf16 x and h instead
     const bool inter = c->layout == OFB_LAYOUT_INTERLEAVED;
@@ -231,6 +351,10 @@ int run_moe_layer(const ofb_moe_config *cfg, const ofb_moe_weights *wt, const fl
     p.slot_start = (int *)(base + L.slot_start);
     p.assign = (int *)(base + L.assign);
     int st;
+    // the plan also lays out the tensor-core tiles when the layer goes there
+    const bool tc_path = cfg->layout == OFB_LAYOUT_CONTIGUOUS && !use_gemv(T, K, E, H) && H <= PREFILL_MAX_H &&
+                         (size_t)prefill_max_tiles(T, K, E) <= L.prefill_tiles;
+    int *plan_tiles = tc_path ? (int *)(base + L.tiles) : nullptr;
     if (T == 1 && !given_idx && wt->router && cfg->layout == OFB_LAYOUT_CONTIGUOUS) {
         // decode batch 1: the whole layer in one launch when the shape fits
         const bool has_sh = wt->gate_shexp && wt->up_shexp && wt->down_shexp;
@@ -268,7 +392,7 @@ int run_moe_layer(const ofb_moe_config *cfg, const ofb_moe_weights *wt, const fl
                                           (int *)(base + L.logits), ctr, ctr + FAST_ROUTE_MAX_T + 1, idx, w, s)))
             return st;
         mark(1);
-        plan_kernel<<<1, 1024, 0, s>>>(p);
+        if ((st = launch_plan(p, (int *)(base + L.phist), plan_tiles, prefill_max_tiles(T, K, E), s))) return st;
         if (p.has_shared && p.shared_gate)
             shared_gate_kernel<<<(T + 7) / 8, 256, 0, s>>>(x, p.gate_v, T, D, p.gsc);
         OFB_CHECK_LAUNCH("plan");
@@ -283,7 +407,7 @@ int run_moe_layer(const ofb_moe_config *cfg, const ofb_moe_weights *wt, const fl
             return st;
         }
         mark(1);
-        plan_kernel<<<1, 1024, 0, s>>>(p);
+        if ((st = launch_plan(p, (int *)(base + L.phist), plan_tiles, prefill_max_tiles(T, K, E), s))) return st;
         if (p.has_shared && p.shared_gate)
             shared_gate_kernel<<<(T + 7) / 8, 256, 0, s>>>(x, p.gate_v, T, D, p.gsc);
         OFB_CHECK_LAUNCH("plan");
@@ -347,7 +471,7 @@ int run_moe_layer(const ofb_moe_config *cfg, const ofb_moe_weights *wt, const fl
     }
     int *err = (int *)(base + L.counters) + FAST_ROUTE_MAX_T + 4 + D / DOWN_TICKET_ROWS;
     if ((st = launch_prefill(a, x, p.n_slots, (__nv_bfloat16 *)(base + L.xb), (__nv_bfloat16 *)(base + L.hb),
-                             (int *)(base + L.tiles), err, s, ev ? ev[2] : nullptr, ev ? ev[3] : nullptr)))
+                             (int *)(base + L.tiles), !fast && plan_tiles != nullptr, err, s, ev ? ev[2] : nullptr, ev ? ev[3] : nullptr)))
         return st;
     mark(4);
     return OFB_OK;

@@ -42,6 +42,7 @@ struct WorkspaceLayout {
     // shape, so a fixed scratch keeps it in place across calls of any size.
     size_t fsync, fcand, fh, fused_bytes;
     size_t logits, idx, w, gsc, n_slots, slot_expert, slot_start, assign, h, y;
+    size_t phist;     // per-CTA expert counts of the many-CTA plan (plan_hist_ints)
     size_t cand;      // fast routing: (approximate logit, bound) per (token, row)
     size_t norms;     // large-batch routing: segment norms of x rows and router rows
     size_t xq;        // decode: quantised activations [T][xq_stride(D)]
@@ -80,8 +81,18 @@ __host__ __device__ inline bool use_gemv(int T, int K, int E, int H) {
 
 int launch_quantize_x(const float *x, int T, int D, unsigned char *xq, cudaStream_t s);
 int prefill_max_tiles(int T, int K, int E);
+constexpr int PF_NMAX = 192;  // token rows per tensor-core tile (the MMA's N, at most)
+// Dispatch plan over many CTAs (large batches): per-CTA histograms, one
+// scan block (slots, and the tensor-core tile list when `tiles` is given),
+// then the scatter. `hist` holds plan_hist_ints(T, K, E) ints.
+constexpr int PLAN_CH = 256;  // routed assignments per histogram CTA
+inline size_t plan_hist_ints(int T, int K, int E) {
+    const size_t nb = ((size_t)T * K + PLAN_CH - 1) / PLAN_CH;
+    return (nb + 1) * (size_t)E + 1;
+}
+int launch_plan(const PlanArgs &p, int *hist, int *tiles, int max_tiles, cudaStream_t s);
 int launch_prefill(const LayerArgs &la, const float *x, int *n_slots, __nv_bfloat16 *xb, __nv_bfloat16 *hb,
-                   int *tiles, int *err, cudaStream_t s, cudaEvent_t before = nullptr,
+                   int *tiles, bool tiles_ready, int *err, cudaStream_t s, cudaEvent_t before = nullptr,
                    cudaEvent_t between = nullptr);
 int launch_up_q(const LayerArgs &a, const unsigned char *xq, int max_slots, cudaStream_t s);
 int launch_down_q(const LayerArgs &a, int *tickets, int max_slots, cudaStream_t s);

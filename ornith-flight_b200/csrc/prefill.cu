@@ -48,7 +48,6 @@
 namespace ofb {
 
 constexpr int PF_M = 128;        // weight rows per CTA (MMA M)
-constexpr int PF_NMAX = 192;     // token rows per tile (MMA N, max; bounded by TMEM columns)
 constexpr int PF_KS = 64;        // K elements per pipeline stage (= one 128-byte swizzle row)
 constexpr int PF_DQ0 = 128;      // first dequantising thread
 constexpr int PF_NDQW = 16;      // dequantising warps
@@ -1101,7 +1100,7 @@ static int encode_q4_rows(CUtensorMap *map, const void *base, int D, uint64_t ro
 }
 
 int launch_prefill(const LayerArgs &la, const float *x, int *n_slots, __nv_bfloat16 *xb, __nv_bfloat16 *hb,
-                   int *tiles, int *err, cudaStream_t s, cudaEvent_t before, cudaEvent_t between) {
+                   int *tiles, bool tiles_ready, int *err, cudaStream_t s, cudaEvent_t before, cudaEvent_t between) {
     const int T = la.T, D = la.D, H = la.H;
     const int max_tiles = prefill_max_tiles(T, la.K, la.E);
     const int n_asg = T * la.K + T;
@@ -1125,7 +1124,7 @@ int launch_prefill(const LayerArgs &la, const float *x, int *n_slots, __nv_bfloa
                                                          D, xb);
     else
         gather_rows_kernel<<<148 * 8, 256, 0, s>>>(x, la.assign, n_slots, la.slot_start, T * la.K, la.K, D, xb);
-    tile_plan_kernel<<<1, 1024, 0, s>>>(n_slots, la.slot_start, n_tiles, tile_slot, tile_start, tile_n);
+    if (!tiles_ready) tile_plan_kernel<<<1, 1024, 0, s>>>(n_slots, la.slot_start, n_tiles, tile_slot, tile_start, tile_n);
     PrefillArgs a;
     a.T = T; a.D = D; a.H = H; a.E = la.E; a.K = la.K;
     a.shared_gate = la.shared_gate;
