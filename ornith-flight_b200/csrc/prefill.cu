@@ -958,11 +958,12 @@ __global__ void gather_rows_kernel(const float *__restrict__ x, const int *__res
     const int rows = slot_start[*n_slots];
     const int lane = threadIdx.x & 31;
     for (int p = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; p < rows; p += (gridDim.x * blockDim.x) >> 5) {
+        // 8 elements per lane and step: two 16-byte loads, one 16-byte store
         const float4 *src = reinterpret_cast<const float4 *>(x + (size_t)asg_token_p(assign[p], TK, K) * D);
-        uint2 *dst = reinterpret_cast<uint2 *>(xg + (size_t)p * D);
-        for (int c = lane; c < D / 4; c += 32) {
-            const float4 v = __ldg(src + c);
-            dst[c] = make_uint2(pack_bf16(v.x, v.y), pack_bf16(v.z, v.w));
+        uint4 *dst = reinterpret_cast<uint4 *>(xg + (size_t)p * D);
+        for (int c = lane; c < D / 8; c += 32) {
+            const float4 v = __ldg(src + 2 * c), u = __ldg(src + 2 * c + 1);
+            dst[c] = make_uint4(pack_bf16(v.x, v.y), pack_bf16(v.z, v.w), pack_bf16(u.x, u.y), pack_bf16(u.z, u.w));
         }
     }
 }
