@@ -881,7 +881,7 @@ __global__ void __launch_bounds__(FD_THREADS, 1) decode_fused_kernel(FusedDecode
         }
         if (wid == 0) {
             if (s_full) {
-                for (int i = 0; i < K; i++) exchange_pass(val, id, oval, oid, E, i, lane);
+                exchange_topk(val, id, oval, oid, E, K, lane);
                 if (lane == 0) {
                     float ssum = 0.0f;
                     for (int q = 0; q < K; q++) ssum = __fadd_rn(ssum, val[q]);
@@ -892,7 +892,7 @@ __global__ void __launch_bounds__(FD_THREADS, 1) decode_fused_kernel(FusedDecode
                     s_mode = 2;
                 }
             } else {
-                for (int i = 0; i < K; i++) exchange_pass(cv, cid, cov, coid, nc, i, lane);
+                exchange_topk(cv, cid, cov, coid, nc, K, lane);
                 __syncwarp();
                 const int tk = lane < K ? cid[lane] : 0;
                 const float m = Lf[cid[0]];

@@ -51,4 +51,40 @@ static __device__ void exchange_pass(float *val, int *id, float *oval, int *oid,
     __syncwarp();
 }
 
+// The first k passes of the reference's exchange sort (engine/src/model.c:
+// 1042-1049) over a[0..n), literally, by one thread: for short candidate
+// lists this is much faster than k warp passes. Same result as exchange_pass
+// for i = 0..k-1.
+static __device__ __forceinline__ void exchange_sort_serial(float *val, int *id, int n, int k) {
+    for (int i = 0; i < k && i < n; i++) {
+        float vi = val[i];
+        int ii = id[i];
+        for (int j = i + 1; j < n; j++) {
+            const float vj = val[j];
+            if (vj > vi) {
+                val[j] = vi;
+                const int ij = id[j];
+                id[j] = ii;
+                vi = vj;
+                ii = ij;
+            }
+        }
+        val[i] = vi;
+        id[i] = ii;
+    }
+}
+
+// Top-k passes over n candidates by warp `lane`s: serial for short lists,
+// else the warp emulation.
+constexpr int EXCHANGE_SERIAL_MAX = 64;
+static __device__ __forceinline__ void exchange_topk(float *val, int *id, float *oval, int *oid, int n, int k,
+                                                     int lane) {
+    if (n <= EXCHANGE_SERIAL_MAX) {
+        if (lane == 0) exchange_sort_serial(val, id, n, k);
+        __syncwarp();
+    } else {
+        for (int i = 0; i < k; i++) exchange_pass(val, id, oval, oid, n, i, lane);
+    }
+}
+
 }  // namespace ofb

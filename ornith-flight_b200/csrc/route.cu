@@ -140,7 +140,7 @@ __global__ void __launch_bounds__(128) route_select(const float *__restrict__ lo
     for (int e = lane; e < E; e += 32) { val[e] = lg[e]; id[e] = e; }
     __syncwarp();
     if (routing == OFB_ROUTE_GET_ROUTING) {
-        for (int i = 0; i < K; i++) exchange_pass(val, id, oval, oid, E, i, lane);
+        exchange_topk(val, id, oval, oid, E, K, lane);
         if (lane == 0) {
             // model.c:306-317: softmax over the kept logits
             float mx = val[0], sum = 0.0f, s[16];
@@ -166,7 +166,7 @@ __global__ void __launch_bounds__(128) route_select(const float *__restrict__ lo
     sum = __shfl_sync(0xffffffffu, sum, 0);
     for (int e = lane; e < E; e += 32) val[e] = __fdiv_rn(val[e], sum);
     __syncwarp();
-    for (int i = 0; i < K; i++) exchange_pass(val, id, oval, oid, E, i, lane);
+    exchange_topk(val, id, oval, oid, E, K, lane);
     if (lane == 0) {
         float ssum = 0.0f;
         for (int a = 0; a < K; a++) ssum = __fadd_rn(ssum, val[a]);

@@ -50,7 +50,21 @@ namespace ofb {
 
 DTRACE_DEFINE(rf)
 
-constexpr int RR_WARPS = 2;  // router rows per block in the row kernel
+// Optional per-block timeline of route_select_fast (build with
+// -DOFB_RS_TRACE): globaltimer at each step of the last launch, one row per
+// token block, read back with ofb_debug_rs_trace.
+#ifdef OFB_RS_TRACE
+__device__ unsigned long long g_rs_tr[64][16];
+#define RS_MARK(i) \
+    if (threadIdx.x == 0 && blockIdx.x < 64) { unsigned long long t_; asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t_)); g_rs_tr[blockIdx.x][i] = t_; }
+extern "C" int ofb_debug_rs_trace(unsigned long long *host) {
+    return cudaMemcpyFromSymbol(host, g_rs_tr, sizeof(g_rs_tr)) == cudaSuccess ? 0 : 1;
+}
+#else
+#define RS_MARK(i)
+#endif
+
+constexpr int RR_WARPS = 8;  // router rows per block in the row kernel (at most)
 constexpr int FR_WARPS = 8;
 constexpr int FR_THREADS = FR_WARPS * 32;
 constexpr double FR_MARGIN = 0x1.0p-14;
@@ -96,64 +110,70 @@ __device__ __forceinline__ void quantize_subblock(float v, unsigned char *q, int
 }
 
 // ---- kernel 1: router rows ---------------------------------------------------
+// Lane l of a row's warp owns the contiguous segment [l*seg, (l+1)*seg),
+// seg = D/32 (the prefix bound below needs contiguous segments). Reading such
+// segments straight from global memory makes every 16-byte load of a warp
+// touch 32 sectors, so the block first moves its router rows (before the
+// dependent-launch wait: the router is static) and the token's x (after it)
+// into shared memory with coalesced loads, in a segment-major layout padded
+// by 4 floats per segment (a quarter-warp's 16-byte reads hit distinct banks).
+__host__ __device__ inline int rr_seg_ld(int D) { return D / 32 + 4; }  // floats per lane segment
+__host__ __device__ inline size_t rr_smem(int D, int nw) { return (size_t)(nw + 1) * 32 * rr_seg_ld(D) * 4; }
+
+// Coalesced copy of n floats (n a multiple of 4) into the segment-major layout.
+__device__ __forceinline__ void rr_stage(float *dst, const float *__restrict__ src, int D, int i0, int step) {
+    const int seg = D / 32, ld = rr_seg_ld(D);
+    const float4 *s4 = reinterpret_cast<const float4 *>(src);
+#pragma unroll 4
+    for (int q = i0; q < D / 4; q += step) {
+        const int e = 4 * q, l = e / seg;
+        *reinterpret_cast<float4 *>(dst + l * ld + (e - l * seg)) = __ldg(s4 + q);
+    }
+}
+
 __global__ void __launch_bounds__(RR_WARPS * 32) route_rows_kernel(FastRouteArgs a) {
     DTRACE_START(rf, 0)
     pdl_trigger();
-    const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+    extern __shared__ __align__(16) float rr_sm[];
+    const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5, nw = blockDim.x >> 5;
     const int t = blockIdx.y;
-    const int E = a.E, D = a.D;
-    const int r = blockIdx.x * RR_WARPS + wid;  // router row; r == E is the gate vector
+    const int E = a.E, D = a.D, ld = rr_seg_ld(D);
+    const int r = blockIdx.x * nw + wid;  // router row; r == E is the gate vector
     const float *xt = a.x + (size_t)t * D;
     const bool has_row = (r < E) || (r == E && a.gate_v);
     const int seg = D / 32;  // multiple of 8
-    constexpr int PF = 16;   // float4 per lane held in flight
-    const float *wr = (r < E) ? a.W + (size_t)r * D : a.gate_v;
-    const float4 *w4 = reinterpret_cast<const float4 *>(wr + lane * seg);
-    const float4 *x4 = reinterpret_cast<const float4 *>(xt + lane * seg);
-    float4 wv[PF], xv[PF];
-    // the router is static: load it before waiting for the producer of x
-    if (has_row) {
-#pragma unroll
-        for (int j = 0; j < PF; j++)
-            if (j < seg / 4) wv[j] = __ldg(w4 + j);
-    }
+    float *xs = rr_sm, *wrow = rr_sm + (size_t)(1 + wid) * 32 * ld;
+    // the router is static: stage it before waiting for the producer of x
+    if (has_row) rr_stage(wrow, (r < E) ? a.W + (size_t)r * D : a.gate_v, D, lane, 32);
     pdl_wait();
     DTRACE_WAITED(rf, 0)
-    if (has_row) {
-#pragma unroll
-        for (int j = 0; j < PF; j++)
-            if (j < seg / 4) xv[j] = __ldg(x4 + j);
-    }
+    rr_stage(xs, xt, D, threadIdx.x, blockDim.x);
     if (a.xq && r > E) {
         // warps past the router rows and the gate vector quantise x, beside
         // the rows rather than in front of them
         unsigned char *q = a.xq + (size_t)t * xq_stride(D);
-        const int nq = gridDim.x * RR_WARPS - (E + 1);
+        const int nq = gridDim.x * nw - (E + 1);
         for (int sb = r - (E + 1); sb < D / 32; sb += nq)
             quantize_subblock(__ldg(xt + sb * 32 + lane), q, D, sb, lane);
     }
+    __syncthreads();
     if (!has_row) {
         DTRACE_END(rf, 0)
         return;
     }
+    const float4 *w4 = reinterpret_cast<const float4 *>(wrow + lane * ld);
+    const float4 *x4 = reinterpret_cast<const float4 *>(xs + lane * ld);
     double P = 0.0, SP = 0.0, A = 0.0;
-    for (int i0 = 0; i0 < seg / 4; i0 += PF) {
-        if (i0) {
-#pragma unroll
-            for (int j = 0; j < PF; j++)
-                if (i0 + j < seg / 4) { wv[j] = __ldg(w4 + i0 + j); xv[j] = __ldg(x4 + i0 + j); }
-        }
-#pragma unroll
-        for (int j = 0; j < PF; j++) {
-            if (i0 + j >= seg / 4) break;
-            const double p0 = (double)xv[j].x * wv[j].x, p1 = (double)xv[j].y * wv[j].y;
-            const double p2 = (double)xv[j].z * wv[j].z, p3 = (double)xv[j].w * wv[j].w;
-            P += p0; SP += fabs(P);
-            P += p1; SP += fabs(P);
-            P += p2; SP += fabs(P);
-            P += p3; SP += fabs(P);
-            A += (fabs(p0) + fabs(p1)) + (fabs(p2) + fabs(p3));
-        }
+#pragma unroll 4
+    for (int j = 0; j < seg / 4; j++) {
+        const float4 wv = w4[j], xv = x4[j];
+        const double p0 = (double)xv.x * wv.x, p1 = (double)xv.y * wv.y;
+        const double p2 = (double)xv.z * wv.z, p3 = (double)xv.w * wv.w;
+        P += p0; SP += fabs(P);
+        P += p1; SP += fabs(P);
+        P += p2; SP += fabs(P);
+        P += p3; SP += fabs(P);
+        A += (fabs(p0) + fabs(p1)) + (fabs(p2) + fabs(p3));
     }
     // exclusive scan of segment sums -> |prefix| bound of this segment
     double inc = P;
@@ -356,7 +376,7 @@ __global__ void __launch_bounds__(256) route_certify_warps(FastRouteArgs a, int 
 // Forward routing whose candidate probabilities come within a few ulps
 // recomputes every logit and the reference's softmax exactly.
 constexpr int FB_WARPS = 2;                  // tokens per block (two blocks fit an SM)
-constexpr int FB_CK = 64, FB_LD = FB_CK + 4;  // chain chunk (floats) and padded lane stride
+constexpr int FB_CK = XL_CK, FB_LD = XL_LD;  // chain chunk (floats) and padded lane stride
 constexpr int FB_ST = 4;                      // chunks in flight per lane
 
 __device__ __forceinline__ float warp_max(float v) {
@@ -367,39 +387,6 @@ __device__ __forceinline__ float warp_max(float v) {
 
 __host__ __device__ inline size_t fb_warp_smem(int E, int D) {
     return ((size_t)FB_ST * 32 * FB_LD * 4 + (size_t)D * 4 + (size_t)E * 6 * 4 + 15) & ~(size_t)15;
-}
-
-// Reference-order logit of one router row (exact_logit's chain), the row
-// streamed through this lane's FB_ST shared-memory chunk slots.
-__device__ float exact_logit_staged(const float *__restrict__ wrow, const float *xs, int D, float *slots) {
-    const int nch = D / FB_CK;
-    auto issue = [&](int ch) {
-        if (ch < nch) {
-            float *dst = slots + (ch % FB_ST) * 32 * FB_LD;
-#pragma unroll
-            for (int q = 0; q < FB_CK / 4; q++) xl_cp16(dst + 4 * q, wrow + ch * FB_CK + 4 * q);
-        }
-        asm volatile("cp.async.commit_group;" ::: "memory");
-    };
-#pragma unroll
-    for (int c = 0; c < FB_ST - 1; c++) issue(c);
-    float s = 0.0f;
-    for (int ch = 0; ch < nch; ch++) {
-        issue(ch + FB_ST - 1);  // its slot was read by chunk ch - 1
-        asm volatile("cp.async.wait_group %0;" ::"n"(FB_ST - 1) : "memory");
-        const float *wc = slots + (ch % FB_ST) * 32 * FB_LD, *xc = xs + ch * FB_CK;
-#pragma unroll
-        for (int k = 0; k < FB_CK; k += 4) {
-            const float4 w4 = *reinterpret_cast<const float4 *>(wc + k);
-            const float4 x4 = *reinterpret_cast<const float4 *>(xc + k);
-            s = __fadd_rn(s, __fmul_rn(x4.x, w4.x));
-            s = __fadd_rn(s, __fmul_rn(x4.y, w4.y));
-            s = __fadd_rn(s, __fmul_rn(x4.z, w4.z));
-            s = __fadd_rn(s, __fmul_rn(x4.w, w4.w));
-        }
-    }
-    asm volatile("cp.async.wait_group 0;" ::: "memory");
-    return s;
 }
 
 __global__ void __launch_bounds__(FB_WARPS * 32) route_fallback_warps(FastRouteArgs a) {
@@ -445,7 +432,7 @@ __global__ void __launch_bounds__(FB_WARPS * 32) route_fallback_warps(FastRouteA
             const int c = c0 + lane;
             if (c < nc) {
                 const int e = clist[c];
-                cv[c] = exact_logit_staged(a.W + (size_t)e * D, xs, D, slots);
+                cv[c] = exact_logit_lane<FB_ST>(a.W + (size_t)e * D, xs, D, slots);
                 cid[c] = e;
             }
         }
@@ -469,7 +456,7 @@ __global__ void __launch_bounds__(FB_WARPS * 32) route_fallback_warps(FastRouteA
                 for (int e0 = 0; e0 < E; e0 += 32) {
                     const int e = e0 + lane;
                     if (e < E) {
-                        cv[e] = exact_logit_staged(a.W + (size_t)e * D, xs, D, slots);
+                        cv[e] = exact_logit_lane<FB_ST>(a.W + (size_t)e * D, xs, D, slots);
                         cid[e] = e;
                     }
                 }
@@ -488,7 +475,7 @@ __global__ void __launch_bounds__(FB_WARPS * 32) route_fallback_warps(FastRouteA
                 nc = E;
             }
         }
-        for (int i = 0; i < K; i++) exchange_pass(cv, cid, cov, coid, nc, i, lane);
+        exchange_topk(cv, cid, cov, coid, nc, K, lane);
         uint32_t *io = a.idx + (size_t)t * K;
         float *wo = a.w + (size_t)t * K;
         if (mode == 2) {
@@ -559,8 +546,10 @@ __global__ void __launch_bounds__(FR_THREADS) route_select_fast(FastRouteArgs a)
     __shared__ float s_cv[1024], s_cov[1024];
     __shared__ int s_nc, s_full, s_wcnt[FR_WARPS];
 
+    RS_MARK(0)
     pdl_wait();
     DTRACE_WAITED(rf, 1)
+    RS_MARK(1)
     // one token per block
     {
     const int t = blockIdx.x;
@@ -635,6 +624,7 @@ __global__ void __launch_bounds__(FR_THREADS) route_select_fast(FastRouteArgs a)
     __syncthreads();
     }
     const bool warp_done = (E <= 32 * FW_PER_LANE) && s_mode == 0;  // weights already written
+    RS_MARK(2)
 
     if (s_mode != 0) {
         // ---- candidate recompute with the reference's exact chain --------
@@ -669,8 +659,13 @@ __global__ void __launch_bounds__(FR_THREADS) route_select_fast(FastRouteArgs a)
             __syncthreads();
         }
         const int nc = s_nc;
+        RS_MARK(5)
+#ifdef OFB_RS_TRACE
+        if (tid == 0 && blockIdx.x < 64) g_rs_tr[blockIdx.x][11] = (unsigned long long)nc;
+#endif
         exact_logits_block(a.W, D, xs, s_clist, nc, s_cv, wbuf, tid, FR_THREADS);
         __syncthreads();
+        RS_MARK(6)
         for (int c = tid; c < nc; c += FR_THREADS) {
             const int e = s_clist[c];
             val[e] = s_cv[c];
@@ -721,20 +716,24 @@ __global__ void __launch_bounds__(FR_THREADS) route_select_fast(FastRouteArgs a)
                 __syncthreads();
             }
         }
+        RS_MARK(7)
         if (wid == 0) {
             if (s_full) {
-                for (int i = 0; i < K; i++) exchange_pass(val, id, oval, oid, E, i, lane);
+                exchange_topk(val, id, oval, oid, E, K, lane);
                 if (lane == 0)
                     for (int q = 0; q < K; q++) s_top[q] = id[q];
             } else {
-                for (int i = 0; i < K; i++) exchange_pass(s_cv, s_cid, s_cov, s_coid, nc, i, lane);
+                exchange_topk(s_cv, s_cid, s_cov, s_coid, nc, K, lane);
+                RS_MARK(9)
                 if (lane == 0)
                     for (int q = 0; q < K; q++) s_top[q] = s_cid[q];
+                RS_MARK(10)
             }
         }
         __syncthreads();
     }
 
+    RS_MARK(3)
     // ---- weights --------------------------------------------------------------
     uint32_t *io = a.idx + (size_t)t * K;
     float *wo = a.w + (size_t)t * K;
@@ -769,6 +768,7 @@ __global__ void __launch_bounds__(FR_THREADS) route_select_fast(FastRouteArgs a)
         }
     }
     if (tid == 0 && a.stats && !warp_done) atomicAdd(&a.stats[s_mode], 1);
+    RS_MARK(4)
     __syncthreads();  // the plan below reuses the shared arrays
     }
 
@@ -998,8 +998,15 @@ int launch_route_fast(const float *W, const float *x, const float *gate_v, int T
     // rows: E router rows, the gate vector, then (when x is quantised) one
     // warp per 32-element sub-block of x
     const int rr_rows = E + 1 + (xq ? D / 32 : 0);
-    cudaError_t e = launch_pdl(route_rows_kernel, dim3((rr_rows + RR_WARPS - 1) / RR_WARPS, T),
-                               dim3(RR_WARPS * 32), 0, s, a);
+    // rows per block: 8 while the staged rows fit comfortably, fewer for wide rows
+    int rw = RR_WARPS;
+    while (rw > 1 && rr_smem(D, rw) > 120 * 1024) rw >>= 1;
+    const size_t rsm = rr_smem(D, rw);
+    if (rsm > 227 * 1024) { set_error("route_fast: d_model %d too large for the row kernel", D); return OFB_EUNSUPPORTED; }
+    static size_t rr_attr[64];
+    cudaError_t e = ensure_dyn_smem(route_rows_kernel, rsm, rr_attr);
+    if (e != cudaSuccess) return cuda_status(e, "route_rows smem attribute");
+    e = launch_pdl(route_rows_kernel, dim3((rr_rows + rw - 1) / rw, T), dim3(rw * 32), rsm, s, a);
     if (e == cudaSuccess) e = launch_pdl(route_select_fast, dim3(T), dim3(FR_THREADS), smem, s, a);
     if (e != cudaSuccess) return cuda_status(e, "route_fast launch");
     return OFB_OK;
