@@ -460,13 +460,14 @@ __global__ void __launch_bounds__(FD_THREADS, 1) decode_fused_kernel(FusedDecode
             const int p = u0 + S.start[sg] + m * S.c[sg], q = p / H;
             uint64_t *b = mb_up + (q == slot_first ? 0 : 1);
             const size_t src = (size_t)s_top[q] * exp4 + (size_t)(p - q * H) * rb4;
-            ax::bulk_g2s((mat ? upu : upg) + S.off[sg] + (size_t)m * S.as[sg], (mat ? a.up : a.gate) + src,
-                         (uint32_t)S.c[sg] * rb4, b);
+            ax::bulk_g2s_hint((mat ? upu : upg) + S.off[sg] + (size_t)m * S.as[sg], (mat ? a.up : a.gate) + src,
+                              (uint32_t)S.c[sg] * rb4, b, ax::l2_evict_first());
         }
     };
     auto issue_dn = [&](int q, int e) {
         ax::mbar_arrive_expect(mb_dn + q, nrow_out ? slab : 0u);
-        if (nrow_out) ax::bulk_g2s(dnp(q), a.down + (size_t)e * exp6 + (size_t)a0 * rb6, slab, mb_dn + q);
+        if (nrow_out)
+            ax::bulk_g2s_hint(dnp(q), a.down + (size_t)e * exp6 + (size_t)a0 * rb6, slab, mb_dn + q, ax::l2_evict_first());
     };
 
     // ---- step 0: static bytes, before waiting for the producer of x ----

@@ -263,8 +263,34 @@ __device__ __forceinline__ uint32_t bf2_bits(__nv_bfloat162 v) { return *reinter
 // Raw bytes of one matrix for one raw stage: Q4_K block b of 128 rows, one
 // 2D TMA box of 128 rows x 144 bytes, [row][144] in shared memory (header at
 // 0, quant chunk c of the block at 16 + 32c: elements 64c..64c+63).
+// L2 policy for bytes read once per call (expert weights): evict them first,
+// so the weight stream does not push the router, token rows and code out of L2.
+__device__ __forceinline__ uint64_t l2_evict_first() {
+    uint64_t pol;
+    asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
+    return pol;
+}
+// tma_tile2d with an L2 cache hint.
+__device__ __forceinline__ void tma_tile2d_hint(uint32_t dst, const CUtensorMap *map, int x, int y, uint64_t *bar,
+                                                uint64_t pol) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint"
+        " [%0], [%1, {%2, %3}], [%4], %5;" ::"r"(dst),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar)), "l"(pol)
+        : "memory");
+}
+// bulk_copy with an L2 cache hint.
+__device__ __forceinline__ void bulk_copy_hint(void *dst, const void *src, uint32_t bytes, uint64_t *bar, uint64_t pol) {
+    mbar_expect_tx(bar, bytes);
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;" ::"r"(
+            smem_u32(dst)),
+        "l"(src), "r"(bytes), "r"(smem_u32(bar)), "l"(pol)
+        : "memory");
+}
+
 __device__ __forceinline__ void q4_issue(const CUtensorMap *map, int row0, uint32_t dst, int b, uint64_t *bar) {
-    tma_tile2d(dst, map, b * Q4K_BYTES, row0, bar);
+    tma_tile2d_hint(dst, map, b * Q4K_BYTES, row0, bar, l2_evict_first());
 }
 
 // A dequantising thread owns one (row r, nibble half hh) of one matrix: in
@@ -764,8 +790,8 @@ __global__ void __launch_bounds__(DN_THREADS, 1)
                 const int sb = k & 1;
                 if (k >= 2) ok = mbar_wait(&R.sempty[sb], ((k >> 1) - 1) & 1);
                 if (!ok) break;
-                bulk_copy(slab + sb * slab_bytes, (e == a.E ? a.down_sh : a.down + e * exp_bytes) + (size_t)n0 * row_bytes,
-                          slab_bytes, &R.sfull[sb]);
+                bulk_copy_hint(slab + sb * slab_bytes, (e == a.E ? a.down_sh : a.down + e * exp_bytes) + (size_t)n0 * row_bytes,
+                               slab_bytes, &R.sfull[sb], l2_evict_first());
             }
         }
     } else if (warp == 0) {
