@@ -303,6 +303,8 @@ WorkspaceLayout workspace_layout(const ofb_moe_config *c, int max_tokens) {
     // contiguous layout (the large-batch router too), else the decode sizes
     L.cand = take((inter ? Tf : T) * (E + 1) * 16);
     L.norms = take(inter ? 0 : (T + E) * (size_t)(c->d_model / 64) * 4);
+    const size_t Ts = T > (size_t)FAST_ROUTE_MAX_T ? (T < (size_t)ROUTE_SPLIT_MAX_T ? T : ROUTE_SPLIT_MAX_T - 1) : 0;
+    L.segsum = take(inter ? 0 : Ts * E * (size_t)(c->d_model / 64) * 4);
     L.xq = take((Tf > Td ? Tf : Td) * xq_stride(c->d_model));
     // route tickets [64] + [1], route stats [3], pad [1], down-combine tickets [D/4]
     // ... then the prefill error flag [1]
@@ -389,7 +391,7 @@ int run_moe_layer(const ofb_moe_config *cfg, const ofb_moe_weights *wt, const fl
         int *ctr = (int *)(base + L.counters);
         if ((st = launch_route_fast_large(wt->router, x, T, D, E, K, cfg->routing, cfg->renorm,
                                           (double2 *)(base + L.cand), (float *)(base + L.norms),
-                                          (int *)(base + L.logits), ctr, ctr + FAST_ROUTE_MAX_T + 1, idx, w, s)))
+                                          (float *)(base + L.segsum), (int *)(base + L.logits), ctr, ctr + FAST_ROUTE_MAX_T + 1, idx, w, s)))
             return st;
         mark(1);
         if ((st = launch_plan(p, (int *)(base + L.phist), plan_tiles, prefill_max_tiles(T, K, E), s))) return st;
@@ -563,7 +565,7 @@ extern "C" int ofb_route_certified(const ofb_moe_config *cfg, const float *route
                                  idx, w, (float *)(ws->base + L.gsc), nullptr, nullptr, s);
     return launch_route_fast_large(router, x, n_tokens, D, E, K, cfg->routing, cfg->renorm,
                                    (double2 *)(ws->base + L.cand), (float *)(ws->base + L.norms),
-                                   (int *)(ws->base + L.logits), ctr, ctr + FAST_ROUTE_MAX_T + 1, idx, w, s);
+                                   (float *)(ws->base + L.segsum), (int *)(ws->base + L.logits), ctr, ctr + FAST_ROUTE_MAX_T + 1, idx, w, s);
 }
 
 extern "C" int ofb_moe_forward(const ofb_moe_config *cfg, const ofb_moe_weights *w,

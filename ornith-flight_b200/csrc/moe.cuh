@@ -45,6 +45,7 @@ struct WorkspaceLayout {
     size_t phist;     // per-CTA expert counts of the many-CTA plan (plan_hist_ints)
     size_t cand;      // fast routing: (approximate logit, bound) per (token, row)
     size_t norms;     // large-batch routing: segment norms of x rows and router rows
+    size_t segsum;    // large-batch routing below ROUTE_SPLIT_MAX_T tokens: segment sums [seg][token][expert]
     size_t xq;        // decode: quantised activations [T][xq_stride(D)]
     size_t xb, hb;    // prefill: bf16 x rows [A][D] and h rows [A][H], both in slot order
     size_t tiles;     // prefill: tile count + (slot, start, n) per tile
@@ -102,8 +103,11 @@ int launch_down_q(const LayerArgs &a, int *tickets, int max_slots, cudaStream_t 
 // fallback for the tokens it leaves (flagged list, T ints; *n_flagged is
 // scratch). norms: scratch of (T + E) * d_model / 64 floats.
 int launch_route_fast_large(const float *W, const float *x, int T, int D, int E, int K, int routing, int renorm,
-                            double2 *cand, float *norms, int *flagged, int *n_flagged, int *stats, uint32_t *idx,
-                            float *w, cudaStream_t s);
+                            double2 *cand, float *norms, float *segsum, int *flagged, int *n_flagged, int *stats,
+                            uint32_t *idx, float *w, cudaStream_t s);
+// Tokens below which the large-batch router splits its GEMM over segments
+// (segsum holds T * E * d_model / 64 floats for those batches).
+constexpr int ROUTE_SPLIT_MAX_T = 1024;
 int launch_route_fast(const float *W, const float *x, const float *gate_v, int T, int D, int E, int K,
                       int routing, int renorm, double2 *cand, int *all_cnt, int *stats,
                       uint32_t *idx, float *w, float *gsc, unsigned char *xq, const PlanArgs *plan,

@@ -960,6 +960,105 @@ __global__ void __launch_bounds__(RG_THREADS) router_bound_gemm(const float *__r
     }
 }
 
+// ---- batches below 1024 tokens: the same (L~, B), split over segments -------
+// router_bound_gemm walks the 32 segments of a tile in order, so a few
+// hundred tokens give ~128 CTAs each with a long serial loop. The segment
+// sums c_s do not depend on each other: router_seg_gemm computes them with
+// one CTA per (64-token tile, 64-expert tile, segment pair) - the same fp32
+// FMA chain per segment, in the same k order - into segsum[s][t][e], and
+// router_seg_scan then runs router_bound_gemm's per-segment recurrence (the
+// fp64 sum and the bound terms, the same operations in the same order) for
+// one (token, expert) per thread. Results are identical to router_bound_gemm.
+constexpr int RS_SEGS = 2;  // segments per CTA (the two cp.async stages)
+__global__ void __launch_bounds__(RG_THREADS) router_seg_gemm(const float *__restrict__ W, const float *__restrict__ x,
+                                                              int T, int D, int E, float *__restrict__ segsum) {
+    constexpr int TI = 8, TJ = 4, TT = 8 * TI, TE = 16 * TJ;
+    extern __shared__ __align__(16) float rg_sm[];
+    float *xs = rg_sm;                   // [2][TT][RG_LD]
+    float *ws = rg_sm + 2 * TT * RG_LD;  // [2][TE][RG_LD]
+    const int tid = threadIdx.x, ty = tid >> 4, tx = tid & 15;
+    const int t0 = blockIdx.x * TT, e0 = blockIdx.y * TE, sg0 = blockIdx.z * RS_SEGS;
+    const int nseg = D / RG_SEG, ns = min(RS_SEGS, nseg - sg0);
+    auto issue = [&](int sg, int buf) {
+#pragma unroll
+        for (int q = 0; q < (TT * 16) / RG_THREADS; q++) {
+            const int c = tid + RG_THREADS * q, r = c >> 4, kq = c & 15;
+            const int tr = min(t0 + r, T - 1);
+            rg_cp16(xs + (buf * TT + r) * RG_LD + 4 * kq, x + (size_t)tr * D + sg * RG_SEG + 4 * kq, t0 + r < T);
+        }
+#pragma unroll
+        for (int q = 0; q < (TE * 16) / RG_THREADS; q++) {
+            const int c = tid + RG_THREADS * q, r = c >> 4, kq = c & 15;
+            const int er = min(e0 + r, E - 1);
+            rg_cp16(ws + (buf * TE + r) * RG_LD + 4 * kq, W + (size_t)er * D + sg * RG_SEG + 4 * kq, e0 + r < E);
+        }
+        asm volatile("cp.async.commit_group;" ::: "memory");
+    };
+    for (int q = 0; q < ns; q++) issue(sg0 + q, q);
+    for (int q = 0; q < ns; q++) {
+        if (q + 1 < ns) asm volatile("cp.async.wait_group 1;" ::: "memory");
+        else asm volatile("cp.async.wait_group 0;" ::: "memory");
+        __syncthreads();
+        float acc[TI][TJ];
+#pragma unroll
+        for (int i = 0; i < TI; i++)
+#pragma unroll
+            for (int j = 0; j < TJ; j++) acc[i][j] = 0.f;
+        const float *xb = xs + (q * TT + ty) * RG_LD, *wb = ws + (q * TE + tx) * RG_LD;
+#pragma unroll 2
+        for (int k = 0; k < RG_SEG; k += 4) {
+            float4 b[TJ];
+#pragma unroll
+            for (int j = 0; j < TJ; j++) b[j] = *reinterpret_cast<const float4 *>(wb + 16 * j * RG_LD + k);
+#pragma unroll
+            for (int i = 0; i < TI; i++) {
+                const float4 av = *reinterpret_cast<const float4 *>(xb + 8 * i * RG_LD + k);
+#pragma unroll
+                for (int j = 0; j < TJ; j++) {
+                    acc[i][j] = fmaf(av.x, b[j].x, acc[i][j]);
+                    acc[i][j] = fmaf(av.y, b[j].y, acc[i][j]);
+                    acc[i][j] = fmaf(av.z, b[j].z, acc[i][j]);
+                    acc[i][j] = fmaf(av.w, b[j].w, acc[i][j]);
+                }
+            }
+        }
+        float *out = segsum + (size_t)(sg0 + q) * T * E;
+#pragma unroll
+        for (int i = 0; i < TI; i++) {
+            const int t = t0 + ty + 8 * i;
+            if (t >= T) continue;
+#pragma unroll
+            for (int j = 0; j < TJ; j++) {
+                const int e = e0 + tx + 16 * j;
+                if (e < E) out[(size_t)t * E + e] = acc[i][j];
+            }
+        }
+    }
+}
+
+__global__ void __launch_bounds__(256) router_seg_scan(const float *__restrict__ segsum, const float *__restrict__ nx,
+                                                       const float *__restrict__ nw, int T, int D, int E,
+                                                       double bound_scale, double ngam, double gam64,
+                                                       double2 *__restrict__ cand) {
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= T * E) return;
+    const int t = i / E, e = i - t * E, nseg = D / RG_SEG;
+    const float g64 = (float)gam64;
+    double P = 0.0;
+    float SP = 0.f, Ab = 0.f;
+    for (int sg = 0; sg < nseg; sg++) {
+        const float c = __ldg(segsum + (size_t)sg * T * E + i);
+        const float as = __fmul_ru(__ldg(nx + (size_t)t * nseg + sg), __ldg(nw + (size_t)e * nseg + sg)), a0 = Ab;
+        const float pb = __fmaf_ru(g64, a0, __double2float_ru(fabs(P)));
+        SP = __fmaf_ru(64.f, __fadd_ru(pb, as), SP);
+        Ab = __fadd_ru(a0, as);
+        P += (double)c;
+    }
+    const double A = Ab;
+    const double B = bound_scale * (A + (double)SP + ngam * A) + (1.0 + 0x1.0p-9) * gam64 * A + 0x1.0p-60;
+    cand[i] = make_double2(P, B);
+}
+
 template <int TI, int TJ>
 static void launch_rg(const float *W, const float *x, const float *nx, const float *nw, int T, int D, int E,
                       double bound_scale, double ngam, double gam64, double2 *cand, cudaStream_t s) {
@@ -1013,8 +1112,8 @@ int launch_route_fast(const float *W, const float *x, const float *gate_v, int T
 }
 
 int launch_route_fast_large(const float *W, const float *x, int T, int D, int E, int K, int routing, int renorm,
-                            double2 *cand, float *norms, int *flagged, int *n_flagged, int *stats, uint32_t *idx,
-                            float *w, cudaStream_t s) {
+                            double2 *cand, float *norms, float *segsum, int *flagged, int *n_flagged, int *stats,
+                            uint32_t *idx, float *w, cudaStream_t s) {
     if (D % RG_SEG) { set_error("route_fast_large: d_model must be a multiple of %d", RG_SEG); return OFB_EUNSUPPORTED; }
     FastRouteArgs a;
     a.W = W; a.x = x; a.gate_v = nullptr;
@@ -1035,8 +1134,17 @@ int launch_route_fast_large(const float *W, const float *x, int T, int D, int E,
     const int nseg = D / RG_SEG;
     segment_norms_kernel<<<grid_for((uint64_t)T * nseg / 2, 8, 148 * 16), 256, 0, s>>>(x, T, D, nx);
     segment_norms_kernel<<<grid_for((uint64_t)E * nseg / 2, 8, 148 * 16), 256, 0, s>>>(W, E, D, nw);
-    if (T >= 1024) launch_rg<8, 4>(W, x, nx, nw, T, D, E, a.bound_scale, a.ngam, gam64, cand, s);
-    else launch_rg<2, 2>(W, x, nx, nw, T, D, E, a.bound_scale, a.ngam, gam64, cand, s);
+    if (T >= ROUTE_SPLIT_MAX_T || !segsum) {
+        if (T >= 1024) launch_rg<8, 4>(W, x, nx, nw, T, D, E, a.bound_scale, a.ngam, gam64, cand, s);
+        else launch_rg<2, 2>(W, x, nx, nw, T, D, E, a.bound_scale, a.ngam, gam64, cand, s);
+    } else {
+        const int ops = rg_smem_ops(8, 4);
+        cudaFuncSetAttribute(router_seg_gemm, cudaFuncAttributeMaxDynamicSharedMemorySize, ops);
+        router_seg_gemm<<<dim3((T + 63) / 64, (E + 63) / 64, (nseg + RS_SEGS - 1) / RS_SEGS), RG_THREADS, ops, s>>>(
+            W, x, T, D, E, segsum);
+        router_seg_scan<<<(T * E + 255) / 256, 256, 0, s>>>(segsum, nx, nw, T, D, E, a.bound_scale, a.ngam, gam64,
+                                                           cand);
+    }
     if (E > 32 * FW_PER_LANE) { set_error("route_fast_large: at most %d experts", 32 * FW_PER_LANE); return OFB_EUNSUPPORTED; }
     cudaError_t e = cudaMemsetAsync(n_flagged, 0, sizeof(int), s);
     if (e != cudaSuccess) return cuda_status(e, "route_fast_large memset");
