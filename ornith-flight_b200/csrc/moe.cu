@@ -62,10 +62,16 @@ __global__ void __launch_bounds__(1024) plan_scan_kernel(PlanArgs p, int *__rest
     const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5, E = p.E;
     int c = 0;
     if (tid < E)
-        for (int b = 0; b < nb; b++) {
-            const int v = hist[(size_t)b * E + tid];
-            hist[(size_t)b * E + tid] = c;
-            c += v;
+        for (int b0 = 0; b0 < nb; b0 += 16) {
+            // 16 counts loaded before any store (independent loads in flight)
+            int v[16];
+#pragma unroll
+            for (int q = 0; q < 16; q++) v[q] = b0 + q < nb ? hist[(size_t)(b0 + q) * E + tid] : 0;
+#pragma unroll
+            for (int q = 0; q < 16; q++) {
+                if (b0 + q < nb) hist[(size_t)(b0 + q) * E + tid] = c;
+                c += v[q];
+            }
         }
     // exclusive scans over experts of (has slot, count, tiles)
     const int nt = (c + PF_NMAX - 1) / PF_NMAX;
@@ -389,15 +395,14 @@ int run_moe_layer(const ofb_moe_config *cfg, const ofb_moe_weights *wt, const fl
         // large batches: certified routing from a bounded fp32 GEMM; the last
         // selection block builds the plan
         int *ctr = (int *)(base + L.counters);
-        if ((st = launch_route_fast_large(wt->router, x, T, D, E, K, cfg->routing, cfg->renorm,
+        // the certify warps also compute the shared-expert gates
+        if ((st = launch_route_fast_large(wt->router, x, p.has_shared && p.shared_gate ? p.gate_v : nullptr, p.gsc, T,
+                                          D, E, K, cfg->routing, cfg->renorm,
                                           (double2 *)(base + L.cand), (float *)(base + L.norms),
                                           (float *)(base + L.segsum), (int *)(base + L.logits), ctr, ctr + FAST_ROUTE_MAX_T + 1, idx, w, s)))
             return st;
         mark(1);
         if ((st = launch_plan(p, (int *)(base + L.phist), plan_tiles, prefill_max_tiles(T, K, E), s))) return st;
-        if (p.has_shared && p.shared_gate)
-            shared_gate_kernel<<<(T + 7) / 8, 256, 0, s>>>(x, p.gate_v, T, D, p.gsc);
-        OFB_CHECK_LAUNCH("plan");
         mark(2);
     } else {
         if (given_idx) {
@@ -563,7 +568,7 @@ extern "C" int ofb_route_certified(const ofb_moe_config *cfg, const float *route
         return launch_route_fast(router, x, nullptr, n_tokens, D, E, K, cfg->routing, cfg->renorm,
                                  (double2 *)(ws->base + L.cand), ctr + FAST_ROUTE_MAX_T, ctr + FAST_ROUTE_MAX_T + 1,
                                  idx, w, (float *)(ws->base + L.gsc), nullptr, nullptr, s);
-    return launch_route_fast_large(router, x, n_tokens, D, E, K, cfg->routing, cfg->renorm,
+    return launch_route_fast_large(router, x, nullptr, nullptr, n_tokens, D, E, K, cfg->routing, cfg->renorm,
                                    (double2 *)(ws->base + L.cand), (float *)(ws->base + L.norms),
                                    (float *)(ws->base + L.segsum), (int *)(ws->base + L.logits), ctr, ctr + FAST_ROUTE_MAX_T + 1, idx, w, s);
 }

@@ -102,8 +102,8 @@ int launch_down_q(const LayerArgs &a, int *tickets, int max_slots, cudaStream_t 
 // rigorous bounds, the same per-token certificate (one warp per token), exact
 // fallback for the tokens it leaves (flagged list, T ints; *n_flagged is
 // scratch). norms: scratch of (T + E) * d_model / 64 floats.
-int launch_route_fast_large(const float *W, const float *x, int T, int D, int E, int K, int routing, int renorm,
-                            double2 *cand, float *norms, float *segsum, int *flagged, int *n_flagged, int *stats,
+int launch_route_fast_large(const float *W, const float *x, const float *gate_v, float *gsc, int T, int D, int E,
+                            int K, int routing, int renorm, double2 *cand, float *norms, float *segsum, int *flagged, int *n_flagged, int *stats,
                             uint32_t *idx, float *w, cudaStream_t s);
 // Tokens below which the large-batch router splits its GEMM over segments
 // (segsum holds T * E * d_model / 64 floats for those batches).

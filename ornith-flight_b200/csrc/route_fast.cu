@@ -363,6 +363,19 @@ __global__ void __launch_bounds__(256) route_certify_warps(FastRouteArgs a, int 
     if (t >= a.T) return;
     const bool ok = certify_token_warp(a, t, sel[wid], nullptr, nullptr);
     if (!ok && lane == 0) flagged[atomicAdd(n_flagged, 1)] = t;
+    if (a.gate_v && a.gsc) {
+        // the token's shared-expert gate sigmoid(x . v), as shared_gate_kernel
+        // computes it (same order), while this warp has the token
+        const float4 *x4 = reinterpret_cast<const float4 *>(a.x + (size_t)t * a.D);
+        const float4 *v4 = reinterpret_cast<const float4 *>(a.gate_v);
+        float z = 0.f;
+        for (int i = lane; i < a.D / 4; i += 32) {
+            const float4 p = __ldg(x4 + i), q = __ldg(v4 + i);
+            z += p.x * q.x + p.y * q.y + p.z * q.z + p.w * q.w;
+        }
+        z = warp_sum(z);
+        if (lane == 0) a.gsc[t] = 1.0f / (1.0f + expf(-z));
+    }
 }
 
 // ---- large batches: the tokens the warp certificate left, one warp each ----
@@ -1111,19 +1124,19 @@ int launch_route_fast(const float *W, const float *x, const float *gate_v, int T
     return OFB_OK;
 }
 
-int launch_route_fast_large(const float *W, const float *x, int T, int D, int E, int K, int routing, int renorm,
-                            double2 *cand, float *norms, float *segsum, int *flagged, int *n_flagged, int *stats,
+int launch_route_fast_large(const float *W, const float *x, const float *gate_v, float *gsc, int T, int D, int E,
+                            int K, int routing, int renorm, double2 *cand, float *norms, float *segsum, int *flagged, int *n_flagged, int *stats,
                             uint32_t *idx, float *w, cudaStream_t s) {
     if (D % RG_SEG) { set_error("route_fast_large: d_model must be a multiple of %d", RG_SEG); return OFB_EUNSUPPORTED; }
     FastRouteArgs a;
-    a.W = W; a.x = x; a.gate_v = nullptr;
+    a.W = W; a.x = x; a.gate_v = gate_v;  // with gsc: the shared-expert gates, by the certify warps
     a.T = T; a.D = D; a.E = E; a.K = K; a.routing = routing; a.renorm = renorm;
     const double u = 0x1.0p-24, n = (double)D;
     a.bound_scale = (1.0 + 0x1.0p-9) * u;
     a.ngam = n * (n * u / (1.0 - n * u));
     const double gam64 = 64.0 * u / (1.0 - 64.0 * u);
     a.cand = cand; a.all_cnt = nullptr; a.stats = stats;
-    a.idx = idx; a.w = w; a.gsc = nullptr; a.xq = nullptr;
+    a.idx = idx; a.w = w; a.gsc = gate_v ? gsc : nullptr; a.xq = nullptr;
     memset(&a.plan, 0, sizeof(a.plan));
     a.flagged = flagged;
     a.n_flagged = n_flagged;
