@@ -8,7 +8,7 @@ namespace ofb {
 // ---- plan ------------------------------------------------------------------
 // Device histogram of kept assignments per expert, exclusive scan, and the
 // CSR slot list. Works for any block size (E <= 1024); scratch in `sm`
-// (2*1024 ints + 64). Called by plan_kernel (large T) and by the last block of
+// (2*1024 ints + 64). Called by the last block of
 // the fast routing kernel (small T).
 static __device__ void build_plan(const PlanArgs &p, int *cnt, int *cursor, int *wsum) {
     const int tid = threadIdx.x, nt = blockDim.x, lane = tid & 31, wid = tid >> 5, nw = nt >> 5;
