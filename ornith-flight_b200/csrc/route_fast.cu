@@ -977,12 +977,12 @@ __global__ void __launch_bounds__(RG_THREADS) router_bound_gemm(const float *__r
 // router_bound_gemm walks the 32 segments of a tile in order, so a few
 // hundred tokens give ~128 CTAs each with a long serial loop. The segment
 // sums c_s do not depend on each other: router_seg_gemm computes them with
-// one CTA per (64-token tile, 64-expert tile, segment pair) - the same fp32
+// one CTA per (64-token tile, 64-expert tile, segment) - the same fp32
 // FMA chain per segment, in the same k order - into segsum[s][t][e], and
 // router_seg_scan then runs router_bound_gemm's per-segment recurrence (the
 // fp64 sum and the bound terms, the same operations in the same order) for
 // one (token, expert) per thread. Results are identical to router_bound_gemm.
-constexpr int RS_SEGS = 2;  // segments per CTA (the two cp.async stages)
+constexpr int RS_SEGS = 1;  // segments per CTA (up to two cp.async stages)
 __global__ void __launch_bounds__(RG_THREADS) router_seg_gemm(const float *__restrict__ W, const float *__restrict__ x,
                                                               int T, int D, int E, float *__restrict__ segsum) {
     constexpr int TI = 8, TJ = 4, TT = 8 * TI, TE = 16 * TJ;
@@ -1059,9 +1059,15 @@ __global__ void __launch_bounds__(256) router_seg_scan(const float *__restrict__
     const float g64 = (float)gam64;
     double P = 0.0;
     float SP = 0.f, Ab = 0.f;
+    // this expert's segment norms, 16 bytes at a time (a warp's threads are
+    // nseg floats apart, so one float per load would touch a sector each)
+    const float4 *nw4 = reinterpret_cast<const float4 *>(nw + (size_t)e * nseg);
+    float4 wq = make_float4(0.f, 0.f, 0.f, 0.f);
     for (int sg = 0; sg < nseg; sg++) {
+        if ((sg & 3) == 0) wq = __ldg(nw4 + (sg >> 2));
+        const float wn = (sg & 3) == 0 ? wq.x : (sg & 3) == 1 ? wq.y : (sg & 3) == 2 ? wq.z : wq.w;
         const float c = __ldg(segsum + (size_t)sg * T * E + i);
-        const float as = __fmul_ru(__ldg(nx + (size_t)t * nseg + sg), __ldg(nw + (size_t)e * nseg + sg)), a0 = Ab;
+        const float as = __fmul_ru(__ldg(nx + (size_t)t * nseg + sg), wn), a0 = Ab;
         const float pb = __fmaf_ru(g64, a0, __double2float_ru(fabs(P)));
         SP = __fmaf_ru(64.f, __fadd_ru(pb, as), SP);
         Ab = __fadd_ru(a0, as);
